@@ -1,0 +1,428 @@
+// attend_bf16.cu -- absorbed MLA decode attention over a bf16 latent state on
+// sm_100a: TMA streams 64-row KV tiles into shared memory, tcgen05 computes the
+// scores S^T[64 rows x 16 heads] and the mix O^T[512 x 16 heads] into tensor
+// memory, and four softmax warps run an online softmax between the two MMAs.
+//
+// Reference semantics: src/mla_compressed_state.c:132-148 (attend core of
+// kvl_mla_decode_compressed_bf16).  Differences that are format choices of
+// this build: the cached rows are bf16 (the reference keeps fp32 rows), the
+// absorbed query is rounded to bf16 for the tensor core, the probabilities are
+// rounded to bf16 for the P.V MMA, and accumulation is fp32 instead of double.
+//
+// Roles (256 threads, one CTA per SM):
+//   warp 0      TMA producer: latent ring (10 slots x 16 KB) and rope ring
+//               (3 slots x 8 KB)
+//   warp 1      TMEM owner and tcgen05 issuer
+//   warp 2      query loader: fp32 absorbed query -> bf16 SW128 tile, per segment
+//   warps 4-7   softmax + epilogue (TMEM subpartitions 0-3)
+#include "attend_common.cuh"
+#include "sm100.cuh"
+
+namespace kvl {
+namespace bf16dec {
+
+constexpr int kLatSlots = 10;
+constexpr int kRopeSlots = 3;
+constexpr uint32_t kLatSlotBytes = 16384;  // 64 rows x 128 dims: two SW128 boxes
+constexpr uint32_t kRopeSlotBytes = 8192;  // 64 rows x 64 dims: one SW128 box
+constexpr uint32_t kQBytes = 9 * 2048;     // 16 heads x 576: nine SW128 boxes of 16 rows
+constexpr uint32_t kPBytes = 2048;         // 16 heads x 64 rows, 8x16B core matrices
+constexpr uint32_t OFF_LAT = 0;
+constexpr uint32_t OFF_ROPE = OFF_LAT + kLatSlots * kLatSlotBytes;
+constexpr uint32_t OFF_Q = OFF_ROPE + kRopeSlots * kRopeSlotBytes;
+constexpr uint32_t OFF_P = OFF_Q + 2 * kQBytes;
+constexpr uint32_t OFF_BAR = OFF_P + 2 * kPBytes;
+
+struct Bars {
+  uint64_t lat_full[kLatSlots], lat_empty[kLatSlots];
+  uint64_t rope_full[kRopeSlots], rope_empty[kRopeSlots];
+  uint64_t q_full[2], q_empty[2];
+  uint64_t s_full[2], s_empty[2];
+  uint64_t p_full[2], p_empty[2];
+  uint64_t o_full, o_empty, drain;
+  uint32_t tmem_base;
+  int abort;
+  float red[4][kHeads];
+};
+
+constexpr uint32_t kSmemBytes = OFF_BAR + sizeof(Bars) + 1024;  // + alignment slack
+static_assert(OFF_Q % 1024 == 0 && OFF_P % 1024 == 0 && OFF_ROPE % 1024 == 0, "align");
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+
+constexpr uint32_t kTmemCols = 128;  // S: 2 x 16 cols; O: 4 x 16 cols at col 32
+constexpr uint32_t kColO = 32;
+constexpr uint32_t kThreads = 256;
+
+}  // namespace bf16dec
+
+using namespace bf16dec;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    mla_attend_bf16_kernel(const __grid_constant__ AttendParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  Bars *B = reinterpret_cast<Bars *>(smem + OFF_BAR);
+  const uint32_t s_base = smem_u32(smem);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int seg_lo = p.cta_seg[blockIdx.x];
+  const int seg_hi = p.cta_seg[blockIdx.x + 1];
+  volatile int *abort = &B->abort;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kLatSlots; ++i) { mbar_init(&B->lat_full[i], 1); mbar_init(&B->lat_empty[i], 1); }
+    for (int i = 0; i < kRopeSlots; ++i) { mbar_init(&B->rope_full[i], 1); mbar_init(&B->rope_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B->q_full[i], 1);
+      mbar_init(&B->q_empty[i], 1);
+      mbar_init(&B->s_full[i], 1);
+      mbar_init(&B->s_empty[i], 4);
+      mbar_init(&B->p_full[i], 4);
+      mbar_init(&B->p_empty[i], 1);
+    }
+    mbar_init(&B->o_full, 1);
+    mbar_init(&B->o_empty, 4);
+    mbar_init(&B->drain, 1);
+    B->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&B->tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = B->tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_kv);
+      uint32_t g = 0, n_lat = 0, n_rope = 0;
+      bool ok = true;
+      for (int si = seg_lo; si < seg_hi && ok; ++si) {
+        const AttendSegment sg = p.segs[si];
+        const long long row0 = p.seq_row0[sg.seq] + sg.tok_begin;
+        const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
+        for (int t = 0; t < nt && ok; ++t, ++g) {
+          const int32_t y = static_cast<int32_t>(row0 + static_cast<long long>(kTileTok) * t);
+          for (int c = 0; c < 4 && ok; ++c) {
+            const uint32_t li = 4 * g + c, ls = li % kLatSlots, lu = li / kLatSlots;
+            ok = mbar_wait(&B->lat_empty[ls], (lu & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+            if (!ok) break;
+            uint8_t *dst = smem + OFF_LAT + ls * kLatSlotBytes;
+            mbar_arrive_expect_tx(&B->lat_full[ls], kLatSlotBytes);
+            tma_load_2d(dst, &p.tm_kv, &B->lat_full[ls], 128 * c, y);
+            tma_load_2d(dst + 8192, &p.tm_kv, &B->lat_full[ls], 128 * c + 64, y);
+            n_lat = li + 1;
+          }
+          if (!ok) break;
+          const uint32_t rs = g % kRopeSlots, ru = g / kRopeSlots;
+          ok = mbar_wait(&B->rope_empty[rs], (ru & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&B->rope_full[rs], kRopeSlotBytes);
+          tma_load_2d(smem + OFF_ROPE + rs * kRopeSlotBytes, &p.tm_kv, &B->rope_full[rs], kLatent, y);
+          n_rope = g + 1;
+        }
+      }
+      if (!ok) {
+        // Drain: the most recent load issued into each slot must land before
+        // the CTA exits (earlier ones completed before the slot was reissued).
+        for (uint32_t s = 0; s < kLatSlots && s < n_lat; ++s) {
+          const uint32_t last = s + kLatSlots * ((n_lat - 1 - s) / kLatSlots);
+          drain_wait(&B->lat_full[s], (last / kLatSlots) & 1, p.err);
+        }
+        for (uint32_t s = 0; s < kRopeSlots && s < n_rope; ++s) {
+          const uint32_t last = s + kRopeSlots * ((n_rope - 1 - s) / kRopeSlots);
+          drain_wait(&B->rope_full[s], (last / kRopeSlots) & 1, p.err);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = idesc_f16(1, 1, 0, 0, 64, kHeads);
+      constexpr uint32_t idesc_pv = idesc_f16(1, 1, 1, 0, 128, kHeads);
+      uint32_t g = 0;
+      int seg_i = 0;
+      bool ok = true;
+      auto issue_pv = [&](uint32_t gp, bool first, int segi) -> bool {
+        const uint32_t pb = gp & 1;
+        if (!mbar_wait(&B->p_full[pb], (gp >> 1) & 1, abort, p.err, ERR_TIMEOUT_FULL)) return false;
+        if (first && segi > 0)
+          if (!mbar_wait(&B->o_empty, (segi - 1) & 1, abort, p.err, ERR_TIMEOUT_FULL)) return false;
+        tc_fence_after();
+        const uint32_t p_addr = s_base + OFF_P + pb * kPBytes;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t ls = (4 * gp + c) % kLatSlots;
+          const uint32_t a_addr = s_base + OFF_LAT + ls * kLatSlotBytes;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t a = smem_desc(a_addr + kk * 2048, 8192, 1024, LAYOUT_SW128);
+            const uint64_t b = smem_desc(p_addr + kk * 256, 128, 1024, LAYOUT_INTERLEAVE);
+            mma_f16_ss(tmem + kColO + 16 * c, a, b, idesc_pv, (first && kk == 0) ? 0u : 1u);
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) mma_commit(&B->lat_empty[(4 * gp + c) % kLatSlots]);
+        mma_commit(&B->p_empty[pb]);
+        return true;
+      };
+      for (int si = seg_lo; si < seg_hi && ok; ++si, ++seg_i) {
+        const AttendSegment sg = p.segs[si];
+        const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
+        const uint32_t qb = seg_i & 1;
+        ok = mbar_wait(&B->q_full[qb], (seg_i >> 1) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+        const uint32_t q_addr = s_base + OFF_Q + qb * kQBytes;
+        for (int t = 0; t < nt && ok; ++t, ++g) {
+          const uint32_t sb = g & 1;
+          ok = mbar_wait(&B->s_empty[sb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+          for (int c = 0; c < 4 && ok; ++c) {
+            const uint32_t li = 4 * g + c;
+            ok = mbar_wait(&B->lat_full[li % kLatSlots], (li / kLatSlots) & 1, abort, p.err,
+                           ERR_TIMEOUT_FULL);
+          }
+          const uint32_t rs = g % kRopeSlots;
+          if (ok) ok = mbar_wait(&B->rope_full[rs], (g / kRopeSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll 1
+          for (int k = 0; k < 9; ++k) {
+            const uint32_t a_box = (k < 8) ? s_base + OFF_LAT + ((4 * g + (k >> 1)) % kLatSlots) * kLatSlotBytes +
+                                                 (k & 1) * 8192
+                                           : s_base + OFF_ROPE + rs * kRopeSlotBytes;
+            const uint32_t b_box = q_addr + k * 2048;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t a = smem_desc(a_box + kk * 32, 16, 1024, LAYOUT_SW128);
+              const uint64_t b = smem_desc(b_box + kk * 32, 16, 1024, LAYOUT_SW128);
+              mma_f16_ss(tmem + sb * 16, a, b, idesc_qk, (k | kk) ? 1u : 0u);
+            }
+          }
+          mma_commit(&B->s_full[sb]);
+          mma_commit(&B->rope_empty[rs]);
+          if (t == nt - 1) mma_commit(&B->q_empty[qb]);
+          if (t > 0) ok = issue_pv(g - 1, t == 1, seg_i);
+        }
+        if (!ok) break;
+        ok = issue_pv(g - 1, nt == 1, seg_i);
+        if (ok) mma_commit(&B->o_full);
+      }
+      // All issued tensor-core work must finish before TMEM is released.
+      mma_commit(&B->drain);
+      drain_wait(&B->drain, 0, p.err);
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ query loader
+    int seg_i = 0;
+    for (int si = seg_lo; si < seg_hi; ++si, ++seg_i) {
+      const AttendSegment sg = p.segs[si];
+      const uint32_t qb = seg_i & 1;
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(&B->q_empty[qb], ((seg_i >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) break;
+      const float *qs = p.q + static_cast<size_t>(sg.seq) * kHeads * kRow;
+      uint8_t *qd = smem + OFF_Q + qb * kQBytes;
+      for (int idx = lane; idx < kHeads * (kRow / 8); idx += 32) {
+        const int h = idx / (kRow / 8), c8 = idx % (kRow / 8);
+        const float4 a = *reinterpret_cast<const float4 *>(qs + h * kRow + c8 * 8);
+        const float4 b = *reinterpret_cast<const float4 *>(qs + h * kRow + c8 * 8 + 4);
+        uint4 v;
+        v.x = pack_bf16(a.x, a.y);
+        v.y = pack_bf16(a.z, a.w);
+        v.z = pack_bf16(b.x, b.y);
+        v.w = pack_bf16(b.z, b.w);
+        const uint32_t off = (c8 >> 3) * 2048 + sw128_offset(h, (c8 & 7) * 8);
+        *reinterpret_cast<uint4 *>(qd + off) = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B->q_full[qb]);
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax + epilogue
+    const int w = warp - 4;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * w) << 16;
+    uint32_t g = 0;
+    int seg_i = 0;
+    for (int si = seg_lo; si < seg_hi; ++si, ++seg_i) {
+      const AttendSegment sg = p.segs[si];
+      const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
+      float m_ref[kHeads], l_part[kHeads];
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) { m_ref[h] = -INFINITY; l_part[h] = 0.f; }
+      bool bad = false;
+      for (int t = 0; t < nt; ++t, ++g) {
+        const uint32_t sb = g & 1;
+        bad = !mbar_wait(&B->s_full[sb], (g >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
+        if (named_bar_or(1, 128, bad)) { bad = true; break; }
+        tc_fence_after();
+        float v[kHeads];
+        tmem_ld16(tmem + sb * 16 + lane_base, v);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&B->s_empty[sb]);
+        const int tok = sg.tok_begin + kTileTok * t + 16 * w + lane;
+        const bool valid = lane < 16 && tok < sg.tok_end;
+        if (p.dbg_s != nullptr && blockIdx.x == 0 && static_cast<int>(g) < p.dbg_tiles && lane < 16) {
+#pragma unroll
+          for (int h = 0; h < kHeads; ++h) p.dbg_s[(static_cast<size_t>(g) * 64 + 16 * w + lane) * kHeads + h] = v[h];
+        }
+        float s[kHeads];
+        bool need = false;
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) {
+          s[h] = valid ? v[h] * p.scale_log2 : -INFINITY;
+          need |= s[h] > m_ref[h] + 8.0f;
+        }
+        if (named_bar_or(1, 128, need)) {
+          float mx[kHeads];
+#pragma unroll
+          for (int h = 0; h < kHeads; ++h) mx[h] = s[h];
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+            for (int h = 0; h < kHeads; ++h) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], off));
+          if (lane == 0)
+#pragma unroll
+            for (int h = 0; h < kHeads; ++h) B->red[w][h] = mx[h];
+          named_bar_sync(1, 128);
+          float alpha[kHeads];
+#pragma unroll
+          for (int h = 0; h < kHeads; ++h) {
+            const float tm = fmaxf(fmaxf(B->red[0][h], B->red[1][h]), fmaxf(B->red[2][h], B->red[3][h]));
+            const float mn = fmaxf(m_ref[h], tm);
+            alpha[h] = (m_ref[h] == -INFINITY) ? 0.f : exp2f(m_ref[h] - mn);
+            m_ref[h] = mn;
+          }
+          named_bar_sync(1, 128);
+          if (t > 0) {
+            // O holds tiles [0, t) of this segment: rescale after P.V(t-1) lands.
+            const uint32_t pp = (g - 1) & 1;
+            bad = !mbar_wait(&B->p_empty[pp], ((g - 1) >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
+            if (named_bar_or(1, 128, bad)) { bad = true; break; }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              float o[kHeads];
+              tmem_ld16(tmem + kColO + 16 * c + lane_base, o);
+              tmem_wait_ld();
+#pragma unroll
+              for (int h = 0; h < kHeads; ++h) o[h] *= alpha[h];
+              tmem_st16(tmem + kColO + 16 * c + lane_base, o);
+            }
+            tmem_wait_st();
+          }
+#pragma unroll
+          for (int h = 0; h < kHeads; ++h) l_part[h] *= alpha[h];
+        }
+        float pr[kHeads];
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) {
+          pr[h] = exp2f(s[h] - m_ref[h]);
+          l_part[h] += pr[h];
+        }
+        const uint32_t pb = g & 1;
+        bad = !mbar_wait(&B->p_empty[pb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_MMA);
+        if (named_bar_or(1, 128, bad)) { bad = true; break; }
+        if (lane < 16 && !valid) {
+          // Rows past the segment end get p = 0, but 0 * (NaN/Inf garbage) is
+          // NaN in the P.V MMA: clear their latent rows (the scores MMA of this
+          // tile has completed, so the slots are free to modify).
+          const int tt = 16 * w + lane;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint8_t *slot = smem + OFF_LAT + ((4 * g + c) % kLatSlots) * kLatSlotBytes + tt * 128;
+#pragma unroll
+            for (int half = 0; half < 2; ++half)
+#pragma unroll
+              for (int k = 0; k < 8; ++k)
+                *reinterpret_cast<uint4 *>(slot + half * 8192 + k * 16) = make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+        if (lane < 16) {
+          const int tt = 16 * w + lane;
+          uint8_t *pd = smem + OFF_P + pb * kPBytes + (tt >> 3) * 128 + (tt & 7) * 2;
+#pragma unroll
+          for (int h = 0; h < kHeads; ++h)
+            *reinterpret_cast<__nv_bfloat16 *>(pd + (h >> 3) * 1024 + (h & 7) * 16) = __float2bfloat16_rn(pr[h]);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&B->p_full[pb]);
+      }
+      if (bad) break;
+      // ---- epilogue: O / l, lse
+      bad = !mbar_wait(&B->o_full, seg_i & 1, abort, p.err, ERR_TIMEOUT_MMA);
+      if (named_bar_or(1, 128, bad)) break;
+      tc_fence_after();
+      float lt[kHeads];
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) {
+        float l = l_part[h];
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+        lt[h] = l;
+      }
+      if (lane == 0)
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) B->red[w][h] = lt[h];
+      named_bar_sync(1, 128);
+#pragma unroll
+      for (int h = 0; h < kHeads; ++h) lt[h] = (B->red[0][h] + B->red[1][h]) + (B->red[2][h] + B->red[3][h]);
+      named_bar_sync(1, 128);
+      float *dst = (sg.slot < 0) ? p.out + static_cast<size_t>(sg.seq) * kHeads * kLatent
+                                 : p.part_o + static_cast<size_t>(sg.slot) * kHeads * kLatent;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        float o[kHeads];
+        tmem_ld16(tmem + kColO + 16 * c + lane_base, o);
+        tmem_wait_ld();
+        const int d = 128 * c + 32 * w + lane;
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h) dst[h * kLatent + d] = o[h] / lt[h];
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B->o_empty);
+      if (w == 0 && lane < kHeads) {
+        float m = 0.f, l = 1.f;
+#pragma unroll
+        for (int h = 0; h < kHeads; ++h)
+          if (h == lane) { m = m_ref[h]; l = lt[h]; }
+        const float lse = (m + log2f(l)) * 0.69314718055994531f;
+        float *ldst = (sg.slot < 0) ? p.lse : p.part_lse;
+        const int row = (sg.slot < 0) ? sg.seq : sg.slot;
+        if (ldst) ldst[row * kHeads + lane] = lse;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// Host launcher (declared in attend_host.cuh).
+cudaError_t launch_attend_bf16(const AttendParams &p, int grid, cudaStream_t stream) {
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(mla_attend_bf16_kernel,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  mla_attend_bf16_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
+}  // namespace kvl

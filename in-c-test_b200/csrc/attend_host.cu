@@ -1,0 +1,358 @@
+// attend_host.cu -- host half of the decode attend path: TMA descriptor
+// encoding, the stream-K work plan, the partial (o, lse) merge kernel, and the
+// generic attend kernel used for head shapes the tcgen05 kernel does not cover
+// (tiny test configurations such as the reference probes' NH=2, R=6).
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "attend_common.cuh"
+#include "attend_host.cuh"
+#include "sm100.cuh"
+
+namespace kvl {
+
+cudaError_t launch_attend_bf16(const AttendParams &p, int grid, cudaStream_t stream);
+cudaError_t launch_attend_q8(const AttendParams &p, int grid, cudaStream_t stream);
+
+// ------------------------------------------------------------------ TMA maps
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+bool make_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint64_t inner,
+                  uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+                  CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// ------------------------------------------------------------------ plan
+int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long long *seq_row0,
+                      int max_ctas) {
+  if (batch <= 0 || !seq_len || !seq_row0 || max_ctas <= 0) return -1;
+  hp = HostPlan();
+  hp.batch = batch;
+  std::vector<long long> tiles(batch);
+  long long total = 0;
+  for (int b = 0; b < batch; ++b) {
+    if (seq_len[b] <= 0 || seq_row0[b] < 0) return -1;
+    tiles[b] = (seq_len[b] + kTileTok - 1) / kTileTok;
+    total += tiles[b];
+  }
+  const int grid = static_cast<int>(std::min<long long>(max_ctas, total));
+  hp.grid = grid;
+  hp.cta_seg.assign(grid + 1, 0);
+  hp.seq_row0.assign(seq_row0, seq_row0 + batch);
+  hp.seq_len.assign(seq_len, seq_len + batch);
+  std::vector<int> first_slot(batch, -1), nslot(batch, 0);
+  int b = 0;
+  long long ob = 0;  // tiles of sequence b already assigned
+  for (int c = 0; c < grid; ++c) {
+    hp.cta_seg[c] = static_cast<int>(hp.segs.size());
+    long long remaining = (total * (c + 1)) / grid - (total * c) / grid;
+    while (remaining > 0) {
+      const long long take = std::min(remaining, tiles[b] - ob);
+      AttendSegment s;
+      s.seq = b;
+      s.tok_begin = static_cast<int>(ob * kTileTok);
+      s.tok_end = static_cast<int>(std::min<long long>((ob + take) * kTileTok, seq_len[b]));
+      const bool whole = (ob == 0 && take == tiles[b]);
+      if (whole) {
+        s.slot = -1;
+      } else {
+        s.slot = hp.nparts++;
+        if (first_slot[b] < 0) first_slot[b] = s.slot;
+        ++nslot[b];
+      }
+      hp.segs.push_back(s);
+      ob += take;
+      remaining -= take;
+      if (ob == tiles[b]) { ++b; ob = 0; }
+    }
+  }
+  hp.cta_seg[grid] = static_cast<int>(hp.segs.size());
+  for (int i = 0; i < batch; ++i)
+    if (nslot[i] > 0) hp.merges.push_back(MergeEntry{i, first_slot[i], nslot[i], 1});
+  return 0;
+}
+
+// ------------------------------------------------------------------ merge
+// out[seq][h][:] = sum_p w_p o_p / sum_p w_p,  w_p = exp(lse_p - max_p lse_p);
+// lse[seq][h] = max + log(sum_p w_p).  Part p of an entry lives at part index
+// first + p * step (each part is [16][R] floats and [16] lse values).
+__global__ void merge_partials_kernel(float *out, float *lse, const float *part_o,
+                                      const float *part_lse, const MergeEntry *entries, int nh,
+                                      int R) {
+  const MergeEntry e = entries[blockIdx.x];
+  extern __shared__ float sh[];  // [nh] max, [nh] inverse weight sum
+  for (int h = threadIdx.x; h < nh; h += blockDim.x) {
+    float m = -INFINITY;
+    for (int p = 0; p < e.count; ++p) m = fmaxf(m, part_lse[(size_t)(e.first + p * e.step) * nh + h]);
+    float sum = 0.f;
+    for (int p = 0; p < e.count; ++p) sum += expf(part_lse[(size_t)(e.first + p * e.step) * nh + h] - m);
+    sh[h] = m;
+    sh[nh + h] = 1.0f / sum;
+    if (lse) lse[(size_t)e.seq * nh + h] = m + logf(sum);
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nh * R; i += blockDim.x) {
+    const int h = i / R;
+    float acc = 0.f;
+    for (int p = 0; p < e.count; ++p) {
+      const size_t part = (size_t)(e.first + p * e.step);
+      acc += expf(part_lse[part * nh + h] - sh[h]) * part_o[part * nh * R + i];
+    }
+    out[(size_t)e.seq * nh * R + i] = acc * sh[nh + h];
+  }
+}
+
+cudaError_t launch_merge(float *out, float *lse, const float *part_o, const float *part_lse,
+                         const MergeEntry *d_entries, int n_entries, int nh, int R,
+                         cudaStream_t stream) {
+  if (n_entries <= 0) return cudaSuccess;
+  merge_partials_kernel<<<n_entries, 256, 2 * nh * sizeof(float), stream>>>(out, lse, part_o, part_lse,
+                                                                           d_entries, nh, R);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ generic attend
+// One CTA per (head, sequence); online softmax over chunks of 1024 rows in
+// fp32.  Used only when (NH, R, DR) is not the production (16, 512, 64).
+template <bool Q8>
+__global__ void attend_generic_kernel(float *out, float *lse, const float *q,
+                                      const uint16_t *kv, const int8_t *lat8, const float *lscale,
+                                      const uint16_t *rope16, const long long *row0,
+                                      const int *len, int nh, int R, int DR, float scale_log2) {
+  constexpr int kChunk = 1024;
+  const int h = blockIdx.x, b = blockIdx.y;
+  extern __shared__ float sm[];
+  float *qv = sm;                 // R + DR
+  float *sc = qv + R + DR;        // kChunk
+  float *acc = sc + kChunk;       // R
+  float *red = acc + R;           // 32
+  const int L = len[b];
+  const long long r0 = row0[b];
+  const float *qs = q + ((size_t)b * nh + h) * (R + DR);
+  for (int i = threadIdx.x; i < R + DR; i += blockDim.x) qv[i] = qs[i];
+  for (int i = threadIdx.x; i < R; i += blockDim.x) acc[i] = 0.f;
+  __syncthreads();
+  auto lat = [&](long long row, int r) -> float {
+    if (Q8) return __fmul_rn((float)lat8[row * R + r], lscale[row]);
+    return __bfloat162float(__ushort_as_bfloat16(kv[row * (R + DR) + r]));
+  };
+  auto rp = [&](long long row, int d) -> float {
+    if (Q8) return __bfloat162float(__ushort_as_bfloat16(rope16[row * DR + d]));
+    return __bfloat162float(__ushort_as_bfloat16(kv[row * (R + DR) + R + d]));
+  };
+  auto block_reduce = [&](float v, bool is_max) -> float {
+    for (int off = 16; off > 0; off >>= 1) {
+      const float o = __shfl_xor_sync(0xffffffffu, v, off);
+      v = is_max ? fmaxf(v, o) : v + o;
+    }
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float r = is_max ? -INFINITY : 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) r = is_max ? fmaxf(r, red[i]) : r + red[i];
+    return r;
+  };
+  float m = -INFINITY, l = 0.f;
+  for (int j0 = 0; j0 < L; j0 += kChunk) {
+    const int n = min(kChunk, L - j0);
+    float cmax = -INFINITY;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+      const long long row = r0 + j0 + j;
+      float s = 0.f;
+      for (int r = 0; r < R; ++r) s = fmaf(qv[r], lat(row, r), s);
+      for (int d = 0; d < DR; ++d) s = fmaf(qv[R + d], rp(row, d), s);
+      s *= scale_log2;
+      sc[j] = s;
+      cmax = fmaxf(cmax, s);
+    }
+    cmax = block_reduce(cmax, true);
+    const float mn = fmaxf(m, cmax);
+    const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - mn);
+    float psum = 0.f;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+      sc[j] = exp2f(sc[j] - mn);
+      psum += sc[j];
+    }
+    psum = block_reduce(psum, false);
+    __syncthreads();
+    for (int r = threadIdx.x; r < R; r += blockDim.x) {
+      float a = acc[r] * alpha;
+      for (int j = 0; j < n; ++j) a = fmaf(sc[j], lat(r0 + j0 + j, r), a);
+      acc[r] = a;
+    }
+    l = l * alpha + psum;
+    m = mn;
+    __syncthreads();
+  }
+  float *os = out + ((size_t)b * nh + h) * R;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) os[r] = acc[r] / l;
+  if (lse && threadIdx.x == 0) lse[(size_t)b * nh + h] = (m + log2f(l)) * 0.69314718055994531f;
+}
+
+cudaError_t launch_attend_generic(bool q8, float *out, float *lse, const float *q, const uint16_t *kv,
+                                  const int8_t *lat8, const float *lscale, const uint16_t *rope16,
+                                  const long long *d_row0, const int *d_len, int batch, int nh,
+                                  int R, int DR, float scale_log2, cudaStream_t stream) {
+  const size_t sm = (size_t)(R + DR + 1024 + R + 32) * sizeof(float);
+  if (sm > 48 * 1024) {
+    auto f = q8 ? attend_generic_kernel<true> : attend_generic_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid(nh, batch);
+  if (q8)
+    attend_generic_kernel<true><<<grid, 128, sm, stream>>>(out, lse, q, kv, lat8, lscale, rope16, d_row0,
+                                                           d_len, nh, R, DR, scale_log2);
+  else
+    attend_generic_kernel<false><<<grid, 128, sm, stream>>>(out, lse, q, kv, lat8, lscale, rope16, d_row0,
+                                                            d_len, nh, R, DR, scale_log2);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ device plan
+void DevicePlan::release() {
+  cudaFree(d_meta);
+  cudaFree(d_work);
+  d_meta = nullptr;
+  d_work = nullptr;
+  meta_bytes = work_bytes = 0;
+}
+
+// Packs the host plan's arrays into one device allocation (grown on demand)
+// and sizes the partial workspace.
+int DevicePlan::upload(const HostPlan &hp, int nh, int R, cudaStream_t stream, void *pinned,
+                       size_t pinned_bytes) {
+  host = hp;
+  const size_t seg_b = hp.segs.size() * sizeof(AttendSegment);
+  const size_t cta_b = hp.cta_seg.size() * sizeof(int);
+  const size_t row_b = hp.seq_row0.size() * sizeof(long long);
+  const size_t mer_b = hp.merges.size() * sizeof(MergeEntry);
+  const size_t len_b = hp.seq_len.size() * sizeof(int);
+  auto al = [](size_t x) { return (x + 255) & ~size_t(255); };
+  off_segs = 0;
+  off_cta = off_segs + al(seg_b);
+  off_row0 = off_cta + al(cta_b);
+  off_merge = off_row0 + al(row_b);
+  off_len = off_merge + al(mer_b);
+  off_err = off_len + al(len_b);
+  const size_t need = off_err + 256;
+  if (need > meta_bytes) {
+    cudaFree(d_meta);
+    d_meta = nullptr;
+    if (cudaMalloc(&d_meta, need) != cudaSuccess) { meta_bytes = 0; return -1; }
+    meta_bytes = need;
+  }
+  const size_t wneed = (size_t)std::max(hp.nparts, 1) * nh * (R + 1) * sizeof(float);
+  if (wneed > work_bytes) {
+    cudaFree(d_work);
+    d_work = nullptr;
+    if (cudaMalloc(&d_work, wneed) != cudaSuccess) { work_bytes = 0; return -1; }
+    work_bytes = wneed;
+  }
+  std::vector<uint8_t> tmp;
+  uint8_t *stage = static_cast<uint8_t *>(pinned);
+  if (!stage || pinned_bytes < need) {
+    tmp.resize(need);
+    stage = tmp.data();
+  }
+  std::memset(stage + off_err, 0, 256);
+  if (seg_b) std::memcpy(stage + off_segs, hp.segs.data(), seg_b);
+  std::memcpy(stage + off_cta, hp.cta_seg.data(), cta_b);
+  std::memcpy(stage + off_row0, hp.seq_row0.data(), row_b);
+  if (mer_b) std::memcpy(stage + off_merge, hp.merges.data(), mer_b);
+  if (len_b) std::memcpy(stage + off_len, hp.seq_len.data(), len_b);
+  cudaError_t e = cudaMemcpyAsync(d_meta, stage, need, cudaMemcpyHostToDevice, stream);
+  if (e != cudaSuccess) return -1;
+  if (stage == tmp.data()) cudaStreamSynchronize(stream);  // pageable staging must outlive the copy
+  part_o = static_cast<float *>(d_work);
+  part_lse = part_o + (size_t)std::max(hp.nparts, 1) * nh * R;
+  return 0;
+}
+
+int DevicePlan::launch(const AttendLaunch &a, cudaStream_t stream) const {
+  const uint8_t *m = static_cast<const uint8_t *>(d_meta);
+  const int nh = a.nh, R = a.R, DR = a.DR;
+  const float scale_log2 = a.softmax_scale * 1.4426950408889634f;
+  const bool fast = (nh == kHeads && R == kLatent && DR == kRope);
+  if (!fast) {
+    return launch_attend_generic(a.q8, a.out, a.lse, a.q, a.kv, a.lat8, a.lscale, a.rope16,
+                                 reinterpret_cast<const long long *>(m + off_row0),
+                                 reinterpret_cast<const int *>(m + off_len), host.batch, nh, R, DR,
+                                 scale_log2, stream) == cudaSuccess
+               ? 0
+               : -1;
+  }
+  if (a.rows <= 0 || a.rows >= (1LL << 31)) return -1;
+  AttendParams p;
+  std::memset(&p, 0, sizeof(p));
+  if (!a.q8) {
+    if ((reinterpret_cast<uintptr_t>(a.kv) & 15) != 0) return -1;
+    if (!make_tmap_2d(&p.tm_kv, a.kv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kRow, a.rows, kRow * 2, 64,
+                      kTileTok, CU_TENSOR_MAP_SWIZZLE_128B))
+      return -1;
+  } else {
+    if (((reinterpret_cast<uintptr_t>(a.lat8) | reinterpret_cast<uintptr_t>(a.rope16) |
+          reinterpret_cast<uintptr_t>(a.lscale)) & 15) != 0)
+      return -1;
+    if (!make_tmap_2d(&p.tm_lat8, a.lat8, CU_TENSOR_MAP_DATA_TYPE_UINT8, kLatent, a.rows, kLatent, 128,
+                      kTileTok, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_2d(&p.tm_rope, a.rope16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kRope, a.rows, kRope * 2,
+                      64, kTileTok, CU_TENSOR_MAP_SWIZZLE_128B))
+      return -1;
+    p.latent_scale = a.lscale;
+  }
+  p.q = a.q;
+  p.out = a.out;
+  p.lse = a.lse;
+  p.part_o = part_o;
+  p.part_lse = part_lse;
+  p.segs = reinterpret_cast<const AttendSegment *>(m + off_segs);
+  p.cta_seg = reinterpret_cast<const int *>(m + off_cta);
+  p.seq_row0 = reinterpret_cast<const long long *>(m + off_row0);
+  p.rows = a.rows;
+  p.scale_log2 = scale_log2;
+  p.err = reinterpret_cast<uint32_t *>(const_cast<uint8_t *>(m + off_err));
+  p.dbg_s = a.dbg_s;
+  p.dbg_tiles = a.dbg_tiles;
+  cudaError_t e = a.q8 ? launch_attend_q8(p, host.grid, stream) : launch_attend_bf16(p, host.grid, stream);
+  if (e != cudaSuccess) return -1;
+  if (!host.merges.empty()) {
+    e = launch_merge(a.out, a.lse, part_o, part_lse, reinterpret_cast<const MergeEntry *>(m + off_merge),
+                     static_cast<int>(host.merges.size()), nh, R, stream);
+    if (e != cudaSuccess) return -1;
+  }
+  return 0;
+}
+
+uint32_t *DevicePlan::err_word() const {
+  return reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(d_meta) + off_err);
+}
+
+}  // namespace kvl

@@ -1,0 +1,1011 @@
+// mla_capi.cu -- the C ABI of libkvl_mla_cuda: the reference runtime's MLA
+// state / decode / prefill functions (include/kvl/mla_compressed_state.h,
+// include/kvl/mla_compressed_q8_state.h, kvl_mla_prefill_bf16 of
+// include/kvl/ops.h) served from GPU memory, plus the device-pointer entry
+// points of include/kvl/mla_cuda.h.
+//
+// Conventions kept from the reference: every call validates its arguments in
+// the reference's order and returns -1 without touching the state when a check
+// fails (src/mla_compressed_state.c:92-98); decode appends the current token
+// before attending; truncate/reset are O(1) on `len`; free zeroes the struct.
+// CUDA failures also return -1.  There is no CPU fallback: without a usable
+// GPU every compute call fails.
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "attend_host.cuh"
+#include "kvl/mla_compressed_q8_state.h"
+#include "kvl/mla_compressed_state.h"
+#include "kvl/mla_cuda.h"
+#include "mla_kernels.cuh"
+
+#define KVL_EXPORT extern "C" __attribute__((visibility("default")))
+
+namespace kvl {
+namespace {
+
+thread_local std::string g_err;
+
+void set_err(const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  static const bool verbose = [] {
+    const char *v = getenv("KVL_CUDA_VERBOSE");
+    return v && *v && *v != '0';
+  }();
+  if (verbose) fprintf(stderr, "kvl_mla_cuda: %s\n", buf);
+}
+
+#define CK(expr)                                                                        \
+  do {                                                                                  \
+    cudaError_t _e = (expr);                                                            \
+    if (_e != cudaSuccess) {                                                            \
+      set_err("%s failed: %s (%s:%d)", #expr, cudaGetErrorString(_e), __FILE__, __LINE__); \
+      return -1;                                                                        \
+    }                                                                                   \
+  } while (0)
+
+struct DBuf {
+  void *p = nullptr;
+  size_t n = 0;
+  bool ensure(size_t bytes) {
+    if (bytes <= n) return true;
+    cudaFree(p);
+    p = nullptr;
+    n = 0;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return false;
+    n = bytes;
+    return true;
+  }
+  template <typename T>
+  T *as() const { return static_cast<T *>(p); }
+};
+
+struct PBuf {  // pinned host staging
+  void *p = nullptr;
+  size_t n = 0;
+  bool ensure(size_t bytes) {
+    if (bytes <= n) return true;
+    cudaFreeHost(p);
+    p = nullptr;
+    n = 0;
+    if (cudaMallocHost(&p, bytes) != cudaSuccess) return false;
+    n = bytes;
+    return true;
+  }
+  template <typename T>
+  T *as() const { return static_cast<T *>(p); }
+};
+
+std::atomic<int> g_weight_cache{-1};
+
+bool weight_cache_enabled() {
+  int v = g_weight_cache.load();
+  if (v < 0) {
+    int en = 0;
+    const char *a = getenv("KVL_CUDA_WEIGHT_CACHE");
+    if (a && *a && *a != '0') en = 1;
+    const char *t = getenv("KVL_TRUNK_CACHE_MIB");
+    if (t && atol(t) >= 1706) en = 1;
+    int expected = -1;
+    g_weight_cache.compare_exchange_strong(expected, en);
+    v = g_weight_cache.load();
+  }
+  return v == 1;
+}
+
+struct DevW {
+  const uint16_t *q, *kva, *kvan, *kvb, *o;
+};
+
+struct Ctx {
+  int device = 0;
+  int sms = 148;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+  DBuf x, q, ka, qabs, mix, ho, y, rowf, kvtmp;
+  DBuf wq, wkva, wkvan, wkvb, wo;  // per-call weight upload
+  PBuf pin_io, pin_plan;
+  DevicePlan plan;
+  std::unordered_map<const void *, std::pair<size_t, void *>> wcache;
+};
+
+std::mutex g_ctx_mu;
+std::unordered_map<int, Ctx *> g_ctx;
+
+Ctx *get_ctx(int device) {
+  std::lock_guard<std::mutex> lk(g_ctx_mu);
+  auto it = g_ctx.find(device);
+  if (it != g_ctx.end()) return it->second;
+  Ctx *c = new Ctx();
+  c->device = device;
+  if (cudaSetDevice(device) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+    set_err("cannot open CUDA device %d", device);
+    delete c;
+    return nullptr;
+  }
+  cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device);
+  g_ctx[device] = c;
+  return c;
+}
+
+int current_device() {
+  int d = -1;
+  if (cudaGetDevice(&d) != cudaSuccess) {
+    set_err("no CUDA device available");
+    return -1;
+  }
+  return d;
+}
+
+// One weight tensor on the device: cached by host pointer, or uploaded into a
+// per-context buffer on every call.
+int stage_weight(Ctx &c, DBuf &buf, const uint16_t *host, size_t elems, const uint16_t **dev) {
+  const size_t bytes = elems * sizeof(uint16_t);
+  if (weight_cache_enabled()) {
+    auto it = c.wcache.find(host);
+    if (it != c.wcache.end() && it->second.first == bytes) {
+      *dev = static_cast<const uint16_t *>(it->second.second);
+      return 0;
+    }
+    void *p = nullptr;
+    CK(cudaMalloc(&p, bytes));
+    CK(cudaMemcpy(p, host, bytes, cudaMemcpyHostToDevice));
+    if (it != c.wcache.end()) cudaFree(it->second.second);
+    c.wcache[host] = {bytes, p};
+    *dev = static_cast<const uint16_t *>(p);
+    return 0;
+  }
+  if (!buf.ensure(bytes)) {
+    set_err("cudaMalloc of %zu weight bytes failed", bytes);
+    return -1;
+  }
+  CK(cudaMemcpyAsync(buf.p, host, bytes, cudaMemcpyHostToDevice, c.stream));
+  *dev = buf.as<const uint16_t>();
+  return 0;
+}
+
+int stage_weights(Ctx &c, const KvlMlaConfig &cfg, const KvlMlaBF16 &w, DevW &d, bool need_q) {
+  const size_t H = cfg.hidden_size, NH = cfg.num_heads, DN = cfg.qk_nope_dim, DR = cfg.qk_rope_dim;
+  const size_t DV = cfg.v_head_dim, R = cfg.kv_lora_rank;
+  d = DevW{nullptr, nullptr, nullptr, nullptr, nullptr};
+  if (need_q) {
+    if (stage_weight(c, c.wq, w.q_proj, NH * (DN + DR) * H, &d.q)) return -1;
+    if (stage_weight(c, c.wkvb, w.kv_b_proj, NH * (DN + DV) * R, &d.kvb)) return -1;
+    if (stage_weight(c, c.wo, w.o_proj, H * NH * DV, &d.o)) return -1;
+  }
+  if (stage_weight(c, c.wkva, w.kv_a_proj, (R + DR) * H, &d.kva)) return -1;
+  if (stage_weight(c, c.wkvan, w.kv_a_norm, R, &d.kvan)) return -1;
+  return 0;
+}
+
+// ------------------------------------------------------------------ states
+enum Fmt { FMT_BF16 = 0, FMT_Q8 = 1 };
+
+struct DevState {
+  int fmt = FMT_BF16;
+  int device = 0;
+  int capacity = 0, cap_pad = 0, R = 0, DR = 0;
+  int dev_len = 0;
+  uint16_t *kv = nullptr;     // bf16 [cap_pad][R+DR]
+  int8_t *lat8 = nullptr;     // q8 [cap_pad][R]
+  float *lscale = nullptr;    // q8 [cap_pad]
+  uint16_t *rope16 = nullptr; // q8 [cap_pad][DR]
+  size_t bytes = 0;
+  void release() {
+    cudaFree(kv);
+    cudaFree(lat8);
+    cudaFree(lscale);
+    cudaFree(rope16);
+    kv = nullptr;
+    lat8 = nullptr;
+    lscale = nullptr;
+    rope16 = nullptr;
+  }
+};
+
+std::mutex g_reg_mu;
+std::unordered_map<const void *, DevState *> g_reg;  // key: host mirror pointer
+
+DevState *find_state(const void *key) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_reg.find(key);
+  return it == g_reg.end() ? nullptr : it->second;
+}
+
+void register_state(const void *key, DevState *ds) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  g_reg[key] = ds;
+}
+
+DevState *unregister_state(const void *key) {
+  std::lock_guard<std::mutex> lk(g_reg_mu);
+  auto it = g_reg.find(key);
+  if (it == g_reg.end()) return nullptr;
+  DevState *ds = it->second;
+  g_reg.erase(it);
+  return ds;
+}
+
+int alloc_dev_state(DevState &ds, int fmt, int capacity, int R, int DR) {
+  ds.fmt = fmt;
+  ds.capacity = capacity;
+  ds.cap_pad = (capacity + kTileTok - 1) / kTileTok * kTileTok;
+  ds.R = R;
+  ds.DR = DR;
+  ds.device = current_device();
+  if (ds.device < 0) return -1;
+  const size_t rows = ds.cap_pad;
+  if (fmt == FMT_BF16) {
+    ds.bytes = rows * (R + DR) * sizeof(uint16_t);
+    CK(cudaMalloc(&ds.kv, ds.bytes));
+    CK(cudaMemset(ds.kv, 0, ds.bytes));
+  } else {
+    CK(cudaMalloc(&ds.lat8, rows * R));
+    CK(cudaMalloc(&ds.lscale, rows * sizeof(float)));
+    CK(cudaMalloc(&ds.rope16, rows * DR * sizeof(uint16_t)));
+    CK(cudaMemset(ds.lat8, 0, rows * R));
+    CK(cudaMemset(ds.lscale, 0, rows * sizeof(float)));
+    CK(cudaMemset(ds.rope16, 0, rows * DR * sizeof(uint16_t)));
+    ds.bytes = rows * (R + sizeof(float) + DR * sizeof(uint16_t));
+  }
+  return 0;
+}
+
+// Brings the device rows in line with the host struct: rows the caller wrote
+// into the mirrors and published by raising `len` are uploaded; a lower `len`
+// truncates.
+int sync_bf16_state(Ctx &c, DevState &ds, const KvlMlaCompressedState &st) {
+  if (st.len < ds.dev_len) {
+    ds.dev_len = st.len;
+    return 0;
+  }
+  if (st.len == ds.dev_len) return 0;
+  const int n = st.len - ds.dev_len, R = ds.R, DR = ds.DR;
+  if (!c.kvtmp.ensure(static_cast<size_t>(n) * (R + DR) * sizeof(float))) {
+    set_err("cudaMalloc failed while uploading host rows");
+    return -1;
+  }
+  float *tmp = c.kvtmp.as<float>();
+  CK(cudaMemcpy2DAsync(tmp, (R + DR) * sizeof(float), st.latent + static_cast<size_t>(ds.dev_len) * R,
+                       R * sizeof(float), R * sizeof(float), n, cudaMemcpyHostToDevice, c.stream));
+  CK(cudaMemcpy2DAsync(tmp + R, (R + DR) * sizeof(float), st.rope + static_cast<size_t>(ds.dev_len) * DR,
+                       DR * sizeof(float), DR * sizeof(float), n, cudaMemcpyHostToDevice, c.stream));
+  CK(f32_to_bf16(ds.kv + static_cast<size_t>(ds.dev_len) * (R + DR), tmp, static_cast<long long>(n) * (R + DR),
+                 c.stream));
+  CK(cudaStreamSynchronize(c.stream));
+  ds.dev_len = st.len;
+  return 0;
+}
+
+int sync_q8_state(Ctx &c, DevState &ds, const KvlMlaCompressedQ8State &st) {
+  if (st.len < ds.dev_len) {
+    ds.dev_len = st.len;
+    return 0;
+  }
+  if (st.len == ds.dev_len) return 0;
+  const size_t a = ds.dev_len, n = st.len - ds.dev_len, R = ds.R, DR = ds.DR;
+  CK(cudaMemcpyAsync(ds.lat8 + a * R, st.latent_q8 + a * R, n * R, cudaMemcpyHostToDevice, c.stream));
+  CK(cudaMemcpyAsync(ds.lscale + a, st.latent_scale + a, n * sizeof(float), cudaMemcpyHostToDevice, c.stream));
+  CK(cudaMemcpyAsync(ds.rope16 + a * DR, st.rope_bf16 + a * DR, n * DR * sizeof(uint16_t),
+                     cudaMemcpyHostToDevice, c.stream));
+  CK(cudaStreamSynchronize(c.stream));
+  ds.dev_len = st.len;
+  return 0;
+}
+
+bool cfg_dims_ok(const KvlMlaConfig &c) {
+  return c.hidden_size > 0 && c.num_heads > 0 && c.qk_nope_dim > 0 && c.qk_rope_dim > 0 &&
+         (c.qk_rope_dim & 1) == 0 && c.v_head_dim > 0 && c.kv_lora_rank > 0 && c.rope_theta > 0.0f;
+}
+
+// Attends the single-sequence plan [0, L) of a state into c.mix.
+int attend_state(Ctx &c, const DevState &ds, int L, int nh, float scale) {
+  HostPlan hp;
+  const long long row0 = 0;
+  if (build_attend_plan(hp, 1, &L, &row0, c.sms) != 0) {
+    set_err("attend plan failed (L=%d)", L);
+    return -1;
+  }
+  if (!c.pin_plan.ensure(64 * 1024) ||
+      c.plan.upload(hp, nh, ds.R, c.stream, c.pin_plan.p, c.pin_plan.n) != 0) {
+    set_err("attend plan upload failed");
+    return -1;
+  }
+  AttendLaunch a;
+  a.q8 = ds.fmt == FMT_Q8;
+  a.nh = nh;
+  a.R = ds.R;
+  a.DR = ds.DR;
+  a.rows = ds.cap_pad;
+  a.q = c.qabs.as<float>();
+  a.out = c.mix.as<float>();
+  a.kv = ds.kv;
+  a.lat8 = ds.lat8;
+  a.lscale = ds.lscale;
+  a.rope16 = ds.rope16;
+  a.softmax_scale = scale;
+  if (c.plan.launch(a, c.stream) != 0) {
+    set_err("attend launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return -1;
+  }
+  return 0;
+}
+
+// One decode step of one token against a device state (both formats).
+// Host x[H] -> host out[H]; the appended row is mirrored into the host arrays
+// through the callback target pointers.
+int decode_one(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, const float *x, float *out,
+               int position, float *mir_lat, float *mir_rope, int8_t *mir_q8, float *mir_scale,
+               uint16_t *mir_rope16) {
+  const int H = cfg.hidden_size, NH = cfg.num_heads, DN = cfg.qk_nope_dim, DR = cfg.qk_rope_dim;
+  const int DV = cfg.v_head_dim, R = cfg.kv_lora_rank, QD = DN + DR;
+  if (!c.x.ensure(H * 4) || !c.q.ensure(static_cast<size_t>(NH) * QD * 4) || !c.ka.ensure((R + DR) * 4) ||
+      !c.qabs.ensure(static_cast<size_t>(NH) * (R + DR) * 4) || !c.mix.ensure(static_cast<size_t>(NH) * R * 4) ||
+      !c.ho.ensure(static_cast<size_t>(NH) * DV * 4) || !c.y.ensure(H * 4) || !c.rowf.ensure((R + DR) * 4)) {
+    set_err("cudaMalloc of decode scratch failed");
+    return -1;
+  }
+  const size_t io = static_cast<size_t>(2 * H + (R + DR) + 64) * 4 + R + 16;
+  if (!c.pin_io.ensure(io)) {
+    set_err("cudaMallocHost failed");
+    return -1;
+  }
+  float *px = c.pin_io.as<float>();
+  float *py = px + H;
+  float *prow = py + H;
+  uint32_t *perr = reinterpret_cast<uint32_t *>(prow + R + DR);
+  int8_t *pq8 = reinterpret_cast<int8_t *>(perr + 16);
+  memcpy(px, x, H * sizeof(float));
+  CK(cudaMemcpyAsync(c.x.p, px, H * 4, cudaMemcpyHostToDevice, c.stream));
+  CK(gemv_bf16(c.q.as<float>(), c.x.as<float>(), W.q, H, NH * QD, 1, c.stream));
+  CK(gemv_bf16(c.ka.as<float>(), c.x.as<float>(), W.kva, H, R + DR, 1, c.stream));
+  if (ds.fmt == FMT_BF16)
+    CK(append_bf16(ds.kv, 0, c.ka.as<float>(), W.kvan, 1, R, DR, position, cfg.rms_eps, cfg.rope_theta,
+                   c.rowf.as<float>(), c.stream));
+  else
+    CK(append_q8(ds.lat8, ds.lscale, ds.rope16, 0, c.ka.as<float>(), W.kvan, 1, R, DR, position, cfg.rms_eps,
+                 cfg.rope_theta, c.stream));
+  CK(absorb(c.qabs.as<float>(), c.q.as<float>(), W.kvb, 1, NH, DN, DV, DR, R, position, cfg.rope_theta, c.stream));
+  if (attend_state(c, ds, position + 1, NH, 1.0f / sqrtf(static_cast<float>(QD))) != 0) return -1;
+  CK(vup(c.ho.as<float>(), c.mix.as<float>(), W.kvb, 1, NH, DN, DV, R, c.stream));
+  CK(gemv_bf16(c.y.as<float>(), c.ho.as<float>(), W.o, NH * DV, H, 1, c.stream));
+  CK(cudaMemcpyAsync(py, c.y.p, H * 4, cudaMemcpyDeviceToHost, c.stream));
+  CK(cudaMemcpyAsync(perr, c.plan.err_word(), 4, cudaMemcpyDeviceToHost, c.stream));
+  if (ds.fmt == FMT_BF16) {
+    CK(cudaMemcpyAsync(prow, c.rowf.p, (R + DR) * 4, cudaMemcpyDeviceToHost, c.stream));
+  } else {
+    const size_t pos = position;
+    CK(cudaMemcpyAsync(pq8, ds.lat8 + pos * R, R, cudaMemcpyDeviceToHost, c.stream));
+    CK(cudaMemcpyAsync(prow, ds.lscale + pos, 4, cudaMemcpyDeviceToHost, c.stream));
+    CK(cudaMemcpyAsync(prow + 1, ds.rope16 + pos * DR, DR * 2, cudaMemcpyDeviceToHost, c.stream));
+  }
+  CK(cudaStreamSynchronize(c.stream));
+  if (*perr != 0) {
+    set_err("attend kernel reported device error 0x%x", *perr);
+    return -1;
+  }
+  memcpy(out, py, H * sizeof(float));
+  if (ds.fmt == FMT_BF16) {
+    memcpy(mir_lat, prow, R * sizeof(float));
+    memcpy(mir_rope, prow + R, DR * sizeof(float));
+  } else {
+    memcpy(mir_q8, pq8, R);
+    memcpy(mir_scale, prow, 4);
+    memcpy(mir_rope16, prow + 1, DR * 2);
+  }
+  return 0;
+}
+
+// kv_a projection + append of rows 0..S-1 (state prefill, both formats).
+int prefill_state(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, const float *x, int S) {
+  const int H = cfg.hidden_size, R = cfg.kv_lora_rank, DR = cfg.qk_rope_dim;
+  if (!c.x.ensure(static_cast<size_t>(S) * H * 4) || !c.ka.ensure(static_cast<size_t>(S) * (R + DR) * 4) ||
+      !c.rowf.ensure(static_cast<size_t>(S) * (R + DR) * 4)) {
+    set_err("cudaMalloc of prefill scratch failed");
+    return -1;
+  }
+  CK(cudaMemcpyAsync(c.x.p, x, static_cast<size_t>(S) * H * 4, cudaMemcpyHostToDevice, c.stream));
+  CK(gemv_bf16(c.ka.as<float>(), c.x.as<float>(), W.kva, H, R + DR, S, c.stream));
+  if (ds.fmt == FMT_BF16)
+    CK(append_bf16(ds.kv, 0, c.ka.as<float>(), W.kvan, S, R, DR, 0, cfg.rms_eps, cfg.rope_theta,
+                   c.rowf.as<float>(), c.stream));
+  else
+    CK(append_q8(ds.lat8, ds.lscale, ds.rope16, 0, c.ka.as<float>(), W.kvan, S, R, DR, 0, cfg.rms_eps,
+                 cfg.rope_theta, c.stream));
+  return 0;
+}
+
+}  // namespace
+}  // namespace kvl
+
+using namespace kvl;
+
+// =================================================================== misc
+KVL_EXPORT const char *kvl_mla_cuda_last_error(void) { return g_err.c_str(); }
+
+KVL_EXPORT int kvl_mla_cuda_weight_cache(int enable) {
+  const int prev = weight_cache_enabled() ? 1 : 0;
+  g_weight_cache.store(enable ? 1 : 0);
+  return prev;
+}
+
+KVL_EXPORT size_t kvl_mla_cuda_state_device_bytes(const void *state) {
+  if (!state) return 0;
+  // Both state structs start with (capacity, len, R, DR) followed by the first
+  // host mirror pointer, which is the registry key.
+  const KvlMlaCompressedState *s = static_cast<const KvlMlaCompressedState *>(state);
+  DevState *ds = find_state(s->latent);
+  return ds ? ds->bytes : 0;
+}
+
+// =================================================================== bf16 (fp32-mirrored) state
+// Reference: src/mla_compressed_state.c:24-50.
+KVL_EXPORT int kvl_mla_compressed_state_init(KvlMlaCompressedState *state, const KvlMlaConfig *cfg, int capacity) {
+  if (!state || !cfg || capacity <= 0 || cfg->kv_lora_rank <= 0 || cfg->qk_rope_dim <= 0 ||
+      (cfg->qk_rope_dim & 1))
+    return -1;
+  memset(state, 0, sizeof(*state));
+  const int R = cfg->kv_lora_rank, DR = cfg->qk_rope_dim;
+  state->latent = static_cast<float *>(calloc(static_cast<size_t>(capacity) * R, sizeof(float)));
+  state->rope = static_cast<float *>(calloc(static_cast<size_t>(capacity) * DR, sizeof(float)));
+  DevState *ds = new DevState();
+  if (!state->latent || !state->rope || alloc_dev_state(*ds, FMT_BF16, capacity, R, DR) != 0) {
+    ds->release();
+    delete ds;
+    free(state->latent);
+    free(state->rope);
+    memset(state, 0, sizeof(*state));
+    return -1;
+  }
+  register_state(state->latent, ds);
+  state->capacity = capacity;
+  state->kv_lora_rank = R;
+  state->qk_rope_dim = DR;
+  return 0;
+}
+
+KVL_EXPORT void kvl_mla_compressed_state_reset(KvlMlaCompressedState *state) {
+  if (state) state->len = 0;
+}
+
+KVL_EXPORT int kvl_mla_compressed_state_truncate(KvlMlaCompressedState *state, int new_len) {
+  if (!state || new_len < 0 || new_len > state->len) return -1;
+  state->len = new_len;
+  return 0;
+}
+
+KVL_EXPORT void kvl_mla_compressed_state_free(KvlMlaCompressedState *state) {
+  if (!state) return;
+  if (state->latent) {
+    DevState *ds = unregister_state(state->latent);
+    if (ds) {
+      ds->release();
+      delete ds;
+    }
+  }
+  free(state->latent);
+  free(state->rope);
+  memset(state, 0, sizeof(*state));
+}
+
+KVL_EXPORT size_t kvl_mla_compressed_state_bytes(const KvlMlaCompressedState *state) {
+  if (!state || state->capacity <= 0) return 0;
+  return sizeof(*state) + static_cast<size_t>(state->capacity) *
+                              (static_cast<size_t>(state->kv_lora_rank) + state->qk_rope_dim) * sizeof(float);
+}
+
+// Reference: src/mla_compressed_state.c:52-84.
+KVL_EXPORT int kvl_mla_compressed_state_prefill_bf16(const float *x, int seq_len, const KvlMlaConfig *cfg,
+                                                     const KvlMlaBF16 *w, KvlMlaCompressedState *state) {
+  if (!x || !cfg || !w || !state || !w->kv_a_proj || !w->kv_a_norm || seq_len <= 0 || state->len != 0 ||
+      seq_len > state->capacity || state->kv_lora_rank != cfg->kv_lora_rank ||
+      state->qk_rope_dim != cfg->qk_rope_dim)
+    return -1;
+  const int H = cfg->hidden_size, R = cfg->kv_lora_rank, DR = cfg->qk_rope_dim;
+  if (H <= 0 || R <= 0 || DR <= 0 || (DR & 1) || cfg->rope_theta <= 0.0f) return -1;
+  DevState *ds = find_state(state->latent);
+  if (!ds || ds->fmt != FMT_BF16) {
+    set_err("state was not created by kvl_mla_compressed_state_init");
+    return -1;
+  }
+  Ctx *c = get_ctx(ds->device);
+  if (!c) return -1;
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (cudaSetDevice(ds->device) != cudaSuccess) return -1;
+  DevW W;
+  if (stage_weights(*c, *cfg, *w, W, false) != 0) return -1;
+  if (prefill_state(*c, *ds, *cfg, W, x, seq_len) != 0) return -1;
+  const float *rf = c->rowf.as<float>();
+  CK(cudaMemcpy2DAsync(state->latent, R * 4, rf, (R + DR) * 4, R * 4, seq_len, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaMemcpy2DAsync(state->rope, DR * 4, rf + R, (R + DR) * 4, DR * 4, seq_len, cudaMemcpyDeviceToHost,
+                       c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  ds->dev_len = seq_len;
+  state->len = seq_len;
+  return 0;
+}
+
+// Reference: src/mla_compressed_state.c:86-161.
+KVL_EXPORT int kvl_mla_decode_compressed_bf16(float *out, const float *x, int position, const KvlMlaConfig *cfg,
+                                              const KvlMlaBF16 *w, KvlMlaCompressedState *state) {
+  if (!out || !x || !cfg || !w || !state || !w->q_proj || !w->kv_a_proj || !w->kv_a_norm || !w->kv_b_proj ||
+      !w->o_proj || position != state->len || position < 0 || position >= state->capacity ||
+      state->kv_lora_rank != cfg->kv_lora_rank || state->qk_rope_dim != cfg->qk_rope_dim)
+    return -1;
+  if (!cfg_dims_ok(*cfg)) return -1;
+  DevState *ds = find_state(state->latent);
+  if (!ds || ds->fmt != FMT_BF16) {
+    set_err("state was not created by kvl_mla_compressed_state_init");
+    return -1;
+  }
+  Ctx *c = get_ctx(ds->device);
+  if (!c) return -1;
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (cudaSetDevice(ds->device) != cudaSuccess) return -1;
+  if (sync_bf16_state(*c, *ds, *state) != 0) return -1;
+  DevW W;
+  if (stage_weights(*c, *cfg, *w, W, true) != 0) return -1;
+  const size_t R = cfg->kv_lora_rank, DR = cfg->qk_rope_dim;
+  if (decode_one(*c, *ds, *cfg, W, x, out, position, state->latent + position * R, state->rope + position * DR,
+                 nullptr, nullptr, nullptr) != 0)
+    return -1;
+  ds->dev_len = position + 1;
+  state->len = position + 1;
+  return 0;
+}
+
+// Reference: src/mla_compressed_state.c:163-184 (serial steps).
+KVL_EXPORT int kvl_mla_decode_compressed_block_bf16(float *out, const float *x, int count, int start_position,
+                                                    const KvlMlaConfig *cfg, const KvlMlaBF16 *w,
+                                                    KvlMlaCompressedState *state) {
+  if (!out || !x || !cfg || !w || !state || count <= 0 || start_position != state->len || start_position < 0 ||
+      count > state->capacity - start_position)
+    return -1;
+  const int H = cfg->hidden_size;
+  if (H <= 0) return -1;
+  for (int t = 0; t < count; ++t)
+    if (kvl_mla_decode_compressed_bf16(out + static_cast<size_t>(t) * H, x + static_cast<size_t>(t) * H,
+                                       start_position + t, cfg, w, state) != 0)
+      return -1;
+  return 0;
+}
+
+// =================================================================== Q8 state
+// Reference: src/mla_compressed_q8_state.c:63-109.
+KVL_EXPORT int kvl_mla_compressed_q8_state_init(KvlMlaCompressedQ8State *state, const KvlMlaConfig *cfg,
+                                                int capacity) {
+  if (!state || !cfg || capacity <= 0 || cfg->kv_lora_rank <= 0 || cfg->qk_rope_dim <= 0 ||
+      (cfg->qk_rope_dim & 1))
+    return -1;
+  memset(state, 0, sizeof(*state));
+  const int R = cfg->kv_lora_rank, DR = cfg->qk_rope_dim;
+  state->latent_q8 = static_cast<int8_t *>(calloc(static_cast<size_t>(capacity) * R, 1));
+  state->latent_scale = static_cast<float *>(calloc(static_cast<size_t>(capacity), sizeof(float)));
+  state->rope_bf16 = static_cast<uint16_t *>(calloc(static_cast<size_t>(capacity) * DR, sizeof(uint16_t)));
+  DevState *ds = new DevState();
+  if (!state->latent_q8 || !state->latent_scale || !state->rope_bf16 ||
+      alloc_dev_state(*ds, FMT_Q8, capacity, R, DR) != 0) {
+    ds->release();
+    delete ds;
+    free(state->latent_q8);
+    free(state->latent_scale);
+    free(state->rope_bf16);
+    memset(state, 0, sizeof(*state));
+    return -1;
+  }
+  register_state(state->latent_q8, ds);
+  state->capacity = capacity;
+  state->kv_lora_rank = R;
+  state->qk_rope_dim = DR;
+  return 0;
+}
+
+KVL_EXPORT void kvl_mla_compressed_q8_state_reset(KvlMlaCompressedQ8State *state) {
+  if (state) state->len = 0;
+}
+
+KVL_EXPORT int kvl_mla_compressed_q8_state_truncate(KvlMlaCompressedQ8State *state, int new_len) {
+  if (!state || new_len < 0 || new_len > state->len) return -1;
+  state->len = new_len;
+  return 0;
+}
+
+KVL_EXPORT void kvl_mla_compressed_q8_state_free(KvlMlaCompressedQ8State *state) {
+  if (!state) return;
+  if (state->latent_q8) {
+    DevState *ds = unregister_state(state->latent_q8);
+    if (ds) {
+      ds->release();
+      delete ds;
+    }
+  }
+  free(state->latent_q8);
+  free(state->latent_scale);
+  free(state->rope_bf16);
+  memset(state, 0, sizeof(*state));
+}
+
+KVL_EXPORT size_t kvl_mla_compressed_q8_state_bytes(const KvlMlaCompressedQ8State *state) {
+  if (!state || state->capacity <= 0) return 0;
+  return sizeof(*state) + static_cast<size_t>(state->capacity) *
+                              (static_cast<size_t>(state->kv_lora_rank) * sizeof(int8_t) + sizeof(float) +
+                               static_cast<size_t>(state->qk_rope_dim) * sizeof(uint16_t));
+}
+
+// Reference: src/mla_compressed_q8_state.c:129-159.
+KVL_EXPORT int kvl_mla_compressed_q8_state_prefill_bf16(const float *x, int seq_len, const KvlMlaConfig *cfg,
+                                                        const KvlMlaBF16 *w, KvlMlaCompressedQ8State *state) {
+  if (!x || !cfg || !w || !state || !w->kv_a_proj || !w->kv_a_norm || seq_len <= 0 || state->len != 0 ||
+      seq_len > state->capacity || state->kv_lora_rank != cfg->kv_lora_rank ||
+      state->qk_rope_dim != cfg->qk_rope_dim)
+    return -1;
+  const int H = cfg->hidden_size, R = cfg->kv_lora_rank, DR = cfg->qk_rope_dim;
+  if (H <= 0 || R <= 0 || DR <= 0 || (DR & 1) || cfg->rope_theta <= 0.0f) return -1;
+  DevState *ds = find_state(state->latent_q8);
+  if (!ds || ds->fmt != FMT_Q8) {
+    set_err("state was not created by kvl_mla_compressed_q8_state_init");
+    return -1;
+  }
+  Ctx *c = get_ctx(ds->device);
+  if (!c) return -1;
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (cudaSetDevice(ds->device) != cudaSuccess) return -1;
+  DevW W;
+  if (stage_weights(*c, *cfg, *w, W, false) != 0) return -1;
+  if (prefill_state(*c, *ds, *cfg, W, x, seq_len) != 0) return -1;
+  const size_t S = seq_len;
+  CK(cudaMemcpyAsync(state->latent_q8, ds->lat8, S * R, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaMemcpyAsync(state->latent_scale, ds->lscale, S * 4, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaMemcpyAsync(state->rope_bf16, ds->rope16, S * DR * 2, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  ds->dev_len = seq_len;
+  state->len = seq_len;
+  return 0;
+}
+
+// Reference: src/mla_compressed_q8_state.c:161-255.
+KVL_EXPORT int kvl_mla_decode_compressed_q8_bf16(float *out, const float *x, int position, const KvlMlaConfig *cfg,
+                                                 const KvlMlaBF16 *w, KvlMlaCompressedQ8State *state) {
+  if (!out || !x || !cfg || !w || !state || !w->q_proj || !w->kv_a_proj || !w->kv_a_norm || !w->kv_b_proj ||
+      !w->o_proj || position != state->len || position < 0 || position >= state->capacity ||
+      state->kv_lora_rank != cfg->kv_lora_rank || state->qk_rope_dim != cfg->qk_rope_dim)
+    return -1;
+  if (!cfg_dims_ok(*cfg)) return -1;
+  DevState *ds = find_state(state->latent_q8);
+  if (!ds || ds->fmt != FMT_Q8) {
+    set_err("state was not created by kvl_mla_compressed_q8_state_init");
+    return -1;
+  }
+  Ctx *c = get_ctx(ds->device);
+  if (!c) return -1;
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (cudaSetDevice(ds->device) != cudaSuccess) return -1;
+  if (sync_q8_state(*c, *ds, *state) != 0) return -1;
+  DevW W;
+  if (stage_weights(*c, *cfg, *w, W, true) != 0) return -1;
+  const size_t R = cfg->kv_lora_rank, DR = cfg->qk_rope_dim;
+  if (decode_one(*c, *ds, *cfg, W, x, out, position, nullptr, nullptr, state->latent_q8 + position * R,
+                 state->latent_scale + position, state->rope_bf16 + position * DR) != 0)
+    return -1;
+  ds->dev_len = position + 1;
+  state->len = position + 1;
+  return 0;
+}
+
+// =================================================================== prefill
+// Reference: src/mla_prefill_streaming.c:78-206 (validation :80-85).  Causal
+// attention runs in the absorbed form over a temporary bf16 latent pool: query
+// t attends rows [0, t] through the same attend kernel as decode.
+KVL_EXPORT int kvl_mla_prefill_bf16(float *out, const float *x, int seq_len, const KvlMlaConfig *cfg,
+                                    const KvlMlaBF16 *w) {
+  if (!out || !x || !cfg || !w || !w->q_proj || !w->kv_a_proj || !w->kv_a_norm || !w->kv_b_proj || !w->o_proj ||
+      seq_len <= 0 || cfg->hidden_size <= 0 || cfg->num_heads <= 0 || cfg->qk_nope_dim <= 0 ||
+      cfg->qk_rope_dim <= 0 || (cfg->qk_rope_dim & 1) || cfg->v_head_dim <= 0 || cfg->kv_lora_rank <= 0 ||
+      cfg->rope_theta <= 0.0f)
+    return -1;
+  const int dev = current_device();
+  if (dev < 0) return -1;
+  Ctx *c = get_ctx(dev);
+  if (!c) return -1;
+  std::lock_guard<std::mutex> lk(c->mu);
+  const int S = seq_len, H = cfg->hidden_size, NH = cfg->num_heads, DN = cfg->qk_nope_dim;
+  const int DR = cfg->qk_rope_dim, DV = cfg->v_head_dim, R = cfg->kv_lora_rank, QD = DN + DR;
+  const size_t s = S;
+  DevW W;
+  if (stage_weights(*c, *cfg, *w, W, true) != 0) return -1;
+  if (!c->x.ensure(s * H * 4) || !c->q.ensure(s * NH * QD * 4) || !c->ka.ensure(s * (R + DR) * 4) ||
+      !c->qabs.ensure(s * NH * (R + DR) * 4) || !c->mix.ensure(s * NH * R * 4) || !c->ho.ensure(s * NH * DV * 4) ||
+      !c->y.ensure(s * H * 4) || !c->kvtmp.ensure((s + kTileTok) * (R + DR) * 2)) {
+    set_err("cudaMalloc of prefill scratch failed");
+    return -1;
+  }
+  CK(cudaMemcpyAsync(c->x.p, x, s * H * 4, cudaMemcpyHostToDevice, c->stream));
+  CK(gemv_bf16(c->q.as<float>(), c->x.as<float>(), W.q, H, NH * QD, S, c->stream));
+  CK(gemv_bf16(c->ka.as<float>(), c->x.as<float>(), W.kva, H, R + DR, S, c->stream));
+  uint16_t *pool = c->kvtmp.as<uint16_t>();
+  CK(append_bf16(pool, 0, c->ka.as<float>(), W.kvan, S, R, DR, 0, cfg->rms_eps, cfg->rope_theta, nullptr,
+                 c->stream));
+  CK(absorb(c->qabs.as<float>(), c->q.as<float>(), W.kvb, S, NH, DN, DV, DR, R, 0, cfg->rope_theta, c->stream));
+  std::vector<int> lens(S);
+  std::vector<long long> row0(S, 0);
+  for (int t = 0; t < S; ++t) lens[t] = t + 1;
+  HostPlan hp;
+  if (build_attend_plan(hp, S, lens.data(), row0.data(), c->sms) != 0) {
+    set_err("prefill attend plan failed");
+    return -1;
+  }
+  if (c->plan.upload(hp, NH, R, c->stream, nullptr, 0) != 0) {
+    set_err("prefill attend plan upload failed");
+    return -1;
+  }
+  AttendLaunch a;
+  a.nh = NH;
+  a.R = R;
+  a.DR = DR;
+  a.rows = static_cast<long long>(s + kTileTok);
+  a.q = c->qabs.as<float>();
+  a.out = c->mix.as<float>();
+  a.kv = pool;
+  a.softmax_scale = 1.0f / sqrtf(static_cast<float>(QD));
+  if (c->plan.launch(a, c->stream) != 0) {
+    set_err("prefill attend launch failed");
+    return -1;
+  }
+  CK(vup(c->ho.as<float>(), c->mix.as<float>(), W.kvb, S, NH, DN, DV, R, c->stream));
+  CK(gemv_bf16(c->y.as<float>(), c->ho.as<float>(), W.o, NH * DV, H, S, c->stream));
+  uint32_t err = 0;
+  CK(cudaMemcpyAsync(out, c->y.p, s * H * 4, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaMemcpyAsync(&err, c->plan.err_word(), 4, cudaMemcpyDeviceToHost, c->stream));
+  CK(cudaStreamSynchronize(c->stream));
+  if (err != 0) {
+    set_err("prefill attend reported device error 0x%x", err);
+    return -1;
+  }
+  return 0;
+}
+
+// =================================================================== attend plans
+struct KvlMlaAttendPlan {
+  int device = 0;
+  int nh = 0, R = 0;
+  kvl::DevicePlan dp;
+};
+
+KVL_EXPORT int kvl_mla_attend_plan_create(KvlMlaAttendPlan **plan, int batch, const int *seq_len,
+                                          const int64_t *seq_row0, int num_heads, int kv_lora_rank, int max_ctas) {
+  if (!plan || batch <= 0 || !seq_len || !seq_row0 || num_heads <= 0 || kv_lora_rank <= 0 || max_ctas < 0) {
+    set_err("invalid plan arguments");
+    return -1;
+  }
+  *plan = nullptr;
+  const int dev = current_device();
+  if (dev < 0) return -1;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  HostPlan hp;
+  std::vector<long long> r0(seq_row0, seq_row0 + batch);
+  if (build_attend_plan(hp, batch, seq_len, r0.data(), max_ctas > 0 ? max_ctas : sms) != 0) {
+    set_err("invalid sequence lengths or rows");
+    return -1;
+  }
+  KvlMlaAttendPlan *p = new KvlMlaAttendPlan();
+  p->device = dev;
+  p->nh = num_heads;
+  p->R = kv_lora_rank;
+  if (p->dp.upload(hp, num_heads, kv_lora_rank, nullptr, nullptr, 0) != 0 || cudaDeviceSynchronize() != cudaSuccess) {
+    set_err("plan upload failed");
+    p->dp.release();
+    delete p;
+    return -1;
+  }
+  *plan = p;
+  return 0;
+}
+
+KVL_EXPORT void kvl_mla_attend_plan_destroy(KvlMlaAttendPlan *plan) {
+  if (!plan) return;
+  plan->dp.release();
+  delete plan;
+}
+
+KVL_EXPORT int kvl_mla_attend_plan_info(const KvlMlaAttendPlan *plan, int *ctas, int *partials, int *segments) {
+  if (!plan) return -1;
+  if (ctas) *ctas = plan->dp.host.grid;
+  if (partials) *partials = plan->dp.host.nparts;
+  if (segments) *segments = static_cast<int>(plan->dp.host.segs.size());
+  return 0;
+}
+
+static int attend_common(const KvlMlaAttendPlan *plan, AttendLaunch &a, int num_heads, int R, int DR,
+                         void *stream) {
+  if (!plan || !a.out || !a.q || a.rows <= 0 || num_heads != plan->nh || R != plan->R || DR <= 0 || (DR & 1)) {
+    set_err("invalid attend arguments");
+    return -1;
+  }
+  a.nh = num_heads;
+  a.R = R;
+  a.DR = DR;
+  for (int b = 0; b < plan->dp.host.batch; ++b)
+    if (plan->dp.host.seq_row0[b] + plan->dp.host.seq_len[b] > a.rows) {
+      set_err("sequence %d extends past the pool (%lld rows)", b, static_cast<long long>(a.rows));
+      return -1;
+    }
+  if (plan->dp.launch(a, static_cast<cudaStream_t>(stream)) != 0) {
+    set_err("attend launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return -1;
+  }
+  return 0;
+}
+
+KVL_EXPORT int kvl_mla_attend_bf16(const KvlMlaAttendPlan *plan, float *d_out, float *d_lse, const float *d_q,
+                                   const uint16_t *d_kv, int64_t rows, int num_heads, int kv_lora_rank, int rope_dim,
+                                   float softmax_scale, void *stream) {
+  if (!d_kv) {
+    set_err("null kv pool");
+    return -1;
+  }
+  AttendLaunch a;
+  a.q8 = false;
+  a.rows = rows;
+  a.q = d_q;
+  a.out = d_out;
+  a.lse = d_lse;
+  a.kv = d_kv;
+  a.softmax_scale = softmax_scale;
+  return attend_common(plan, a, num_heads, kv_lora_rank, rope_dim, stream);
+}
+
+KVL_EXPORT int kvl_mla_attend_q8(const KvlMlaAttendPlan *plan, float *d_out, float *d_lse, const float *d_q,
+                                 const int8_t *d_latent_q8, const float *d_latent_scale, const uint16_t *d_rope_bf16,
+                                 int64_t rows, int num_heads, int kv_lora_rank, int rope_dim, float softmax_scale,
+                                 void *stream) {
+  if (!d_latent_q8 || !d_latent_scale || !d_rope_bf16) {
+    set_err("null q8 pool");
+    return -1;
+  }
+  AttendLaunch a;
+  a.q8 = true;
+  a.rows = rows;
+  a.q = d_q;
+  a.out = d_out;
+  a.lse = d_lse;
+  a.lat8 = d_latent_q8;
+  a.lscale = d_latent_scale;
+  a.rope16 = d_rope_bf16;
+  a.softmax_scale = softmax_scale;
+  return attend_common(plan, a, num_heads, kv_lora_rank, rope_dim, stream);
+}
+
+KVL_EXPORT int kvl_mla_attend_check(const KvlMlaAttendPlan *plan, void *stream) {
+  if (!plan) return -1;
+  CK(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  uint32_t err = 0;
+  CK(cudaMemcpy(&err, plan->dp.err_word(), 4, cudaMemcpyDeviceToHost));
+  if (err) {
+    CK(cudaMemset(plan->dp.err_word(), 0, 4));
+    set_err("attend kernel reported device error 0x%x", err);
+    return -1;
+  }
+  return 0;
+}
+
+KVL_EXPORT int kvl_mla_merge_partials(float *d_out, float *d_lse, const float *d_part_o, const float *d_part_lse,
+                                      int parts, int batch, int num_heads, int kv_lora_rank, void *stream) {
+  if (!d_out || !d_part_o || !d_part_lse || parts <= 0 || batch <= 0 || num_heads <= 0 || kv_lora_rank <= 0) {
+    set_err("invalid merge arguments");
+    return -1;
+  }
+  std::vector<MergeEntry> e(batch);
+  for (int b = 0; b < batch; ++b) e[b] = MergeEntry{b, b, parts, batch};
+  void *d_e = nullptr;
+  CK(cudaMallocAsync(&d_e, e.size() * sizeof(MergeEntry), static_cast<cudaStream_t>(stream)));
+  CK(cudaMemcpyAsync(d_e, e.data(), e.size() * sizeof(MergeEntry), cudaMemcpyHostToDevice,
+                     static_cast<cudaStream_t>(stream)));
+  CK(launch_merge(d_out, d_lse, d_part_o, d_part_lse, static_cast<const MergeEntry *>(d_e), batch, num_heads,
+                  kv_lora_rank, static_cast<cudaStream_t>(stream)));
+  CK(cudaFreeAsync(d_e, static_cast<cudaStream_t>(stream)));
+  CK(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  return 0;
+}
+
+// =================================================================== batched decode step
+static size_t step_ws_layout(const KvlMlaConfig &c, int B, size_t off[6]) {
+  const size_t NH = c.num_heads, QD = c.qk_nope_dim + c.qk_rope_dim, R = c.kv_lora_rank, DR = c.qk_rope_dim;
+  const size_t DV = c.v_head_dim;
+  const size_t sz[5] = {B * NH * QD * 4, B * (R + DR) * 4, B * NH * (R + DR) * 4, B * NH * R * 4, B * NH * DV * 4};
+  size_t o = 0;
+  for (int i = 0; i < 5; ++i) {
+    off[i] = o;
+    o += (sz[i] + 255) & ~size_t(255);
+  }
+  off[5] = o;
+  return o;
+}
+
+KVL_EXPORT size_t kvl_mla_decode_step_workspace_bytes(const KvlMlaConfig *cfg, int batch) {
+  if (!cfg || batch <= 0) return 0;
+  size_t off[6];
+  return step_ws_layout(*cfg, batch, off);
+}
+
+KVL_EXPORT int kvl_mla_decode_step_bf16(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w,
+                                        const KvlMlaAttendPlan *plan, float *d_out, const float *d_x, uint16_t *d_kv,
+                                        int64_t rows, const int64_t *d_row, const int *d_pos, int batch,
+                                        void *d_workspace, void *stream) {
+  if (!cfg || !w || !plan || !d_out || !d_x || !d_kv || !d_row || !d_pos || batch <= 0 || !d_workspace ||
+      !cfg_dims_ok(*cfg) || plan->dp.host.batch != batch) {
+    set_err("invalid decode step arguments");
+    return -1;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int H = cfg->hidden_size, NH = cfg->num_heads, DN = cfg->qk_nope_dim, DR = cfg->qk_rope_dim;
+  const int DV = cfg->v_head_dim, R = cfg->kv_lora_rank, QD = DN + DR;
+  size_t off[6];
+  step_ws_layout(*cfg, batch, off);
+  uint8_t *ws = static_cast<uint8_t *>(d_workspace);
+  float *q = reinterpret_cast<float *>(ws + off[0]);
+  float *ka = reinterpret_cast<float *>(ws + off[1]);
+  float *qabs = reinterpret_cast<float *>(ws + off[2]);
+  float *mix = reinterpret_cast<float *>(ws + off[3]);
+  float *ho = reinterpret_cast<float *>(ws + off[4]);
+  CK(gemv_bf16(q, d_x, w->q_proj, H, NH * QD, batch, s));
+  CK(gemv_bf16(ka, d_x, w->kv_a_proj, H, R + DR, batch, s));
+  CK(append_bf16(d_kv, 0, ka, w->kv_a_norm, batch, R, DR, 0, cfg->rms_eps, cfg->rope_theta, nullptr, s,
+                 reinterpret_cast<const long long *>(d_row), d_pos));
+  CK(absorb(qabs, q, w->kv_b_proj, batch, NH, DN, DV, DR, R, 0, cfg->rope_theta, s, d_pos));
+  AttendLaunch a;
+  a.rows = rows;
+  a.q = qabs;
+  a.out = mix;
+  a.kv = d_kv;
+  a.softmax_scale = 1.0f / sqrtf(static_cast<float>(QD));
+  if (attend_common(plan, a, NH, R, DR, stream) != 0) return -1;
+  CK(vup(ho, mix, w->kv_b_proj, batch, NH, DN, DV, R, s));
+  CK(gemv_bf16(d_out, ho, w->o_proj, NH * DV, H, batch, s));
+  return 0;
+}
+
+// =================================================================== Q8 helpers
+KVL_EXPORT int kvl_mla_q8_quantize_rows(int8_t *d_q, float *d_scale, const float *d_x, int rows, int R, void *stream) {
+  if (!d_q || !d_scale || !d_x || rows <= 0 || R <= 0) {
+    set_err("invalid quantize arguments");
+    return -1;
+  }
+  CK(quantize_rows(d_q, d_scale, d_x, rows, R, static_cast<cudaStream_t>(stream)));
+  return 0;
+}
+
+KVL_EXPORT int kvl_mla_q8_dequant(float *d_out, const int8_t *d_q, const float *d_scale, int64_t rows, int R,
+                                  void *stream) {
+  if (!d_out || !d_q || !d_scale || rows <= 0 || R <= 0) {
+    set_err("invalid dequant arguments");
+    return -1;
+  }
+  CK(dequant(d_out, d_q, d_scale, rows, R, static_cast<cudaStream_t>(stream)));
+  return 0;
+}
+
+KVL_EXPORT int kvl_mla_bf16_rne(uint16_t *d_out, const float *d_x, int64_t n, void *stream) {
+  if (!d_out || !d_x || n <= 0) {
+    set_err("invalid bf16 arguments");
+    return -1;
+  }
+  CK(bf16_rne(d_out, d_x, n, static_cast<cudaStream_t>(stream)));
+  return 0;
+}

@@ -1,0 +1,378 @@
+// mla_kernels.cu -- the small kernels around the attend core of one absorbed
+// MLA decode step (src/mla_compressed_state.c:86-161):
+//   gemv_bf16      y = W x for the q_proj / kv_a_proj / o_proj projections
+//                  (src/ops.c:53-66; fp32 accumulation like the AVX2 build)
+//   append_*       RMSNorm of the latent (src/ops.c:76-83) and interleaved
+//                  RoPE of the rope slice (src/mla_compressed_state.c:8-22),
+//                  stored as a bf16 state row or quantised into the Q8 state
+//                  (src/mla_compressed_q8_state.c:9-16, 34-55, 111-127)
+//   absorb         q_lat = W_UK^T q_nope per head and RoPE of q_pe
+//                  (src/mla_compressed_state.c:119-131)
+//   vup            head_out = W_UV mix per head (src/mla_compressed_state.c:149-155)
+//
+// The float arithmetic of RMSNorm, RoPE and the quantiser uses explicitly
+// rounded intrinsics (no FMA contraction) and double-precision angles, so the
+// Q8 rows are bit-identical to the reference's given the same fp32 inputs.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "mla_kernels.cuh"
+
+namespace kvl {
+
+__device__ __forceinline__ float bf16f(uint16_t h) { return __uint_as_float(static_cast<uint32_t>(h) << 16); }
+
+// src/mla_compressed_q8_state.c:9-16: RNE, Inf/NaN keep their high half.
+__device__ __forceinline__ uint16_t f32_to_bf16_rne_ref(float f) {
+  uint32_t u = __float_as_uint(f);
+  if ((u & 0x7f800000u) != 0x7f800000u) u += 0x7fffu + ((u >> 16) & 1u);
+  return static_cast<uint16_t>(u >> 16);
+}
+
+template <typename T>
+__device__ __forceinline__ T block_sum(T v, T *red) {
+  for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  T r = 0;
+  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) r += red[i];
+  return r;
+}
+
+__device__ __forceinline__ float block_max(float v, float *red) {
+  for (int off = 16; off > 0; off >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, off));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = red[0];
+  for (int i = 1; i < static_cast<int>(blockDim.x >> 5); ++i) r = fmaxf(r, red[i]);
+  return r;
+}
+
+// --------------------------------------------------------------------- gemv
+// One warp per output row, NB tokens per block share each weight load.  The
+// per-row reduction order depends only on `in`, so a row's result is the same
+// whichever tokens it is batched with.
+template <int NB>
+__global__ void gemv_bf16_kernel(float *y, const float *x, const uint16_t *W, int in, int out, int n) {
+  extern __shared__ float xs[];  // [NB][in]
+  const int t0 = blockIdx.y * NB;
+  const int nb = min(NB, n - t0);
+  for (int i = threadIdx.x; i < nb * in; i += blockDim.x) xs[i] = x[static_cast<size_t>(t0) * in + i];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int o = blockIdx.x * 8 + warp;
+  if (o >= out) return;
+  const uint16_t *row = W + static_cast<size_t>(o) * in;
+  float acc[NB];
+#pragma unroll
+  for (int b = 0; b < NB; ++b) acc[b] = 0.f;
+  const bool vec = ((in & 7) == 0) && ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
+  if (vec) {
+    for (int i8 = lane; i8 < (in >> 3); i8 += 32) {
+      const uint4 wv = *reinterpret_cast<const uint4 *>(row + i8 * 8);
+      const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+      float wf[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        wf[2 * k] = __uint_as_float(wr[k] << 16);
+        wf[2 * k + 1] = __uint_as_float(wr[k] & 0xffff0000u);
+      }
+#pragma unroll
+      for (int b = 0; b < NB; ++b) {
+        if (b < nb) {
+          const float *xb = xs + b * in + i8 * 8;
+#pragma unroll
+          for (int k = 0; k < 8; ++k) acc[b] = fmaf(wf[k], xb[k], acc[b]);
+        }
+      }
+    }
+  } else {
+    for (int i = lane; i < in; i += 32) {
+      const float wf = bf16f(row[i]);
+#pragma unroll
+      for (int b = 0; b < NB; ++b)
+        if (b < nb) acc[b] = fmaf(wf, xs[b * in + i], acc[b]);
+    }
+  }
+#pragma unroll
+  for (int b = 0; b < NB; ++b) {
+    float v = acc[b];
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (lane == 0 && b < nb) y[static_cast<size_t>(t0 + b) * out + o] = v;
+  }
+}
+
+cudaError_t gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  constexpr int NB = 4;
+  const size_t sm = static_cast<size_t>(NB) * in * sizeof(float);
+  if (sm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(gemv_bf16_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(sm));
+    if (e != cudaSuccess) return e;
+  }
+  dim3 grid((out + 7) / 8, (n + NB - 1) / NB);
+  gemv_bf16_kernel<NB><<<grid, 256, sm, s>>>(y, x, W, in, out, n);
+  return cudaGetLastError();
+}
+
+// --------------------------------------------------------------------- rope / rmsnorm
+// src/mla_compressed_state.c:8-22: angle in double, cos/sin rounded to float,
+// rotation in float with separately rounded products.
+__device__ __forceinline__ void rope_pair(float a, float b, int i, int dim, int pos, float theta, float &lo,
+                                          float &hi) {
+  const double inv_freq = pow(static_cast<double>(theta), -(static_cast<double>(2 * i) / static_cast<double>(dim)));
+  const double ang = static_cast<double>(pos) * inv_freq;
+  const float c = static_cast<float>(cos(ang));
+  const float s = static_cast<float>(sin(ang));
+  lo = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+  hi = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+}
+
+// RMSNorm of ka[0:R] into lat (shared memory), src/ops.c:76-83.
+__device__ void rmsnorm_row(float *lat, const float *ka, const uint16_t *w, int R, float eps, double *dred) {
+  double ss = 0.0;
+  for (int i = threadIdx.x; i < R; i += blockDim.x) ss += static_cast<double>(ka[i]) * static_cast<double>(ka[i]);
+  ss = block_sum<double>(ss, dred);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ss / static_cast<double>(R)), eps)));
+  for (int i = threadIdx.x; i < R; i += blockDim.x) lat[i] = __fmul_rn(__fmul_rn(ka[i], inv), bf16f(w[i]));
+  __syncthreads();
+}
+
+// bf16 state row [R latent | DR rope] at row (row0 + pos0 + t) of `kv` for each
+// of the n tokens; ka is [n][R + DR] (kv_a_proj output).  rows_f32 (optional)
+// receives the fp32 row before bf16 rounding.
+__global__ void append_bf16_kernel(uint16_t *kv, long long row0, const float *ka, const uint16_t *norm_w, int R,
+                                   int DR, int pos0, float eps, float theta, float *rows_f32,
+                                   const long long *row_of, const int *pos_of) {
+  extern __shared__ float sh[];
+  float *lat = sh;
+  double *dred = reinterpret_cast<double *>(sh + ((R + 1) & ~1));
+  const int t = blockIdx.x;
+  const float *kt = ka + static_cast<size_t>(t) * (R + DR);
+  rmsnorm_row(lat, kt, norm_w, R, eps, dred);
+  const int pos = pos_of ? pos_of[t] : pos0 + t;
+  const long long row = row_of ? row_of[t] : row0 + pos0 + t;
+  uint16_t *dst = kv + static_cast<size_t>(row) * (R + DR);
+  float *df = rows_f32 ? rows_f32 + static_cast<size_t>(t) * (R + DR) : nullptr;
+  for (int i = threadIdx.x; i < R; i += blockDim.x) {
+    dst[i] = __bfloat16_as_ushort(__float2bfloat16_rn(lat[i]));
+    if (df) df[i] = lat[i];
+  }
+  const int half = DR / 2;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    float lo, hi;
+    rope_pair(kt[R + 2 * i], kt[R + 2 * i + 1], i, DR, pos, theta, lo, hi);
+    dst[R + i] = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+    dst[R + half + i] = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+    if (df) { df[R + i] = lo; df[R + half + i] = hi; }
+  }
+}
+
+// src/mla_compressed_q8_state.c:34-55 for one row held in shared memory.
+__device__ void quantize_row(int8_t *q, float *scale_out, const float *lat, int R, float *fred) {
+  float amax = 0.f;
+  for (int i = threadIdx.x; i < R; i += blockDim.x) amax = fmaxf(amax, fabsf(lat[i]));
+  amax = block_max(amax, fred);
+  if (!(amax > 0.0f) || !isfinite(amax)) {
+    for (int i = threadIdx.x; i < R; i += blockDim.x) q[i] = 0;
+    if (threadIdx.x == 0) *scale_out = 1.0f;
+    return;
+  }
+  const float scale = __fdiv_rn(amax, 127.0f);
+  const float inv = __fdiv_rn(1.0f, scale);
+  for (int i = threadIdx.x; i < R; i += blockDim.x) {
+    const float r = roundf(__fmul_rn(lat[i], inv));
+    // A NaN element of a finite row passes the reference's clamp unchanged and
+    // its (int8_t) conversion on x86-64 keeps the low byte of INT32_MIN: 0.
+    q[i] = isnan(r) ? static_cast<int8_t>(0) : static_cast<int8_t>(fminf(fmaxf(r, -127.0f), 127.0f));
+  }
+  if (threadIdx.x == 0) *scale_out = scale;
+}
+
+__global__ void append_q8_kernel(int8_t *lat8, float *lscale, uint16_t *rope16, long long row0, const float *ka,
+                                 const uint16_t *norm_w, int R, int DR, int pos0, float eps, float theta,
+                                 const long long *row_of, const int *pos_of) {
+  extern __shared__ float sh[];
+  float *lat = sh;
+  double *dred = reinterpret_cast<double *>(sh + ((R + 1) & ~1));
+  float *fred = reinterpret_cast<float *>(dred + 32);
+  const int t = blockIdx.x;
+  const int pos = pos_of ? pos_of[t] : pos0 + t;
+  const long long row = row_of ? row_of[t] : row0 + pos0 + t;
+  const float *kt = ka + static_cast<size_t>(t) * (R + DR);
+  rmsnorm_row(lat, kt, norm_w, R, eps, dred);
+  quantize_row(lat8 + static_cast<size_t>(row) * R, lscale + row, lat, R, fred);
+  const int half = DR / 2;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    float lo, hi;
+    rope_pair(kt[R + 2 * i], kt[R + 2 * i + 1], i, DR, pos, theta, lo, hi);
+    rope16[static_cast<size_t>(row) * DR + i] = f32_to_bf16_rne_ref(lo);
+    rope16[static_cast<size_t>(row) * DR + half + i] = f32_to_bf16_rne_ref(hi);
+  }
+}
+
+static size_t append_smem(int R) { return static_cast<size_t>((R + 1) & ~1) * 4 + 32 * 8 + 32 * 4; }
+
+cudaError_t append_bf16(uint16_t *kv, long long row0, const float *ka, const uint16_t *norm_w, int n, int R,
+                        int DR, int pos0, float eps, float theta, float *rows_f32, cudaStream_t s,
+                        const long long *row_of, const int *pos_of) {
+  if (n <= 0) return cudaSuccess;
+  append_bf16_kernel<<<n, 128, append_smem(R), s>>>(kv, row0, ka, norm_w, R, DR, pos0, eps, theta, rows_f32,
+                                                    row_of, pos_of);
+  return cudaGetLastError();
+}
+
+cudaError_t append_q8(int8_t *lat8, float *lscale, uint16_t *rope16, long long row0, const float *ka,
+                      const uint16_t *norm_w, int n, int R, int DR, int pos0, float eps, float theta,
+                      cudaStream_t s, const long long *row_of, const int *pos_of) {
+  if (n <= 0) return cudaSuccess;
+  append_q8_kernel<<<n, 128, append_smem(R), s>>>(lat8, lscale, rope16, row0, ka, norm_w, R, DR, pos0, eps, theta,
+                                                  row_of, pos_of);
+  return cudaGetLastError();
+}
+
+// --------------------------------------------------------------------- absorb / vup
+// qabs[t][h] = [ W_UK[h]^T q_nope[t][h] (R values) | rope(q_pe[t][h]) (DR values) ]
+__global__ void absorb_kernel(float *qabs, const float *q, const uint16_t *kvb, int NH, int DN, int DV, int DR,
+                              int R, int pos0, float theta, const int *pos_of) {
+  extern __shared__ float qn[];
+  const int h = blockIdx.x, t = blockIdx.y;
+  const float *qh = q + (static_cast<size_t>(t) * NH + h) * (DN + DR);
+  for (int d = threadIdx.x; d < DN; d += blockDim.x) qn[d] = qh[d];
+  __syncthreads();
+  float *dst = qabs + (static_cast<size_t>(t) * NH + h) * (R + DR);
+  const uint16_t *wh = kvb + static_cast<size_t>(h) * (DN + DV) * R;
+  for (int r = threadIdx.x; r < R; r += blockDim.x) {
+    float acc = 0.f;
+    for (int d = 0; d < DN; ++d) acc = fmaf(bf16f(wh[static_cast<size_t>(d) * R + r]), qn[d], acc);
+    dst[r] = acc;
+  }
+  const int half = DR / 2;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    float lo, hi;
+    rope_pair(qh[DN + 2 * i], qh[DN + 2 * i + 1], i, DR, pos_of ? pos_of[t] : pos0 + t, theta, lo, hi);
+    dst[R + i] = lo;
+    dst[R + half + i] = hi;
+  }
+}
+
+cudaError_t absorb(float *qabs, const float *q, const uint16_t *kvb, int n, int NH, int DN, int DV, int DR, int R,
+                   int pos0, float theta, cudaStream_t s, const int *pos_of) {
+  if (n <= 0) return cudaSuccess;
+  absorb_kernel<<<dim3(NH, n), 256, DN * sizeof(float), s>>>(qabs, q, kvb, NH, DN, DV, DR, R, pos0, theta, pos_of);
+  return cudaGetLastError();
+}
+
+// ho[t][h*DV + d] = sum_r W_UV[h][d][r] * mix[t][h][r]; one warp per (h, d).
+__global__ void vup_kernel(float *ho, const float *mix, const uint16_t *kvb, int NH, int DN, int DV, int R) {
+  const int t = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hd = blockIdx.x * 8 + warp;
+  if (hd >= NH * DV) return;
+  const int h = hd / DV, d = hd % DV;
+  const uint16_t *row = kvb + (static_cast<size_t>(h) * (DN + DV) + DN + d) * R;
+  const float *m = mix + (static_cast<size_t>(t) * NH + h) * R;
+  float acc = 0.f;
+  if ((R & 7) == 0 && (reinterpret_cast<uintptr_t>(row) & 15) == 0) {
+    for (int i8 = lane; i8 < R / 8; i8 += 32) {
+      const uint4 wv = *reinterpret_cast<const uint4 *>(row + i8 * 8);
+      const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        acc = fmaf(__uint_as_float(wr[k] << 16), m[i8 * 8 + 2 * k], acc);
+        acc = fmaf(__uint_as_float(wr[k] & 0xffff0000u), m[i8 * 8 + 2 * k + 1], acc);
+      }
+    }
+  } else {
+    for (int i = lane; i < R; i += 32) acc = fmaf(bf16f(row[i]), m[i], acc);
+  }
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) ho[static_cast<size_t>(t) * NH * DV + hd] = acc;
+}
+
+cudaError_t vup(float *ho, const float *mix, const uint16_t *kvb, int n, int NH, int DN, int DV, int R,
+                cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  vup_kernel<<<dim3((NH * DV + 7) / 8, n), 256, 0, s>>>(ho, mix, kvb, NH, DN, DV, R);
+  return cudaGetLastError();
+}
+
+// --------------------------------------------------------------------- Q8 helpers
+__global__ void quantize_rows_kernel(int8_t *q, float *scale, const float *x, int R) {
+  extern __shared__ float sh[];
+  float *row = sh;
+  float *fred = sh + R;
+  const int t = blockIdx.x;
+  for (int i = threadIdx.x; i < R; i += blockDim.x) row[i] = x[static_cast<size_t>(t) * R + i];
+  __syncthreads();
+  quantize_row(q + static_cast<size_t>(t) * R, scale + t, row, R, fred);
+}
+
+cudaError_t quantize_rows(int8_t *q, float *scale, const float *x, int rows, int R, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  quantize_rows_kernel<<<rows, 128, (R + 32) * sizeof(float), s>>>(q, scale, x, R);
+  return cudaGetLastError();
+}
+
+// src/mla_compressed_q8_state.c:57-61: one float multiply per element.
+__global__ void dequant_kernel(float *out, const int8_t *q, const float *scale, long long rows, int R) {
+  const long long n = rows * R;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    out[i] = __fmul_rn(static_cast<float>(q[i]), scale[i / R]);
+}
+
+cudaError_t dequant(float *out, const int8_t *q, const float *scale, long long rows, int R, cudaStream_t s) {
+  if (rows <= 0) return cudaSuccess;
+  const long long n = rows * R;
+  const int grid = static_cast<int>((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+  dequant_kernel<<<grid, 256, 0, s>>>(out, q, scale, rows, R);
+  return cudaGetLastError();
+}
+
+__global__ void bf16_rne_kernel(uint16_t *out, const float *x, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    out[i] = f32_to_bf16_rne_ref(x[i]);
+}
+
+cudaError_t bf16_rne(uint16_t *out, const float *x, long long n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const int grid = static_cast<int>((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+  bf16_rne_kernel<<<grid, 256, 0, s>>>(out, x, n);
+  return cudaGetLastError();
+}
+
+// bf16 state row -> fp32 (the host mirror of the reference's fp32 state).
+__global__ void bf16_to_f32_kernel(float *out, const uint16_t *x, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    out[i] = bf16f(x[i]);
+}
+
+cudaError_t bf16_to_f32(float *out, const uint16_t *x, long long n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const int grid = static_cast<int>((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+  bf16_to_f32_kernel<<<grid, 256, 0, s>>>(out, x, n);
+  return cudaGetLastError();
+}
+
+__global__ void f32_to_bf16_kernel(uint16_t *out, const float *x, long long n) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    out[i] = __bfloat16_as_ushort(__float2bfloat16_rn(x[i]));
+}
+
+cudaError_t f32_to_bf16(uint16_t *out, const float *x, long long n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const int grid = static_cast<int>((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+  f32_to_bf16_kernel<<<grid, 256, 0, s>>>(out, x, n);
+  return cudaGetLastError();
+}
+
+}  // namespace kvl

@@ -1,0 +1,26 @@
+// mla_kernels.cuh -- launchers of the decode-step kernels in mla_kernels.cu.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace kvl {
+
+cudaError_t gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int n, cudaStream_t s);
+cudaError_t append_bf16(uint16_t *kv, long long row0, const float *ka, const uint16_t *norm_w, int n, int R,
+                        int DR, int pos0, float eps, float theta, float *rows_f32, cudaStream_t s,
+                        const long long *row_of = nullptr, const int *pos_of = nullptr);
+cudaError_t append_q8(int8_t *lat8, float *lscale, uint16_t *rope16, long long row0, const float *ka,
+                      const uint16_t *norm_w, int n, int R, int DR, int pos0, float eps, float theta,
+                      cudaStream_t s, const long long *row_of = nullptr, const int *pos_of = nullptr);
+cudaError_t absorb(float *qabs, const float *q, const uint16_t *kvb, int n, int NH, int DN, int DV, int DR, int R,
+                   int pos0, float theta, cudaStream_t s, const int *pos_of = nullptr);
+cudaError_t vup(float *ho, const float *mix, const uint16_t *kvb, int n, int NH, int DN, int DV, int R,
+                cudaStream_t s);
+cudaError_t quantize_rows(int8_t *q, float *scale, const float *x, int rows, int R, cudaStream_t s);
+cudaError_t dequant(float *out, const int8_t *q, const float *scale, long long rows, int R, cudaStream_t s);
+cudaError_t bf16_rne(uint16_t *out, const float *x, long long n, cudaStream_t s);
+cudaError_t bf16_to_f32(float *out, const uint16_t *x, long long n, cudaStream_t s);
+cudaError_t f32_to_bf16(uint16_t *out, const float *x, long long n, cudaStream_t s);
+
+}  // namespace kvl

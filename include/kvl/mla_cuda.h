@@ -1,0 +1,126 @@
+/*
+ * kvl/mla_cuda.h -- B200 entry points of libkvl_mla_cuda beyond the
+ * reference's state API.
+ *
+ * The reference exposes the MLA hot path only through the hidden-state calls
+ * of kvl/mla_compressed_state.h, kvl/mla_compressed_q8_state.h and
+ * kvl_mla_prefill_bf16.  The calls below expose the same computation on device
+ * memory, batched, for callers that keep their states on the GPU (the batched
+ * and long-context decode configurations, multi-GPU sharding, benchmarks):
+ *
+ *   attend core  (src/mla_compressed_state.c:132-148 and
+ *                 src/mla_compressed_q8_state.c:216-238): absorbed query
+ *                 [B][16][576] fp32 against cached rows -> mix [B][16][512]
+ *   merge        combine (o, lse) partials of one sequence split across GPUs
+ *   Q8 helpers   the row quantiser (src/mla_compressed_q8_state.c:34-55), the
+ *                dequantiser (:57-61) and bf16 RNE (:9-16), bit-exact
+ *
+ * Pointers named d_* are device pointers; `stream` is a cudaStream_t (NULL =
+ * the legacy default stream).  Every call returns 0, or -1 with a message
+ * available from kvl_mla_cuda_last_error().  Set KVL_CUDA_VERBOSE=1 to also
+ * print failures on stderr.
+ */
+#ifndef KVL_MLA_CUDA_H
+#define KVL_MLA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+#include "kvl/ops.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Message of the last failure on this thread ("" when none). */
+const char *kvl_mla_cuda_last_error(void);
+
+/* Device-side weight cache keyed by host pointer (enable = 1) or per-call
+ * upload (0).  The cache is only correct while the host weight buffers stay
+ * allocated and unchanged, which holds in the reference runtime when its trunk
+ * cache covers every tensor (KVL_TRUNK_CACHE_MIB >= 1706); that setting, or
+ * KVL_CUDA_WEIGHT_CACHE=1, enables it at start-up.  Returns the previous mode. */
+int kvl_mla_cuda_weight_cache(int enable);
+
+/* Device bytes held by a state created by kvl_mla_compressed_state_init /
+ * kvl_mla_compressed_q8_state_init (0 for an unknown state). */
+size_t kvl_mla_cuda_state_device_bytes(const void *state);
+
+/* ------------------------------------------------------------------ attend */
+
+/* Work plan of one batch: cached lengths and the first pool row of every
+ * sequence (host arrays), split into equal contiguous ranges of 64-row tiles,
+ * one per CTA (max_ctas = 0: one per SM).  Owns the partial-output workspace,
+ * sized for num_heads x kv_lora_rank outputs per piece.  Created on, and used
+ * with, the current CUDA device. */
+typedef struct KvlMlaAttendPlan KvlMlaAttendPlan;
+
+int kvl_mla_attend_plan_create(KvlMlaAttendPlan **plan, int batch, const int *seq_len,
+                               const int64_t *seq_row0, int num_heads, int kv_lora_rank,
+                               int max_ctas);
+void kvl_mla_attend_plan_destroy(KvlMlaAttendPlan *plan);
+/* ctas: grid size; partials: split-sequence pieces; segments: total pieces. */
+int kvl_mla_attend_plan_info(const KvlMlaAttendPlan *plan, int *ctas, int *partials,
+                             int *segments);
+
+/* bf16 pool d_kv [rows][kv_lora_rank + rope_dim] (latent | rope).
+ * d_q [B][num_heads][kv_lora_rank + rope_dim] fp32 absorbed query,
+ * d_out [B][num_heads][kv_lora_rank] fp32, d_lse [B][num_heads] (natural log;
+ * may be NULL).  Production shape (16, 512, 64) runs the tcgen05 kernel; other
+ * shapes run a CUDA-core kernel. */
+int kvl_mla_attend_bf16(const KvlMlaAttendPlan *plan, float *d_out, float *d_lse,
+                        const float *d_q, const uint16_t *d_kv, int64_t rows, int num_heads,
+                        int kv_lora_rank, int rope_dim, float softmax_scale, void *stream);
+
+/* Q8 pool (reference layout): d_latent_q8 [rows][R] int8, d_latent_scale
+ * [rows] fp32, d_rope_bf16 [rows][DR] bf16. */
+int kvl_mla_attend_q8(const KvlMlaAttendPlan *plan, float *d_out, float *d_lse,
+                      const float *d_q, const int8_t *d_latent_q8, const float *d_latent_scale,
+                      const uint16_t *d_rope_bf16, int64_t rows, int num_heads, int kv_lora_rank,
+                      int rope_dim, float softmax_scale, void *stream);
+
+/* Waits for `stream` and returns -1 if a kernel of the plan's last launch
+ * reported a device-side error (a bounded wait that ran out); clears it. */
+int kvl_mla_attend_check(const KvlMlaAttendPlan *plan, void *stream);
+
+/* Combines `parts` partial results per sequence, stored part-major:
+ * d_part_o [parts][batch][num_heads][R], d_part_lse [parts][batch][num_heads]
+ * (e.g. gathered from the GPUs of a split-KV decode) into d_out / d_lse. */
+int kvl_mla_merge_partials(float *d_out, float *d_lse, const float *d_part_o,
+                           const float *d_part_lse, int parts, int batch, int num_heads,
+                           int kv_lora_rank, void *stream);
+
+/* ------------------------------------------------------------------ batched decode step */
+
+/* Device-resident layer weights (bf16, same shapes as KvlMlaBF16). */
+typedef struct {
+    const uint16_t *q_proj;
+    const uint16_t *kv_a_proj;
+    const uint16_t *kv_a_norm;
+    const uint16_t *kv_b_proj;
+    const uint16_t *o_proj;
+} KvlMlaDeviceWeights;
+
+/* Per-call scratch of kvl_mla_decode_step_bf16 for `batch` tokens. */
+size_t kvl_mla_decode_step_workspace_bytes(const KvlMlaConfig *cfg, int batch);
+
+/* One absorbed decode step for `batch` sequences of a bf16 pool, all on the
+ * device: projections, append of each token's row at d_row[b] (RoPE position
+ * d_pos[b]), attend over the plan's ranges (which must already include the
+ * appended rows), V up-projection and o_proj.  d_x/d_out [batch][H] fp32. */
+int kvl_mla_decode_step_bf16(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w,
+                             const KvlMlaAttendPlan *plan, float *d_out, const float *d_x,
+                             uint16_t *d_kv, int64_t rows, const int64_t *d_row,
+                             const int *d_pos, int batch, void *d_workspace, void *stream);
+
+/* ------------------------------------------------------------------ Q8 helpers */
+int kvl_mla_q8_quantize_rows(int8_t *d_q, float *d_scale, const float *d_x, int rows, int R,
+                             void *stream);
+int kvl_mla_q8_dequant(float *d_out, const int8_t *d_q, const float *d_scale, int64_t rows, int R,
+                       void *stream);
+int kvl_mla_bf16_rne(uint16_t *d_out, const float *d_x, int64_t n, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif
