@@ -1,0 +1,597 @@
+#!/usr/bin/env python3
+"""Benchmark of the MLA hot path on B200 (BASELINE metric: "MLA decode KV GB/s
+(% HBM peak) & prefill TFLOP/s at 1/2/4/8 B200").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload prefill|decode_q8|decode_long|decode_stack|decode_parity]
+
+Default workload: BASELINE config 2 (causal MLA prefill, one sequence of 4096
+tokens, H=2048, 16 heads; the configuration the metric's prefill half is quoted
+on and the largest that fits one GPU).  The decode half of the metric is
+reported in the same JSON line under "decode" (config 3 Q8 batched decode and
+config 5 long-context decode, KV GB/s against measured HBM bandwidth).
+
+Multi-GPU (torchrun, one rank per GPU): prefill runs one independent sequence
+per rank (weak scaling); batched decode shards sequences across ranks; the
+long-context decode splits the KV range across ranks and merges the (o, lse)
+partials with an NCCL all-gather and the library's merge kernel.
+
+Inputs are synthetic, seeded (seed = configuration index), created once on the
+device; every timed step is preceded by an untimed 256 MiB write that flushes
+L2, and each step is timed with CUDA events on the launching stream; the
+reported time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import datetime
+import json
+import math
+import os
+import pathlib
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ----------------------------------------------------------------------------- helpers
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+def prefill_flops(S, H=2048, NH=16, DN=128, DR=64, DV=128, R=512):
+    proj = 2 * S * (H * (NH * (DN + DR) + R + DR) + R * NH * (DN + DV) + NH * DV * H)
+    attn = S * (S + 1) // 2 * NH * 2 * ((DN + DR) + DV)
+    return proj, attn
+
+
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = None
+
+    def init(self, torch, backend="nccl"):
+        if self.world > 1:
+            import torch.distributed as dist
+            torch.cuda.set_device(self.local)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", self.local))
+            self.pg = dist
+        elif torch.cuda.is_available():
+            torch.cuda.set_device(0)
+
+    def barrier(self):
+        if self.pg:
+            self.pg.barrier()
+
+    def max(self, torch, v: float) -> float:
+        if not self.pg:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
+        return float(t.item())
+
+    def sum(self, torch, v: float) -> float:
+        if not self.pg:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        self.pg.all_reduce(t, op=self.pg.ReduceOp.SUM)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.pg.destroy_process_group()
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        self.gpu = gpu_index
+        self.path = ROOT / "gpurun_out" / f"clocks_rank{gpu_index}.csv"
+
+    def start(self):
+        try:
+            self.path.parent.mkdir(exist_ok=True)
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.f.close()
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": smax, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def timed_steps(torch, dist, step, K, W, flush):
+    """W untimed warm-ups, then K steps each timed with CUDA events (L2 flushed
+    before every step, outside the timed interval).  Returns max-over-ranks ms."""
+    stream = torch.cuda.current_stream()
+    for _ in range(W):
+        flush()
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    for a, b in ev:
+        flush()
+        a.record(stream)
+        step()
+        b.record(stream)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    total = sum(a.elapsed_time(b) for a, b in ev)
+    return dist.max(torch, total)
+
+
+def profile_read(lib):
+    buf = C.create_string_buffer(1 << 16)
+    n = lib.kvl_mla_cuda_profile_read(buf, len(buf))
+    out = {}
+    if n > 0:
+        for line in buf.value.decode().splitlines():
+            name, ms, cnt = line.split(",")
+            out[name] = (float(ms), int(cnt))
+    return out
+
+
+def load_lib():
+    import kvl_pkg
+    kvl_pkg.load()
+    import kvl_b200.kvl_mla as K
+    lib = K.load()
+    lib.kvl_mla_cuda_profile.argtypes = [C.c_int]
+    lib.kvl_mla_cuda_profile.restype = C.c_int
+    lib.kvl_mla_cuda_profile_read.argtypes = [C.c_char_p, C.c_size_t]
+    lib.kvl_mla_cuda_profile_read.restype = C.c_int
+    return K, lib
+
+
+def dev_bf16(torch, shape, std, gen, device):
+    return (torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std).to(torch.bfloat16)
+
+
+def device_weights(torch, K, cfg, gen, device, std=0.02):
+    H, NH, DN, DR, DV, R = cfg.hidden_size, cfg.num_heads, cfg.qk_nope_dim, cfg.qk_rope_dim, cfg.v_head_dim, \
+        cfg.kv_lora_rank
+    t = {
+        "q_proj": dev_bf16(torch, (NH * (DN + DR), H), std, gen, device),
+        "kv_a_proj": dev_bf16(torch, (R + DR, H), std, gen, device),
+        "kv_a_norm": torch.ones(R, dtype=torch.bfloat16, device=device),
+        "kv_b_proj": dev_bf16(torch, (NH * (DN + DV), R), std, gen, device),
+        "o_proj": dev_bf16(torch, (H, NH * DV), std, gen, device),
+    }
+    w = K.KvlMlaDeviceWeights(*[t[k].data_ptr() for k in ("q_proj", "kv_a_proj", "kv_a_norm", "kv_b_proj",
+                                                           "o_proj")])
+    return t, w
+
+
+# ----------------------------------------------------------------------------- CPU side (reference)
+_REF_INPUTS = {}
+
+
+def cpu_reference_prefill(S, theta=50000.0):
+    """Times the reference's own kvl_mla_prefill_bf16 (oracle/_ref, AVX2 + OpenMP)
+    on one S-token sequence at the config-2 head shapes.  Inputs are generated
+    once per S.  Returns (seconds, flops)."""
+    from oracle.oracle import REF_SO, Reference, cfg_of
+    import kvl_pkg
+    kvl_pkg.load()
+    import kvl_b200.synth as SY
+    H, NH, DN, DR, DV, R = 2048, 16, 128, 64, 128, 512
+    if S not in _REF_INPUTS:
+        w = [SY.normal_bf16(2, SY.S_WQ, (NH * (DN + DR), H), 0.02), SY.normal_bf16(2, SY.S_WKVA, (R + DR, H), 0.02),
+             SY.f32_to_bf16_bits(np.ones(R, np.float32)), SY.normal_bf16(2, SY.S_WKVB, (NH * (DN + DV), R), 0.02),
+             SY.normal_bf16(2, SY.S_WO, (H, NH * DV), 0.02)]
+        x = SY.bf16_bits_to_f32(SY.normal_bf16(2, SY.S_X, (S, H), 1.0))
+        _REF_INPUTS[S] = (Reference(REF_SO), w, x)
+    ref, w, x = _REF_INPUTS[S]
+    cfg = cfg_of(H, NH, DN, DR, DV, R, 1e-5, theta)
+    t0 = time.perf_counter()
+    ref.prefill(x, cfg, w)
+    dt = time.perf_counter() - t0
+    proj, attn = prefill_flops(S)
+    return dt, proj + attn
+
+
+def cpu_reference_decode_q8(lens, threads):
+    """Times the reference's attend work for a Q8 batch through its public
+    kvl_mla_decode_compressed_q8_bf16 call is not attend-only; the attend core
+    (src/mla_compressed_q8_state.c:216-238) is timed through the C restatement
+    with one worker per core.  Returns (seconds, bytes)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle.oracle import Oracle
+    import kvl_pkg
+    kvl_pkg.load()
+    import kvl_b200.synth as SY
+    orc = Oracle()
+    R, DR, NH = 512, 64, 16
+    jobs = []
+    for b, L in enumerate(lens):
+        lat8 = SY.uniform_int8(100 + b, SY.S_LAT, (L, R))
+        sc = SY.uniform_f32(100 + b, SY.S_SCALE, (L,), 0.001, 0.02)
+        rp = SY.normal_bf16(100 + b, SY.S_ROPE, (L, DR))
+        q = SY.bf16_bits_to_f32(SY.normal_bf16(100 + b, SY.S_Q, (NH, R + DR), 0.1))
+        jobs.append((q, lat8, sc, rp))
+    t0 = time.perf_counter()
+    with ThreadPoolExecutor(max_workers=threads) as ex:
+        list(ex.map(lambda j: orc.attend_q8(j[0], j[1], j[2], j[3], 1.0 / math.sqrt(192.0)), jobs))
+    return time.perf_counter() - t0, sum(lens) * 644
+
+
+# ----------------------------------------------------------------------------- workloads
+class Prefill:
+    """one 4096-token causal MLA prefill per rank."""
+    name = "prefill"
+    metric = "MLA prefill TFLOP/s (config 2: S=4096, H=2048, 16 heads, causal)"
+    unit = "TFLOP/s"
+    bound = "tensor"
+
+    def __init__(self, torch, K, lib, dist, S=4096, theta=50000.0):
+        self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
+        self.S = S
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev)
+        g.manual_seed(2 + 1000 * dist.rank)
+        self.cfg = K.make_config(2048, 16, 128, 64, 128, 512, 1e-5, theta)
+        self.wt, self.w = device_weights(torch, K, self.cfg, g, dev)
+        self.x = dev_bf16(torch, (S, 2048), 1.0, g, dev)
+        self.out = torch.empty((S, 2048), dtype=torch.float32, device=dev)
+        nbytes = lib.kvl_mla_prefill_workspace_bytes(C.byref(self.cfg), S)
+        self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.proj, self.attn = prefill_flops(S)
+        self.units = self.proj + self.attn
+
+    def kernel_flops(self):
+        """Algorithmic FLOPs per step of each library kernel of the prefill path."""
+        S, H, NH, QD, DV, R, DR = self.S, 2048, 16, 192, 128, 512, 64
+        return {"gemv_bf16": 2.0 * S * (H * (NH * QD + R + DR) + NH * DV * H),
+                "vup": 2.0 * S * NH * DV * R, "absorb": 2.0 * S * NH * 128 * R,
+                "mla_attend_bf16": float(self.attn), "gemm_bf16": float(self.proj),
+                "flash_prefill": float(self.attn)}
+
+    def step(self):
+        s = self.torch.cuda.current_stream().cuda_stream
+        rc = self.lib.kvl_mla_prefill_dev(C.byref(self.cfg), C.byref(self.w), self.out.data_ptr(),
+                                          self.x.data_ptr(), self.S, self.ws.data_ptr(), self.ws.numel(), s)
+        if rc != 0:
+            raise RuntimeError(self.K.last_error())
+
+    def value(self, ms_per_step):
+        return self.dist.world * self.units / (ms_per_step * 1e-3) / 1e12
+
+    def e2e(self, K_steps, W_steps):
+        """Public host API kvl_mla_prefill_bf16 with host fp32 activations (weights
+        cached on the device, as with a full trunk cache)."""
+        torch, K, lib = self.torch, self.K, self.lib
+        lib.kvl_mla_cuda_weight_cache(1)
+        hw = K.Weights(*[self.wt[k].view(torch.int16).cpu().numpy().view(np.uint16)
+                         for k in ("q_proj", "kv_a_proj", "kv_a_norm", "kv_b_proj", "o_proj")])
+        x = self.x.float().cpu().numpy()
+        x_pinned = torch.from_numpy(x).pin_memory().numpy()
+        out = torch.empty((self.S, 2048), dtype=torch.float32).pin_memory().numpy()
+
+        def call():
+            rc = lib.kvl_mla_prefill_bf16(K.ptr(out, K.f32p), K.ptr(x_pinned, K.f32p), self.S, C.byref(self.cfg),
+                                          C.byref(hw.c))
+            if rc != 0:
+                raise RuntimeError(K.last_error())
+        for _ in range(W_steps):
+            call()
+        self.dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(K_steps):
+            call()
+        dt = (time.perf_counter() - t0) * 1e3 / K_steps
+        dt = self.dist.max(torch, dt)
+        return {"value": self.value(dt), "unit": self.unit, "ms_per_step": dt,
+                "h2d_bytes_per_step": int(x.nbytes), "d2h_bytes_per_step": int(out.nbytes),
+                "path": "kvl_mla_prefill_bf16 (host fp32 in/out)"}
+
+    def config(self):
+        return {"workload": "config 2: causal MLA prefill, 1 sequence x 4096 tokens per rank", "seq_len": self.S,
+                "hidden": 2048, "heads": 16, "qk_nope": 128, "qk_rope": 64, "v_head": 128, "kv_lora_rank": 512,
+                "rope_theta": self.cfg.rope_theta, "x_dtype": "bf16", "weights": "bf16 ~N(0,0.02), kv_a_norm=1",
+                "flops_per_step_per_rank": self.units, "flops_projections": self.proj, "flops_attention": self.attn,
+                "l2": "flushed (256 MiB write) before every step", "parallelism": f"sequence-sharded x{self.dist.world}"}
+
+    def cpu_baseline(self):
+        cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+        dt, fl = cpu_reference_prefill(self.S)
+        return {"value": fl / dt / 1e12, "unit": self.unit, "cores": cores, "kind": "reference",
+                "sample": f"one full config-2 step: reference kvl_mla_prefill_bf16 (AVX2+OpenMP, oracle/_ref) on "
+                          f"one {self.S}-token sequence ({fl / 1e9:.2f} GFLOP, {dt:.2f} s)"}
+
+
+class DecodeQ8:
+    """64 sequences, ragged L ~ U[512, 8192], Q8 latent."""
+    name = "decode_q8"
+    metric = "MLA Q8 decode KV GB/s (config 3: 64 seqs, L~U[512,8192])"
+    unit = "GB/s"
+    bound = "hbm"
+
+    def __init__(self, torch, K, lib, dist):
+        import kvl_b200.synth as SY
+        import kvl_b200.parallel as PAR
+        self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
+        lens_all = [int(v) for v in SY.uniform_ints(3, SY.S_LEN, 64, 512, 8192)]
+        mine = PAR.shard_sequences(lens_all, dist.world)[dist.rank]
+        self.lens = [lens_all[i] for i in mine]
+        self.total_bytes = sum(lens_all) * 644
+        rows = sum(self.lens)
+        row0 = np.concatenate([[0], np.cumsum(self.lens)[:-1]]).astype(np.int64)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev)
+        g.manual_seed(3 + 1000 * dist.rank)
+        self.lat8 = torch.randint(-127, 128, (rows, 512), generator=g, device=dev, dtype=torch.int8)
+        self.scale = torch.rand((rows,), generator=g, device=dev) * 0.019 + 0.001
+        self.rope = dev_bf16(torch, (rows, 64), 1.0, g, dev)
+        self.q = dev_bf16(torch, (len(self.lens), 16, 576), 0.1, g, dev).float()
+        self.out = torch.empty((len(self.lens), 16, 512), device=dev)
+        self.plan = K.AttendPlan(self.lens, row0, 16, 512)
+        self.rows = rows
+        self.units = rows * 644
+
+    def step(self):
+        s = self.torch.cuda.current_stream().cuda_stream
+        rc = self.plan.attend_q8(self.out, None, self.q, self.lat8, self.scale, self.rope, self.rows, stream=s)
+        if rc != 0:
+            raise RuntimeError(self.K.last_error())
+
+    def value(self, ms):
+        return self.total_bytes / (ms * 1e-3) / 1e9
+
+    def config(self):
+        return {"workload": "config 3: Q8 batched decode attend, 64 seqs", "lens_sum": int(sum(self.lens)),
+                "bytes_per_token": 644, "parallelism": f"sequence-sharded x{self.dist.world}"}
+
+
+class DecodeLong:
+    """one sequence at 131072 cached tokens (bf16 latent),
+    split-KV across ranks with an (o, lse) merge over NCCL."""
+    name = "decode_long"
+    metric = "MLA long-context decode KV GB/s (config 5: L=131072)"
+    unit = "GB/s"
+    bound = "hbm"
+
+    def __init__(self, torch, K, lib, dist, L=131072):
+        self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
+        self.L = L
+        per = (L + dist.world - 1) // dist.world
+        lo = min(L, dist.rank * per)
+        hi = min(L, lo + per)
+        self.n = hi - lo
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev)
+        g.manual_seed(5)
+        self.kv = dev_bf16(torch, (max(self.n, 1), 576), 1.0, g, dev)
+        gq = torch.Generator(device=dev)
+        gq.manual_seed(55)
+        self.q = dev_bf16(torch, (1, 16, 576), 0.1, gq, dev).float()
+        self.o = torch.empty((1, 16, 512), device=dev)
+        self.lse = torch.empty((1, 16), device=dev)
+        self.plan = K.AttendPlan([self.n], [0], 16, 512)
+        if dist.world > 1:
+            self.go = torch.empty((dist.world, 1, 16, 512), device=dev)
+            self.gl = torch.empty((dist.world, 1, 16), device=dev)
+            self.final = torch.empty((1, 16, 512), device=dev)
+            self.final_lse = torch.empty((1, 16), device=dev)
+        self.units = self.n * 1152
+        self.total_bytes = L * 1152
+
+    def step(self):
+        torch = self.torch
+        s = torch.cuda.current_stream().cuda_stream
+        rc = self.plan.attend_bf16(self.o, self.lse, self.q, self.kv, self.n, stream=s)
+        if rc != 0:
+            raise RuntimeError(self.K.last_error())
+        if self.dist.world > 1:
+            d = self.dist.pg
+            d.all_gather_into_tensor(self.go, self.o)
+            d.all_gather_into_tensor(self.gl, self.lse)
+            rc = self.lib.kvl_mla_merge_partials(self.final.data_ptr(), self.final_lse.data_ptr(), self.go.data_ptr(),
+                                                 self.gl.data_ptr(), self.dist.world, 1, 16, 512, s)
+            if rc != 0:
+                raise RuntimeError(self.K.last_error())
+
+    def value(self, ms):
+        return self.total_bytes / (ms * 1e-3) / 1e9
+
+    def config(self):
+        return {"workload": "config 5: long-context decode attend, L=131072", "rows_per_rank": self.n,
+                "parallelism": f"split-KV x{self.dist.world} + NCCL all-gather merge"}
+
+
+WORKLOADS = {"prefill": Prefill, "decode_q8": DecodeQ8, "decode_long": DecodeLong}
+
+
+def measure(torch, K, lib, dist, wl, steps, warmup, flush, peaks):
+    """Runs the timed loop, then a second profiled loop for the per-kernel
+    durations of the dominant kernel (CUDA events on its launching stream)."""
+    ms_total = timed_steps(torch, dist, wl.step, steps, warmup, flush)
+    ms = ms_total / steps
+    lib.kvl_mla_cuda_profile(1)
+    for _ in range(steps):
+        flush()
+        wl.step()
+    torch.cuda.synchronize()
+    prof = profile_read(lib)
+    lib.kvl_mla_cuda_profile(0)
+    wl.profiled_steps = steps
+    launches = sum(c for _, c in prof.values()) // max(steps, 1)
+    return ms, prof, launches
+
+
+def roofline_for(wl, prof, peaks, peak_kind):
+    """Dominant kernel = the library kernel with the largest device time."""
+    if not prof:
+        return None, None
+    name, (tot_ms, cnt) = max(prof.items(), key=lambda kv: kv[1][0])
+    per_launch_ms = tot_ms / max(cnt, 1)
+    launches_per_step = max(1, round(cnt / max(1, getattr(wl, "profiled_steps", 1))))
+    if wl.bound == "hbm":
+        # one attend launch per step reads the rank's KV bytes once
+        achieved = wl.units / launches_per_step / (per_launch_ms * 1e-3) / 1e9
+        peak = peaks["hbm_gbs"]
+        unit = "GB/s"
+    else:
+        algo_step = wl.kernel_flops().get(name, 0.0)
+        achieved = algo_step / launches_per_step / (per_launch_ms * 1e-3) / 1e12
+        peak = peaks["bf16_tflops"]
+        unit = "TFLOP/s"
+    return {"kernel": name, "bound": wl.bound, "achieved": achieved, "peak": peak, "unit": unit,
+            "frac": achieved / peak, "peak_source": peak_kind, "ms_per_launch": per_launch_ms,
+            "launches_measured": cnt, "traffic": None}, name
+
+
+# ----------------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="prefill")
+    ap.add_argument("--no-extras", action="store_true", help="skip the decode sub-measurements")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    args = ap.parse_args()
+    dist = Dist()
+
+    if args.impl == "reference":
+        return run_reference(args, dist)
+
+    import torch
+    dist.init(torch)
+    K, lib = load_lib()
+    peaks, peak_kind = load_peaks()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def flush():
+        flush_buf.fill_(1)
+
+    wl = WORKLOADS[args.workload](torch, K, lib, dist)
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    ms, prof, launches = measure(torch, K, lib, dist, wl, args.steps, args.warmup, flush, peaks)
+    clk = clocks.stop()
+    roof, dom = roofline_for(wl, prof, peaks, peak_kind)
+    line = {
+        "metric": wl.metric, "value": wl.value(ms), "unit": wl.unit, "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak"
+        if wl.name == "prefill" else "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        "config": wl.config(), "roofline": roof, "gpu_launches": int(launches) * args.steps,
+        "kernels": {k: {"ms_total": v[0], "launches": v[1]} for k, v in prof.items()}, "clocks": clk,
+    }
+    if hasattr(wl, "e2e"):
+        line["e2e"] = wl.e2e(max(2, args.steps // 2), 1)
+    if not args.no_extras and args.workload == "prefill":
+        extras = {}
+        for name in ("decode_q8", "decode_long"):
+            try:
+                w2 = WORKLOADS[name](torch, K, lib, dist)
+                ms2, prof2, l2 = measure(torch, K, lib, dist, w2, args.steps, args.warmup, flush, peaks)
+                r2, _ = roofline_for(w2, prof2, peaks, peak_kind)
+                extras[name] = {"metric": w2.metric, "value": w2.value(ms2), "unit": w2.unit, "ms_per_step": ms2,
+                                "frac_of_hbm": w2.value(ms2) / peaks["hbm_gbs"], "roofline": r2,
+                                "config": w2.config(), "gpu_launches_per_step": int(l2)}
+                del w2
+            except Exception as e:  # noqa: BLE001 - report, keep the headline
+                extras[name] = {"error": str(e)}
+        line["decode"] = extras
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu and hasattr(wl, "cpu_baseline"):
+        try:
+            line["cpu_baseline"] = wl.cpu_baseline()
+        except Exception as e:  # noqa: BLE001
+            line["cpu_baseline"] = {"error": str(e)}
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+    dist.close()
+    return 0
+
+
+def run_reference(args, dist):
+    """The reference's own CPU implementation of the path on this host's cores
+    (oracle/_ref: the reference sources compiled with AVX2 + OpenMP).  Under
+    torchrun only rank 0 runs; the others exit without work."""
+    if dist.rank != 0:
+        return 0
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    cores = int(os.environ["OMP_NUM_THREADS"])
+    from oracle.oracle import reference_available
+    if not reference_available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built (reference sources absent)"}))
+        return 0
+    if args.workload != "prefill":
+        print(json.dumps({"impl": "reference", "unavailable": f"reference arm implemented for prefill only"}))
+        return 0
+    S = 4096
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_reference_prefill(S)
+    times, fl = [], 0
+    for _ in range(args.steps):
+        dt, fl = cpu_reference_prefill(S)
+        times.append(dt)
+    ms = 1e3 * sum(times) / len(times)
+    value = fl / (ms * 1e-3) / 1e12
+    sample = (f"reference kvl_mla_prefill_bf16 (AVX2+OpenMP, {cores} threads) on one {S}-token sequence at config-2 "
+              f"shapes per step ({fl / 1e9:.2f} GFLOP): the full config-2 workload")
+    print(json.dumps({
+        "impl": "reference", "metric": Prefill.metric, "value": value, "unit": Prefill.unit, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32 (bf16 weights)", "data": "synthetic (seeded)",
+        "config": {"workload": "config 2: causal MLA prefill, 1 sequence x 4096 tokens", "seq_len": S},
+        "cpu_baseline": {"value": value, "unit": Prefill.unit, "cores": cores, "kind": "reference", "sample": sample},
+        "e2e": {"value": value, "unit": Prefill.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,42 +1,53 @@
 // attend_bf16.cu -- absorbed MLA decode attention over a bf16 latent state on
-// sm_100a: TMA streams 64-row KV tiles into shared memory, tcgen05 computes the
-// scores S^T[64 rows x 16 heads] and the mix O^T[512 x 16 heads] into tensor
-// memory, and four softmax warps run an online softmax between the two MMAs.
+// sm_100a: TMA streams 128-row KV tiles into shared memory, tcgen05 computes
+// the scores S^T[128 rows x 16 heads] and the mix O^T[512 x 16 heads] into
+// tensor memory, and four softmax warps run an online softmax between them.
 //
 // Reference semantics: src/mla_compressed_state.c:132-148 (attend core of
-// kvl_mla_decode_compressed_bf16).  Differences that are format choices of
-// this build: the cached rows are bf16 (the reference keeps fp32 rows), the
-// absorbed query is rounded to bf16 for the tensor core, the probabilities are
-// rounded to bf16 for the P.V MMA, and accumulation is fp32 instead of double.
+// kvl_mla_decode_compressed_bf16).  Format choices of this build: the cached
+// rows are bf16 (the reference keeps fp32 rows), the absorbed query is rounded
+// to bf16 for the tensor core, the probabilities are rounded to bf16 for the
+// P.V MMA, and accumulation is fp32 instead of double.
+//
+// Cost model (measured on B200): a kind::f16 tcgen05.mma with N=16 takes ~48
+// cycles whether M is 64 or 128, so rows go on M=128 and a 128-row tile costs
+// 36 score MMAs + 32 P.V MMAs.  Shared memory holds one tile plus one chunk:
+//   latent ring  5 slots x 32 KB (128 rows x 128 dims = two SW128 boxes), a
+//                tile uses 4; a slot is released as soon as its P.V MMAs end
+//   rope ring    2 slots x 16 KB (128 rows x 64 dims), released after scores
+// and the MMA issuer runs scores(t), then P.V(t) once the softmax has written
+// P(t), so the next tile's chunks stream in behind the P.V of this one.
 //
 // Roles (256 threads, one CTA per SM):
-//   warp 0      TMA producer: latent ring (10 slots x 16 KB) and rope ring
-//               (3 slots x 8 KB)
+//   warp 0      TMA producer
 //   warp 1      TMEM owner and tcgen05 issuer
-//   warp 2      query loader: fp32 absorbed query -> bf16 SW128 tile, per segment
-//   warps 4-7   softmax + epilogue (TMEM subpartitions 0-3)
+//   warps 4-7   query load per segment (fp32 -> bf16 SW128 tile), softmax and
+//               epilogue (TMEM subpartitions 0-3; thread = KV row)
 #include "attend_common.cuh"
+#include "prof.cuh"
 #include "sm100.cuh"
 
 namespace kvl {
 namespace bf16dec {
 
-constexpr int kLatSlots = 10;
-constexpr int kRopeSlots = 3;
-constexpr uint32_t kLatSlotBytes = 16384;  // 64 rows x 128 dims: two SW128 boxes
-constexpr uint32_t kRopeSlotBytes = 8192;  // 64 rows x 64 dims: one SW128 box
-constexpr uint32_t kQBytes = 9 * 2048;     // 16 heads x 576: nine SW128 boxes of 16 rows
-constexpr uint32_t kPBytes = 2048;         // 16 heads x 64 rows, 8x16B core matrices
+constexpr int kLatSlots = 5;
+constexpr int kRopeSlots = 2;
+constexpr uint32_t kBox = kTileTok * 128;       // 128 rows x 64 dims bf16 = 16 KB
+constexpr uint32_t kLatSlotBytes = 2 * kBox;    // 128 dims
+constexpr uint32_t kRopeSlotBytes = kBox;       // 64 dims
+constexpr uint32_t kQBytes = 9 * 2048;          // 16 heads x 576: nine SW128 boxes of 16 rows
+constexpr uint32_t kPChunkSbo = (kTileTok / 8) * 128;  // stride between the two 8-head groups
+constexpr uint32_t kPBytes = 2 * kPChunkSbo;    // P^T: 16 heads x 128 rows, 8x16B core matrices
 constexpr uint32_t OFF_LAT = 0;
 constexpr uint32_t OFF_ROPE = OFF_LAT + kLatSlots * kLatSlotBytes;
 constexpr uint32_t OFF_Q = OFF_ROPE + kRopeSlots * kRopeSlotBytes;
-constexpr uint32_t OFF_P = OFF_Q + 2 * kQBytes;
+constexpr uint32_t OFF_P = OFF_Q + kQBytes;
 constexpr uint32_t OFF_BAR = OFF_P + 2 * kPBytes;
 
 struct Bars {
   uint64_t lat_full[kLatSlots], lat_empty[kLatSlots];
   uint64_t rope_full[kRopeSlots], rope_empty[kRopeSlots];
-  uint64_t q_full[2], q_empty[2];
+  uint64_t q_full;
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full[2], p_empty[2];
   uint64_t o_full, o_empty, drain;
@@ -46,10 +57,10 @@ struct Bars {
 };
 
 constexpr uint32_t kSmemBytes = OFF_BAR + sizeof(Bars) + 1024;  // + alignment slack
-static_assert(OFF_Q % 1024 == 0 && OFF_P % 1024 == 0 && OFF_ROPE % 1024 == 0, "align");
+static_assert(OFF_ROPE % 1024 == 0 && OFF_Q % 1024 == 0 && OFF_P % 1024 == 0 && OFF_BAR % 8 == 0, "align");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-constexpr uint32_t kTmemCols = 128;  // S: 2 x 16 cols; O: 4 x 16 cols at col 32
+constexpr uint32_t kTmemCols = 128;  // S: 2 buffers x 16 columns; O: 4 chunks x 16 columns
 constexpr uint32_t kColO = 32;
 constexpr uint32_t kThreads = 256;
 
@@ -74,13 +85,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kLatSlots; ++i) { mbar_init(&B->lat_full[i], 1); mbar_init(&B->lat_empty[i], 1); }
     for (int i = 0; i < kRopeSlots; ++i) { mbar_init(&B->rope_full[i], 1); mbar_init(&B->rope_empty[i], 1); }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&B->q_full[i], 1);
-      mbar_init(&B->q_empty[i], 1);
       mbar_init(&B->s_full[i], 1);
       mbar_init(&B->s_empty[i], 4);
       mbar_init(&B->p_full[i], 4);
       mbar_init(&B->p_empty[i], 1);
     }
+    mbar_init(&B->q_full, 4);
     mbar_init(&B->o_full, 1);
     mbar_init(&B->o_empty, 4);
     mbar_init(&B->drain, 1);
@@ -109,22 +119,24 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < nt && ok; ++t, ++g) {
           const int32_t y = static_cast<int32_t>(row0 + static_cast<long long>(kTileTok) * t);
           for (int c = 0; c < 4 && ok; ++c) {
-            const uint32_t li = 4 * g + c, ls = li % kLatSlots, lu = li / kLatSlots;
-            ok = mbar_wait(&B->lat_empty[ls], (lu & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+            const uint32_t li = 4 * g + c, ls = li % kLatSlots;
+            ok = mbar_wait(&B->lat_empty[ls], ((li / kLatSlots) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
             if (!ok) break;
             uint8_t *dst = smem + OFF_LAT + ls * kLatSlotBytes;
             mbar_arrive_expect_tx(&B->lat_full[ls], kLatSlotBytes);
             tma_load_2d(dst, &p.tm_kv, &B->lat_full[ls], 128 * c, y);
-            tma_load_2d(dst + 8192, &p.tm_kv, &B->lat_full[ls], 128 * c + 64, y);
+            tma_load_2d(dst + kBox, &p.tm_kv, &B->lat_full[ls], 128 * c + 64, y);
             n_lat = li + 1;
+            if (c == 0) {
+              // the rope box rides with the first chunk so scores can start early
+              const uint32_t rs = g % kRopeSlots;
+              ok = mbar_wait(&B->rope_empty[rs], ((g / kRopeSlots) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+              if (!ok) break;
+              mbar_arrive_expect_tx(&B->rope_full[rs], kRopeSlotBytes);
+              tma_load_2d(smem + OFF_ROPE + rs * kRopeSlotBytes, &p.tm_kv, &B->rope_full[rs], kLatent, y);
+              n_rope = g + 1;
+            }
           }
-          if (!ok) break;
-          const uint32_t rs = g % kRopeSlots, ru = g / kRopeSlots;
-          ok = mbar_wait(&B->rope_empty[rs], (ru & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
-          if (!ok) break;
-          mbar_arrive_expect_tx(&B->rope_full[rs], kRopeSlotBytes);
-          tma_load_2d(smem + OFF_ROPE + rs * kRopeSlotBytes, &p.tm_kv, &B->rope_full[rs], kLatent, y);
-          n_rope = g + 1;
         }
       }
       if (!ok) {
@@ -143,115 +155,87 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_qk = idesc_f16(1, 1, 0, 0, 64, kHeads);
-      constexpr uint32_t idesc_pv = idesc_f16(1, 1, 1, 0, 128, kHeads);
+      constexpr uint32_t idesc_qk = idesc_f16(1, 1, 0, 0, 128, kHeads);  // A = KV rows (K-major)
+      constexpr uint32_t idesc_pv = idesc_f16(1, 1, 1, 0, 128, kHeads);  // A = latent^T (MN-major)
       uint32_t g = 0;
       int seg_i = 0;
       bool ok = true;
-      auto issue_pv = [&](uint32_t gp, bool first, int segi) -> bool {
-        const uint32_t pb = gp & 1;
-        if (!mbar_wait(&B->p_full[pb], (gp >> 1) & 1, abort, p.err, ERR_TIMEOUT_FULL)) return false;
-        if (first && segi > 0)
-          if (!mbar_wait(&B->o_empty, (segi - 1) & 1, abort, p.err, ERR_TIMEOUT_FULL)) return false;
-        tc_fence_after();
-        const uint32_t p_addr = s_base + OFF_P + pb * kPBytes;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint32_t ls = (4 * gp + c) % kLatSlots;
-          const uint32_t a_addr = s_base + OFF_LAT + ls * kLatSlotBytes;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t a = smem_desc(a_addr + kk * 2048, 8192, 1024, LAYOUT_SW128);
-            const uint64_t b = smem_desc(p_addr + kk * 256, 128, 1024, LAYOUT_INTERLEAVE);
-            mma_f16_ss(tmem + kColO + 16 * c, a, b, idesc_pv, (first && kk == 0) ? 0u : 1u);
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) mma_commit(&B->lat_empty[(4 * gp + c) % kLatSlots]);
-        mma_commit(&B->p_empty[pb]);
-        return true;
-      };
       for (int si = seg_lo; si < seg_hi && ok; ++si, ++seg_i) {
         const AttendSegment sg = p.segs[si];
         const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
-        const uint32_t qb = seg_i & 1;
-        ok = mbar_wait(&B->q_full[qb], (seg_i >> 1) & 1, abort, p.err, ERR_TIMEOUT_FULL);
-        const uint32_t q_addr = s_base + OFF_Q + qb * kQBytes;
+        ok = mbar_wait(&B->q_full, seg_i & 1, abort, p.err, ERR_TIMEOUT_FULL);
+        const uint32_t q_addr = s_base + OFF_Q;
         for (int t = 0; t < nt && ok; ++t, ++g) {
-          const uint32_t sb = g & 1;
-          ok = mbar_wait(&B->s_empty[sb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
-          for (int c = 0; c < 4 && ok; ++c) {
-            const uint32_t li = 4 * g + c;
-            ok = mbar_wait(&B->lat_full[li % kLatSlots], (li / kLatSlots) & 1, abort, p.err,
-                           ERR_TIMEOUT_FULL);
-          }
-          const uint32_t rs = g % kRopeSlots;
-          if (ok) ok = mbar_wait(&B->rope_full[rs], (g / kRopeSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+          // ---- scores S^T(g) = KV(g) . Q^T
+          const uint32_t sb = g & 1, rs = g % kRopeSlots;
+          ok = mbar_wait(&B->s_empty[sb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY) &&
+               mbar_wait(&B->rope_full[rs], (g / kRopeSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL);
           if (!ok) break;
           tc_fence_after();
-#pragma unroll 1
-          for (int k = 0; k < 9; ++k) {
-            const uint32_t a_box = (k < 8) ? s_base + OFF_LAT + ((4 * g + (k >> 1)) % kLatSlots) * kLatSlotBytes +
-                                                 (k & 1) * 8192
-                                           : s_base + OFF_ROPE + rs * kRopeSlotBytes;
-            const uint32_t b_box = q_addr + k * 2048;
+          const uint32_t rope_box = s_base + OFF_ROPE + rs * kRopeSlotBytes;
 #pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
-              const uint64_t a = smem_desc(a_box + kk * 32, 16, 1024, LAYOUT_SW128);
-              const uint64_t b = smem_desc(b_box + kk * 32, 16, 1024, LAYOUT_SW128);
-              mma_f16_ss(tmem + sb * 16, a, b, idesc_qk, (k | kk) ? 1u : 0u);
-            }
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16_ss(tmem + sb * 16, smem_desc(rope_box + kk * 32, 16, 1024, LAYOUT_SW128),
+                       smem_desc(q_addr + 8 * 2048 + kk * 32, 16, 1024, LAYOUT_SW128), idesc_qk, kk ? 1u : 0u);
+          for (int c = 0; c < 4 && ok; ++c) {
+            const uint32_t li = 4 * g + c;
+            ok = mbar_wait(&B->lat_full[li % kLatSlots], (li / kLatSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t slot = s_base + OFF_LAT + (li % kLatSlots) * kLatSlotBytes;
+#pragma unroll
+            for (int half = 0; half < 2; ++half)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_f16_ss(tmem + sb * 16, smem_desc(slot + half * kBox + kk * 32, 16, 1024, LAYOUT_SW128),
+                           smem_desc(q_addr + (2 * c + half) * 2048 + kk * 32, 16, 1024, LAYOUT_SW128), idesc_qk,
+                           1u);
           }
+          if (!ok) break;
           mma_commit(&B->s_full[sb]);
           mma_commit(&B->rope_empty[rs]);
-          if (t == nt - 1) mma_commit(&B->q_empty[qb]);
-          if (t > 0) ok = issue_pv(g - 1, t == 1, seg_i);
+          // ---- O^T += latent(g)^T . P^T(g), slot by slot
+          const bool first = (t == 0);
+          ok = mbar_wait(&B->p_full[sb], (g >> 1) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+          if (ok && first && seg_i > 0) ok = mbar_wait(&B->o_empty, (seg_i - 1) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t p_addr = s_base + OFF_P + sb * kPBytes;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t li = 4 * g + c;
+            const uint32_t slot = s_base + OFF_LAT + (li % kLatSlots) * kLatSlotBytes;
+#pragma unroll
+            for (int kk = 0; kk < kTileTok / 16; ++kk)
+              mma_f16_ss(tmem + kColO + 16 * c, smem_desc(slot + kk * 2048, kBox, 1024, LAYOUT_SW128),
+                         smem_desc(p_addr + kk * 256, 128, kPChunkSbo, LAYOUT_INTERLEAVE), idesc_pv,
+                         (first && kk == 0) ? 0u : 1u);
+            mma_commit(&B->lat_empty[li % kLatSlots]);
+          }
+          mma_commit(&B->p_empty[sb]);
         }
-        if (!ok) break;
-        ok = issue_pv(g - 1, nt == 1, seg_i);
         if (ok) mma_commit(&B->o_full);
       }
       // All issued tensor-core work must finish before TMEM is released.
       mma_commit(&B->drain);
       drain_wait(&B->drain, 0, p.err);
     }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------ query loader
-    int seg_i = 0;
-    for (int si = seg_lo; si < seg_hi; ++si, ++seg_i) {
-      const AttendSegment sg = p.segs[si];
-      const uint32_t qb = seg_i & 1;
-      int ok = 1;
-      if (lane == 0) ok = mbar_wait(&B->q_empty[qb], ((seg_i >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      const float *qs = p.q + static_cast<size_t>(sg.seq) * kHeads * kRow;
-      uint8_t *qd = smem + OFF_Q + qb * kQBytes;
-      for (int idx = lane; idx < kHeads * (kRow / 8); idx += 32) {
-        const int h = idx / (kRow / 8), c8 = idx % (kRow / 8);
-        const float4 a = *reinterpret_cast<const float4 *>(qs + h * kRow + c8 * 8);
-        const float4 b = *reinterpret_cast<const float4 *>(qs + h * kRow + c8 * 8 + 4);
-        uint4 v;
-        v.x = pack_bf16(a.x, a.y);
-        v.y = pack_bf16(a.z, a.w);
-        v.z = pack_bf16(b.x, b.y);
-        v.w = pack_bf16(b.z, b.w);
-        const uint32_t off = (c8 >> 3) * 2048 + sw128_offset(h, (c8 & 7) * 8);
-        *reinterpret_cast<uint4 *>(qd + off) = v;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&B->q_full[qb]);
-    }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax + epilogue
     const int w = warp - 4;
+    const int tt = 32 * w + lane;  // KV row of the tile owned by this thread
     const uint32_t lane_base = static_cast<uint32_t>(32 * w) << 16;
     uint32_t g = 0;
     int seg_i = 0;
     for (int si = seg_lo; si < seg_hi; ++si, ++seg_i) {
       const AttendSegment sg = p.segs[si];
       const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
+      // The query tile is free here: every score MMA of the previous segment
+      // has completed (its scores were read above).
+      load_query_tile(smem + OFF_Q, p.q + static_cast<size_t>(sg.seq) * kHeads * kRow, tt, false);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B->q_full);
       float m_ref[kHeads], l_part[kHeads];
 #pragma unroll
       for (int h = 0; h < kHeads; ++h) { m_ref[h] = -INFINITY; l_part[h] = 0.f; }
@@ -267,11 +251,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&B->s_empty[sb]);
-        const int tok = sg.tok_begin + kTileTok * t + 16 * w + lane;
-        const bool valid = lane < 16 && tok < sg.tok_end;
-        if (p.dbg_s != nullptr && blockIdx.x == 0 && static_cast<int>(g) < p.dbg_tiles && lane < 16) {
+        const int tok = sg.tok_begin + kTileTok * t + tt;
+        const bool valid = tok < sg.tok_end;
+        if (p.dbg_s != nullptr && blockIdx.x == 0 && static_cast<int>(g) < p.dbg_tiles) {
 #pragma unroll
-          for (int h = 0; h < kHeads; ++h) p.dbg_s[(static_cast<size_t>(g) * 64 + 16 * w + lane) * kHeads + h] = v[h];
+          for (int h = 0; h < kHeads; ++h) p.dbg_s[(static_cast<size_t>(g) * kTileTok + tt) * kHeads + h] = v[h];
         }
         float s[kHeads];
         bool need = false;
@@ -303,8 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           named_bar_sync(1, 128);
           if (t > 0) {
             // O holds tiles [0, t) of this segment: rescale after P.V(t-1) lands.
-            const uint32_t pp = (g - 1) & 1;
-            bad = !mbar_wait(&B->p_empty[pp], ((g - 1) >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
+            bad = !mbar_wait(&B->p_empty[(g - 1) & 1], ((g - 1) >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
             if (named_bar_or(1, 128, bad)) { bad = true; break; }
             tc_fence_after();
 #pragma unroll
@@ -327,35 +310,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           pr[h] = exp2f(s[h] - m_ref[h]);
           l_part[h] += pr[h];
         }
-        const uint32_t pb = g & 1;
-        bad = !mbar_wait(&B->p_empty[pb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_MMA);
+        bad = !mbar_wait(&B->p_empty[sb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_MMA);
         if (named_bar_or(1, 128, bad)) { bad = true; break; }
-        if (lane < 16 && !valid) {
+        if (!valid) {
           // Rows past the segment end get p = 0, but 0 * (NaN/Inf garbage) is
-          // NaN in the P.V MMA: clear their latent rows (the scores MMA of this
-          // tile has completed, so the slots are free to modify).
-          const int tt = 16 * w + lane;
+          // NaN in the P.V MMA: clear their latent rows (the score MMAs of this
+          // tile have completed, so the slots may be modified).
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
-            uint8_t *slot = smem + OFF_LAT + ((4 * g + c) % kLatSlots) * kLatSlotBytes + tt * 128;
+            uint8_t *row = smem + OFF_LAT + ((4 * g + c) % kLatSlots) * kLatSlotBytes + tt * 128;
 #pragma unroll
             for (int half = 0; half < 2; ++half)
 #pragma unroll
               for (int k = 0; k < 8; ++k)
-                *reinterpret_cast<uint4 *>(slot + half * 8192 + k * 16) = make_uint4(0u, 0u, 0u, 0u);
+                *reinterpret_cast<uint4 *>(row + half * kBox + k * 16) = make_uint4(0u, 0u, 0u, 0u);
           }
         }
-        if (lane < 16) {
-          const int tt = 16 * w + lane;
-          uint8_t *pd = smem + OFF_P + pb * kPBytes + (tt >> 3) * 128 + (tt & 7) * 2;
+        {
+          uint8_t *pd = smem + OFF_P + sb * kPBytes + (tt >> 3) * 128 + (tt & 7) * 2;
 #pragma unroll
           for (int h = 0; h < kHeads; ++h)
-            *reinterpret_cast<__nv_bfloat16 *>(pd + (h >> 3) * 1024 + (h & 7) * 16) = __float2bfloat16_rn(pr[h]);
+            *reinterpret_cast<__nv_bfloat16 *>(pd + (h >> 3) * kPChunkSbo + (h & 7) * 16) =
+                __float2bfloat16_rn(pr[h]);
         }
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&B->p_full[pb]);
+        if (lane == 0) mbar_arrive(&B->p_full[sb]);
       }
       if (bad) break;
       // ---- epilogue: O / l, lse
@@ -412,7 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Host launcher (declared in attend_host.cuh).
+// Host launcher.
 cudaError_t launch_attend_bf16(const AttendParams &p, int grid, cudaStream_t stream) {
   static bool attr_set = false;
   if (!attr_set) {
@@ -421,6 +402,7 @@ cudaError_t launch_attend_bf16(const AttendParams &p, int grid, cudaStream_t str
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
+  ProfScope ps("mla_attend_bf16", stream);
   mla_attend_bf16_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError();
 }

@@ -13,6 +13,7 @@
 #include "attend_common.cuh"
 #include "attend_host.cuh"
 #include "sm100.cuh"
+#include "prof.cuh"
 
 namespace kvl {
 
@@ -95,7 +96,10 @@ int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long lo
   }
   hp.cta_seg[grid] = static_cast<int>(hp.segs.size());
   for (int i = 0; i < batch; ++i)
-    if (nslot[i] > 0) hp.merges.push_back(MergeEntry{i, first_slot[i], nslot[i], 1});
+    if (nslot[i] > 0) {
+      hp.merges.push_back(MergeEntry{i, first_slot[i], nslot[i], 1});
+      hp.max_merge_count = std::max(hp.max_merge_count, nslot[i]);
+    }
   return 0;
 }
 
@@ -103,38 +107,74 @@ int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long lo
 // out[seq][h][:] = sum_p w_p o_p / sum_p w_p,  w_p = exp(lse_p - max_p lse_p);
 // lse[seq][h] = max + log(sum_p w_p).  Part p of an entry lives at part index
 // first + p * step (each part is [16][R] floats and [16] lse values).
+// Grid (entry, head, 256-wide chunk of R): the normalised weights of the
+// entry's parts for one head go to shared memory once, then every thread
+// combines one output element.
 __global__ void merge_partials_kernel(float *out, float *lse, const float *part_o,
                                       const float *part_lse, const MergeEntry *entries, int nh,
-                                      int R) {
-  const MergeEntry e = entries[blockIdx.x];
-  extern __shared__ float sh[];  // [nh] max, [nh] inverse weight sum
-  for (int h = threadIdx.x; h < nh; h += blockDim.x) {
-    float m = -INFINITY;
-    for (int p = 0; p < e.count; ++p) m = fmaxf(m, part_lse[(size_t)(e.first + p * e.step) * nh + h]);
-    float sum = 0.f;
-    for (int p = 0; p < e.count; ++p) sum += expf(part_lse[(size_t)(e.first + p * e.step) * nh + h] - m);
-    sh[h] = m;
-    sh[nh + h] = 1.0f / sum;
-    if (lse) lse[(size_t)e.seq * nh + h] = m + logf(sum);
-  }
+                                      int R, int uniform_parts) {
+  // entries == nullptr: sequence b combines parts b, b + B, b + 2B, ... (part-major layout)
+  const MergeEntry e = entries ? entries[blockIdx.x]
+                               : MergeEntry{(int)blockIdx.x, (int)blockIdx.x, uniform_parts, (int)gridDim.x};
+  const int h = blockIdx.y;
+  extern __shared__ float wsh[];  // [count] weights, then [32] reduction scratch
+  float *red = wsh + e.count;
+  float m = -INFINITY;
+  for (int p = threadIdx.x; p < e.count; p += blockDim.x)
+    m = fmaxf(m, part_lse[(size_t)(e.first + p * e.step) * nh + h]);
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
   __syncthreads();
-  for (int i = threadIdx.x; i < nh * R; i += blockDim.x) {
-    const int h = i / R;
-    float acc = 0.f;
-    for (int p = 0; p < e.count; ++p) {
-      const size_t part = (size_t)(e.first + p * e.step);
-      acc += expf(part_lse[part * nh + h] - sh[h]) * part_o[part * nh * R + i];
-    }
-    out[(size_t)e.seq * nh * R + i] = acc * sh[nh + h];
+  m = red[0];
+  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
+  __syncthreads();
+  float sum = 0.f;
+  for (int p = threadIdx.x; p < e.count; p += blockDim.x) {
+    const float w = expf(part_lse[(size_t)(e.first + p * e.step) * nh + h] - m);
+    wsh[p] = w;
+    sum += w;
+  }
+  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  sum = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) sum += red[i];
+  const float inv = 1.0f / sum;
+  if (lse && blockIdx.z == 0 && threadIdx.x == 0) lse[(size_t)e.seq * nh + h] = m + logf(sum);
+  // 32 output elements x 8 groups of parts per block; the groups' partial sums
+  // meet in shared memory (reusing the reduction scratch after a barrier).
+  __syncthreads();
+  const int dl = threadIdx.x & 31, grp = threadIdx.x >> 5;
+  const int d = blockIdx.z * 32 + dl;
+  float acc = 0.f;
+  if (d < R)
+    for (int p = grp; p < e.count; p += 8)
+      acc = fmaf(wsh[p], part_o[((size_t)(e.first + p * e.step) * nh + h) * R + d], acc);
+  float *gs = red + 32;  // [8][32]
+  gs[grp * 32 + dl] = acc;
+  __syncthreads();
+  if (grp == 0 && d < R) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += gs[i * 32 + dl];
+    out[((size_t)e.seq * nh + h) * R + d] = s * inv;
   }
 }
 
 cudaError_t launch_merge(float *out, float *lse, const float *part_o, const float *part_lse,
                          const MergeEntry *d_entries, int n_entries, int nh, int R,
-                         cudaStream_t stream) {
+                         cudaStream_t stream, int max_count) {
+  // d_entries == nullptr selects the part-major layout with max_count parts per sequence.
   if (n_entries <= 0) return cudaSuccess;
-  merge_partials_kernel<<<n_entries, 256, 2 * nh * sizeof(float), stream>>>(out, lse, part_o, part_lse,
-                                                                           d_entries, nh, R);
+  const size_t sm = (static_cast<size_t>(max_count) + 32 + 256) * sizeof(float);
+  if (sm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(merge_partials_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(sm));
+    if (e != cudaSuccess) return e;
+  }
+  ProfScope ps("merge_partials", stream);
+  dim3 grid(n_entries, nh, (R + 31) / 32);
+  merge_partials_kernel<<<grid, 256, sm, stream>>>(out, lse, part_o, part_lse, d_entries, nh, R, max_count);
   return cudaGetLastError();
 }
 
@@ -227,6 +267,7 @@ cudaError_t launch_attend_generic(bool q8, float *out, float *lse, const float *
     if (e != cudaSuccess) return e;
   }
   dim3 grid(nh, batch);
+  ProfScope ps("attend_generic", stream);
   if (q8)
     attend_generic_kernel<true><<<grid, 128, sm, stream>>>(out, lse, q, kv, lat8, lscale, rope16, d_row0,
                                                            d_len, nh, R, DR, scale_log2);
@@ -345,7 +386,7 @@ int DevicePlan::launch(const AttendLaunch &a, cudaStream_t stream) const {
   if (e != cudaSuccess) return -1;
   if (!host.merges.empty()) {
     e = launch_merge(a.out, a.lse, part_o, part_lse, reinterpret_cast<const MergeEntry *>(m + off_merge),
-                     static_cast<int>(host.merges.size()), nh, R, stream);
+                     static_cast<int>(host.merges.size()), nh, R, stream, host.max_merge_count);
     if (e != cudaSuccess) return -1;
   }
   return 0;

@@ -29,6 +29,7 @@ struct HostPlan {
   std::vector<long long> seq_row0;   // batch
   std::vector<int> seq_len;          // batch
   std::vector<MergeEntry> merges;
+  int max_merge_count = 0;
 };
 
 int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long long *seq_row0,
@@ -73,6 +74,6 @@ bool make_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint
 
 cudaError_t launch_merge(float *out, float *lse, const float *part_o, const float *part_lse,
                          const MergeEntry *d_entries, int n_entries, int nh, int R,
-                         cudaStream_t stream);
+                         cudaStream_t stream, int max_count);
 
 }  // namespace kvl

@@ -10,42 +10,46 @@
 //     O    = sum_j (p_j * scale_j) q_j           (P' = p * scale in fp16)
 // which equals sum_j p_j * dequant(q_j) up to the rounding of P'.
 //
+// Tiles of 128 KV rows (see attend_bf16.cu for the MMA cost model).  Shared
+// memory: int8 staging ring 2 x 16 KB (128 rows x 128 dims), fp16 ring 4 x
+// 32 KB (one tile; a slot is released when its P.V MMAs end), rope ring 2 x
+// 16 KB.
+//
 // Roles (384 threads, one CTA per SM):
-//   warp 0      TMA producer: int8 staging ring (6 x 8 KB) + rope ring (3 x 8 KB)
+//   warp 0      TMA producer (int8 staging + rope)
 //   warp 1      TMEM owner and tcgen05 issuer
-//   warp 2      query loader: q_lat -> fp16, q_rope -> bf16, SW128 tiles
-//   warps 4-7   softmax + epilogue (TMEM subpartitions 0-3)
-//   warps 8-11  converters: int8 staging -> fp16 SW128 ring (8 x 16 KB)
+//   warps 4-7   query load per segment (q_lat -> fp16, q_rope -> bf16 SW128
+//               tiles), softmax and epilogue (TMEM subpartitions 0-3; thread = KV row)
+//   warps 8-11  converters: int8 staging -> fp16 SW128 ring
 #include "attend_common.cuh"
+#include "prof.cuh"
 #include "sm100.cuh"
 
 namespace kvl {
 namespace q8dec {
 
-// The converted ring must hold two whole tiles: the MMA issuer computes the
-// scores of tile g before the P.V of tile g-1, so converting tile g may only
-// wait on the P.V of tile g-2.
-constexpr int kStgSlots = 6;    // 64 rows x 128 int8 dims (one SW128 box)
-constexpr int kCvtSlots = 8;    // 64 rows x 128 fp16 dims (two SW128 boxes)
-constexpr int kRopeSlots = 3;
-constexpr int kQBufs = 1;       // one query tile; refilled between segments
-constexpr uint32_t kStgBytes = 8192;
-constexpr uint32_t kCvtBytes = 16384;
-constexpr uint32_t kRopeBytes = 8192;
+constexpr int kStgSlots = 2;
+constexpr int kCvtSlots = 4;
+constexpr int kRopeSlots = 2;
+constexpr uint32_t kBox = kTileTok * 128;      // 128 rows x 128 B = 16 KB
+constexpr uint32_t kStgBytes = kBox;           // int8: 128 rows x 128 dims
+constexpr uint32_t kCvtBytes = 2 * kBox;       // fp16: 128 rows x 128 dims (two 64-dim boxes)
+constexpr uint32_t kRopeBytes = kBox;          // bf16: 128 rows x 64 dims
 constexpr uint32_t kQBytes = 9 * 2048;
-constexpr uint32_t kPBytes = 2048;
+constexpr uint32_t kPChunkSbo = (kTileTok / 8) * 128;
+constexpr uint32_t kPBytes = 2 * kPChunkSbo;
 constexpr uint32_t OFF_CVT = 0;
 constexpr uint32_t OFF_STG = OFF_CVT + kCvtSlots * kCvtBytes;
 constexpr uint32_t OFF_ROPE = OFF_STG + kStgSlots * kStgBytes;
 constexpr uint32_t OFF_Q = OFF_ROPE + kRopeSlots * kRopeBytes;
-constexpr uint32_t OFF_P = OFF_Q + kQBufs * kQBytes;
+constexpr uint32_t OFF_P = OFF_Q + kQBytes;
 constexpr uint32_t OFF_BAR = OFF_P + 2 * kPBytes;
 
 struct Bars {
   uint64_t stg_full[kStgSlots], stg_empty[kStgSlots];
   uint64_t cvt_full[kCvtSlots], cvt_empty[kCvtSlots];
   uint64_t rope_full[kRopeSlots], rope_empty[kRopeSlots];
-  uint64_t q_full[kQBufs], q_empty[kQBufs];
+  uint64_t q_full;
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full[2], p_empty[2];
   uint64_t o_full, o_empty, drain;
@@ -55,13 +59,13 @@ struct Bars {
 };
 
 constexpr uint32_t kSmemBytes = OFF_BAR + sizeof(Bars) + 1024;
-static_assert(OFF_STG % 1024 == 0 && OFF_ROPE % 1024 == 0 && OFF_Q % 1024 == 0 && OFF_P % 1024 == 0,
-              "align");
+static_assert(OFF_STG % 1024 == 0 && OFF_ROPE % 1024 == 0 && OFF_Q % 1024 == 0 && OFF_P % 1024 == 0, "align");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-constexpr uint32_t kTmemCols = 128;  // S_lat 2x16 @0, S_rope 2x16 @32, O 4x16 @64
+// TMEM columns: latent scores 2 buffers x 16 @0, rope scores 2 x 16 @32, O 4 x 16 @64.
 constexpr uint32_t kColRope = 32;
 constexpr uint32_t kColO = 64;
+constexpr uint32_t kTmemCols = 128;
 constexpr uint32_t kThreads = 384;
 
 // Four signed bytes -> four fp16 values, exactly: bias each byte by 128 so it
@@ -105,10 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&B->p_full[i], 4);
       mbar_init(&B->p_empty[i], 1);
     }
-    for (int i = 0; i < kQBufs; ++i) {
-      mbar_init(&B->q_full[i], 1);
-      mbar_init(&B->q_empty[i], 1);
-    }
+    mbar_init(&B->q_full, 4);
     mbar_init(&B->o_full, 1);
     mbar_init(&B->o_empty, 4);
     mbar_init(&B->drain, 1);
@@ -144,14 +145,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_arrive_expect_tx(&B->stg_full[ls], kStgBytes);
             tma_load_2d(smem + OFF_STG + ls * kStgBytes, &p.tm_lat8, &B->stg_full[ls], 128 * c, y);
             n_stg = li + 1;
+            if (c == 0) {
+              const uint32_t rs = g % kRopeSlots;
+              ok = mbar_wait(&B->rope_empty[rs], ((g / kRopeSlots) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+              if (!ok) break;
+              mbar_arrive_expect_tx(&B->rope_full[rs], kRopeBytes);
+              tma_load_2d(smem + OFF_ROPE + rs * kRopeBytes, &p.tm_rope, &B->rope_full[rs], 0, y);
+              n_rope = g + 1;
+            }
           }
-          if (!ok) break;
-          const uint32_t rs = g % kRopeSlots;
-          ok = mbar_wait(&B->rope_empty[rs], ((g / kRopeSlots) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
-          if (!ok) break;
-          mbar_arrive_expect_tx(&B->rope_full[rs], kRopeBytes);
-          tma_load_2d(smem + OFF_ROPE + rs * kRopeBytes, &p.tm_rope, &B->rope_full[rs], 0, y);
-          n_rope = g + 1;
         }
       }
       if (!ok) {
@@ -168,113 +170,68 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_lat = idesc_f16(0, 0, 0, 0, 64, kHeads);   // fp16 x fp16
-      constexpr uint32_t idesc_rope = idesc_f16(1, 1, 0, 0, 64, kHeads);  // bf16 x bf16
-      constexpr uint32_t idesc_pv = idesc_f16(0, 0, 1, 0, 128, kHeads);   // fp16, A MN-major
+      constexpr uint32_t idesc_lat = idesc_f16(0, 0, 0, 0, 128, kHeads);   // fp16 x fp16
+      constexpr uint32_t idesc_rope = idesc_f16(1, 1, 0, 0, 128, kHeads);  // bf16 x bf16
+      constexpr uint32_t idesc_pv = idesc_f16(0, 0, 1, 0, 128, kHeads);    // fp16, A MN-major
       uint32_t g = 0;
       int seg_i = 0;
       bool ok = true;
-      auto issue_pv = [&](uint32_t gp, bool first, int segi) -> bool {
-        const uint32_t pb = gp & 1;
-        if (!mbar_wait(&B->p_full[pb], (gp >> 1) & 1, abort, p.err, ERR_TIMEOUT_FULL)) return false;
-        if (first && segi > 0)
-          if (!mbar_wait(&B->o_empty, (segi - 1) & 1, abort, p.err, ERR_TIMEOUT_FULL)) return false;
-        tc_fence_after();
-        const uint32_t p_addr = s_base + OFF_P + pb * kPBytes;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint32_t a_addr = s_base + OFF_CVT + ((4 * gp + c) % kCvtSlots) * kCvtBytes;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t a = smem_desc(a_addr + kk * 2048, 8192, 1024, LAYOUT_SW128);
-            const uint64_t b = smem_desc(p_addr + kk * 256, 128, 1024, LAYOUT_INTERLEAVE);
-            mma_f16_ss(tmem + kColO + 16 * c, a, b, idesc_pv, (first && kk == 0) ? 0u : 1u);
-          }
-        }
-#pragma unroll
-        for (int c = 0; c < 4; ++c) mma_commit(&B->cvt_empty[(4 * gp + c) % kCvtSlots]);
-        mma_commit(&B->p_empty[pb]);
-        return true;
-      };
       for (int si = seg_lo; si < seg_hi && ok; ++si, ++seg_i) {
         const AttendSegment sg = p.segs[si];
         const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
-        const uint32_t qb = seg_i % kQBufs;
-        ok = mbar_wait(&B->q_full[qb], (seg_i / kQBufs) & 1, abort, p.err, ERR_TIMEOUT_FULL);
-        const uint32_t q_addr = s_base + OFF_Q + qb * kQBytes;
+        ok = mbar_wait(&B->q_full, seg_i & 1, abort, p.err, ERR_TIMEOUT_FULL);
+        const uint32_t q_addr = s_base + OFF_Q;
         for (int t = 0; t < nt && ok; ++t, ++g) {
-          const uint32_t sb = g & 1;
-          ok = mbar_wait(&B->s_empty[sb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+          const uint32_t sb = g & 1, rs = g % kRopeSlots;
+          ok = mbar_wait(&B->s_empty[sb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY) &&
+               mbar_wait(&B->rope_full[rs], (g / kRopeSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t rope_box = s_base + OFF_ROPE + rs * kRopeBytes;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16_ss(tmem + kColRope + sb * 16, smem_desc(rope_box + kk * 32, 16, 1024, LAYOUT_SW128),
+                       smem_desc(q_addr + 8 * 2048 + kk * 32, 16, 1024, LAYOUT_SW128), idesc_rope, kk ? 1u : 0u);
           for (int c = 0; c < 4 && ok; ++c) {
             const uint32_t li = 4 * g + c;
             ok = mbar_wait(&B->cvt_full[li % kCvtSlots], (li / kCvtSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t slot = s_base + OFF_CVT + (li % kCvtSlots) * kCvtBytes;
+#pragma unroll
+            for (int half = 0; half < 2; ++half)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_f16_ss(tmem + sb * 16, smem_desc(slot + half * kBox + kk * 32, 16, 1024, LAYOUT_SW128),
+                           smem_desc(q_addr + (2 * c + half) * 2048 + kk * 32, 16, 1024, LAYOUT_SW128), idesc_lat,
+                           (c | half | kk) ? 1u : 0u);
           }
-          const uint32_t rs = g % kRopeSlots;
-          if (ok) ok = mbar_wait(&B->rope_full[rs], (g / kRopeSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL);
           if (!ok) break;
-          tc_fence_after();
-#pragma unroll 1
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t a_box = s_base + OFF_CVT + ((4 * g + (k >> 1)) % kCvtSlots) * kCvtBytes + (k & 1) * 8192;
-            const uint32_t b_box = q_addr + k * 2048;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_f16_ss(tmem + sb * 16, smem_desc(a_box + kk * 32, 16, 1024, LAYOUT_SW128),
-                         smem_desc(b_box + kk * 32, 16, 1024, LAYOUT_SW128), idesc_lat, (k | kk) ? 1u : 0u);
-          }
-          {
-            const uint32_t a_box = s_base + OFF_ROPE + rs * kRopeBytes;
-            const uint32_t b_box = q_addr + 8 * 2048;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_f16_ss(tmem + kColRope + sb * 16, smem_desc(a_box + kk * 32, 16, 1024, LAYOUT_SW128),
-                         smem_desc(b_box + kk * 32, 16, 1024, LAYOUT_SW128), idesc_rope, kk ? 1u : 0u);
-          }
           mma_commit(&B->s_full[sb]);
           mma_commit(&B->rope_empty[rs]);
-          if (t == nt - 1) mma_commit(&B->q_empty[qb]);
-          if (t > 0) ok = issue_pv(g - 1, t == 1, seg_i);
+          const bool first = (t == 0);
+          ok = mbar_wait(&B->p_full[sb], (g >> 1) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+          if (ok && first && seg_i > 0) ok = mbar_wait(&B->o_empty, (seg_i - 1) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t p_addr = s_base + OFF_P + sb * kPBytes;
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const uint32_t li = 4 * g + c;
+            const uint32_t slot = s_base + OFF_CVT + (li % kCvtSlots) * kCvtBytes;
+#pragma unroll
+            for (int kk = 0; kk < kTileTok / 16; ++kk)
+              mma_f16_ss(tmem + kColO + 16 * c, smem_desc(slot + kk * 2048, kBox, 1024, LAYOUT_SW128),
+                         smem_desc(p_addr + kk * 256, 128, kPChunkSbo, LAYOUT_INTERLEAVE), idesc_pv,
+                         (first && kk == 0) ? 0u : 1u);
+            mma_commit(&B->cvt_empty[li % kCvtSlots]);
+          }
+          mma_commit(&B->p_empty[sb]);
         }
-        if (!ok) break;
-        ok = issue_pv(g - 1, nt == 1, seg_i);
         if (ok) mma_commit(&B->o_full);
       }
       mma_commit(&B->drain);
       drain_wait(&B->drain, 0, p.err);
-    }
-  } else if (warp == 2) {
-    // ------------------------------------------------------------ query loader
-    int seg_i = 0;
-    for (int si = seg_lo; si < seg_hi; ++si, ++seg_i) {
-      const AttendSegment sg = p.segs[si];
-      const uint32_t qb = seg_i % kQBufs;
-      int ok = 1;
-      if (lane == 0) ok = mbar_wait(&B->q_empty[qb], ((seg_i / kQBufs) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      const float *qs = p.q + static_cast<size_t>(sg.seq) * kHeads * kRow;
-      uint8_t *qd = smem + OFF_Q + qb * kQBytes;
-      for (int idx = lane; idx < kHeads * (kRow / 8); idx += 32) {
-        const int h = idx / (kRow / 8), c8 = idx % (kRow / 8);
-        const float4 a = *reinterpret_cast<const float4 *>(qs + h * kRow + c8 * 8);
-        const float4 b = *reinterpret_cast<const float4 *>(qs + h * kRow + c8 * 8 + 4);
-        uint4 v;
-        if (c8 < kLatent / 8) {
-          v.x = pack_f16(a.x, a.y);
-          v.y = pack_f16(a.z, a.w);
-          v.z = pack_f16(b.x, b.y);
-          v.w = pack_f16(b.z, b.w);
-        } else {
-          v.x = pack_bf16(a.x, a.y);
-          v.y = pack_bf16(a.z, a.w);
-          v.z = pack_bf16(b.x, b.y);
-          v.w = pack_bf16(b.z, b.w);
-        }
-        *reinterpret_cast<uint4 *>(qd + (c8 >> 3) * 2048 + sw128_offset(h, (c8 & 7) * 8)) = v;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&B->q_full[qb]);
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ converters
@@ -296,9 +253,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!w_ok) { ok = false; break; }
           const uint8_t *src = smem + OFF_STG + ss * kStgBytes;
           uint8_t *dst = smem + OFF_CVT + cs * kCvtBytes;
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int idx = ct + 128 * i;  // 512 source chunks of 16 int8
+#pragma unroll 4
+          for (int i = 0; i < 8; ++i) {
+            const int idx = ct + 128 * i;  // 1024 chunks of 16 int8 (128 rows x 8)
             const int row = idx >> 3, k = idx & 7;
             const uint4 v = *reinterpret_cast<const uint4 *>(src + row * 128 + ((k ^ (row & 7)) << 4));
             uint4 o0, o1;
@@ -307,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             i8x4_to_f16x4(v.z, o1.x, o1.y);
             i8x4_to_f16x4(v.w, o1.z, o1.w);
             // dims 16k..16k+15 of this 128-dim chunk -> fp16 box (k >> 2), 16B chunks 2(k&3), 2(k&3)+1
-            uint8_t *box = dst + (k >> 2) * 8192;
+            uint8_t *box = dst + (k >> 2) * kBox;
             const int fc = 2 * (k & 3);
             *reinterpret_cast<uint4 *>(box + sw128_offset(row, fc * 8)) = o0;
             *reinterpret_cast<uint4 *>(box + sw128_offset(row, fc * 8 + 8)) = o1;
@@ -324,6 +281,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax + epilogue
     const int w = warp - 4;
+    const int tt = 32 * w + lane;
     const uint32_t lane_base = static_cast<uint32_t>(32 * w) << 16;
     uint32_t g = 0;
     int seg_i = 0;
@@ -331,13 +289,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const AttendSegment sg = p.segs[si];
       const long long srow0 = p.seq_row0[sg.seq];
       const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
+      // The query tile is free here: every score MMA of the previous segment
+      // has completed (its scores were read above).
+      load_query_tile(smem + OFF_Q, p.q + static_cast<size_t>(sg.seq) * kHeads * kRow, tt, true);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B->q_full);
       float m_ref[kHeads], l_part[kHeads];
 #pragma unroll
       for (int h = 0; h < kHeads; ++h) { m_ref[h] = -INFINITY; l_part[h] = 0.f; }
       bool bad = false;
       for (int t = 0; t < nt; ++t, ++g) {
-        const int tok = sg.tok_begin + kTileTok * t + 16 * w + lane;
-        const bool valid = lane < 16 && tok < sg.tok_end;
+        const int tok = sg.tok_begin + kTileTok * t + tt;
+        const bool valid = tok < sg.tok_end;
         const float rs = valid ? p.latent_scale[srow0 + tok] : 0.f;
         const uint32_t sb = g & 1;
         bad = !mbar_wait(&B->s_full[sb], (g >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
@@ -379,8 +343,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           named_bar_sync(1, 128);
           if (t > 0) {
-            const uint32_t pp = (g - 1) & 1;
-            bad = !mbar_wait(&B->p_empty[pp], ((g - 1) >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
+            bad = !mbar_wait(&B->p_empty[(g - 1) & 1], ((g - 1) >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
             if (named_bar_or(1, 128, bad)) { bad = true; break; }
             tc_fence_after();
 #pragma unroll
@@ -403,20 +366,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           pr[h] = exp2f(s[h] - m_ref[h]);
           l_part[h] += pr[h];
         }
-        const uint32_t pb = g & 1;
-        bad = !mbar_wait(&B->p_empty[pb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_MMA);
+        bad = !mbar_wait(&B->p_empty[sb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_MMA);
         if (named_bar_or(1, 128, bad)) { bad = true; break; }
-        if (lane < 16) {
-          const int tt = 16 * w + lane;
-          uint8_t *pd = smem + OFF_P + pb * kPBytes + (tt >> 3) * 128 + (tt & 7) * 2;
+        {
+          // Rows past the segment end carry rs = 0, so P' = 0; the converted
+          // int8 rows are always finite, so 0 * row is 0 in the P.V MMA.
+          uint8_t *pd = smem + OFF_P + sb * kPBytes + (tt >> 3) * 128 + (tt & 7) * 2;
 #pragma unroll
           for (int h = 0; h < kHeads; ++h)
-            *reinterpret_cast<__half *>(pd + (h >> 3) * 1024 + (h & 7) * 16) = __float2half_rn(pr[h] * rs);
+            *reinterpret_cast<__half *>(pd + (h >> 3) * kPChunkSbo + (h & 7) * 16) = __float2half_rn(pr[h] * rs);
         }
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&B->p_full[pb]);
+        if (lane == 0) mbar_arrive(&B->p_full[sb]);
       }
       if (bad) break;
       bad = !mbar_wait(&B->o_full, seg_i & 1, abort, p.err, ERR_TIMEOUT_MMA);
@@ -480,6 +443,7 @@ cudaError_t launch_attend_q8(const AttendParams &p, int grid, cudaStream_t strea
     if (e != cudaSuccess) return e;
     attr_set = true;
   }
+  ProfScope ps("mla_attend_q8", stream);
   mla_attend_q8_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError();
 }

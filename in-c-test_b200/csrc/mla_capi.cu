@@ -709,9 +709,99 @@ KVL_EXPORT int kvl_mla_decode_compressed_q8_bf16(float *out, const float *x, int
 }
 
 // =================================================================== prefill
-// Reference: src/mla_prefill_streaming.c:78-206 (validation :80-85).  Causal
-// attention runs in the absorbed form over a temporary bf16 latent pool: query
-// t attends rows [0, t] through the same attend kernel as decode.
+// Causal attention runs in the absorbed form over a bf16 latent pool: query t
+// attends rows [0, t] through the same attend kernel as decode.
+namespace kvl {
+namespace {
+
+struct PrefillWs {
+  size_t off[8];
+  size_t total;
+};
+
+PrefillWs prefill_layout(const KvlMlaConfig &c, int S) {
+  const size_t s = S, H = c.hidden_size, NH = c.num_heads, QD = c.qk_nope_dim + c.qk_rope_dim;
+  const size_t R = c.kv_lora_rank, DR = c.qk_rope_dim, DV = c.v_head_dim;
+  const size_t sz[7] = {s * H * 4, s * NH * QD * 4, s * (R + DR) * 4, s * NH * (R + DR) * 4, s * NH * R * 4,
+                        s * NH * DV * 4, (s + kTileTok) * (R + DR) * 2};
+  PrefillWs w;
+  size_t o = 0;
+  for (int i = 0; i < 7; ++i) {
+    w.off[i] = o;
+    o += (sz[i] + 255) & ~size_t(255);
+  }
+  w.off[7] = o;
+  w.total = o;
+  return w;
+}
+
+// Plans of the prefill attend, cached per (device, S): query t covers rows [0, t].
+std::mutex g_pplan_mu;
+std::unordered_map<long long, DevicePlan *> g_pplan;
+
+const DevicePlan *prefill_plan(int device, int S, int nh, int R, int sms) {
+  const long long key = (static_cast<long long>(device) << 40) ^ (static_cast<long long>(nh) << 32) ^
+                        (static_cast<long long>(R) << 20) ^ S;
+  std::lock_guard<std::mutex> lk(g_pplan_mu);
+  auto it = g_pplan.find(key);
+  if (it != g_pplan.end()) return it->second;
+  std::vector<int> lens(S);
+  std::vector<long long> row0(S, 0);
+  for (int t = 0; t < S; ++t) lens[t] = t + 1;
+  HostPlan hp;
+  if (build_attend_plan(hp, S, lens.data(), row0.data(), sms) != 0) return nullptr;
+  DevicePlan *dp = new DevicePlan();
+  if (dp->upload(hp, nh, R, nullptr, nullptr, 0) != 0 || cudaDeviceSynchronize() != cudaSuccess) {
+    dp->release();
+    delete dp;
+    return nullptr;
+  }
+  g_pplan[key] = dp;
+  return dp;
+}
+
+// xf: fp32 tokens already on the device.
+int prefill_core(int device, int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, const float *xf,
+                 int S, uint8_t *ws, const PrefillWs &L, cudaStream_t st) {
+  const int H = cfg.hidden_size, NH = cfg.num_heads, DN = cfg.qk_nope_dim, DR = cfg.qk_rope_dim;
+  const int DV = cfg.v_head_dim, R = cfg.kv_lora_rank, QD = DN + DR;
+  float *q = reinterpret_cast<float *>(ws + L.off[1]);
+  float *ka = reinterpret_cast<float *>(ws + L.off[2]);
+  float *qabs = reinterpret_cast<float *>(ws + L.off[3]);
+  float *mix = reinterpret_cast<float *>(ws + L.off[4]);
+  float *ho = reinterpret_cast<float *>(ws + L.off[5]);
+  uint16_t *pool = reinterpret_cast<uint16_t *>(ws + L.off[6]);
+  CK(gemv_bf16(q, xf, W.q, H, NH * QD, S, st));
+  CK(gemv_bf16(ka, xf, W.kva, H, R + DR, S, st));
+  CK(append_bf16(pool, 0, ka, W.kvan, S, R, DR, 0, cfg.rms_eps, cfg.rope_theta, nullptr, st));
+  CK(absorb(qabs, q, W.kvb, S, NH, DN, DV, DR, R, 0, cfg.rope_theta, st));
+  const DevicePlan *dp = prefill_plan(device, S, NH, R, sms);
+  if (!dp) {
+    set_err("prefill attend plan failed");
+    return -1;
+  }
+  AttendLaunch a;
+  a.nh = NH;
+  a.R = R;
+  a.DR = DR;
+  a.rows = static_cast<long long>(S) + kTileTok;
+  a.q = qabs;
+  a.out = mix;
+  a.kv = pool;
+  a.softmax_scale = 1.0f / sqrtf(static_cast<float>(QD));
+  if (dp->launch(a, st) != 0) {
+    set_err("prefill attend launch failed");
+    return -1;
+  }
+  CK(vup(ho, mix, W.kvb, S, NH, DN, DV, R, st));
+  CK(gemv_bf16(d_out, ho, W.o, NH * DV, H, S, st));
+  return 0;
+}
+
+}  // namespace
+}  // namespace kvl
+
+// Reference: src/mla_prefill_streaming.c:78-206 (validation :80-85).
 KVL_EXPORT int kvl_mla_prefill_bf16(float *out, const float *x, int seq_len, const KvlMlaConfig *cfg,
                                     const KvlMlaBF16 *w) {
   if (!out || !x || !cfg || !w || !w->q_proj || !w->kv_a_proj || !w->kv_a_norm || !w->kv_b_proj || !w->o_proj ||
@@ -724,60 +814,51 @@ KVL_EXPORT int kvl_mla_prefill_bf16(float *out, const float *x, int seq_len, con
   Ctx *c = get_ctx(dev);
   if (!c) return -1;
   std::lock_guard<std::mutex> lk(c->mu);
-  const int S = seq_len, H = cfg->hidden_size, NH = cfg->num_heads, DN = cfg->qk_nope_dim;
-  const int DR = cfg->qk_rope_dim, DV = cfg->v_head_dim, R = cfg->kv_lora_rank, QD = DN + DR;
-  const size_t s = S;
+  const size_t s = seq_len, H = cfg->hidden_size;
   DevW W;
   if (stage_weights(*c, *cfg, *w, W, true) != 0) return -1;
-  if (!c->x.ensure(s * H * 4) || !c->q.ensure(s * NH * QD * 4) || !c->ka.ensure(s * (R + DR) * 4) ||
-      !c->qabs.ensure(s * NH * (R + DR) * 4) || !c->mix.ensure(s * NH * R * 4) || !c->ho.ensure(s * NH * DV * 4) ||
-      !c->y.ensure(s * H * 4) || !c->kvtmp.ensure((s + kTileTok) * (R + DR) * 2)) {
+  const PrefillWs L = prefill_layout(*cfg, seq_len);
+  if (!c->kvtmp.ensure(L.total) || !c->y.ensure(s * H * 4)) {
     set_err("cudaMalloc of prefill scratch failed");
     return -1;
   }
-  CK(cudaMemcpyAsync(c->x.p, x, s * H * 4, cudaMemcpyHostToDevice, c->stream));
-  CK(gemv_bf16(c->q.as<float>(), c->x.as<float>(), W.q, H, NH * QD, S, c->stream));
-  CK(gemv_bf16(c->ka.as<float>(), c->x.as<float>(), W.kva, H, R + DR, S, c->stream));
-  uint16_t *pool = c->kvtmp.as<uint16_t>();
-  CK(append_bf16(pool, 0, c->ka.as<float>(), W.kvan, S, R, DR, 0, cfg->rms_eps, cfg->rope_theta, nullptr,
-                 c->stream));
-  CK(absorb(c->qabs.as<float>(), c->q.as<float>(), W.kvb, S, NH, DN, DV, DR, R, 0, cfg->rope_theta, c->stream));
-  std::vector<int> lens(S);
-  std::vector<long long> row0(S, 0);
-  for (int t = 0; t < S; ++t) lens[t] = t + 1;
-  HostPlan hp;
-  if (build_attend_plan(hp, S, lens.data(), row0.data(), c->sms) != 0) {
-    set_err("prefill attend plan failed");
-    return -1;
-  }
-  if (c->plan.upload(hp, NH, R, c->stream, nullptr, 0) != 0) {
-    set_err("prefill attend plan upload failed");
-    return -1;
-  }
-  AttendLaunch a;
-  a.nh = NH;
-  a.R = R;
-  a.DR = DR;
-  a.rows = static_cast<long long>(s + kTileTok);
-  a.q = c->qabs.as<float>();
-  a.out = c->mix.as<float>();
-  a.kv = pool;
-  a.softmax_scale = 1.0f / sqrtf(static_cast<float>(QD));
-  if (c->plan.launch(a, c->stream) != 0) {
-    set_err("prefill attend launch failed");
-    return -1;
-  }
-  CK(vup(c->ho.as<float>(), c->mix.as<float>(), W.kvb, S, NH, DN, DV, R, c->stream));
-  CK(gemv_bf16(c->y.as<float>(), c->ho.as<float>(), W.o, NH * DV, H, S, c->stream));
-  uint32_t err = 0;
+  uint8_t *ws = c->kvtmp.as<uint8_t>();
+  float *xf = reinterpret_cast<float *>(ws + L.off[0]);
+  CK(cudaMemcpyAsync(xf, x, s * H * 4, cudaMemcpyHostToDevice, c->stream));
+  if (prefill_core(dev, c->sms, *cfg, W, c->y.as<float>(), xf, seq_len, ws, L, c->stream) != 0) return -1;
   CK(cudaMemcpyAsync(out, c->y.p, s * H * 4, cudaMemcpyDeviceToHost, c->stream));
-  CK(cudaMemcpyAsync(&err, c->plan.err_word(), 4, cudaMemcpyDeviceToHost, c->stream));
   CK(cudaStreamSynchronize(c->stream));
-  if (err != 0) {
-    set_err("prefill attend reported device error 0x%x", err);
+  return 0;
+}
+
+KVL_EXPORT size_t kvl_mla_prefill_workspace_bytes(const KvlMlaConfig *cfg, int seq_len) {
+  if (!cfg || seq_len <= 0 || !cfg_dims_ok(*cfg)) return 0;
+  return prefill_layout(*cfg, seq_len).total;
+}
+
+KVL_EXPORT int kvl_mla_prefill_dev(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, float *d_out,
+                                   const uint16_t *d_x, int seq_len, void *d_workspace, size_t workspace_bytes,
+                                   void *stream) {
+  if (!cfg || !w || !d_out || !d_x || seq_len <= 0 || !d_workspace || !cfg_dims_ok(*cfg) || !w->q_proj ||
+      !w->kv_a_proj || !w->kv_a_norm || !w->kv_b_proj || !w->o_proj) {
+    set_err("invalid prefill arguments");
     return -1;
   }
-  return 0;
+  const PrefillWs L = prefill_layout(*cfg, seq_len);
+  if (workspace_bytes < L.total) {
+    set_err("prefill workspace too small (%zu < %zu)", workspace_bytes, L.total);
+    return -1;
+  }
+  const int dev = current_device();
+  if (dev < 0) return -1;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *ws = static_cast<uint8_t *>(d_workspace);
+  float *xf = reinterpret_cast<float *>(ws + L.off[0]);
+  CK(bf16_to_f32(xf, d_x, static_cast<long long>(seq_len) * cfg->hidden_size, st));
+  DevW W{w->q_proj, w->kv_a_proj, w->kv_a_norm, w->kv_b_proj, w->o_proj};
+  return prefill_core(dev, sms, *cfg, W, d_out, xf, seq_len, ws, L, st);
 }
 
 // =================================================================== attend plans
@@ -911,16 +992,8 @@ KVL_EXPORT int kvl_mla_merge_partials(float *d_out, float *d_lse, const float *d
     set_err("invalid merge arguments");
     return -1;
   }
-  std::vector<MergeEntry> e(batch);
-  for (int b = 0; b < batch; ++b) e[b] = MergeEntry{b, b, parts, batch};
-  void *d_e = nullptr;
-  CK(cudaMallocAsync(&d_e, e.size() * sizeof(MergeEntry), static_cast<cudaStream_t>(stream)));
-  CK(cudaMemcpyAsync(d_e, e.data(), e.size() * sizeof(MergeEntry), cudaMemcpyHostToDevice,
-                     static_cast<cudaStream_t>(stream)));
-  CK(launch_merge(d_out, d_lse, d_part_o, d_part_lse, static_cast<const MergeEntry *>(d_e), batch, num_heads,
-                  kv_lora_rank, static_cast<cudaStream_t>(stream)));
-  CK(cudaFreeAsync(d_e, static_cast<cudaStream_t>(stream)));
-  CK(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)));
+  CK(launch_merge(d_out, d_lse, d_part_o, d_part_lse, nullptr, batch, num_heads, kv_lora_rank,
+                  static_cast<cudaStream_t>(stream), parts));
   return 0;
 }
 

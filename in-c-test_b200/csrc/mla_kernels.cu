@@ -19,6 +19,7 @@
 #include <cstdint>
 
 #include "mla_kernels.cuh"
+#include "prof.cuh"
 
 namespace kvl {
 
@@ -116,6 +117,7 @@ cudaError_t gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int o
     if (e != cudaSuccess) return e;
   }
   dim3 grid((out + 7) / 8, (n + NB - 1) / NB);
+  ProfScope ps("gemv_bf16", s);
   gemv_bf16_kernel<NB><<<grid, 256, sm, s>>>(y, x, W, in, out, n);
   return cudaGetLastError();
 }
@@ -222,6 +224,7 @@ cudaError_t append_bf16(uint16_t *kv, long long row0, const float *ka, const uin
                         int DR, int pos0, float eps, float theta, float *rows_f32, cudaStream_t s,
                         const long long *row_of, const int *pos_of) {
   if (n <= 0) return cudaSuccess;
+  ProfScope ps("append_bf16", s);
   append_bf16_kernel<<<n, 128, append_smem(R), s>>>(kv, row0, ka, norm_w, R, DR, pos0, eps, theta, rows_f32,
                                                     row_of, pos_of);
   return cudaGetLastError();
@@ -231,6 +234,7 @@ cudaError_t append_q8(int8_t *lat8, float *lscale, uint16_t *rope16, long long r
                       const uint16_t *norm_w, int n, int R, int DR, int pos0, float eps, float theta,
                       cudaStream_t s, const long long *row_of, const int *pos_of) {
   if (n <= 0) return cudaSuccess;
+  ProfScope ps("append_q8", s);
   append_q8_kernel<<<n, 128, append_smem(R), s>>>(lat8, lscale, rope16, row0, ka, norm_w, R, DR, pos0, eps, theta,
                                                   row_of, pos_of);
   return cudaGetLastError();
@@ -264,6 +268,7 @@ __global__ void absorb_kernel(float *qabs, const float *q, const uint16_t *kvb, 
 cudaError_t absorb(float *qabs, const float *q, const uint16_t *kvb, int n, int NH, int DN, int DV, int DR, int R,
                    int pos0, float theta, cudaStream_t s, const int *pos_of) {
   if (n <= 0) return cudaSuccess;
+  ProfScope ps("absorb", s);
   absorb_kernel<<<dim3(NH, n), 256, DN * sizeof(float), s>>>(qabs, q, kvb, NH, DN, DV, DR, R, pos0, theta, pos_of);
   return cudaGetLastError();
 }
@@ -298,6 +303,7 @@ __global__ void vup_kernel(float *ho, const float *mix, const uint16_t *kvb, int
 cudaError_t vup(float *ho, const float *mix, const uint16_t *kvb, int n, int NH, int DN, int DV, int R,
                 cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
+  ProfScope ps("vup", s);
   vup_kernel<<<dim3((NH * DV + 7) / 8, n), 256, 0, s>>>(ho, mix, kvb, NH, DN, DV, R);
   return cudaGetLastError();
 }
@@ -358,6 +364,7 @@ __global__ void bf16_to_f32_kernel(float *out, const uint16_t *x, long long n) {
 cudaError_t bf16_to_f32(float *out, const uint16_t *x, long long n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   const int grid = static_cast<int>((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+  ProfScope ps("bf16_to_f32", s);
   bf16_to_f32_kernel<<<grid, 256, 0, s>>>(out, x, n);
   return cudaGetLastError();
 }

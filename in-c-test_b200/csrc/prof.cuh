@@ -1,0 +1,23 @@
+// prof.cuh -- optional per-kernel timing: when enabled, every kernel launch of
+// the library is bracketed by CUDA events recorded on the launching stream, and
+// kvl_mla_cuda_profile_read() reports the accumulated device time per kernel.
+// Disabled (the default) it costs one relaxed atomic load per launch.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace kvl {
+
+bool prof_enabled();
+int prof_begin(const char *name, cudaStream_t s);  // returns a record id, or -1
+void prof_end(int id, cudaStream_t s);
+
+struct ProfScope {
+  int id;
+  cudaStream_t s;
+  ProfScope(const char *name, cudaStream_t st) : id(prof_enabled() ? prof_begin(name, st) : -1), s(st) {}
+  ~ProfScope() {
+    if (id >= 0) prof_end(id, s);
+  }
+};
+
+}  // namespace kvl

@@ -81,6 +81,8 @@ SIGNATURES = {
     "kvl_mla_cuda_last_error": (C.c_char_p, []),
     "kvl_mla_cuda_weight_cache": (C.c_int, [C.c_int]),
     "kvl_mla_cuda_state_device_bytes": (C.c_size_t, [C.c_void_p]),
+    "kvl_mla_cuda_profile": (C.c_int, [C.c_int]),
+    "kvl_mla_cuda_profile_read": (C.c_int, [C.c_char_p, C.c_size_t]),
     "kvl_mla_attend_plan_create": (C.c_int, [C.POINTER(C.c_void_p), C.c_int, i32p, i64p, C.c_int, C.c_int, C.c_int]),
     "kvl_mla_attend_plan_destroy": (None, [C.c_void_p]),
     "kvl_mla_attend_plan_info": (C.c_int, [C.c_void_p, i32p, i32p, i32p]),
@@ -95,6 +97,9 @@ SIGNATURES = {
     "kvl_mla_decode_step_bf16": (C.c_int, [C.POINTER(KvlMlaConfig), C.POINTER(KvlMlaDeviceWeights), C.c_void_p,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
                                            C.c_int, C.c_void_p, C.c_void_p]),
+    "kvl_mla_prefill_workspace_bytes": (C.c_size_t, [C.POINTER(KvlMlaConfig), C.c_int]),
+    "kvl_mla_prefill_dev": (C.c_int, [C.POINTER(KvlMlaConfig), C.POINTER(KvlMlaDeviceWeights), C.c_void_p,
+                                      C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
     "kvl_mla_q8_quantize_rows": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "kvl_mla_q8_dequant": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int, C.c_void_p]),
     "kvl_mla_bf16_rne": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),

@@ -41,6 +41,15 @@ const char *kvl_mla_cuda_last_error(void);
  * KVL_CUDA_WEIGHT_CACHE=1, enables it at start-up.  Returns the previous mode. */
 int kvl_mla_cuda_weight_cache(int enable);
 
+/* Per-kernel timing.  Enabled (1), every kernel the library launches is
+ * bracketed by CUDA events on its launching stream; enabling clears the
+ * totals.  Returns the previous mode. */
+int kvl_mla_cuda_profile(int enable);
+/* Waits for the recorded launches and writes one "kernel,total_ms,launches"
+ * line per kernel into buf (NUL-terminated).  Returns the number of kernels,
+ * or -1 if cap is too small. */
+int kvl_mla_cuda_profile_read(char *buf, size_t cap);
+
 /* Device bytes held by a state created by kvl_mla_compressed_state_init /
  * kvl_mla_compressed_q8_state_init (0 for an unknown state). */
 size_t kvl_mla_cuda_state_device_bytes(const void *state);
@@ -111,6 +120,18 @@ int kvl_mla_decode_step_bf16(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights 
                              const KvlMlaAttendPlan *plan, float *d_out, const float *d_x,
                              uint16_t *d_kv, int64_t rows, const int64_t *d_row,
                              const int *d_pos, int batch, void *d_workspace, void *stream);
+
+/* ------------------------------------------------------------------ prefill on device */
+
+/* Scratch bytes kvl_mla_prefill_dev needs for seq_len tokens. */
+size_t kvl_mla_prefill_workspace_bytes(const KvlMlaConfig *cfg, int seq_len);
+
+/* Causal MLA prefill of one sequence entirely on the device (the computation
+ * of kvl_mla_prefill_bf16): d_x [seq_len][H] bf16 token activations ->
+ * d_out [seq_len][H] fp32.  Asynchronous on `stream`. */
+int kvl_mla_prefill_dev(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, float *d_out,
+                        const uint16_t *d_x, int seq_len, void *d_workspace, size_t workspace_bytes,
+                        void *stream);
 
 /* ------------------------------------------------------------------ Q8 helpers */
 int kvl_mla_q8_quantize_rows(int8_t *d_q, float *d_scale, const float *d_x, int rows, int R,
