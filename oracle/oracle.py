@@ -194,6 +194,39 @@ class Oracle:
                                 _p(kv_a, u16p), _p(kv_a_norm, u16p))
         return lat, rp
 
+    def append_q8(self, x, position, cfg: Cfg, kv_a, kv_a_norm):
+        R, DR = cfg.kv_lora_rank, cfg.qk_rope_dim
+        q = np.zeros(R, np.int8)
+        s = np.zeros(1, np.float32)
+        rp = np.zeros(DR, np.uint16)
+        x = np.ascontiguousarray(x, np.float32)
+        self.lib.orc_append_q8(_p(q, i8p), _p(s, f32p), _p(rp, u16p), _p(x, f32p), position, C.byref(cfg),
+                               _p(kv_a, u16p), _p(kv_a_norm, u16p))
+        return q, s[0], rp
+
+    def decode_sequence(self, x, cfg: Cfg, warrays, prefix=0, q8=False):
+        """Same protocol as Reference.decode_sequence, on the restatement."""
+        x = np.ascontiguousarray(x, np.float32)
+        S = x.shape[0]
+        R, DR = cfg.kv_lora_rank, cfg.qk_rope_dim
+        outs = np.zeros((S - prefix, cfg.hidden_size), np.float32)
+        if q8:
+            l8 = np.zeros((S, R), np.int8)
+            ls = np.zeros(S, np.float32)
+            r16 = np.zeros((S, DR), np.uint16)
+            for t in range(prefix):
+                l8[t], ls[t], r16[t] = self.append_q8(x[t], t, cfg, warrays[1], warrays[2])
+            for t in range(prefix, S):
+                outs[t - prefix] = self.decode_q8(x[t], t, cfg, warrays, l8, ls, r16)
+            return outs, (l8, ls, r16)
+        lat = np.zeros((S, R), np.float32)
+        rope = np.zeros((S, DR), np.float32)
+        for t in range(prefix):
+            lat[t], rope[t] = self.append_f32(x[t], t, cfg, warrays[1], warrays[2])
+        for t in range(prefix, S):
+            outs[t - prefix] = self.decode_f32(x[t], t, cfg, warrays, lat, rope)
+        return outs, (lat, rope)
+
 
 class Reference:
     """The reference runtime's own MLA functions, compiled from its sources."""
