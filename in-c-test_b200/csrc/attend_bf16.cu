@@ -407,4 +407,14 @@ cudaError_t launch_attend_bf16(const AttendParams &p, int grid, cudaStream_t str
   return cudaGetLastError();
 }
 
+// Same launch without the optional per-kernel timing, whose CUDA events are
+// created on demand: used by the entry point that must not allocate.
+cudaError_t launch_attend_bf16_unprofiled(const AttendParams &p, int grid, cudaStream_t stream) {
+  cudaError_t e = cudaFuncSetAttribute(mla_attend_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       kSmemBytes);
+  if (e != cudaSuccess) return e;
+  mla_attend_bf16_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
 }  // namespace kvl

@@ -178,6 +178,19 @@ cudaError_t launch_merge(float *out, float *lse, const float *part_o, const floa
   return cudaGetLastError();
 }
 
+// The merge launch without per-kernel timing (its events are created on
+// demand); for the entry point that must not allocate.
+cudaError_t launch_merge_unprofiled(float *out, float *lse, const float *part_o, const float *part_lse,
+                                   const MergeEntry *d_entries, int n_entries, int nh, int R,
+                                   cudaStream_t stream, int max_count) {
+  if (n_entries <= 0) return cudaSuccess;
+  const size_t sm = (static_cast<size_t>(max_count) + 32 + 256) * sizeof(float);
+  if (sm > 48 * 1024) return cudaErrorInvalidValue;
+  dim3 grid(n_entries, nh, (R + 31) / 32);
+  merge_partials_kernel<<<grid, 256, sm, stream>>>(out, lse, part_o, part_lse, d_entries, nh, R, max_count);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ generic attend
 // One CTA per (head, sequence); online softmax over chunks of 1024 rows in
 // fp32.  Used only when (NH, R, DR) is not the production (16, 512, 64).

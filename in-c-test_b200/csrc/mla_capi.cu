@@ -432,6 +432,10 @@ int prefill_state(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, 
 }
 
 }  // namespace
+
+// Failure message for kvl_mla_cuda_last_error() from the other translation units.
+void set_error_text(const char *msg) { set_err("%s", msg); }
+
 }  // namespace kvl
 
 using namespace kvl;

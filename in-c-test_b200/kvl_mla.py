@@ -90,6 +90,9 @@ SIGNATURES = {
                                       C.c_int, C.c_int, C.c_int, C.c_float, C.c_void_p]),
     "kvl_mla_attend_q8": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                     C.c_void_p, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_float, C.c_void_p]),
+    "kvl_mla_attend_bf16_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int,
+                                              C.c_int64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float,
+                                              C.c_void_p]),
     "kvl_mla_attend_check": (C.c_int, [C.c_void_p, C.c_void_p]),
     "kvl_mla_merge_partials": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                          C.c_int, C.c_void_p]),

@@ -87,6 +87,25 @@ int kvl_mla_attend_q8(const KvlMlaAttendPlan *plan, float *d_out, float *d_lse,
                       const uint16_t *d_rope_bf16, int64_t rows, int num_heads, int kv_lora_rank,
                       int rope_dim, float softmax_scale, void *stream);
 
+/* Single-sequence bf16 attend that allocates nothing.  This call has no
+ * counterpart in the reference runtime.  It serves callers that cannot
+ * allocate device memory while they decode: a runtime that reserves its whole
+ * device-memory budget up front, or a decode loop that must not stall on
+ * cudaMalloc (which can synchronise the device and fails once memory is
+ * fragmented).  It computes what kvl_mla_attend_bf16 computes for one sequence
+ * of seq_len rows starting at pool row seq_row0, split over `splits` KV ranges
+ * (0 = one per SM), with its plan and partial outputs in a fixed 4.9 MB device
+ * array that the library reserves on every GPU it is loaded on until the
+ * process exits.  splits above 148 are rejected; only the (16, 512, 64) shape
+ * is accepted.  The first call on a device looks up that array's address and
+ * should come before any stream capture.  All calls share the array: calls
+ * that overlap on the GPU race and must be serialised by the caller.  Returns
+ * after the result is in d_out (it waits for `stream`). */
+int kvl_mla_attend_bf16_noalloc(float *d_out, float *d_lse, const float *d_q, const uint16_t *d_kv,
+                                int64_t rows, int seq_len, int64_t seq_row0, int num_heads,
+                                int kv_lora_rank, int rope_dim, int splits, float softmax_scale,
+                                void *stream);
+
 /* Waits for `stream` and returns -1 if a kernel of the plan's last launch
  * reported a device-side error (a bounded wait that ran out); clears it. */
 int kvl_mla_attend_check(const KvlMlaAttendPlan *plan, void *stream);
