@@ -50,6 +50,19 @@ bool make_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint
   return r == CUDA_SUCCESS;
 }
 
+bool make_tmap_3d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, const uint64_t dims[3],
+                  const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t s[2] = {strides_bytes[0], strides_bytes[1]};
+  cuuint32_t b[3] = {box[0], box[1], box[2]};
+  cuuint32_t e[3] = {1, 1, 1};
+  CUresult r = fn(m, dt, 3, const_cast<void *>(base), d, s, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 // ------------------------------------------------------------------ plan
 int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long long *seq_row0,
                       int max_ctas) {

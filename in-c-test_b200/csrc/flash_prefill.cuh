@@ -1,0 +1,27 @@
+// flash_prefill.cuh -- causal MLA prefill attention (see flash_prefill.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace kvl {
+
+struct FlashParams {
+  CUtensorMap tm_q;    // q [S][16][192] bf16 (nope 128 | rotated rope 64), 3-D box {64, 1, 128}
+  CUtensorMap tm_kv;   // kv [S][16][256] bf16 (k_nope 128 | v 128), 3-D box {64, 1, 128}
+  CUtensorMap tm_kr;   // rotated k_rope: columns [kr_col, kr_col + 64) of a [S][ld] bf16 pool, box {64, 128}
+  int kr_col;
+  int S;
+  float scale_log2;    // softmax scale * log2(e)
+  __nv_bfloat16 *out;  // [S][16][128] bf16
+  uint32_t *err;
+};
+
+cudaError_t launch_flash_prefill(const FlashParams &p, int sms, cudaStream_t stream);
+
+bool make_tmap_3d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, const uint64_t dims[3],
+                  const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle sw);
+
+}  // namespace kvl

@@ -1,0 +1,26 @@
+// gemm.cuh -- tcgen05 GEMM (C = A . B^T, bf16 in, fp32 accumulate) used by the
+// prefill projections; see gemm.cu.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace kvl {
+
+enum : int { EPI_F32 = 0, EPI_BF16 = 1, EPI_QROPE = 2 };
+
+struct GemmParams {
+  CUtensorMap tm_a;     // A [M][K] bf16, box 64 x 128
+  CUtensorMap tm_b;     // B [N][K] bf16, box 64 x BN
+  int M, N, K;
+  void *c;              // output, row-major with leading dimension ldc (elements)
+  int ldc;
+  const float2 *rope_cs;  // EPI_QROPE: cos/sin table [M][32]
+  uint32_t *err;
+};
+
+cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream);
+cudaError_t launch_rope_table(float2 *cs, int rows, int dim, float theta, cudaStream_t stream);
+
+}  // namespace kvl

@@ -27,6 +27,8 @@
 #include "kvl/mla_compressed_q8_state.h"
 #include "kvl/mla_compressed_state.h"
 #include "kvl/mla_cuda.h"
+#include "flash_prefill.cuh"
+#include "gemm.cuh"
 #include "mla_kernels.cuh"
 
 #define KVL_EXPORT extern "C" __attribute__((visibility("default")))
@@ -713,33 +715,54 @@ KVL_EXPORT int kvl_mla_decode_compressed_q8_bf16(float *out, const float *x, int
 }
 
 // =================================================================== prefill
-// Causal attention runs in the absorbed form over a bf16 latent pool: query t
-// attends rows [0, t] through the same attend kernel as decode.
+// Production shape (16 heads, DN 128, DR 64, DV 128, R 512): tcgen05 GEMMs for
+// the projections (RoPE of q fused into the q_proj epilogue), the latent pool
+// by append_bf16, and the causal flash kernel in the non-absorbed form.  Other
+// shapes (the reference probes' tiny ones) run the causal attention in the
+// absorbed form through the decode attend kernel (query t attends [0, t]).
 namespace kvl {
 namespace {
 
+bool fast_prefill_shape(const KvlMlaConfig &c) {
+  return c.num_heads == 16 && c.qk_nope_dim == 128 && c.qk_rope_dim == 64 && c.v_head_dim == 128 &&
+         c.kv_lora_rank == 512 && c.hidden_size % 8 == 0;
+}
+
 struct PrefillWs {
-  size_t off[8];
+  size_t off[10];
   size_t total;
 };
 
 PrefillWs prefill_layout(const KvlMlaConfig &c, int S) {
   const size_t s = S, H = c.hidden_size, NH = c.num_heads, QD = c.qk_nope_dim + c.qk_rope_dim;
-  const size_t R = c.kv_lora_rank, DR = c.qk_rope_dim, DV = c.v_head_dim;
-  const size_t sz[7] = {s * H * 4, s * NH * QD * 4, s * (R + DR) * 4, s * NH * (R + DR) * 4, s * NH * R * 4,
-                        s * NH * DV * 4, (s + kTileTok) * (R + DR) * 2};
+  const size_t R = c.kv_lora_rank, DR = c.qk_rope_dim, DV = c.v_head_dim, DN = c.qk_nope_dim;
+  size_t sz[9];
+  int n;
+  if (fast_prefill_shape(c)) {
+    // xf, xb, q (bf16, rope applied), kva (fp32), pool (bf16 latent|rope), kv (bf16), o (bf16), cos/sin, err
+    const size_t f[9] = {s * H * 4, s * H * 2, s * NH * QD * 2, s * (R + DR) * 4, s * (R + DR) * 2,
+                         s * NH * (DN + DV) * 2, s * NH * DV * 2, s * (DR / 2) * 8, 256};
+    for (int i = 0; i < 9; ++i) sz[i] = f[i];
+    n = 9;
+  } else {
+    // xf, q, kva, qabs, mix, head_out, pool
+    const size_t f[7] = {s * H * 4, s * NH * QD * 4, s * (R + DR) * 4, s * NH * (R + DR) * 4, s * NH * R * 4,
+                         s * NH * DV * 4, (s + kTileTok) * (R + DR) * 2};
+    for (int i = 0; i < 7; ++i) sz[i] = f[i];
+    n = 7;
+  }
   PrefillWs w;
   size_t o = 0;
-  for (int i = 0; i < 7; ++i) {
+  for (int i = 0; i < n; ++i) {
     w.off[i] = o;
     o += (sz[i] + 255) & ~size_t(255);
   }
-  w.off[7] = o;
+  for (int i = n; i < 10; ++i) w.off[i] = o;
   w.total = o;
   return w;
 }
 
-// Plans of the prefill attend, cached per (device, S): query t covers rows [0, t].
+// Plans of the absorbed-form attend, cached per (device, S): query t covers rows [0, t].
 std::mutex g_pplan_mu;
 std::unordered_map<long long, DevicePlan *> g_pplan;
 
@@ -764,9 +787,9 @@ const DevicePlan *prefill_plan(int device, int S, int nh, int R, int sms) {
   return dp;
 }
 
-// xf: fp32 tokens already on the device.
-int prefill_core(int device, int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, const float *xf,
-                 int S, uint8_t *ws, const PrefillWs &L, cudaStream_t st) {
+// Absorbed-form path; xf: fp32 tokens on the device.
+int prefill_absorbed(int device, int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, const float *xf,
+                     int S, uint8_t *ws, const PrefillWs &L, cudaStream_t st) {
   const int H = cfg.hidden_size, NH = cfg.num_heads, DN = cfg.qk_nope_dim, DR = cfg.qk_rope_dim;
   const int DV = cfg.v_head_dim, R = cfg.kv_lora_rank, QD = DN + DR;
   float *q = reinterpret_cast<float *>(ws + L.off[1]);
@@ -802,6 +825,100 @@ int prefill_core(int device, int sms, const KvlMlaConfig &cfg, const DevW &W, fl
   return 0;
 }
 
+bool bf16_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, uint64_t row_bytes, uint32_t box_rows) {
+  return make_tmap_2d(m, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, inner, rows, row_bytes, 64, box_rows,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+// tcgen05 path; xb: bf16 tokens on the device.  Returns -1 with a message.
+int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, const uint16_t *xb, int S,
+                 uint8_t *ws, const PrefillWs &L, cudaStream_t st) {
+  const uint64_t H = cfg.hidden_size, s = S;
+  uint16_t *q = reinterpret_cast<uint16_t *>(ws + L.off[2]);
+  float *kva = reinterpret_cast<float *>(ws + L.off[3]);
+  uint16_t *pool = reinterpret_cast<uint16_t *>(ws + L.off[4]);
+  uint16_t *kv = reinterpret_cast<uint16_t *>(ws + L.off[5]);
+  uint16_t *o = reinterpret_cast<uint16_t *>(ws + L.off[6]);
+  float2 *cs = reinterpret_cast<float2 *>(ws + L.off[7]);
+  uint32_t *err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
+  if ((reinterpret_cast<uintptr_t>(xb) | reinterpret_cast<uintptr_t>(W.q) | reinterpret_cast<uintptr_t>(W.kva) |
+       reinterpret_cast<uintptr_t>(W.kvb) | reinterpret_cast<uintptr_t>(W.o)) & 15) {
+    set_err("prefill: activations and weights must be 16-byte aligned");
+    return -1;
+  }
+  CK(cudaMemsetAsync(err, 0, 4, st));
+  CK(launch_rope_table(cs, S, 64, cfg.rope_theta, st));
+
+  GemmParams g;
+  memset(&g, 0, sizeof g);
+  g.err = err;
+  // q = x Wq^T, RoPE on each head's last 64 columns, bf16 [S][16][192]
+  if (!bf16_map(&g.tm_a, xb, H, s, H * 2, 128) || !bf16_map(&g.tm_b, W.q, H, 16 * 192, H * 2, 192)) {
+    set_err("prefill: tensor map (q_proj)");
+    return -1;
+  }
+  g.M = S;
+  g.N = 16 * 192;
+  g.K = static_cast<int>(H);
+  g.c = q;
+  g.ldc = 16 * 192;
+  g.rope_cs = cs;
+  CK(launch_gemm(g, 192, EPI_QROPE, sms, st));
+  // kva = x Wkva^T, fp32 [S][576]
+  if (!bf16_map(&g.tm_b, W.kva, H, 576, H * 2, 192)) {
+    set_err("prefill: tensor map (kv_a_proj)");
+    return -1;
+  }
+  g.N = 576;
+  g.c = kva;
+  g.ldc = 576;
+  CK(launch_gemm(g, 192, EPI_F32, sms, st));
+  // latent = rmsnorm(kva[:512]) * kv_a_norm, k_rope = rope(kva[512:]) -> pool [S][576] bf16
+  CK(append_bf16(pool, 0, kva, W.kvan, S, 512, 64, 0, cfg.rms_eps, cfg.rope_theta, nullptr, st));
+  // kv = latent Wkvb^T, bf16 [S][16][256]
+  if (!bf16_map(&g.tm_a, pool, 512, s, 576 * 2, 128) || !bf16_map(&g.tm_b, W.kvb, 512, 4096, 512 * 2, 256)) {
+    set_err("prefill: tensor map (kv_b_proj)");
+    return -1;
+  }
+  g.N = 4096;
+  g.K = 512;
+  g.c = kv;
+  g.ldc = 4096;
+  CK(launch_gemm(g, 256, EPI_BF16, sms, st));
+  // causal attention -> o bf16 [S][16][128]
+  FlashParams f;
+  memset(&f, 0, sizeof f);
+  {
+    const uint64_t qd[3] = {192, 16, s}, qs[2] = {192 * 2, 16 * 192 * 2};
+    const uint64_t kd[3] = {256, 16, s}, ks[2] = {256 * 2, 16 * 256 * 2};
+    const uint32_t box[3] = {64, 1, 128};
+    if (!make_tmap_3d(&f.tm_q, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, qd, qs, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_3d(&f.tm_kv, kv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kd, ks, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !bf16_map(&f.tm_kr, pool, 576, s, 576 * 2, 128)) {
+      set_err("prefill: tensor map (attention)");
+      return -1;
+    }
+  }
+  f.kr_col = 512;
+  f.S = S;
+  f.scale_log2 = (1.0f / sqrtf(192.0f)) * 1.4426950408889634f;
+  f.out = reinterpret_cast<__nv_bfloat16 *>(o);
+  f.err = err;
+  CK(launch_flash_prefill(f, sms, st));
+  // out = o Wo^T, fp32 [S][H]
+  if (!bf16_map(&g.tm_a, o, 2048, s, 2048 * 2, 128) || !bf16_map(&g.tm_b, W.o, 2048, H, 2048 * 2, 256)) {
+    set_err("prefill: tensor map (o_proj)");
+    return -1;
+  }
+  g.N = static_cast<int>(H);
+  g.K = 2048;
+  g.c = d_out;
+  g.ldc = static_cast<int>(H);
+  g.rope_cs = nullptr;
+  CK(launch_gemm(g, 256, EPI_F32, sms, st));
+  return 0;
+}
+
 }  // namespace
 }  // namespace kvl
 
@@ -829,9 +946,24 @@ KVL_EXPORT int kvl_mla_prefill_bf16(float *out, const float *x, int seq_len, con
   uint8_t *ws = c->kvtmp.as<uint8_t>();
   float *xf = reinterpret_cast<float *>(ws + L.off[0]);
   CK(cudaMemcpyAsync(xf, x, s * H * 4, cudaMemcpyHostToDevice, c->stream));
-  if (prefill_core(dev, c->sms, *cfg, W, c->y.as<float>(), xf, seq_len, ws, L, c->stream) != 0) return -1;
+  int rc;
+  if (fast_prefill_shape(*cfg)) {
+    uint16_t *xb = reinterpret_cast<uint16_t *>(ws + L.off[1]);
+    CK(f32_to_bf16(xb, xf, static_cast<long long>(s * H), c->stream));
+    rc = prefill_fast(c->sms, *cfg, W, c->y.as<float>(), xb, seq_len, ws, L, c->stream);
+  } else {
+    rc = prefill_absorbed(dev, c->sms, *cfg, W, c->y.as<float>(), xf, seq_len, ws, L, c->stream);
+  }
+  if (rc != 0) return -1;
   CK(cudaMemcpyAsync(out, c->y.p, s * H * 4, cudaMemcpyDeviceToHost, c->stream));
+  uint32_t err = 0;
+  if (fast_prefill_shape(*cfg))
+    CK(cudaMemcpyAsync(&err, ws + L.off[8], 4, cudaMemcpyDeviceToHost, c->stream));
   CK(cudaStreamSynchronize(c->stream));
+  if (err != 0) {
+    set_err("prefill kernel reported device error 0x%x", err);
+    return -1;
+  }
   return 0;
 }
 
@@ -859,10 +991,11 @@ KVL_EXPORT int kvl_mla_prefill_dev(const KvlMlaConfig *cfg, const KvlMlaDeviceWe
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t *ws = static_cast<uint8_t *>(d_workspace);
+  DevW W{w->q_proj, w->kv_a_proj, w->kv_a_norm, w->kv_b_proj, w->o_proj};
+  if (fast_prefill_shape(*cfg)) return prefill_fast(sms, *cfg, W, d_out, d_x, seq_len, ws, L, st);
   float *xf = reinterpret_cast<float *>(ws + L.off[0]);
   CK(bf16_to_f32(xf, d_x, static_cast<long long>(seq_len) * cfg->hidden_size, st));
-  DevW W{w->q_proj, w->kv_a_proj, w->kv_a_norm, w->kv_b_proj, w->o_proj};
-  return prefill_core(dev, sms, *cfg, W, d_out, xf, seq_len, ws, L, st);
+  return prefill_absorbed(dev, sms, *cfg, W, d_out, xf, seq_len, ws, L, st);
 }
 
 // =================================================================== attend plans
