@@ -273,6 +273,9 @@ class Prefill:
     metric = "MLA prefill TFLOP/s (config 2: S=4096, H=2048, 16 heads, causal)"
     unit = "TFLOP/s"
     bound = "tensor"
+    # dram__bytes_read.sum + dram__bytes_write.sum per launch, one ncu capture
+    # (profiles/flash_prefill_config2.txt, profiles/gemm_prefill_config2.txt)
+    ncu_traffic = {"flash_prefill": 59.574528e6 + 3.482624e6, "gemm_qrope": 30.442752e6 + 0.157952e6}
 
     def __init__(self, torch, K, lib, dist, S=4096, theta=50000.0):
         self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
@@ -356,6 +359,8 @@ class DecodeQ8:
     metric = "MLA Q8 decode KV GB/s (config 3: 64 seqs, L~U[512,8192])"
     unit = "GB/s"
     bound = "hbm"
+    # one ncu capture of the attend kernel (profiles/mla_attend_q8_config3.txt)
+    ncu_traffic = {"mla_attend_q8": 193.199872e6 + 5.985024e6}
 
     def __init__(self, torch, K, lib, dist):
         import kvl_b200.synth as SY
@@ -400,6 +405,8 @@ class DecodeLong:
     metric = "MLA long-context decode KV GB/s (config 5: L=131072)"
     unit = "GB/s"
     bound = "hbm"
+    # one ncu capture of the attend kernel at world size 1 (profiles/mla_attend_bf16_config5.txt)
+    ncu_traffic = {"mla_attend_bf16": 151.11936e6 + 4.021504e6}
 
     def __init__(self, torch, K, lib, dist, L=131072):
         self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
@@ -486,9 +493,12 @@ def roofline_for(wl, prof, peaks, peak_kind):
         achieved = algo_step / launches_per_step / (per_launch_ms * 1e-3) / 1e12
         peak = peaks["bf16_tflops"]
         unit = "TFLOP/s"
+    traffic = getattr(wl, "ncu_traffic", {}).get(name) if getattr(wl, "dist", None) is None or \
+        wl.dist.world == 1 else None
     return {"kernel": name, "bound": wl.bound, "achieved": achieved, "peak": peak, "unit": unit,
             "frac": achieved / peak, "peak_source": peak_kind, "ms_per_launch": per_launch_ms,
-            "launches_measured": cnt, "traffic": None}, name
+            "launches_measured": cnt, "traffic": traffic,
+            "traffic_unit": "bytes per launch (ncu dram read+write)" if traffic is not None else None}, name
 
 
 # ----------------------------------------------------------------------------- main
