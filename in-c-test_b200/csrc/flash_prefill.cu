@@ -228,6 +228,11 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16(1, 1, 0, 0, kT, kT);   // A = Q, B = K (both K-major)
       constexpr uint32_t idesc_pv = idesc_f16(1, 1, 0, 1, kT, 128);  // A = P (tensor memory), B = V (MN-major)
+      // K-major SW128 descriptor of ring slot 0; slot s, box offsets and the
+      // 16-element K steps are added to its address field (smem < 256 KB, so
+      // the 14-bit field never carries into the next one)
+      const uint64_t ring_desc = smem_desc(s_base + OFF_RING, 16, 1024, LAYOUT_SW128);
+      const uint64_t ring_desc_v = ring_desc & ~(0x3FFFull << 16);  // LBO field set per value tile
       uint32_t seq = 0;                 // ring boxes consumed
       uint32_t pc[2] = {0, 0};          // P tiles consumed per query tile
       bool ok = true;
@@ -266,25 +271,26 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
               return false;
             if (!wait_v()) return false;
             tc_fence_after();
-            const uint32_t sa = slot_of(vseq), sb = slot_of(vseq + 1);
-            const uint32_t lo = sa < sb ? sa : sb, hi = sa < sb ? sb : sa;
-            const uint32_t vaddr = s_base + OFF_RING + lo * kBox;
+            // V: the low half sits in the lower of the two slots (see the producer)
+            const uint32_t sa = slot_of(vseq);
+            const uint64_t vd = ring_desc_v + (sa == kSlots - 1 ? 0u : sa * (kBox >> 4)) +
+                                (static_cast<uint64_t>(sa == kSlots - 1 ? (kSlots - 1) * (kBox >> 4) : (kBox >> 4)) << 16);
+            const uint32_t a_tm = tmem + 128 * t;
+            const uint32_t d_tm = tmem + 256 + 128 * t;
+            mma_f16_ts(d_tm, a_tm, vd, idesc_pv, j == 1 ? 0u : 1u);
 #pragma unroll
-            for (int kk = 0; kk < kT / 16; ++kk)
-              mma_f16_ts(tmem + 256 + 128 * t, tmem + 128 * t + 8 * kk,
-                         smem_desc(vaddr + kk * 2048, (hi - lo) * kBox, 1024, LAYOUT_SW128), idesc_pv,
-                         (j == 1 && kk == 0) ? 0u : 1u);
+            for (int kk = 1; kk < kT / 16; ++kk) mma_f16_ts(d_tm, a_tm + 8 * kk, vd + 128 * kk, idesc_pv, 1u);
             return true;
           };
           auto issue_qk = [&](int t) {
-            const uint32_t qaddr = s_base + OFF_Q + 3 * t * kBox;
+            const uint64_t qd = ring_desc - (static_cast<uint64_t>(OFF_RING - OFF_Q - 3 * t * kBox) >> 4);
+            const uint32_t d_tm = tmem + 128 * t;
 #pragma unroll
             for (int b = 0; b < 3; ++b) {
-              const uint32_t kaddr = s_base + OFF_RING + slot_of(kseq + b) * kBox;
+              const uint64_t kd = ring_desc + slot_of(kseq + b) * (kBox >> 4);
 #pragma unroll
               for (int kk = 0; kk < 4; ++kk)
-                mma_f16_ss(tmem + 128 * t, smem_desc(qaddr + b * kBox + kk * 32, 16, 1024, LAYOUT_SW128),
-                           smem_desc(kaddr + kk * 32, 16, 1024, LAYOUT_SW128), idesc_qk, (b | kk) ? 1u : 0u);
+                mma_f16_ss(d_tm, qd + b * (kBox >> 4) + 2 * kk, kd + 2 * kk, idesc_qk, (b | kk) ? 1u : 0u);
             }
             mma_commit(&B->s_full[t]);
           };

@@ -8,10 +8,10 @@
 // MMAs of the next.  Epilogues:
 //   EPI_F32    C fp32 row-major (ldc elements)
 //   EPI_BF16   C bf16 row-major
-//   EPI_QROPE  BN = 192 = one head of q_proj (128 nope + 64 rope columns): the
-//              rope half is rotated as src/mla_prefill_streaming.c:15-29 does
+//   EPI_QROPE  q_proj: heads of 192 columns (128 nope + 64 rope); each rope
+//              group is rotated as src/mla_prefill_streaming.c:15-29 does
 //              (pairs (2i, 2i+1) -> i, 32 + i) with cos/sin from a table of
-//              float2 [rows][32] (position = row), and the head is stored bf16.
+//              float2 [rows][32] (position = row); stored bf16.
 //
 // Roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
 // warps 2-5 epilogue (TMEM subpartition = warp % 4).
@@ -50,6 +50,90 @@ struct Bars {
 }  // namespace gemmk
 
 using namespace gemmk;
+
+// One accumulator tile row per thread: TMEM lanes of this warp's quarter,
+// BN fp32 columns -> the epilogue's output row `row`, columns nb * BN + ...
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbase, int row, bool row_ok, int nb) {
+  if constexpr (EPI == EPI_QROPE) {
+    // 64-column groups: a head is 192 columns (128 nope, then 64 rope), and
+    // the tile edges (multiples of BN = 192 or 256) never split a rope group
+    __nv_bfloat16 *dst_row = static_cast<__nv_bfloat16 *>(p.c) + static_cast<size_t>(row) * p.ldc;
+#pragma unroll 1
+    for (int g = 0; g < BN / 64; ++g) {
+      const int col0 = nb * BN + 64 * g;
+      if (col0 >= p.N) break;
+      float r[64];
+      tmem_ld32(tbase + 64 * g, r);
+      tmem_ld32(tbase + 64 * g + 32, r + 32);
+      tmem_wait_ld();
+      if (!row_ok) continue;
+      __nv_bfloat16 *dst = dst_row + col0;
+      if (col0 % 192 == 128) {
+        const float2 *cs = p.rope_cs + static_cast<size_t>(row) * 32;
+        float outv[64];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float2 t = cs[i];
+          const float a = r[2 * i], b = r[2 * i + 1];
+          outv[i] = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y));
+          outv[32 + i] = __fadd_rn(__fmul_rn(b, t.x), __fmul_rn(a, t.y));
+        }
+#pragma unroll
+        for (int k = 0; k < 64; ++k) r[k] = outv[k];
+      }
+#pragma unroll
+      for (int k = 0; k < 64; k += 8) {
+        uint4 o;
+        o.x = pack_bf16(r[k], r[k + 1]);
+        o.y = pack_bf16(r[k + 2], r[k + 3]);
+        o.z = pack_bf16(r[k + 4], r[k + 5]);
+        o.w = pack_bf16(r[k + 6], r[k + 7]);
+        *reinterpret_cast<uint4 *>(dst + k) = o;
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < BN / 32; ++c) {
+      float v[32];
+      tmem_ld32(tbase + 32 * c, v);
+      tmem_wait_ld();
+      const int col0 = nb * BN + 32 * c;
+      if (row_ok && col0 < p.N) {
+        const bool full = col0 + 32 <= p.N;
+        if constexpr (EPI == EPI_F32) {
+          float *dst = static_cast<float *>(p.c) + static_cast<size_t>(row) * p.ldc + col0;
+          if (full) {
+#pragma unroll
+            for (int k = 0; k < 32; k += 4)
+              *reinterpret_cast<float4 *>(dst + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
+          } else {
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
+              if (col0 + k < p.N) dst[k] = v[k];
+          }
+        } else {
+          __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(p.c) + static_cast<size_t>(row) * p.ldc + col0;
+          if (full) {
+#pragma unroll
+            for (int k = 0; k < 32; k += 8) {
+              uint4 o;
+              o.x = pack_bf16(v[k], v[k + 1]);
+              o.y = pack_bf16(v[k + 2], v[k + 3]);
+              o.z = pack_bf16(v[k + 4], v[k + 5]);
+              o.w = pack_bf16(v[k + 6], v[k + 7]);
+              *reinterpret_cast<uint4 *>(dst + k) = o;
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < 32; ++k)
+              if (col0 + k < p.N) dst[k] = __float2bfloat16_rn(v[k]);
+          }
+        }
+      }
+    }
+  }
+}
 
 template <int BN, int EPI>
 __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_constant__ GemmParams p) {
@@ -155,91 +239,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
       const int row = mb * kBM + 32 * sub + lane;
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem + ab * 256 + lane_base;
-      if constexpr (EPI == EPI_QROPE) {
-        // one head: 128 nope columns then 64 interleaved rope columns
-        __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(p.c) + static_cast<size_t>(row) * p.ldc + nb * BN;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float v[32];
-          tmem_ld32(tbase + 32 * c, v);
-          tmem_wait_ld();
-          if (row_ok) {
-#pragma unroll
-            for (int k = 0; k < 32; k += 8) {
-              uint4 o;
-              o.x = pack_bf16(v[k], v[k + 1]);
-              o.y = pack_bf16(v[k + 2], v[k + 3]);
-              o.z = pack_bf16(v[k + 4], v[k + 5]);
-              o.w = pack_bf16(v[k + 6], v[k + 7]);
-              *reinterpret_cast<uint4 *>(dst + 32 * c + k) = o;
-            }
-          }
-        }
-        float r[64];
-        tmem_ld32(tbase + 128, r);
-        tmem_ld32(tbase + 160, r + 32);
-        tmem_wait_ld();
-        if (row_ok) {
-          const float2 *cs = p.rope_cs + static_cast<size_t>(row) * 32;
-          float outv[64];
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float2 t = cs[i];
-            const float a = r[2 * i], b = r[2 * i + 1];
-            outv[i] = __fsub_rn(__fmul_rn(a, t.x), __fmul_rn(b, t.y));
-            outv[32 + i] = __fadd_rn(__fmul_rn(b, t.x), __fmul_rn(a, t.y));
-          }
-#pragma unroll
-          for (int k = 0; k < 64; k += 8) {
-            uint4 o;
-            o.x = pack_bf16(outv[k], outv[k + 1]);
-            o.y = pack_bf16(outv[k + 2], outv[k + 3]);
-            o.z = pack_bf16(outv[k + 4], outv[k + 5]);
-            o.w = pack_bf16(outv[k + 6], outv[k + 7]);
-            *reinterpret_cast<uint4 *>(dst + 128 + k) = o;
-          }
-        }
-      } else {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          float v[32];
-          tmem_ld32(tbase + 32 * c, v);
-          tmem_wait_ld();
-          const int col0 = nb * BN + 32 * c;
-          if (row_ok && col0 < p.N) {
-            const bool full = col0 + 32 <= p.N;
-            if constexpr (EPI == EPI_F32) {
-              float *dst = static_cast<float *>(p.c) + static_cast<size_t>(row) * p.ldc + col0;
-              if (full) {
-#pragma unroll
-                for (int k = 0; k < 32; k += 4)
-                  *reinterpret_cast<float4 *>(dst + k) = make_float4(v[k], v[k + 1], v[k + 2], v[k + 3]);
-              } else {
-#pragma unroll
-                for (int k = 0; k < 32; ++k)
-                  if (col0 + k < p.N) dst[k] = v[k];
-              }
-            } else {
-              __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(p.c) + static_cast<size_t>(row) * p.ldc + col0;
-              if (full) {
-#pragma unroll
-                for (int k = 0; k < 32; k += 8) {
-                  uint4 o;
-                  o.x = pack_bf16(v[k], v[k + 1]);
-                  o.y = pack_bf16(v[k + 2], v[k + 3]);
-                  o.z = pack_bf16(v[k + 4], v[k + 5]);
-                  o.w = pack_bf16(v[k + 6], v[k + 7]);
-                  *reinterpret_cast<uint4 *>(dst + k) = o;
-                }
-              } else {
-#pragma unroll
-                for (int k = 0; k < 32; ++k)
-                  if (col0 + k < p.N) dst[k] = __float2bfloat16_rn(v[k]);
-              }
-            }
-          }
-        }
-      }
+      epilogue_tile<BN, EPI>(p, tbase, row, row_ok, nb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&B->acc_empty[ab]);
@@ -251,6 +251,159 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, Layout<BN>::kTmemCols);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// CTA-pair form: a cluster of two CTAs computes a 256 x BN tile with one
+// M = 256 tcgen05.mma per K step (cta_group::2, issued by rank 0).  Each CTA
+// loads its own 128 rows of A and its own BN / 2 rows of B, so a pair moves
+// (256 + BN) x 64 elements per K step instead of 2 x (128 + BN) for two
+// independent CTAs: half the B traffic per SM.
+//   full[s]      (leader)  one arrival with expect_tx of both CTAs' bytes;
+//                          both CTAs' copies complete on it
+//   empty[s]     (each)    leader's commit, multicast to both CTAs
+//   acc_full[b]  (each)    leader's commit, multicast to both CTAs
+//   acc_empty[b] (leader)  one arrival per epilogue warp of both CTAs
+namespace gemmk {
+constexpr int kPairStages = 6;
+template <int BN>
+struct PairLayout {
+  static constexpr uint32_t kBBytes = (BN / 2) * kBK * 2;
+  static constexpr uint32_t kStageBytes = kABytes + kBBytes;
+  static constexpr uint32_t OFF_BAR = kPairStages * kStageBytes;
+  static constexpr uint32_t kSmem = OFF_BAR + 256 + 1024;
+};
+struct PairBars {
+  uint64_t full[kPairStages], empty[kPairStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+}  // namespace gemmk
+
+template <int BN, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    gemm_pair_bf16_tn_kernel(const __grid_constant__ GemmParams p) {
+  using L = PairLayout<BN>;
+  static_assert(sizeof(PairBars) <= 256, "barrier block");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  PairBars *B = reinterpret_cast<PairBars *>(smem + L::OFF_BAR);
+  const uint32_t s_base = smem_u32(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  volatile int *abort = &B->abort;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+  const int tiles_m = (p.M + 2 * kBM - 1) / (2 * kBM);
+  const int tiles_n = (p.N + BN - 1) / BN;
+  const int tiles = tiles_m * tiles_n;
+  const int ksteps = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPairStages; ++i) {
+      mbar_init(&B->full[i], 1);
+      mbar_init(&B->empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B->acc_full[i], 1);
+      mbar_init(&B->acc_empty[i], 8);
+    }
+    mbar_init(&B->drain, 1);
+    B->abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&B->tmem_base, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
+  tc_fence_after();
+  const uint32_t tmem = B->tmem_base;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&p.tm_a);
+      tma_prefetch_desc(&p.tm_b);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs) {
+        const int mb = tile % tiles_m, nb = tile / tiles_m;
+        for (int ks = 0; ks < ksteps && ok; ++ks, ++it) {
+          const uint32_t s = it % kPairStages;
+          ok = mbar_wait(&B->empty[s], ((it / kPairStages) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+          if (!ok) break;
+          if (leader) mbar_arrive_expect_tx(&B->full[s], 2 * L::kStageBytes);
+          const uint32_t full_l = mapa_shared(smem_u32(&B->full[s]), 0);
+          uint8_t *st = smem + s * L::kStageBytes;
+          tma_load_2d_pair(st, &p.tm_a, full_l, ks * kBK, (2 * mb + static_cast<int>(rank)) * kBM);
+          tma_load_2d_pair(st + kABytes, &p.tm_b, full_l, ks * kBK, nb * BN + static_cast<int>(rank) * (BN / 2));
+        }
+      }
+      if (!ok && leader) {
+        for (uint32_t s = 0; s < kPairStages && s < it; ++s) {
+          const uint32_t last = s + kPairStages * ((it - 1 - s) / kPairStages);
+          drain_wait(&B->full[s], (last / kPairStages) & 1, p.err);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_f16(1, 1, 0, 0, 2 * kBM, BN);
+      const uint64_t desc0 = smem_desc(s_base, 16, 1024, LAYOUT_SW128);
+      uint32_t it = 0, lt = 0;
+      bool ok = true;
+      for (int tile = pair; tile < tiles && ok; tile += npairs, ++lt) {
+        const uint32_t ab = lt & 1;
+        ok = mbar_wait(&B->acc_empty[ab], ((lt >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+        if (!ok) break;
+        tc_fence_after();
+        for (int ks = 0; ks < ksteps && ok; ++ks, ++it) {
+          const uint32_t s = it % kPairStages;
+          ok = mbar_wait(&B->full[s], (it / kPairStages) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t a = desc0 + ((s * L::kStageBytes) >> 4);
+          const uint64_t b = a + (kABytes >> 4);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            mma_f16_ss_pair(tmem + ab * 256, a + 2 * kk, b + 2 * kk, idesc, (ks | kk) ? 1u : 0u);
+          mma_commit_pair(&B->empty[s], 0x3);
+        }
+        if (ok) mma_commit_pair(&B->acc_full[ab], 0x3);
+      }
+      mma_commit_pair(&B->drain, 0x1);
+      drain_wait(&B->drain, 0, p.err);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (both CTAs)
+    const int sub = warp & 3;
+    const uint32_t lane_base = static_cast<uint32_t>(32 * sub) << 16;
+    uint32_t lt = 0;
+    for (int tile = pair; tile < tiles; tile += npairs, ++lt) {
+      const int mb = tile % tiles_m, nb = tile / tiles_m;
+      const uint32_t ab = lt & 1;
+      bool bad = !mbar_wait(&B->acc_full[ab], (lt >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
+      if (__any_sync(0xffffffffu, bad)) break;
+      tc_fence_after();
+      const int row = (2 * mb + static_cast<int>(rank)) * kBM + 32 * sub + lane;
+      epilogue_tile<BN, EPI>(p, tmem + ab * 256 + lane_base, row, row < p.M, nb);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&B->acc_empty[ab]), 0));
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // the leader's MMAs into both CTAs' tensor memory have completed
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 512);
   }
 }
 
@@ -268,7 +421,12 @@ static cudaError_t launch_gemm_t(const GemmParams &p, int sms, cudaStream_t stre
 }
 
 cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream) {
-  if (epi == EPI_QROPE) return bn == 192 ? launch_gemm_t<192, EPI_QROPE>(p, sms, stream, "gemm_qrope") : cudaErrorInvalidValue;
+  if (epi == EPI_QROPE) {
+    if (p.N % 192 != 0) return cudaErrorInvalidValue;
+    if (bn == 256) return launch_gemm_t<256, EPI_QROPE>(p, sms, stream, "gemm_qrope");
+    if (bn == 192) return launch_gemm_t<192, EPI_QROPE>(p, sms, stream, "gemm_qrope");
+    return cudaErrorInvalidValue;
+  }
   if (bn == 256) {
     if (epi == EPI_F32) return launch_gemm_t<256, EPI_F32>(p, sms, stream, "gemm_bf16");
     if (epi == EPI_BF16) return launch_gemm_t<256, EPI_BF16>(p, sms, stream, "gemm_bf16");
@@ -279,21 +437,54 @@ cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStrea
   return cudaErrorInvalidValue;
 }
 
+template <int BN, int EPI>
+static cudaError_t launch_gemm_pair_t(const GemmParams &p, int sms, cudaStream_t stream, const char *name) {
+  using L = PairLayout<BN>;
+  static_assert(L::kSmem <= 232448, "shared memory budget");
+  cudaError_t e = cudaFuncSetAttribute(gemm_pair_bf16_tn_kernel<BN, EPI>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, L::kSmem);
+  if (e != cudaSuccess) return e;
+  const int tiles = ((p.M + 2 * kBM - 1) / (2 * kBM)) * ((p.N + BN - 1) / BN);
+  int pairs = sms / 2;
+  if (pairs > tiles) pairs = tiles;
+  if (pairs < 1) pairs = 1;
+  ProfScope ps(name, stream);
+  gemm_pair_bf16_tn_kernel<BN, EPI><<<2 * pairs, 192, L::kSmem, stream>>>(p);
+  return cudaGetLastError();
+}
+
+// B's tensor map box must be {64, bn / 2} rows for the pair form.
+cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream) {
+  if (bn != 256) return cudaErrorInvalidValue;
+  if (epi == EPI_QROPE) {
+    if (p.N % 192 != 0) return cudaErrorInvalidValue;
+    return launch_gemm_pair_t<256, EPI_QROPE>(p, sms, stream, "gemm_qrope");
+  }
+  if (epi == EPI_F32) return launch_gemm_pair_t<256, EPI_F32>(p, sms, stream, "gemm_bf16");
+  if (epi == EPI_BF16) return launch_gemm_pair_t<256, EPI_BF16>(p, sms, stream, "gemm_bf16");
+  return cudaErrorInvalidValue;
+}
+
 // cos/sin of pos * theta^(-2i/dim) for i < dim/2 and pos < rows: the angle
 // arithmetic of src/mla_compressed_state.c:8-22 (double angle, float result).
 __global__ void rope_table_kernel(float2 *cs, int rows, int dim, float theta) {
+  __shared__ double inv_freq_s[128];
   const int half = dim / 2;
+  // theta^(-2k/dim) once per frequency (half <= 128 is checked by the launcher)
+  for (int k = threadIdx.x; k < half; k += blockDim.x)
+    inv_freq_s[k] = pow(static_cast<double>(theta), -(static_cast<double>(2 * k) / static_cast<double>(dim)));
+  __syncthreads();
   const long long n = static_cast<long long>(rows) * half;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const int pos = static_cast<int>(i / half), k = static_cast<int>(i % half);
-    const double inv_freq = pow(static_cast<double>(theta), -(static_cast<double>(2 * k) / static_cast<double>(dim)));
-    const double ang = static_cast<double>(pos) * inv_freq;
+    const double ang = static_cast<double>(pos) * inv_freq_s[k];
     cs[i] = make_float2(static_cast<float>(cos(ang)), static_cast<float>(sin(ang)));
   }
 }
 
 cudaError_t launch_rope_table(float2 *cs, int rows, int dim, float theta, cudaStream_t stream) {
+  if (dim <= 0 || dim > 256 || (dim & 1)) return cudaErrorInvalidValue;
   const long long n = static_cast<long long>(rows) * (dim / 2);
   const int grid = static_cast<int>((n + 255) / 256 < 148 * 8 ? (n + 255) / 256 : 148 * 8);
   ProfScope ps("rope_table", stream);

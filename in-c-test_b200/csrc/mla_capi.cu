@@ -830,6 +830,35 @@ bool bf16_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t rows, u
                       CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// Second stream of the prefill fork (per device): q_proj does not depend on
+// the kv_a -> RMSNorm/RoPE -> kv_b chain, so the two run concurrently and
+// each fills the SMs the other's last wave leaves idle.  `mu` keeps one
+// fork/join's event records and waits together when threads share a device.
+struct PrefillFork {
+  cudaStream_t s2 = nullptr;
+  cudaEvent_t fork = nullptr, rope = nullptr, qdone = nullptr;
+  std::mutex mu;
+};
+std::mutex g_fork_mu;
+std::unordered_map<int, PrefillFork *> g_fork;
+
+PrefillFork *get_fork(int device) {
+  std::lock_guard<std::mutex> lk(g_fork_mu);
+  auto it = g_fork.find(device);
+  if (it != g_fork.end()) return it->second;
+  PrefillFork *f = new PrefillFork();
+  if (cudaStreamCreateWithFlags(&f->s2, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&f->fork, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&f->rope, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&f->qdone, cudaEventDisableTiming) != cudaSuccess) {
+    set_err("prefill: cannot create the second stream of device %d", device);
+    delete f;
+    return nullptr;
+  }
+  g_fork[device] = f;
+  return f;
+}
+
 // tcgen05 path; xb: bf16 tokens on the device.  Returns -1 with a message.
 int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, const uint16_t *xb, int S,
                  uint8_t *ws, const PrefillWs &L, cudaStream_t st) {
@@ -842,39 +871,57 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   float2 *cs = reinterpret_cast<float2 *>(ws + L.off[7]);
   uint32_t *err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
   if ((reinterpret_cast<uintptr_t>(xb) | reinterpret_cast<uintptr_t>(W.q) | reinterpret_cast<uintptr_t>(W.kva) |
-       reinterpret_cast<uintptr_t>(W.kvb) | reinterpret_cast<uintptr_t>(W.o)) & 15) {
+       reinterpret_cast<uintptr_t>(W.kvb) | reinterpret_cast<uintptr_t>(W.o) | reinterpret_cast<uintptr_t>(W.kvan)) &
+      15) {
     set_err("prefill: activations and weights must be 16-byte aligned");
     return -1;
   }
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  PrefillFork *fk = get_fork(dev);
+  if (!fk) return -1;
+  std::lock_guard<std::mutex> lk(fk->mu);
   CK(cudaMemsetAsync(err, 0, 4, st));
-  CK(launch_rope_table(cs, S, 64, cfg.rope_theta, st));
+  CK(cudaEventRecord(fk->fork, st));
+  CK(cudaStreamWaitEvent(fk->s2, fk->fork, 0));
 
-  GemmParams g;
-  memset(&g, 0, sizeof g);
-  g.err = err;
-  // q = x Wq^T, RoPE on each head's last 64 columns, bf16 [S][16][192]
-  if (!bf16_map(&g.tm_a, xb, H, s, H * 2, 128) || !bf16_map(&g.tm_b, W.q, H, 16 * 192, H * 2, 192)) {
+  // second stream: RoPE table, then q = x Wq^T with RoPE on each head's last
+  // 64 columns, bf16 [S][16][192]
+  GemmParams gq;
+  memset(&gq, 0, sizeof gq);
+  gq.err = err;
+  if (!bf16_map(&gq.tm_a, xb, H, s, H * 2, 128) || !bf16_map(&gq.tm_b, W.q, H, 16 * 192, H * 2, 256)) {
     set_err("prefill: tensor map (q_proj)");
     return -1;
   }
-  g.M = S;
-  g.N = 16 * 192;
-  g.K = static_cast<int>(H);
-  g.c = q;
-  g.ldc = 16 * 192;
-  g.rope_cs = cs;
-  CK(launch_gemm(g, 192, EPI_QROPE, sms, st));
-  // kva = x Wkva^T, fp32 [S][576]
-  if (!bf16_map(&g.tm_b, W.kva, H, 576, H * 2, 192)) {
+  gq.M = S;
+  gq.N = 16 * 192;
+  gq.K = static_cast<int>(H);
+  gq.c = q;
+  gq.ldc = 16 * 192;
+  gq.rope_cs = cs;
+  CK(launch_rope_table(cs, S, 64, cfg.rope_theta, fk->s2));
+  CK(cudaEventRecord(fk->rope, fk->s2));
+  CK(launch_gemm(gq, 256, EPI_QROPE, sms, fk->s2));
+  CK(cudaEventRecord(fk->qdone, fk->s2));
+
+  // caller's stream: kva = x Wkva^T, fp32 [S][576]
+  GemmParams g;
+  memset(&g, 0, sizeof g);
+  g.err = err;
+  if (!bf16_map(&g.tm_a, xb, H, s, H * 2, 128) || !bf16_map(&g.tm_b, W.kva, H, 576, H * 2, 192)) {
     set_err("prefill: tensor map (kv_a_proj)");
     return -1;
   }
+  g.M = S;
+  g.K = static_cast<int>(H);
   g.N = 576;
   g.c = kva;
   g.ldc = 576;
   CK(launch_gemm(g, 192, EPI_F32, sms, st));
   // latent = rmsnorm(kva[:512]) * kv_a_norm, k_rope = rope(kva[512:]) -> pool [S][576] bf16
-  CK(append_bf16(pool, 0, kva, W.kvan, S, 512, 64, 0, cfg.rms_eps, cfg.rope_theta, nullptr, st));
+  CK(cudaStreamWaitEvent(st, fk->rope, 0));
+  CK(append_rows_bf16(pool, kva, W.kvan, cs, S, cfg.rms_eps, st));
   // kv = latent Wkvb^T, bf16 [S][16][256]
   if (!bf16_map(&g.tm_a, pool, 512, s, 576 * 2, 128) || !bf16_map(&g.tm_b, W.kvb, 512, 4096, 512 * 2, 256)) {
     set_err("prefill: tensor map (kv_b_proj)");
@@ -885,6 +932,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   g.c = kv;
   g.ldc = 4096;
   CK(launch_gemm(g, 256, EPI_BF16, sms, st));
+  CK(cudaStreamWaitEvent(st, fk->qdone, 0));  // join the second stream
   // causal attention -> o bf16 [S][16][128]
   FlashParams f;
   memset(&f, 0, sizeof f);
@@ -983,6 +1031,10 @@ KVL_EXPORT int kvl_mla_prefill_dev(const KvlMlaConfig *cfg, const KvlMlaDeviceWe
   const PrefillWs L = prefill_layout(*cfg, seq_len);
   if (workspace_bytes < L.total) {
     set_err("prefill workspace too small (%zu < %zu)", workspace_bytes, L.total);
+    return -1;
+  }
+  if (reinterpret_cast<uintptr_t>(d_workspace) & 255) {
+    set_err("prefill workspace must be 256-byte aligned");
     return -1;
   }
   const int dev = current_device();

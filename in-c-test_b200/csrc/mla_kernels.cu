@@ -175,6 +175,64 @@ __global__ void append_bf16_kernel(uint16_t *kv, long long row0, const float *ka
   }
 }
 
+// Prefill form of append_bf16 for the Kimi shape (R = 512, DR = 64): one warp
+// per token, rows [0, n) of `pool`, RoPE cos/sin from a [n][32] table built by
+// rope_table_kernel with the same double-angle arithmetic as rope_pair.  The
+// same operations as append_bf16 (double sum of squares, float scale, float
+// rotation without contraction); only the order of the double sum differs.
+__global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, const uint16_t *norm_w,
+                                        const float2 *cs, int n, float eps) {
+  constexpr int R = 512, DR = 64;
+  const int warp = static_cast<int>((blockIdx.x * static_cast<unsigned>(blockDim.x) + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (warp >= n) return;
+  const float *kt = ka + static_cast<size_t>(warp) * (R + DR);
+  float4 v[4];
+  double ss = 0.0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    v[k] = reinterpret_cast<const float4 *>(kt)[lane + 32 * k];
+    ss += static_cast<double>(v[k].x) * static_cast<double>(v[k].x);
+    ss += static_cast<double>(v[k].y) * static_cast<double>(v[k].y);
+    ss += static_cast<double>(v[k].z) * static_cast<double>(v[k].z);
+    ss += static_cast<double>(v[k].w) * static_cast<double>(v[k].w);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(static_cast<float>(ss / static_cast<double>(R)), eps)));
+  uint16_t *dst = pool + static_cast<size_t>(warp) * (R + DR);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const int c = 4 * (lane + 32 * k);
+    const uint2 w = *reinterpret_cast<const uint2 *>(norm_w + c);
+    const float y0 = __fmul_rn(__fmul_rn(v[k].x, inv), __uint_as_float(w.x << 16));
+    const float y1 = __fmul_rn(__fmul_rn(v[k].y, inv), __uint_as_float(w.x & 0xffff0000u));
+    const float y2 = __fmul_rn(__fmul_rn(v[k].z, inv), __uint_as_float(w.y << 16));
+    const float y3 = __fmul_rn(__fmul_rn(v[k].w, inv), __uint_as_float(w.y & 0xffff0000u));
+    uint2 o;
+    o.x = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(y0))) |
+          (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(y1))) << 16);
+    o.y = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(y2))) |
+          (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(y3))) << 16);
+    *reinterpret_cast<uint2 *>(dst + c) = o;
+  }
+  // rope pair (2i, 2i+1) -> (i, 32 + i), i = lane
+  const float2 ab = reinterpret_cast<const float2 *>(kt + R)[lane];
+  const float2 t = cs[static_cast<size_t>(warp) * (DR / 2) + lane];
+  const float lo = __fsub_rn(__fmul_rn(ab.x, t.x), __fmul_rn(ab.y, t.y));
+  const float hi = __fadd_rn(__fmul_rn(ab.y, t.x), __fmul_rn(ab.x, t.y));
+  dst[R + lane] = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
+  dst[R + DR / 2 + lane] = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
+}
+
+cudaError_t append_rows_bf16(uint16_t *pool, const float *ka, const uint16_t *norm_w, const float2 *cs, int n,
+                             float eps, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  ProfScope ps("append_bf16", s);
+  append_rows_bf16_kernel<<<(n + 7) / 8, 256, 0, s>>>(pool, ka, norm_w, cs, n, eps);
+  return cudaGetLastError();
+}
+
 // src/mla_compressed_q8_state.c:34-55 for one row held in shared memory.
 __device__ void quantize_row(int8_t *q, float *scale_out, const float *lat, int R, float *fred) {
   float amax = 0.f;

@@ -1,7 +1,8 @@
 // sm100.cuh -- thin inline-PTX layer for the Blackwell (sm_100a) features the
-// MLA kernels use: mbarriers with bounded waits, TMA tile loads (no cluster
-// multicast anywhere), tcgen05 tensor-memory allocation, MMA, commit, loads
-// and stores, and the shared-memory matrix descriptors tcgen05.mma reads.
+// MLA kernels use: mbarriers with bounded waits, TMA tile loads (never with
+// cluster multicast), tcgen05 tensor-memory allocation, MMA (one CTA or a CTA
+// pair), commit, loads and stores, and the shared-memory matrix descriptors
+// tcgen05.mma reads.
 //
 // Every wait is bounded: after KVL_WAIT_LIMIT_NS of spinning the wait records
 // an error code in the kernel's global error word, raises the CTA-wide abort
@@ -308,6 +309,71 @@ __host__ __device__ constexpr uint32_t idesc_f16(uint32_t a_fmt, uint32_t b_fmt,
 __host__ __device__ __forceinline__ uint32_t sw128_offset(uint32_t row, uint32_t col) {
   uint32_t chunk = (col >> 3) ^ (row & 7u);
   return (row >> 3) * 1024u + (row & 7u) * 128u + chunk * 16u + (col & 7u) * 2u;
+}
+
+// ---------------------------------------------------------------- CTA pairs (cta_group::2)
+// A cluster of two CTAs on two SMs runs one M = 256 MMA: rank 0 (the leader)
+// issues it; each CTA supplies its own 128 rows of A and its own half of the
+// N columns of B from its shared memory, at the same offsets, and receives
+// its 128 rows of D in its own tensor memory.  No load here uses multicast.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+// All threads of both CTAs.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Arrive on an mbarrier of another CTA of the cluster (address from mapa_shared).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// 2-D tile load into this CTA's shared memory whose completion is counted on
+// an mbarrier of the pair's leader (cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void *smem_dst, const CUtensorMap *m, uint32_t bar_cluster,
+                                                 int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t *smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// D[tmem] (+)= A . B over the pair (M = 256), issued by the leader only.
+__device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                                uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+// Arrive once on the mbarrier at this offset in every CTA of `cta_mask` when
+// the leader's earlier tcgen05 operations have completed.
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(cta_mask)
+      : "memory");
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {

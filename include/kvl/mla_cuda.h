@@ -147,7 +147,8 @@ size_t kvl_mla_prefill_workspace_bytes(const KvlMlaConfig *cfg, int seq_len);
 
 /* Causal MLA prefill of one sequence entirely on the device (the computation
  * of kvl_mla_prefill_bf16): d_x [seq_len][H] bf16 token activations ->
- * d_out [seq_len][H] fp32.  Asynchronous on `stream`. */
+ * d_out [seq_len][H] fp32.  Asynchronous on `stream`.  d_workspace must be
+ * 256-byte aligned; d_x, d_out and the weights 16-byte aligned. */
 int kvl_mla_prefill_dev(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, float *d_out,
                         const uint16_t *d_x, int seq_len, void *d_workspace, size_t workspace_bytes,
                         void *stream);
