@@ -4,28 +4,30 @@
 //     o_t  = sum_j softmax_j(s_t) v_j
 // per head, with q_rope/k_rope already rotated, k_rope shared by the heads.
 //
-// Work item = (head, block of 256 queries) = two 128-query tiles Q0, Q1 that
-// share every key/value tile the CTA loads.  Items go to persistent CTAs in
-// snake order of decreasing cost.  Per key tile j:
-//     S0 = Q0 K_j^T, S1 = Q1 K_j^T      (12 tcgen05 MMAs each, M = N = 128)
-//     O0 += P0 V_j,  O1 += P1 V_j       (8 MMAs each; P read from tensor memory)
-// Two softmax warpgroups (one per query tile, thread = query row) ping-pong:
-// while group 0 turns S0 into P0 the tensor core runs P1 V and Q1 K^T, and
-// the other way round.  P is written back as bf16 over the first 64 columns
-// of its own S, so tensor memory holds S0 | S1 | O0 | O1 (4 x 128 columns).
-// The running max is rescaled lazily (only when it grows by more than 2^8).
-// The causal mask and the sequence bound are applied on the last key tile of
-// each query tile only; all earlier tiles are entirely visible.
+// Work item = (head, 128-query tile); items go to persistent CTAs in snake
+// order of decreasing cost (query tile i attends key tiles 0..i).  Per key
+// tile j the tensor core computes S_j = Q K_j^T (12 tcgen05 MMAs, M = N = 128)
+// into one of three S buffers in tensor memory and O += P_j V_j (8 MMAs, P
+// read from tensor memory).  With three S buffers the scores of tiles j + 1
+// and j + 2 are ready while the softmax of tile j runs, so the softmax and
+// the MMAs overlap fully: S_{j+3} is issued right after P_j V_j, which has
+// consumed the P_j stored over the first 64 columns of that buffer.
 //
-// Shared memory: Q0, Q1 (3 SW128 boxes of 128 rows x 64 each), and a ring of
-// 8 boxes through which the key tiles (k_nope lo | k_nope hi | k_rope) and
-// value tiles (v lo | v hi) stream in consumption order.  The two value
-// boxes of one tile sit in consecutive ring slots; when the pair wraps past
-// the end of the ring the low half goes to the lower slot, so one MN-major
-// descriptor (LBO = the distance between the halves) always covers V.
-// Roles (384 threads): warps 0-3 softmax of Q0, warps 4-7 softmax of Q1
-// (TMEM lanes 32 * (warp % 4)), warp 8 TMA producer, warp 9 TMEM owner and
-// MMA issuer, warps 10-11 idle.  Every wait is bounded and reports through p.err.
+// Softmax: two warpgroups share each 128 x 128 score tile, one per half of
+// the keys (thread = query row), and exchange their row maxima through shared
+// memory once per tile.  The running max is rescaled lazily (only when it
+// grows by more than 2^8 in the exp2 domain); each group rescales its half of
+// the O row and keeps its own partial row sum, the two sums being added in
+// the epilogue.  The causal mask and the sequence bound are applied on the
+// last key tile of a query tile only; all earlier tiles are entirely visible.
+//
+// Tensor memory: S0 | S1 | S2 | O (4 x 128 columns).  Shared memory: Q (3 SW128
+// boxes of 128 rows x 64), K ring 2 x (k_nope lo, k_nope hi, k_rope), V ring
+// 2 x (v lo, v hi), the max / sum exchange and the barriers.
+// Roles (384 threads): warps 0-3 softmax of keys 0-63, warps 4-7 keys 64-127
+// (TMEM lanes 32 * (warp % 4)), warp 8 Q and K copies, warp 9 TMEM owner and
+// MMA issuer, warp 10 V copies, warp 11 idle.  Every wait is bounded and
+// reports through p.err.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -36,47 +38,40 @@
 namespace kvl {
 namespace fpre {
 
-constexpr int kT = 128;                   // queries / keys per tile
-constexpr uint32_t kBox = kT * 128;       // 128 rows x 64 bf16 = 16 KB
-constexpr uint32_t kSlots = 8;            // ring of boxes
-constexpr uint32_t OFF_Q = 0;             // Q0: 3 boxes, Q1: 3 boxes
-constexpr uint32_t OFF_RING = 6 * kBox;
-constexpr uint32_t OFF_BAR = OFF_RING + kSlots * kBox;
+constexpr int kT = 128;                    // queries / keys per tile
+constexpr uint32_t kBox = kT * 128;        // 128 rows x 64 bf16 = 16 KB
+constexpr int kKSt = 2, kVSt = 2;          // ring stages
+constexpr int kSBuf = 3;                   // S buffers in tensor memory
+constexpr uint32_t OFF_Q = 0;                              // 3 boxes
+constexpr uint32_t OFF_K = 3 * kBox;                       // kKSt x 3 boxes
+constexpr uint32_t OFF_V = OFF_K + kKSt * 3 * kBox;        // kVSt x 2 boxes
+constexpr uint32_t OFF_X = OFF_V + kVSt * 2 * kBox;        // float xm[2][2][128], xl[2][128]
+constexpr uint32_t OFF_BAR = OFF_X + 6 * 128 * 4;
 constexpr int kThreads = 384;
-// Register split (setmaxnreg): the two softmax warpgroups grow to kRegsSoftmax,
-// the producer / MMA warpgroup shrinks to kRegsOther.  The sum must not exceed
-// what the block was launched with (threads x registers per thread), which the
-// host checks before every launch.
-constexpr int kRegsSoftmax = 184;
-constexpr int kRegsOther = 136;
-constexpr int kRegsNeeded = 256 * kRegsSoftmax + 128 * kRegsOther;
+constexpr uint32_t kColO = 384;
 
 struct Bars {
   uint64_t q_full, q_empty;
-  uint64_t full[kSlots], empty[kSlots];
-  uint64_t s_full[2], p_full[2], o_full[2], o_empty[2];
-  uint64_t drain;
+  uint64_t k_full[kKSt], k_empty[kKSt];
+  uint64_t v_full[kVSt], v_empty[kVSt];
+  uint64_t s_full[kSBuf], p_full[kSBuf], pv_done[kSBuf];
+  uint64_t o_full, o_empty, drain;
   uint32_t tmem_base;
   int abort;
 };
 
 constexpr uint32_t kSmem = OFF_BAR + sizeof(Bars) + 1024;
 static_assert(kSmem <= 232448, "shared memory budget");
-constexpr uint32_t kTmemCols = 512;  // S0 @0, S1 @128, O0 @256, O1 @384
+constexpr uint32_t kTmemCols = 512;
 
-// Item k of the CTA: snake order over the items sorted by decreasing cost
-// (a 256-query block b attends 2b + 2 key tiles).
-__device__ __forceinline__ bool item_of(int k, int grid, int cta, int n_items, int nb, int &head, int &blk) {
+// Item k of the CTA: snake order over the items sorted by decreasing cost.
+__device__ __forceinline__ bool item_of(int k, int grid, int cta, int n_items, int nq, int &head, int &qt) {
   const int pos = (k & 1) ? (k + 1) * grid - 1 - cta : k * grid + cta;
   if (pos >= n_items) return false;
-  blk = nb - 1 - pos / 16;
+  qt = nq - 1 - pos / 16;
   head = pos % 16;
   return true;
 }
-
-// Position of the ring box with sequence number n.
-__device__ __forceinline__ uint32_t slot_of(uint32_t n) { return n % kSlots; }
-__device__ __forceinline__ uint32_t use_of(uint32_t n) { return n / kSlots; }
 
 __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
                                            uint32_t accumulate) {
@@ -118,10 +113,6 @@ __device__ __forceinline__ void fadd2(float &a0, float &a1, float b0, float b1) 
   asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(d));
 }
 
-__device__ __forceinline__ void tmem_st32u(uint32_t taddr, const uint32_t *v) {
-  tmem_st32(taddr, reinterpret_cast<const float *>(v));
-}
-
 }  // namespace fpre
 
 using namespace fpre;
@@ -131,26 +122,32 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
   uint8_t *smem = reinterpret_cast<uint8_t *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   Bars *B = reinterpret_cast<Bars *>(smem + OFF_BAR);
+  float *xm = reinterpret_cast<float *>(smem + OFF_X);   // [tile parity][group][row]
+  float *xl = xm + 4 * 128;                               // [group][row]
   const uint32_t s_base = smem_u32(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int *abort = &B->abort;
-  const int nkv = (p.S + kT - 1) / kT;           // key tiles
-  const int nb = (p.S + 2 * kT - 1) / (2 * kT);  // 256-query blocks
-  const int n_items = nb * 16;
+  const int nq = (p.S + kT - 1) / kT;
+  const int n_items = nq * 16;
 
   if (threadIdx.x == 0) {
     mbar_init(&B->q_full, 1);
     mbar_init(&B->q_empty, 1);
-    for (uint32_t i = 0; i < kSlots; ++i) {
-      mbar_init(&B->full[i], 1);
-      mbar_init(&B->empty[i], 1);
+    for (int i = 0; i < kKSt; ++i) {
+      mbar_init(&B->k_full[i], 1);
+      mbar_init(&B->k_empty[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
+    for (int i = 0; i < kVSt; ++i) {
+      mbar_init(&B->v_full[i], 1);
+      mbar_init(&B->v_empty[i], 1);
+    }
+    for (int i = 0; i < kSBuf; ++i) {
       mbar_init(&B->s_full[i], 1);
-      mbar_init(&B->p_full[i], 4);
-      mbar_init(&B->o_full[i], 1);
-      mbar_init(&B->o_empty[i], 4);
+      mbar_init(&B->p_full[i], 8);
+      mbar_init(&B->pv_done[i], 1);
     }
+    mbar_init(&B->o_full, 1);
+    mbar_init(&B->o_empty, 8);
     mbar_init(&B->drain, 1);
     B->abort = 0;
     fence_barrier_init();
@@ -164,63 +161,62 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
   tc_fence_after();
   const uint32_t tmem = B->tmem_base;
 
-  if (warp >= 8) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsOther));
   if (warp == 8) {
-    // ---------------------------------------------------------------- TMA producer
+    // ---------------------------------------------------------------- Q and K copies
     if (lane == 0) {
       tma_prefetch_desc(&p.tm_q);
       tma_prefetch_desc(&p.tm_kv);
       tma_prefetch_desc(&p.tm_kr);
-      uint32_t seq = 0;  // ring boxes issued
-      uint32_t q_issued = 0;
-      int k = 0;
+      uint32_t kc = 0, qc = 0;
       bool ok = true;
-      int head, blk;
-      auto take = [&](uint32_t &s) -> bool {
-        s = slot_of(seq);
-        const bool r = mbar_wait(&B->empty[s], (use_of(seq) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
-        if (r) ++seq;
-        return r;
-      };
-      for (; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nb, head, blk); ++k) {
+      int head, qt;
+      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, head, qt); ++k) {
         ok = mbar_wait(&B->q_empty, (k & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
         if (!ok) break;
-        ++q_issued;
-        mbar_arrive_expect_tx(&B->q_full, 6 * kBox);
-        for (int t = 0; t < 2; ++t)
-          for (int b = 0; b < 3; ++b)
-            tma_load_3d(smem + OFF_Q + (3 * t + b) * kBox, &p.tm_q, &B->q_full, 64 * b, head, (2 * blk + t) * kT);
-        const int n1 = min(2 * blk + 2, nkv);
-        for (int j = 0; j < n1 && ok; ++j) {
-          uint32_t s;
-          // key tile: k_nope lo, k_nope hi, k_rope
-          for (int b = 0; b < 3 && ok; ++b) {
-            ok = take(s);
-            if (!ok) break;
-            mbar_arrive_expect_tx(&B->full[s], kBox);
-            if (b < 2)
-              tma_load_3d(smem + OFF_RING + s * kBox, &p.tm_kv, &B->full[s], 64 * b, head, j * kT);
-            else
-              tma_load_2d(smem + OFF_RING + s * kBox, &p.tm_kr, &B->full[s], p.kr_col, j * kT);
-          }
+        ++qc;
+        mbar_arrive_expect_tx(&B->q_full, 3 * kBox);
+        for (int b = 0; b < 3; ++b) tma_load_3d(smem + OFF_Q + b * kBox, &p.tm_q, &B->q_full, 64 * b, head, qt * kT);
+        for (int j = 0; j <= qt && ok; ++j, ++kc) {
+          const uint32_t s = kc % kKSt;
+          ok = mbar_wait(&B->k_empty[s], ((kc / kKSt) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
           if (!ok) break;
-          // value tile: the low half always in the lower of its two slots
-          const uint32_t lo = min(slot_of(seq), slot_of(seq + 1));
-          for (int h = 0; h < 2 && ok; ++h) {
-            ok = take(s);
-            if (!ok) break;
-            mbar_arrive_expect_tx(&B->full[s], kBox);
-            tma_load_3d(smem + OFF_RING + s * kBox, &p.tm_kv, &B->full[s], s == lo ? 128 : 192, head, j * kT);
-          }
+          uint8_t *kd = smem + OFF_K + s * 3 * kBox;
+          mbar_arrive_expect_tx(&B->k_full[s], 3 * kBox);
+          tma_load_3d(kd, &p.tm_kv, &B->k_full[s], 0, head, j * kT);
+          tma_load_3d(kd + kBox, &p.tm_kv, &B->k_full[s], 64, head, j * kT);
+          tma_load_2d(kd + 2 * kBox, &p.tm_kr, &B->k_full[s], p.kr_col, j * kT);
         }
       }
       if (!ok) {
-        // let every copy already issued land before the CTA exits
-        for (uint32_t s = 0; s < kSlots && s < seq; ++s) {
-          const uint32_t last = s + kSlots * ((seq - 1 - s) / kSlots);
-          drain_wait(&B->full[s], use_of(last) & 1, p.err);
+        for (uint32_t s = 0; s < static_cast<uint32_t>(kKSt) && s < kc; ++s) {
+          const uint32_t last = s + kKSt * ((kc - 1 - s) / kKSt);
+          drain_wait(&B->k_full[s], (last / kKSt) & 1, p.err);
         }
-        if (q_issued > 0) drain_wait(&B->q_full, (q_issued - 1) & 1, p.err);
+        if (qc > 0) drain_wait(&B->q_full, (qc - 1) & 1, p.err);
+      }
+    }
+  } else if (warp == 10) {
+    // ---------------------------------------------------------------- V copies
+    if (lane == 0) {
+      uint32_t vc = 0;
+      bool ok = true;
+      int head, qt;
+      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, head, qt); ++k) {
+        for (int j = 0; j <= qt && ok; ++j, ++vc) {
+          const uint32_t s = vc % kVSt;
+          ok = mbar_wait(&B->v_empty[s], ((vc / kVSt) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+          if (!ok) break;
+          uint8_t *vd = smem + OFF_V + s * 2 * kBox;
+          mbar_arrive_expect_tx(&B->v_full[s], 2 * kBox);
+          tma_load_3d(vd, &p.tm_kv, &B->v_full[s], 128, head, j * kT);
+          tma_load_3d(vd + kBox, &p.tm_kv, &B->v_full[s], 192, head, j * kT);
+        }
+      }
+      if (!ok) {
+        for (uint32_t s = 0; s < static_cast<uint32_t>(kVSt) && s < vc; ++s) {
+          const uint32_t last = s + kVSt * ((vc - 1 - s) / kVSt);
+          drain_wait(&B->v_full[s], (last / kVSt) & 1, p.err);
+        }
       }
     }
   } else if (warp == 9) {
@@ -228,157 +224,118 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_f16(1, 1, 0, 0, kT, kT);   // A = Q, B = K (both K-major)
       constexpr uint32_t idesc_pv = idesc_f16(1, 1, 0, 1, kT, 128);  // A = P (tensor memory), B = V (MN-major)
-      // K-major SW128 descriptor of ring slot 0; slot s, box offsets and the
-      // 16-element K steps are added to its address field (smem < 256 KB, so
-      // the 14-bit field never carries into the next one)
-      const uint64_t ring_desc = smem_desc(s_base + OFF_RING, 16, 1024, LAYOUT_SW128);
-      const uint64_t ring_desc_v = ring_desc & ~(0x3FFFull << 16);  // LBO field set per value tile
-      uint32_t seq = 0;                 // ring boxes consumed
-      uint32_t pc[2] = {0, 0};          // P tiles consumed per query tile
+      // descriptors: the address field of a base descriptor advanced by offsets
+      // (shared memory < 256 KB, so the 14-bit field never carries over)
+      const uint64_t q_desc = smem_desc(s_base + OFF_Q, 16, 1024, LAYOUT_SW128);
+      const uint64_t k_desc = smem_desc(s_base + OFF_K, 16, 1024, LAYOUT_SW128);
+      const uint64_t v_desc = smem_desc(s_base + OFF_V, kBox, 1024, LAYOUT_SW128);
+      uint32_t tc = 0, kc = 0, vc = 0;  // S tiles, K stages, V stages consumed
       bool ok = true;
-      int head, blk;
-      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nb, head, blk); ++k) {
-        const int n0 = min(2 * blk + 1, nkv), n1 = min(2 * blk + 2, nkv);
+      int head, qt;
+      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, head, qt); ++k) {
+        const int n = qt + 1;
         ok = mbar_wait(&B->q_full, k & 1, abort, p.err, ERR_TIMEOUT_FULL);
-        uint32_t vseq = 0;    // sequence number of the previous tile's first value box
-        bool vready = false;  // its full barriers already waited
-        for (int j = 0; j <= n1 && ok; ++j) {
-          const uint32_t kseq = seq;  // this tile's key boxes: kseq .. kseq + 2
-          bool kready = false;
-          auto wait_k = [&]() -> bool {
-            if (kready) return true;
-            for (uint32_t b = 0; b < 3; ++b)
-              if (!mbar_wait(&B->full[slot_of(kseq + b)], use_of(kseq + b) & 1, abort, p.err, ERR_TIMEOUT_FULL))
-                return false;
-            kready = true;
-            tc_fence_after();
-            return true;
-          };
-          auto wait_v = [&]() -> bool {
-            if (vready) return true;
-            for (uint32_t b = 0; b < 2; ++b)
-              if (!mbar_wait(&B->full[slot_of(vseq + b)], use_of(vseq + b) & 1, abort, p.err, ERR_TIMEOUT_FULL))
-                return false;
-            vready = true;
-            tc_fence_after();
-            return true;
-          };
-          auto issue_pv = [&](int t) -> bool {
-            // O_t (+)= P_t V_{j-1}
-            if (!mbar_wait(&B->p_full[t], pc[t] & 1, abort, p.err, ERR_TIMEOUT_MMA)) return false;
-            ++pc[t];
-            if (j == 1 && k > 0 && !mbar_wait(&B->o_empty[t], (k - 1) & 1, abort, p.err, ERR_TIMEOUT_MMA))
-              return false;
-            if (!wait_v()) return false;
-            tc_fence_after();
-            // V: the low half sits in the lower of the two slots (see the producer)
-            const uint32_t sa = slot_of(vseq);
-            const uint64_t vd = ring_desc_v + (sa == kSlots - 1 ? 0u : sa * (kBox >> 4)) +
-                                (static_cast<uint64_t>(sa == kSlots - 1 ? (kSlots - 1) * (kBox >> 4) : (kBox >> 4)) << 16);
-            const uint32_t a_tm = tmem + 128 * t;
-            const uint32_t d_tm = tmem + 256 + 128 * t;
-            mma_f16_ts(d_tm, a_tm, vd, idesc_pv, j == 1 ? 0u : 1u);
+        auto issue_s = [&](int j) -> bool {
+          // S_j = Q K_j^T into buffer (tc + j) % 3
+          const uint32_t b = (tc + j) % kSBuf, s = kc % kKSt;
+          if (!mbar_wait(&B->k_full[s], (kc / kKSt) & 1, abort, p.err, ERR_TIMEOUT_FULL)) return false;
+          tc_fence_after();
+          const uint64_t kd = k_desc + s * (3 * kBox >> 4);
 #pragma unroll
-            for (int kk = 1; kk < kT / 16; ++kk) mma_f16_ts(d_tm, a_tm + 8 * kk, vd + 128 * kk, idesc_pv, 1u);
-            return true;
-          };
-          auto issue_qk = [&](int t) {
-            const uint64_t qd = ring_desc - (static_cast<uint64_t>(OFF_RING - OFF_Q - 3 * t * kBox) >> 4);
-            const uint32_t d_tm = tmem + 128 * t;
+          for (int bx = 0; bx < 3; ++bx)
 #pragma unroll
-            for (int b = 0; b < 3; ++b) {
-              const uint64_t kd = ring_desc + slot_of(kseq + b) * (kBox >> 4);
+            for (int kk = 0; kk < 4; ++kk)
+              mma_f16_ss(tmem + 128 * b, q_desc + bx * (kBox >> 4) + 2 * kk, kd + bx * (kBox >> 4) + 2 * kk,
+                         idesc_qk, (bx | kk) ? 1u : 0u);
+          mma_commit(&B->s_full[b]);
+          mma_commit(&B->k_empty[s]);
+          ++kc;
+          if (j == n - 1) mma_commit(&B->q_empty);
+          return true;
+        };
+        for (int j = 0; j < n && j < kSBuf && ok; ++j) ok = issue_s(j);
+        for (int j = 0; j < n && ok; ++j) {
+          const uint32_t g = tc + j, b = g % kSBuf, s = vc % kVSt;
+          ok = mbar_wait(&B->p_full[b], (g / kSBuf) & 1, abort, p.err, ERR_TIMEOUT_MMA);
+          if (ok && j == 0 && k > 0) ok = mbar_wait(&B->o_empty, (k - 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
+          if (ok) ok = mbar_wait(&B->v_full[s], (vc / kVSt) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+          if (!ok) break;
+          tc_fence_after();
+          // O (+)= P_j V_j
+          const uint64_t vd = v_desc + s * (2 * kBox >> 4);
 #pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                mma_f16_ss(d_tm, qd + b * (kBox >> 4) + 2 * kk, kd + 2 * kk, idesc_qk, (b | kk) ? 1u : 0u);
-            }
-            mma_commit(&B->s_full[t]);
-          };
-          // A: P0 V_{j-1}
-          if (j >= 1 && j <= n0) {
-            ok = issue_pv(0);
-            if (!ok) break;
-            if (j == n0) mma_commit(&B->o_full[0]);
-          }
-          // B: S0 = Q0 K_j^T
-          if (j < n0) {
-            ok = wait_k();
-            if (!ok) break;
-            issue_qk(0);
-          }
-          // C: P1 V_{j-1}, then V_{j-1} is free
-          if (j >= 1) {
-            ok = issue_pv(1);
-            if (!ok) break;
-            mma_commit(&B->empty[slot_of(vseq)]);
-            mma_commit(&B->empty[slot_of(vseq + 1)]);
-            if (j == n1) mma_commit(&B->o_full[1]);
-          }
-          // D: S1 = Q1 K_j^T, then K_j is free
-          if (j < n1) {
-            ok = wait_k();
-            if (!ok) break;
-            issue_qk(1);
-            for (uint32_t b = 0; b < 3; ++b) mma_commit(&B->empty[slot_of(kseq + b)]);
-            if (j == n1 - 1) mma_commit(&B->q_empty);
-            vseq = kseq + 3;
-            vready = false;
-            seq = kseq + 5;
-          }
+          for (int kk = 0; kk < kT / 16; ++kk)
+            mma_f16_ts(tmem + kColO, tmem + 128 * b + 8 * kk, vd + 128 * kk, idesc_pv, (j | kk) ? 1u : 0u);
+          mma_commit(&B->v_empty[s]);
+          mma_commit(&B->pv_done[b]);
+          ++vc;
+          if (j == n - 1) mma_commit(&B->o_full);
+          if (j + kSBuf < n) ok = issue_s(j + kSBuf);
         }
+        tc += n;
       }
       mma_commit(&B->drain);
       drain_wait(&B->drain, 0, p.err);
     }
   } else if (warp < 8) {
     // ---------------------------------------------------------------- softmax + epilogue
-    // (warps 0-7 only: warps 10-11 of the shrunk warpgroup must not come here)
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
-    const int t = warp >> 2;            // query tile of this warpgroup
+    const int w = warp >> 2;            // key half of this warpgroup
     const int sub = warp & 3;           // TMEM lane quarter
     const int r = 32 * sub + lane;      // query row within the tile
     const uint32_t lane_base = static_cast<uint32_t>(32 * sub) << 16;
-    const uint32_t s_col = tmem + lane_base + 128 * t;
-    const uint32_t o_col = tmem + lane_base + 256 + 128 * t;
+    const uint32_t o_col = tmem + lane_base + kColO + 64 * w;
     const float sl = p.scale_log2;
-    uint32_t sc = 0;  // S tiles consumed
-    int head, blk;
+    uint32_t g = 0;  // S tiles consumed (same sequence as the MMA issuer's)
+    int head, qt;
     bool bad = false;
-    for (int k = 0; !bad && item_of(k, gridDim.x, blockIdx.x, n_items, nb, head, blk); ++k) {
-      const int n_t = min(2 * blk + 1 + t, nkv);
-      const int qrow = (2 * blk + t) * kT + r;
+    for (int k = 0; !bad && item_of(k, gridDim.x, blockIdx.x, n_items, nq, head, qt); ++k) {
+      const int n = qt + 1;
+      const int qrow = qt * kT + r;
       float m = -INFINITY, l = 0.f;
-      for (int j = 0; j < n_t; ++j, ++sc) {
-        bad = !mbar_wait(&B->s_full[t], sc & 1, abort, p.err, ERR_TIMEOUT_MMA);
-        if (__any_sync(0xffffffffu, bad)) { bad = true; break; }
-        tc_fence_after();
-        float s[kT];
+      for (int j = 0; j < n; ++j, ++g) {
+        const uint32_t b = g % kSBuf;
+        const uint32_t s_col = tmem + lane_base + 128 * b;
+        bad = !mbar_wait(&B->s_full[b], (g / kSBuf) & 1, abort, p.err, ERR_TIMEOUT_MMA);
+        float s[64];
+        if (!bad) {
+          tc_fence_after();
+          tmem_ld32(s_col + 64 * w, s);
+          tmem_ld32(s_col + 64 * w + 32, s + 32);
+          tmem_wait_ld();
+        }
+        if (j == n - 1) {
+          // diagonal tile and sequence end: key j*128 + 64w + c is visible iff c <= lim
+          const int lim = min(qrow, p.S - 1) - j * kT - 64 * w;
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(s_col + 32 * c, s + 32 * c);
-        tmem_wait_ld();
-        if (j == n_t - 1) {
-          // diagonal tile and sequence end: key kb + c is visible iff c <= lim
-          const int lim = min(qrow, p.S - 1) - j * kT;
-#pragma unroll
-          for (int c = 0; c < kT; ++c) s[c] = c <= lim ? s[c] : -INFINITY;
+          for (int c = 0; c < 64; ++c) s[c] = c <= lim ? s[c] : -INFINITY;
         }
         float mx0 = fmaxf(s[0], s[1]), mx1 = fmaxf(s[2], s[3]), mx2 = fmaxf(s[4], s[5]), mx3 = fmaxf(s[6], s[7]);
 #pragma unroll
-        for (int c = 8; c < kT; c += 8) {
+        for (int c = 8; c < 64; c += 8) {
           mx0 = max3(mx0, s[c], s[c + 1]);
           mx1 = max3(mx1, s[c + 2], s[c + 3]);
           mx2 = max3(mx2, s[c + 4], s[c + 5]);
           mx3 = max3(mx3, s[c + 6], s[c + 7]);
         }
-        const float mx = fmaxf(max3(mx0, mx1, mx2), mx3);
+        xm[((g & 1) * 2 + w) * 128 + r] = fmaxf(max3(mx0, mx1, mx2), mx3);
+        // both halves of the row meet here (the S loads of both are complete,
+        // so P may now overwrite the first 64 columns)
+        if (named_bar_or(1, 256, bad)) { bad = true; break; }
+        const float mx = fmaxf(xm[(g & 1) * 256 + r], xm[(g & 1) * 256 + 128 + r]);
         const bool need = mx * sl > m * sl + 8.0f || m == -INFINITY;
         if (__any_sync(0xffffffffu, need)) {
           const float mn = fmaxf(m, mx);
           const float alpha = (m == -INFINITY) ? 0.f : ex2((m - mn) * sl);
           if (j > 0) {
-            // every earlier P V of this tile has completed (s_full covers them)
+            // this group's half of the O row, once P_{j-1} V_{j-1} (and so every
+            // earlier P V) has landed.  Per-buffer barriers keep the parity
+            // unambiguous: s_full of tile g implies P V of tile g - 3 is done,
+            // and P V of tile g + 2 cannot start before this group's P.
+            const uint32_t gp = g - 1;
+            bad = !mbar_wait(&B->pv_done[gp % kSBuf], (gp / kSBuf) & 1, abort, p.err, ERR_TIMEOUT_MMA);
+            tc_fence_after();
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
+            for (int c = 0; c < 2; ++c) {
               float o[32];
               tmem_ld32(o_col + 32 * c, o);
               tmem_wait_ld();
@@ -392,9 +349,9 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
         }
         const float neg = -m * sl;
         float sum0 = 0.f, sum1 = 0.f, sum2 = 0.f, sum3 = 0.f;
-        uint32_t pk[kT / 2];
+        uint32_t pk[32];
 #pragma unroll
-        for (int c = 0; c < kT; c += 4) {
+        for (int c = 0; c < 64; c += 4) {
           float a0, a1, a2, a3;
           ffma2(a0, a1, s[c], s[c + 1], sl, neg);
           ffma2(a2, a3, s[c + 2], s[c + 3], sl, neg);
@@ -408,23 +365,23 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
           pk[c / 2 + 1] = pack_bf16(a2, a3);
         }
         l += (sum0 + sum1) + (sum2 + sum3);
-        // P over the first 64 columns of S
-        tmem_st32u(s_col, pk);
-        tmem_st32u(s_col + 32, pk + 32);
+        // P (bf16 pairs) over columns [32w, 32w + 32) of this S buffer
+        tmem_st32(s_col + 32 * w, reinterpret_cast<const float *>(pk));
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&B->p_full[t]);
+        if (lane == 0) mbar_arrive(&B->p_full[b]);
       }
       if (bad) break;
-      // ---- epilogue: o = O / l as bf16 into out[row][head][0:128]
-      bad = !mbar_wait(&B->o_full[t], k & 1, abort, p.err, ERR_TIMEOUT_MMA);
-      if (__any_sync(0xffffffffu, bad)) break;
+      // ---- epilogue: o = O / (l_0 + l_1) as bf16 into out[row][head][0:128]
+      bad = !mbar_wait(&B->o_full, k & 1, abort, p.err, ERR_TIMEOUT_MMA);
+      xl[w * 128 + r] = l;
+      if (named_bar_or(2, 256, bad)) break;
       tc_fence_after();
-      const float inv = 1.0f / l;
-      __nv_bfloat16 *dst = p.out + (static_cast<size_t>(qrow) * 16 + head) * 128;
+      const float inv = 1.0f / (xl[r] + xl[128 + r]);
+      __nv_bfloat16 *dst = p.out + (static_cast<size_t>(qrow) * 16 + head) * 128 + 64 * w;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < 2; ++c) {
         float o[32];
         tmem_ld32(o_col + 32 * c, o);
         tmem_wait_ld();
@@ -442,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&B->o_empty[t]);
+      if (lane == 0) mbar_arrive(&B->o_empty);
     }
   }
 
@@ -457,15 +414,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
 cudaError_t launch_flash_prefill(const FlashParams &p, int sms, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(flash_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) return e;
-  static int regs = 0;  // registers per thread the kernel is launched with
-  if (regs == 0) {
-    cudaFuncAttributes fa;
-    e = cudaFuncGetAttributes(&fa, flash_prefill_kernel);
-    if (e != cudaSuccess) return e;
-    regs = fa.numRegs;
-  }
-  if (regs * kThreads < kRegsNeeded) return cudaErrorInvalidConfiguration;  // the split would never be granted
-  const int items = ((p.S + 2 * kT - 1) / (2 * kT)) * 16;
+  const int items = ((p.S + kT - 1) / kT) * 16;
   const int grid = items < sms ? items : sms;
   ProfScope ps("flash_prefill", stream);
   flash_prefill_kernel<<<grid, kThreads, kSmem, stream>>>(p);
@@ -473,3 +422,4 @@ cudaError_t launch_flash_prefill(const FlashParams &p, int sms, cudaStream_t str
 }
 
 }  // namespace kvl
+

@@ -954,7 +954,8 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   f.err = err;
   CK(launch_flash_prefill(f, sms, st));
   // out = o Wo^T, fp32 [S][H]
-  if (!bf16_map(&g.tm_a, o, 2048, s, 2048 * 2, 128) || !bf16_map(&g.tm_b, W.o, 2048, H, 2048 * 2, 256)) {
+  // (CTA-pair GEMM: 256 x 256 tiles, each CTA of a pair loads 128 rows of Wo)
+  if (!bf16_map(&g.tm_a, o, 2048, s, 2048 * 2, 128) || !bf16_map(&g.tm_b, W.o, 2048, H, 2048 * 2, 128)) {
     set_err("prefill: tensor map (o_proj)");
     return -1;
   }
@@ -963,7 +964,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   g.c = d_out;
   g.ldc = static_cast<int>(H);
   g.rope_cs = nullptr;
-  CK(launch_gemm(g, 256, EPI_F32, sms, st));
+  CK(launch_gemm_pair(g, 256, EPI_F32, sms, st));
   return 0;
 }
 
