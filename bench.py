@@ -275,7 +275,7 @@ class Prefill:
     bound = "tensor"
     # dram__bytes_read.sum + dram__bytes_write.sum per launch, one ncu capture
     # (profiles/flash_prefill_config2.txt, profiles/gemm_prefill_config2.txt)
-    ncu_traffic = {"flash_prefill": 59.574528e6 + 3.482624e6, "gemm_qrope": 30.442752e6 + 0.157952e6}
+    ncu_traffic = {"flash_prefill": 59.574528e6 + 3.482624e6, "gemm_q": 30.442752e6 + 0.157952e6}
 
     def __init__(self, torch, K, lib, dist, S=4096, theta=50000.0):
         self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
@@ -297,8 +297,9 @@ class Prefill:
         S, H, NH, QD, DV, R, DR = self.S, 2048, 16, 192, 128, 512, 64
         return {"gemv_bf16": 2.0 * S * (H * (NH * QD + R + DR) + NH * DV * H),
                 "vup": 2.0 * S * NH * DV * R, "absorb": 2.0 * S * NH * 128 * R,
-                "mla_attend_bf16": float(self.attn), "gemm_bf16": float(self.proj),
-                "flash_prefill": float(self.attn)}
+                "mla_attend_bf16": float(self.attn), "flash_prefill": float(self.attn),
+                "gemm_q": 2.0 * S * H * NH * QD, "gemm_kva": 2.0 * S * H * (R + DR),
+                "gemm_kvb": 2.0 * S * R * NH * (128 + DV), "gemm_o": 2.0 * S * NH * DV * H}
 
     def step(self):
         s = self.torch.cuda.current_stream().cuda_stream

@@ -51,9 +51,9 @@ constexpr int kThreads = 384;
 constexpr uint32_t kColO = 384;
 
 struct Bars {
-  uint64_t q_full, q_empty;
-  uint64_t k_full[kKSt], k_empty[kKSt];
-  uint64_t v_full[kVSt], v_empty[kVSt];
+  uint64_t q_full;
+  uint64_t k_full[kKSt];
+  uint64_t v_full[kVSt];
   uint64_t s_full[kSBuf], p_full[kSBuf], pv_done[kSBuf];
   uint64_t o_full, o_empty, drain;
   uint32_t tmem_base;
@@ -132,15 +132,8 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
 
   if (threadIdx.x == 0) {
     mbar_init(&B->q_full, 1);
-    mbar_init(&B->q_empty, 1);
-    for (int i = 0; i < kKSt; ++i) {
-      mbar_init(&B->k_full[i], 1);
-      mbar_init(&B->k_empty[i], 1);
-    }
-    for (int i = 0; i < kVSt; ++i) {
-      mbar_init(&B->v_full[i], 1);
-      mbar_init(&B->v_empty[i], 1);
-    }
+    for (int i = 0; i < kKSt; ++i) mbar_init(&B->k_full[i], 1);
+    for (int i = 0; i < kVSt; ++i) mbar_init(&B->v_full[i], 1);
     for (int i = 0; i < kSBuf; ++i) {
       mbar_init(&B->s_full[i], 1);
       mbar_init(&B->p_full[i], 8);
@@ -167,19 +160,29 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
       tma_prefetch_desc(&p.tm_q);
       tma_prefetch_desc(&p.tm_kv);
       tma_prefetch_desc(&p.tm_kr);
-      uint32_t kc = 0, qc = 0;
+      // A stage is free once the MMAs that read it have completed: Q after
+      // the last S of the previous item, the K of tile g after S_g (s_full of
+      // tile g).  The parity is unambiguous: S_{g+3} needs a K this warp loads
+      // later, and S_{g-3} completed before S_{g-2}, which was waited for.
+      uint32_t kc = 0, qc = 0;  // kc: key tiles issued = global S tile index
       bool ok = true;
       int head, qt;
       for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, head, qt); ++k) {
-        ok = mbar_wait(&B->q_empty, (k & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
-        if (!ok) break;
+        if (kc > 0) {
+          const uint32_t gl = kc - 1;  // last S of the previous item
+          ok = mbar_wait(&B->s_full[gl % kSBuf], (gl / kSBuf) & 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+          if (!ok) break;
+        }
         ++qc;
         mbar_arrive_expect_tx(&B->q_full, 3 * kBox);
         for (int b = 0; b < 3; ++b) tma_load_3d(smem + OFF_Q + b * kBox, &p.tm_q, &B->q_full, 64 * b, head, qt * kT);
         for (int j = 0; j <= qt && ok; ++j, ++kc) {
           const uint32_t s = kc % kKSt;
-          ok = mbar_wait(&B->k_empty[s], ((kc / kKSt) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
-          if (!ok) break;
+          if (kc >= static_cast<uint32_t>(kKSt)) {
+            const uint32_t gp = kc - kKSt;  // the tile that last used this stage
+            ok = mbar_wait(&B->s_full[gp % kSBuf], (gp / kSBuf) & 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+            if (!ok) break;
+          }
           uint8_t *kd = smem + OFF_K + s * 3 * kBox;
           mbar_arrive_expect_tx(&B->k_full[s], 3 * kBox);
           tma_load_3d(kd, &p.tm_kv, &B->k_full[s], 0, head, j * kT);
@@ -203,9 +206,13 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
       int head, qt;
       for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, head, qt); ++k) {
         for (int j = 0; j <= qt && ok; ++j, ++vc) {
+          // the V of tile g is free once P_g V_g has completed (pv_done of tile g)
           const uint32_t s = vc % kVSt;
-          ok = mbar_wait(&B->v_empty[s], ((vc / kVSt) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
-          if (!ok) break;
+          if (vc >= static_cast<uint32_t>(kVSt)) {
+            const uint32_t gp = vc - kVSt;
+            ok = mbar_wait(&B->pv_done[gp % kSBuf], (gp / kSBuf) & 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+            if (!ok) break;
+          }
           uint8_t *vd = smem + OFF_V + s * 2 * kBox;
           mbar_arrive_expect_tx(&B->v_full[s], 2 * kBox);
           tma_load_3d(vd, &p.tm_kv, &B->v_full[s], 128, head, j * kT);
@@ -247,10 +254,8 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
             for (int kk = 0; kk < 4; ++kk)
               mma_f16_ss(tmem + 128 * b, q_desc + bx * (kBox >> 4) + 2 * kk, kd + bx * (kBox >> 4) + 2 * kk,
                          idesc_qk, (bx | kk) ? 1u : 0u);
-          mma_commit(&B->s_full[b]);
-          mma_commit(&B->k_empty[s]);
+          mma_commit(&B->s_full[b]);  // also frees the K stage (and Q after the item's last S)
           ++kc;
-          if (j == n - 1) mma_commit(&B->q_empty);
           return true;
         };
         for (int j = 0; j < n && j < kSBuf && ok; ++j) ok = issue_s(j);
@@ -266,8 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
 #pragma unroll
           for (int kk = 0; kk < kT / 16; ++kk)
             mma_f16_ts(tmem + kColO, tmem + 128 * b + 8 * kk, vd + 128 * kk, idesc_pv, (j | kk) ? 1u : 0u);
-          mma_commit(&B->v_empty[s]);
-          mma_commit(&B->pv_done[b]);
+          mma_commit(&B->pv_done[b]);  // also frees the V stage
           ++vc;
           if (j == n - 1) mma_commit(&B->o_full);
           if (j + kSBuf < n) ok = issue_s(j + kSBuf);

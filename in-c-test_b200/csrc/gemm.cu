@@ -420,19 +420,20 @@ static cudaError_t launch_gemm_t(const GemmParams &p, int sms, cudaStream_t stre
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream) {
+cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream, const char *name) {
+  if (!name) name = epi == EPI_QROPE ? "gemm_qrope" : "gemm_bf16";
   if (epi == EPI_QROPE) {
     if (p.N % 192 != 0) return cudaErrorInvalidValue;
-    if (bn == 256) return launch_gemm_t<256, EPI_QROPE>(p, sms, stream, "gemm_qrope");
-    if (bn == 192) return launch_gemm_t<192, EPI_QROPE>(p, sms, stream, "gemm_qrope");
+    if (bn == 256) return launch_gemm_t<256, EPI_QROPE>(p, sms, stream, name);
+    if (bn == 192) return launch_gemm_t<192, EPI_QROPE>(p, sms, stream, name);
     return cudaErrorInvalidValue;
   }
   if (bn == 256) {
-    if (epi == EPI_F32) return launch_gemm_t<256, EPI_F32>(p, sms, stream, "gemm_bf16");
-    if (epi == EPI_BF16) return launch_gemm_t<256, EPI_BF16>(p, sms, stream, "gemm_bf16");
+    if (epi == EPI_F32) return launch_gemm_t<256, EPI_F32>(p, sms, stream, name);
+    if (epi == EPI_BF16) return launch_gemm_t<256, EPI_BF16>(p, sms, stream, name);
   } else if (bn == 192) {
-    if (epi == EPI_F32) return launch_gemm_t<192, EPI_F32>(p, sms, stream, "gemm_bf16");
-    if (epi == EPI_BF16) return launch_gemm_t<192, EPI_BF16>(p, sms, stream, "gemm_bf16");
+    if (epi == EPI_F32) return launch_gemm_t<192, EPI_F32>(p, sms, stream, name);
+    if (epi == EPI_BF16) return launch_gemm_t<192, EPI_BF16>(p, sms, stream, name);
   }
   return cudaErrorInvalidValue;
 }
@@ -454,14 +455,15 @@ static cudaError_t launch_gemm_pair_t(const GemmParams &p, int sms, cudaStream_t
 }
 
 // B's tensor map box must be {64, bn / 2} rows for the pair form.
-cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream) {
+cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream, const char *name) {
   if (bn != 256) return cudaErrorInvalidValue;
+  if (!name) name = epi == EPI_QROPE ? "gemm_qrope" : "gemm_bf16";
   if (epi == EPI_QROPE) {
     if (p.N % 192 != 0) return cudaErrorInvalidValue;
-    return launch_gemm_pair_t<256, EPI_QROPE>(p, sms, stream, "gemm_qrope");
+    return launch_gemm_pair_t<256, EPI_QROPE>(p, sms, stream, name);
   }
-  if (epi == EPI_F32) return launch_gemm_pair_t<256, EPI_F32>(p, sms, stream, "gemm_bf16");
-  if (epi == EPI_BF16) return launch_gemm_pair_t<256, EPI_BF16>(p, sms, stream, "gemm_bf16");
+  if (epi == EPI_F32) return launch_gemm_pair_t<256, EPI_F32>(p, sms, stream, name);
+  if (epi == EPI_BF16) return launch_gemm_pair_t<256, EPI_BF16>(p, sms, stream, name);
   return cudaErrorInvalidValue;
 }
 

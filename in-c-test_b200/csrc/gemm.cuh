@@ -20,9 +20,12 @@ struct GemmParams {
   uint32_t *err;
 };
 
-cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream);
+// `name` labels the launch in the per-kernel profile (a string literal).
+cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream,
+                        const char *name = nullptr);
 // CTA-pair (2-SM) form, 256 x bn tiles: B's tensor map box is {64, bn / 2}.
-cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream);
+cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream,
+                             const char *name = nullptr);
 cudaError_t launch_rope_table(float2 *cs, int rows, int dim, float theta, cudaStream_t stream);
 
 }  // namespace kvl

@@ -902,7 +902,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   gq.rope_cs = cs;
   CK(launch_rope_table(cs, S, 64, cfg.rope_theta, fk->s2));
   CK(cudaEventRecord(fk->rope, fk->s2));
-  CK(launch_gemm(gq, 256, EPI_QROPE, sms, fk->s2));
+  CK(launch_gemm(gq, 256, EPI_QROPE, sms, fk->s2, "gemm_q"));
   CK(cudaEventRecord(fk->qdone, fk->s2));
 
   // caller's stream: kva = x Wkva^T, fp32 [S][576]
@@ -918,7 +918,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   g.N = 576;
   g.c = kva;
   g.ldc = 576;
-  CK(launch_gemm(g, 192, EPI_F32, sms, st));
+  CK(launch_gemm(g, 192, EPI_F32, sms, st, "gemm_kva"));
   // latent = rmsnorm(kva[:512]) * kv_a_norm, k_rope = rope(kva[512:]) -> pool [S][576] bf16
   CK(cudaStreamWaitEvent(st, fk->rope, 0));
   CK(append_rows_bf16(pool, kva, W.kvan, cs, S, cfg.rms_eps, st));
@@ -931,7 +931,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   g.K = 512;
   g.c = kv;
   g.ldc = 4096;
-  CK(launch_gemm(g, 256, EPI_BF16, sms, st));
+  CK(launch_gemm(g, 256, EPI_BF16, sms, st, "gemm_kvb"));
   CK(cudaStreamWaitEvent(st, fk->qdone, 0));  // join the second stream
   // causal attention -> o bf16 [S][16][128]
   FlashParams f;
@@ -964,7 +964,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   g.c = d_out;
   g.ldc = static_cast<int>(H);
   g.rope_cs = nullptr;
-  CK(launch_gemm_pair(g, 256, EPI_F32, sms, st));
+  CK(launch_gemm_pair(g, 256, EPI_F32, sms, st, "gemm_o"));
   return 0;
 }
 
