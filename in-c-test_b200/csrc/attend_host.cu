@@ -120,9 +120,11 @@ int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long lo
 // out[seq][h][:] = sum_p w_p o_p / sum_p w_p,  w_p = exp(lse_p - max_p lse_p);
 // lse[seq][h] = max + log(sum_p w_p).  Part p of an entry lives at part index
 // first + p * step (each part is [16][R] floats and [16] lse values).
-// Grid (entry, head, 256-wide chunk of R): the normalised weights of the
-// entry's parts for one head go to shared memory once, then every thread
-// combines one output element.
+// Grid (entry, head, 128-wide slice of R); each lane owns 4 consecutive output
+// elements and the block's warps split the entry's parts, so a part's slice is
+// one coalesced 512-byte read.  Every warp derives the normaliser itself from
+// the parts' lse values (few and cached), so the only block-wide step is the
+// final sum over warps.
 __global__ void merge_partials_kernel(float *out, float *lse, const float *part_o,
                                       const float *part_lse, const MergeEntry *entries, int nh,
                                       int R, int uniform_parts) {
@@ -130,48 +132,67 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
   const MergeEntry e = entries ? entries[blockIdx.x]
                                : MergeEntry{(int)blockIdx.x, (int)blockIdx.x, uniform_parts, (int)gridDim.x};
   const int h = blockIdx.y;
-  extern __shared__ float wsh[];  // [count] weights, then [32] reduction scratch
-  float *red = wsh + e.count;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  __shared__ float4 red[16][32];
+  auto lse_of = [&](int q) { return part_lse[(size_t)(e.first + q * e.step) * nh + h]; };
   float m = -INFINITY;
-  for (int p = threadIdx.x; p < e.count; p += blockDim.x)
-    m = fmaxf(m, part_lse[(size_t)(e.first + p * e.step) * nh + h]);
+  for (int q = lane; q < e.count; q += 32) m = fmaxf(m, lse_of(q));
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-  __syncthreads();
-  m = red[0];
-  for (int i = 1; i < (int)(blockDim.x >> 5); ++i) m = fmaxf(m, red[i]);
-  __syncthreads();
   float sum = 0.f;
-  for (int p = threadIdx.x; p < e.count; p += blockDim.x) {
-    const float w = expf(part_lse[(size_t)(e.first + p * e.step) * nh + h] - m);
-    wsh[p] = w;
-    sum += w;
-  }
+  for (int q = lane; q < e.count; q += 32) sum += expf(lse_of(q) - m);
   for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
-  __syncthreads();
-  sum = 0.f;
-  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) sum += red[i];
-  const float inv = 1.0f / sum;
   if (lse && blockIdx.z == 0 && threadIdx.x == 0) lse[(size_t)e.seq * nh + h] = m + logf(sum);
-  // 32 output elements x 8 groups of parts per block; the groups' partial sums
-  // meet in shared memory (reusing the reduction scratch after a barrier).
-  __syncthreads();
-  const int dl = threadIdx.x & 31, grp = threadIdx.x >> 5;
-  const int d = blockIdx.z * 32 + dl;
-  float acc = 0.f;
-  if (d < R)
-    for (int p = grp; p < e.count; p += 8)
-      acc = fmaf(wsh[p], part_o[((size_t)(e.first + p * e.step) * nh + h) * R + d], acc);
-  float *gs = red + 32;  // [8][32]
-  gs[grp * 32 + dl] = acc;
-  __syncthreads();
-  if (grp == 0 && d < R) {
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s += gs[i * 32 + dl];
-    out[((size_t)e.seq * nh + h) * R + d] = s * inv;
+  const int d0 = blockIdx.z * 128 + 4 * lane;
+  const bool vec = (R & 3) == 0 && d0 + 3 < R &&
+                   ((reinterpret_cast<uintptr_t>(part_o) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+  for (int q = warp; q < e.count; q += nw) {
+    const float w = expf(lse_of(q) - m);
+    const float *src = part_o + ((size_t)(e.first + q * e.step) * nh + h) * R + d0;
+    if (vec) {
+      const float4 v = *reinterpret_cast<const float4 *>(src);
+      acc.x = fmaf(w, v.x, acc.x);
+      acc.y = fmaf(w, v.y, acc.y);
+      acc.z = fmaf(w, v.z, acc.z);
+      acc.w = fmaf(w, v.w, acc.w);
+    } else {
+      if (d0 < R) acc.x = fmaf(w, src[0], acc.x);
+      if (d0 + 1 < R) acc.y = fmaf(w, src[1], acc.y);
+      if (d0 + 2 < R) acc.z = fmaf(w, src[2], acc.z);
+      if (d0 + 3 < R) acc.w = fmaf(w, src[3], acc.w);
+    }
   }
+  red[warp][lane] = acc;
+  __syncthreads();
+  if (warp == 0) {
+    float4 t = red[0][lane];
+    for (int i = 1; i < nw; ++i) {
+      const float4 u = red[i][lane];
+      t.x += u.x;
+      t.y += u.y;
+      t.z += u.z;
+      t.w += u.w;
+    }
+    const float inv = 1.0f / sum;
+    float *dst = out + ((size_t)e.seq * nh + h) * R + d0;
+    if (vec) {
+      *reinterpret_cast<float4 *>(dst) = make_float4(t.x * inv, t.y * inv, t.z * inv, t.w * inv);
+    } else {
+      if (d0 < R) dst[0] = t.x * inv;
+      if (d0 + 1 < R) dst[1] = t.y * inv;
+      if (d0 + 2 < R) dst[2] = t.z * inv;
+      if (d0 + 3 < R) dst[3] = t.w * inv;
+    }
+  }
+}
+
+// Warps per merge block: enough to split the largest part count (a few parts
+// per warp), at most 16.
+static int merge_warps(int max_count) {
+  int w = 1;
+  while (w < 16 && 4 * w < max_count) w <<= 1;
+  return w;
 }
 
 cudaError_t launch_merge(float *out, float *lse, const float *part_o, const float *part_lse,
@@ -179,15 +200,10 @@ cudaError_t launch_merge(float *out, float *lse, const float *part_o, const floa
                          cudaStream_t stream, int max_count) {
   // d_entries == nullptr selects the part-major layout with max_count parts per sequence.
   if (n_entries <= 0) return cudaSuccess;
-  const size_t sm = (static_cast<size_t>(max_count) + 32 + 256) * sizeof(float);
-  if (sm > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(merge_partials_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         static_cast<int>(sm));
-    if (e != cudaSuccess) return e;
-  }
   ProfScope ps("merge_partials", stream);
-  dim3 grid(n_entries, nh, (R + 31) / 32);
-  merge_partials_kernel<<<grid, 256, sm, stream>>>(out, lse, part_o, part_lse, d_entries, nh, R, max_count);
+  dim3 grid(n_entries, nh, (R + 127) / 128);
+  merge_partials_kernel<<<grid, 32 * merge_warps(max_count), 0, stream>>>(out, lse, part_o, part_lse, d_entries,
+                                                                          nh, R, max_count);
   return cudaGetLastError();
 }
 
@@ -197,10 +213,9 @@ cudaError_t launch_merge_unprofiled(float *out, float *lse, const float *part_o,
                                    const MergeEntry *d_entries, int n_entries, int nh, int R,
                                    cudaStream_t stream, int max_count) {
   if (n_entries <= 0) return cudaSuccess;
-  const size_t sm = (static_cast<size_t>(max_count) + 32 + 256) * sizeof(float);
-  if (sm > 48 * 1024) return cudaErrorInvalidValue;
-  dim3 grid(n_entries, nh, (R + 31) / 32);
-  merge_partials_kernel<<<grid, 256, sm, stream>>>(out, lse, part_o, part_lse, d_entries, nh, R, max_count);
+  dim3 grid(n_entries, nh, (R + 127) / 128);
+  merge_partials_kernel<<<grid, 32 * merge_warps(max_count), 0, stream>>>(out, lse, part_o, part_lse, d_entries,
+                                                                          nh, R, max_count);
   return cudaGetLastError();
 }
 
