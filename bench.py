@@ -8,8 +8,9 @@
 Default workload: BASELINE config 2 (causal MLA prefill, one sequence of 4096
 tokens, H=2048, 16 heads; the configuration the metric's prefill half is quoted
 on and the largest that fits one GPU).  The decode half of the metric is
-reported in the same JSON line under "decode" (config 3 Q8 batched decode and
-config 5 long-context decode, KV GB/s against measured HBM bandwidth).
+reported in the same JSON line under "decode" (config 1 single-sequence
+attend, config 3 Q8 batched decode, config 5 long-context decode and config 4
+27-layer batched decode step; KV GB/s against measured HBM bandwidth).
 
 Multi-GPU (torchrun, one rank per GPU): prefill runs one independent sequence
 per rank (weak scaling); batched decode shards sequences across ranks; the
@@ -457,7 +458,117 @@ class DecodeLong:
                 "parallelism": f"split-KV x{self.dist.world} + NCCL all-gather merge"}
 
 
-WORKLOADS = {"prefill": Prefill, "decode_q8": DecodeQ8, "decode_long": DecodeLong}
+class DecodeStack:
+    """one decode step of the 27-layer text stack for 256
+    sequences at 32768 cached tokens each (bf16 latent pools), every layer a full
+    kvl_mla_decode_step_bf16 (projections, append of the new row, attend over
+    32769 rows, V up-projection, o_proj).  Sequences are sharded across ranks
+    (equal lengths, so each rank owns 256/N).  27 layers of KV (260.9 GB) do not
+    fit one GPU: below 27 x per-layer bytes of free memory the layers cycle
+    through `nbuf` distinct pools (each far larger than L2), so every layer still
+    reads its full KV bytes from HBM."""
+    name = "decode_stack"
+    metric = "MLA 27-layer decode KV GB/s (config 4: 256 seqs x 32768)"
+    unit = "GB/s"
+    bound = "hbm"
+    LAYERS = 27
+
+    def __init__(self, torch, K, lib, dist, seqs=256, L=32768, mem_frac=0.7):
+        import kvl_b200.parallel as PAR
+        self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
+        self.L = L
+        mine = PAR.shard_sequences([L] * seqs, dist.world)[dist.rank]
+        self.n = len(mine)
+        rows_seq = L + 1  # cached rows + the row this step appends
+        self.rows = self.n * rows_seq
+        dev = torch.device("cuda", torch.cuda.current_device())
+        layer_bytes = self.rows * 1152
+        free, _ = torch.cuda.mem_get_info(dev)
+        self.nbuf = int(max(1, min(self.LAYERS, (free * mem_frac) // layer_bytes)))
+        if self.nbuf < min(4, self.LAYERS):
+            raise RuntimeError(f"config 4 needs 4 layer pools of {layer_bytes / 1e9:.1f} GB; "
+                               f"{free / 1e9:.1f} GB free")
+        g = torch.Generator(device=dev)
+        g.manual_seed(4 + 1000 * dist.rank)
+        self.kv = [torch.randn((self.rows, 576), generator=g, device=dev, dtype=torch.bfloat16)
+                   for _ in range(self.nbuf)]
+        self.cfg = K.make_config(2048, 16, 128, 64, 128, 512, 1e-5, 50000.0)
+        self.wt, self.w = [], []
+        for _ in range(self.LAYERS):
+            t, w = device_weights(torch, K, self.cfg, g, dev)
+            self.wt.append(t)
+            self.w.append(w)
+        self.x = [dev_bf16(torch, (self.n, 2048), 1.0, g, dev).float() for _ in range(self.LAYERS)]
+        self.out = torch.empty((self.LAYERS, self.n, 2048), dtype=torch.float32, device=dev)
+        row0 = np.arange(self.n, dtype=np.int64) * rows_seq
+        self.plan = K.AttendPlan([rows_seq] * self.n, row0, 16, 512)
+        self.d_row = torch.from_numpy(row0 + L).to(dev)
+        self.d_pos = torch.full((self.n,), L, dtype=torch.int32, device=dev)
+        nbytes = lib.kvl_mla_decode_step_workspace_bytes(C.byref(self.cfg), self.n)
+        self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.units = self.LAYERS * self.rows * 1152  # attend bytes this rank reads per step
+        self.total_bytes = self.LAYERS * seqs * L * 1152
+
+    def step(self):
+        s = self.torch.cuda.current_stream().cuda_stream
+        for layer in range(self.LAYERS):
+            kv = self.kv[layer % self.nbuf]
+            rc = self.lib.kvl_mla_decode_step_bf16(
+                C.byref(self.cfg), C.byref(self.w[layer]), self.plan.h, self.out[layer].data_ptr(),
+                self.x[layer].data_ptr(), kv.data_ptr(), self.rows, self.d_row.data_ptr(), self.d_pos.data_ptr(),
+                self.n, self.ws.data_ptr(), s)
+            if rc != 0:
+                raise RuntimeError(self.K.last_error())
+
+    def value(self, ms):
+        return self.total_bytes / (ms * 1e-3) / 1e9
+
+    def config(self):
+        return {"workload": "config 4: 27-layer batched decode step, 256 seqs x 32768 cached tokens",
+                "seqs_per_rank": self.n, "layers": self.LAYERS, "layer_pools": self.nbuf,
+                "pool_note": "all 27 layers resident" if self.nbuf == self.LAYERS else
+                f"layer l reads pool l % {self.nbuf} (27 layers x 9.66 GB exceed one GPU)",
+                "kv_bytes_per_step": self.total_bytes, "weights": "27 distinct layers, bf16 ~N(0,0.02)",
+                "parallelism": f"sequence-sharded x{self.dist.world}"}
+
+
+class DecodeParity:
+    """one sequence, 1024 cached rows, absorbed query
+    [16,576] bf16 ~N(0,0.1), latent + rope bf16 ~N(0,1): the attend alone."""
+    name = "decode_parity"
+    metric = "MLA decode KV GB/s (config 1: 1 seq, L=1024)"
+    unit = "GB/s"
+    bound = "hbm"
+
+    def __init__(self, torch, K, lib, dist, L=1024):
+        self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev)
+        g.manual_seed(1)
+        self.L = L
+        self.kv = dev_bf16(torch, (L, 576), 1.0, g, dev)
+        self.q = dev_bf16(torch, (1, 16, 576), 0.1, g, dev).float()
+        self.o = torch.empty((1, 16, 512), device=dev)
+        self.plan = K.AttendPlan([L], [0], 16, 512)
+        self.units = L * 1152
+        self.total_bytes = dist.world * L * 1152
+
+    def step(self):
+        s = self.torch.cuda.current_stream().cuda_stream
+        rc = self.plan.attend_bf16(self.o, None, self.q, self.kv, self.L, stream=s)
+        if rc != 0:
+            raise RuntimeError(self.K.last_error())
+
+    def value(self, ms):
+        return self.total_bytes / (ms * 1e-3) / 1e9
+
+    def config(self):
+        return {"workload": "config 1: single-sequence decode attend, L=1024", "rows": self.L,
+                "parallelism": f"replicas x{self.dist.world}"}
+
+
+WORKLOADS = {"prefill": Prefill, "decode_q8": DecodeQ8, "decode_long": DecodeLong, "decode_stack": DecodeStack,
+             "decode_parity": DecodeParity}
 
 
 def measure(torch, K, lib, dist, wl, steps, warmup, flush, peaks):
@@ -545,17 +656,26 @@ def main():
         line["e2e"] = wl.e2e(max(2, args.steps // 2), 1)
     if not args.no_extras and args.workload == "prefill":
         extras = {}
-        for name in ("decode_q8", "decode_long"):
+        for name in ("decode_parity", "decode_q8", "decode_long", "decode_stack"):
+            w2, err = None, None
             try:
                 w2 = WORKLOADS[name](torch, K, lib, dist)
-                ms2, prof2, l2 = measure(torch, K, lib, dist, w2, args.steps, args.warmup, flush, peaks)
-                r2, _ = roofline_for(w2, prof2, peaks, peak_kind)
-                extras[name] = {"metric": w2.metric, "value": w2.value(ms2), "unit": w2.unit, "ms_per_step": ms2,
-                                "frac_of_hbm": w2.value(ms2) / peaks["hbm_gbs"], "roofline": r2,
-                                "config": w2.config(), "gpu_launches_per_step": int(l2)}
-                del w2
             except Exception as e:  # noqa: BLE001 - report, keep the headline
-                extras[name] = {"error": str(e)}
+                err = str(e)
+            # every rank takes the same collective steps: skip on all ranks if any failed to set up
+            if dist.sum(torch, 0.0 if err is None else 1.0) > 0:
+                extras[name] = {"error": err or "set-up failed on another rank"}
+                del w2
+                torch.cuda.empty_cache()
+                continue
+            ms2, prof2, l2 = measure(torch, K, lib, dist, w2, args.steps, args.warmup, flush, peaks)
+            r2, _ = roofline_for(w2, prof2, peaks, peak_kind)
+            extras[name] = {"metric": w2.metric, "value": w2.value(ms2), "unit": w2.unit, "ms_per_step": ms2,
+                            "frac_of_hbm": w2.value(ms2) / peaks["hbm_gbs"], "roofline": r2,
+                            "config": w2.config(), "gpu_launches_per_step": int(l2),
+                            "kernels": {k: {"ms_total": v[0], "launches": v[1]} for k, v in prof2.items()}}
+            del w2
+            torch.cuda.empty_cache()
         line["decode"] = extras
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu and hasattr(wl, "cpu_baseline"):
         try:

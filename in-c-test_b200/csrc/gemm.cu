@@ -2,7 +2,7 @@
 //     C[M x N] = A[M x K] . B[N x K]^T      (A, B bf16, K-major; fp32 accumulate)
 // i.e. y = x W^T for the row-major weights of the reference (KvlMlaBF16).
 //
-// Tile 128 x BN (BN = 256 or 192), K step 64; a 4-stage TMA ring (SW128 boxes),
+// Tile 128 x BN (BN = 256, 192 or 128), K step 64; a 4-stage TMA ring (SW128 boxes),
 // one thread issuing tcgen05.mma (M=128, N=BN, K=16), the accumulator
 // double-buffered in tensor memory so the epilogue of one tile overlaps the
 // MMAs of the next.  Epilogues:
@@ -12,6 +12,9 @@
 //              group is rotated as src/mla_prefill_streaming.c:15-29 does
 //              (pairs (2i, 2i+1) -> i, 32 + i) with cos/sin from a table of
 //              float2 [rows][32] (position = row); stored bf16.
+// Batched mode (GemmParams::batch > 1): independent products over a third
+// tensor-map coordinate, e.g. the per-head absorbed-decode products
+// q_nope . W_UK and mix . W_UV^T for a batch of sequences.
 //
 // Roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
 // warps 2-5 epilogue (TMEM subpartition = warp % 4).
@@ -54,7 +57,8 @@ using namespace gemmk;
 // One accumulator tile row per thread: TMEM lanes of this warp's quarter,
 // BN fp32 columns -> the epilogue's output row `row`, columns nb * BN + ...
 template <int BN, int EPI>
-__device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbase, int row, bool row_ok, int nb) {
+__device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbase, int row, bool row_ok, int nb,
+                                              long long cofs = 0) {
   if constexpr (EPI == EPI_QROPE) {
     // 64-column groups: a head is 192 columns (128 nope, then 64 rope), and
     // the tile edges (multiples of BN = 192 or 256) never split a rope group
@@ -102,7 +106,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
       if (row_ok && col0 < p.N) {
         const bool full = col0 + 32 <= p.N;
         if constexpr (EPI == EPI_F32) {
-          float *dst = static_cast<float *>(p.c) + static_cast<size_t>(row) * p.ldc + col0;
+          float *dst = static_cast<float *>(p.c) + cofs + static_cast<size_t>(row) * p.ldc + col0;
           if (full) {
 #pragma unroll
             for (int k = 0; k < 32; k += 4)
@@ -113,7 +117,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmParams &p, uint32_t tbas
               if (col0 + k < p.N) dst[k] = v[k];
           }
         } else {
-          __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(p.c) + static_cast<size_t>(row) * p.ldc + col0;
+          __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(p.c) + cofs + static_cast<size_t>(row) * p.ldc + col0;
           if (full) {
 #pragma unroll
             for (int k = 0; k < 32; k += 8) {
@@ -147,7 +151,9 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
   volatile int *abort = &B->abort;
   const int tiles_m = (p.M + kBM - 1) / kBM;
   const int tiles_n = (p.N + BN - 1) / BN;
-  const int tiles = tiles_m * tiles_n;
+  const int tiles_mn = tiles_m * tiles_n;
+  const bool batched = p.batch > 1;
+  const int tiles = tiles_mn * (batched ? p.batch : 1);
   const int ksteps = (p.K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -179,15 +185,21 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-        const int mb = tile % tiles_m, nb = tile / tiles_m;  // consecutive CTAs share the B tile
+        const int z = tile / tiles_mn, t = tile % tiles_mn;
+        const int mb = t % tiles_m, nb = t / tiles_m;  // consecutive CTAs share the B tile
         for (int ks = 0; ks < ksteps && ok; ++ks, ++it) {
           const uint32_t s = it % kStages;
           ok = mbar_wait(&B->empty[s], ((it / kStages) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
           if (!ok) break;
           uint8_t *st = smem + s * L::kStageBytes;
           mbar_arrive_expect_tx(&B->full[s], L::kStageBytes);
-          tma_load_2d(st, &p.tm_a, &B->full[s], ks * kBK, mb * kBM);
-          tma_load_2d(st + kABytes, &p.tm_b, &B->full[s], ks * kBK, nb * BN);
+          if (batched) {
+            tma_load_3d(st, &p.tm_a, &B->full[s], ks * kBK, mb * kBM, z);
+            tma_load_3d(st + kABytes, &p.tm_b, &B->full[s], ks * kBK, nb * BN, z);
+          } else {
+            tma_load_2d(st, &p.tm_a, &B->full[s], ks * kBK, mb * kBM);
+            tma_load_2d(st + kABytes, &p.tm_b, &B->full[s], ks * kBK, nb * BN);
+          }
         }
       }
       if (!ok) {
@@ -231,7 +243,8 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
     const uint32_t lane_base = static_cast<uint32_t>(32 * sub) << 16;
     uint32_t lt = 0;
     for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++lt) {
-      const int mb = tile % tiles_m, nb = tile / tiles_m;
+      const int z = tile / tiles_mn, t = tile % tiles_mn;
+      const int mb = t % tiles_m, nb = t / tiles_m;
       const uint32_t ab = lt & 1;
       bool bad = !mbar_wait(&B->acc_full[ab], (lt >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
       if (__any_sync(0xffffffffu, bad)) break;
@@ -239,7 +252,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
       const int row = mb * kBM + 32 * sub + lane;
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem + ab * 256 + lane_base;
-      epilogue_tile<BN, EPI>(p, tbase, row, row_ok, nb);
+      epilogue_tile<BN, EPI>(p, tbase, row, row_ok, nb, batched ? z * p.c_bstride : 0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&B->acc_empty[ab]);
@@ -413,7 +426,7 @@ static cudaError_t launch_gemm_t(const GemmParams &p, int sms, cudaStream_t stre
   cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        L::kSmem);
   if (e != cudaSuccess) return e;
-  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN);
+  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * (p.batch > 1 ? p.batch : 1);
   const int grid = tiles < sms ? tiles : sms;
   ProfScope ps(name, stream);
   gemm_bf16_tn_kernel<BN, EPI><<<grid, 192, L::kSmem, stream>>>(p);
@@ -423,7 +436,7 @@ static cudaError_t launch_gemm_t(const GemmParams &p, int sms, cudaStream_t stre
 cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream, const char *name) {
   if (!name) name = epi == EPI_QROPE ? "gemm_qrope" : "gemm_bf16";
   if (epi == EPI_QROPE) {
-    if (p.N % 192 != 0) return cudaErrorInvalidValue;
+    if (p.N % 192 != 0 || p.batch > 1) return cudaErrorInvalidValue;
     if (bn == 256) return launch_gemm_t<256, EPI_QROPE>(p, sms, stream, name);
     if (bn == 192) return launch_gemm_t<192, EPI_QROPE>(p, sms, stream, name);
     return cudaErrorInvalidValue;
@@ -434,6 +447,9 @@ cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStrea
   } else if (bn == 192) {
     if (epi == EPI_F32) return launch_gemm_t<192, EPI_F32>(p, sms, stream, name);
     if (epi == EPI_BF16) return launch_gemm_t<192, EPI_BF16>(p, sms, stream, name);
+  } else if (bn == 128) {
+    if (epi == EPI_F32) return launch_gemm_t<128, EPI_F32>(p, sms, stream, name);
+    if (epi == EPI_BF16) return launch_gemm_t<128, EPI_BF16>(p, sms, stream, name);
   }
   return cudaErrorInvalidValue;
 }
@@ -456,7 +472,7 @@ static cudaError_t launch_gemm_pair_t(const GemmParams &p, int sms, cudaStream_t
 
 // B's tensor map box must be {64, bn / 2} rows for the pair form.
 cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream, const char *name) {
-  if (bn != 256) return cudaErrorInvalidValue;
+  if (bn != 256 || p.batch > 1) return cudaErrorInvalidValue;
   if (!name) name = epi == EPI_QROPE ? "gemm_qrope" : "gemm_bf16";
   if (epi == EPI_QROPE) {
     if (p.N % 192 != 0) return cudaErrorInvalidValue;

@@ -18,6 +18,11 @@ struct GemmParams {
   int ldc;
   const float2 *rope_cs;  // EPI_QROPE: cos/sin table [M][32]
   uint32_t *err;
+  // batch > 1: `batch` independent products (1-SM kernel, EPI_F32/EPI_BF16):
+  // both tensor maps are 3D {K, rows, batch} (box {64, rows, 1}) and product z
+  // writes c + z * c_bstride (elements).  batch <= 1: 2D maps, one product.
+  int batch;
+  long long c_bstride;
 };
 
 // `name` labels the launch in the per-kernel profile (a string literal).

@@ -1188,23 +1188,154 @@ KVL_EXPORT int kvl_mla_merge_partials(float *d_out, float *d_lse, const float *d
 }
 
 // =================================================================== batched decode step
-static size_t step_ws_layout(const KvlMlaConfig &c, int B, size_t off[6]) {
+// Decode-step scratch: [0] q fp32 [B][NH][QD], [1] ka fp32 [B][R+DR], [2] qabs
+// fp32 [B][NH][R+DR], [3] mix fp32 [B][NH][R], [4] ho fp32 [B][NH*DV] (bf16 on
+// the tensor-core path), [5] x bf16 [B][H], [6] q_nope bf16 [NH][B][DN],
+// [7] W_UK^T bf16 [NH][R][DN], [8] mix bf16 [NH][B][R]; 256-byte aligned slots.
+static size_t step_ws_layout(const KvlMlaConfig &c, int B, size_t off[10]) {
   const size_t NH = c.num_heads, QD = c.qk_nope_dim + c.qk_rope_dim, R = c.kv_lora_rank, DR = c.qk_rope_dim;
-  const size_t DV = c.v_head_dim;
-  const size_t sz[5] = {B * NH * QD * 4, B * (R + DR) * 4, B * NH * (R + DR) * 4, B * NH * R * 4, B * NH * DV * 4};
+  const size_t DV = c.v_head_dim, DN = c.qk_nope_dim, H = c.hidden_size;
+  const size_t sz[9] = {B * NH * QD * 4, B * (R + DR) * 4, B * NH * (R + DR) * 4, B * NH * R * 4, B * NH * DV * 4,
+                        B * H * 2,       B * NH * DN * 2,  NH * R * DN * 2,        B * NH * R * 2};
   size_t o = 0;
-  for (int i = 0; i < 5; ++i) {
+  for (int i = 0; i < 9; ++i) {
     off[i] = o;
     o += (sz[i] + 255) & ~size_t(255);
   }
-  off[5] = o;
+  off[9] = o;
   return o;
 }
 
 KVL_EXPORT size_t kvl_mla_decode_step_workspace_bytes(const KvlMlaConfig *cfg, int batch) {
   if (!cfg || batch <= 0) return 0;
-  size_t off[6];
+  size_t off[10];
   return step_ws_layout(*cfg, batch, off);
+}
+
+// Batches of at least this many sequences run their projections as tcgen05
+// GEMMs (activations rounded to bf16); smaller ones use the per-token matvec
+// kernels, which read each weight once per 8 tokens.
+constexpr int kStepGemmBatch = 16;
+
+static bool step_gemm_ok(const KvlMlaConfig &c, const KvlMlaDeviceWeights &w, const float *d_out, const void *ws,
+                         int batch) {
+  const uintptr_t a = reinterpret_cast<uintptr_t>(w.q_proj) | reinterpret_cast<uintptr_t>(w.kv_a_proj) |
+                      reinterpret_cast<uintptr_t>(w.kv_b_proj) | reinterpret_cast<uintptr_t>(w.o_proj) |
+                      reinterpret_cast<uintptr_t>(d_out) | reinterpret_cast<uintptr_t>(ws);
+  // 16-byte tensor-map bases and row strides, 16-byte vector stores
+  return batch >= kStepGemmBatch && (a & 15) == 0 && c.hidden_size % 8 == 0 && c.qk_nope_dim % 8 == 0 &&
+         c.qk_rope_dim % 8 == 0 && c.kv_lora_rank % 8 == 0 && c.v_head_dim % 8 == 0;
+}
+
+// Tensor-core projections of one decode step (batch >= kStepGemmBatch).
+static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &w, const KvlMlaAttendPlan *plan,
+                            float *d_out, const float *d_x, uint16_t *d_kv, int64_t rows, const int64_t *d_row,
+                            const int *d_pos, int B, uint8_t *ws, const size_t *off, cudaStream_t s) {
+  const uint64_t H = cfg.hidden_size, NH = cfg.num_heads, DN = cfg.qk_nope_dim, DR = cfg.qk_rope_dim;
+  const uint64_t DV = cfg.v_head_dim, R = cfg.kv_lora_rank, QD = DN + DR, b = B;
+  float *q = reinterpret_cast<float *>(ws + off[0]);
+  float *ka = reinterpret_cast<float *>(ws + off[1]);
+  float *qabs = reinterpret_cast<float *>(ws + off[2]);
+  float *mix = reinterpret_cast<float *>(ws + off[3]);
+  uint16_t *hob = reinterpret_cast<uint16_t *>(ws + off[4]);
+  uint16_t *xb = reinterpret_cast<uint16_t *>(ws + off[5]);
+  uint16_t *qn = reinterpret_cast<uint16_t *>(ws + off[6]);
+  uint16_t *wukT = reinterpret_cast<uint16_t *>(ws + off[7]);
+  uint16_t *mixb = reinterpret_cast<uint16_t *>(ws + off[8]);
+  int dev = 0, sms = 148;
+  CK(cudaGetDevice(&dev));
+  CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+
+  CK(bf16_rne(xb, d_x, static_cast<long long>(b * H), s));
+  CK(wuk_transpose(wukT, w.kv_b_proj, static_cast<int>(NH), static_cast<int>(DN), static_cast<int>(DV),
+                   static_cast<int>(R), s));
+  GemmParams g;
+  memset(&g, 0, sizeof g);
+  g.err = plan->dp.err_word();  // a bounded wait that ran out: reported by kvl_mla_attend_check
+  // q = x Wq^T fp32 [B][NH*QD]; ka = x Wkva^T fp32 [B][R+DR]
+  if (!bf16_map(&g.tm_a, xb, H, b, H * 2, 128) || !bf16_map(&g.tm_b, w.q_proj, H, NH * QD, H * 2, 256)) {
+    set_err("decode step: tensor map (q_proj)");
+    return -1;
+  }
+  g.M = B;
+  g.N = static_cast<int>(NH * QD);
+  g.K = static_cast<int>(H);
+  g.c = q;
+  g.ldc = g.N;
+  CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_q"));
+  if (!bf16_map(&g.tm_b, w.kv_a_proj, H, R + DR, H * 2, 192)) {
+    set_err("decode step: tensor map (kv_a_proj)");
+    return -1;
+  }
+  g.N = static_cast<int>(R + DR);
+  g.c = ka;
+  g.ldc = g.N;
+  CK(launch_gemm(g, 192, EPI_F32, sms, s, "gemm_kva"));
+  CK(append_bf16(d_kv, 0, ka, w.kv_a_norm, B, static_cast<int>(R), static_cast<int>(DR), 0, cfg.rms_eps,
+                 cfg.rope_theta, nullptr, s, reinterpret_cast<const long long *>(d_row), d_pos));
+  CK(q_split(qn, qabs, q, B, static_cast<int>(NH), static_cast<int>(DN), static_cast<int>(DR), static_cast<int>(R),
+             cfg.rope_theta, d_pos, s));
+  // qabs[:, h, :R] = q_nope[:, h] . W_UK[h]   (NH products, M = B, N = R, K = DN)
+  {
+    const uint64_t ad[3] = {DN, b, NH}, as[2] = {DN * 2, b * DN * 2};
+    const uint64_t bd[3] = {DN, R, NH}, bs[2] = {DN * 2, R * DN * 2};
+    const uint32_t abox[3] = {64, 128, 1}, bbox[3] = {64, 256, 1};
+    if (!make_tmap_3d(&g.tm_a, qn, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, ad, as, abox, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_3d(&g.tm_b, wukT, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, bd, bs, bbox, CU_TENSOR_MAP_SWIZZLE_128B)) {
+      set_err("decode step: tensor map (absorb)");
+      return -1;
+    }
+  }
+  g.N = static_cast<int>(R);
+  g.K = static_cast<int>(DN);
+  g.c = qabs;
+  g.ldc = static_cast<int>(NH * (R + DR));
+  g.batch = static_cast<int>(NH);
+  g.c_bstride = static_cast<long long>(R + DR);
+  CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_absorb"));
+
+  AttendLaunch a;
+  a.rows = rows;
+  a.q = qabs;
+  a.out = mix;
+  a.kv = d_kv;
+  a.softmax_scale = 1.0f / sqrtf(static_cast<float>(QD));
+  if (attend_common(plan, a, static_cast<int>(NH), static_cast<int>(R), static_cast<int>(DR), s) != 0) return -1;
+
+  // ho[:, h, :] = mix[:, h] . W_UV[h]^T   (NH products, M = B, N = DV, K = R), bf16
+  CK(mix_heads_bf16(mixb, mix, B, static_cast<int>(NH), static_cast<int>(R), s));
+  {
+    const uint64_t ad[3] = {R, b, NH}, as[2] = {R * 2, b * R * 2};
+    const uint64_t bd[3] = {R, DV, NH}, bs[2] = {R * 2, (DN + DV) * R * 2};
+    const uint32_t abox[3] = {64, 128, 1}, bbox[3] = {64, 128, 1};
+    if (!make_tmap_3d(&g.tm_a, mixb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, ad, as, abox, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_3d(&g.tm_b, w.kv_b_proj + DN * R, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, bd, bs, bbox,
+                      CU_TENSOR_MAP_SWIZZLE_128B)) {
+      set_err("decode step: tensor map (v up-projection)");
+      return -1;
+    }
+  }
+  g.N = static_cast<int>(DV);
+  g.K = static_cast<int>(R);
+  g.c = hob;
+  g.ldc = static_cast<int>(NH * DV);
+  g.c_bstride = static_cast<long long>(DV);
+  CK(launch_gemm(g, 128, EPI_BF16, sms, s, "gemm_vup"));
+
+  // out = ho Wo^T fp32 [B][H]
+  g.batch = 0;
+  g.c_bstride = 0;
+  if (!bf16_map(&g.tm_a, hob, NH * DV, b, NH * DV * 2, 128) ||
+      !bf16_map(&g.tm_b, w.o_proj, NH * DV, H, NH * DV * 2, 256)) {
+    set_err("decode step: tensor map (o_proj)");
+    return -1;
+  }
+  g.N = static_cast<int>(H);
+  g.K = static_cast<int>(NH * DV);
+  g.c = d_out;
+  g.ldc = static_cast<int>(H);
+  CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_o"));
+  return 0;
 }
 
 KVL_EXPORT int kvl_mla_decode_step_bf16(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w,
@@ -1219,9 +1350,11 @@ KVL_EXPORT int kvl_mla_decode_step_bf16(const KvlMlaConfig *cfg, const KvlMlaDev
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int H = cfg->hidden_size, NH = cfg->num_heads, DN = cfg->qk_nope_dim, DR = cfg->qk_rope_dim;
   const int DV = cfg->v_head_dim, R = cfg->kv_lora_rank, QD = DN + DR;
-  size_t off[6];
+  size_t off[10];
   step_ws_layout(*cfg, batch, off);
   uint8_t *ws = static_cast<uint8_t *>(d_workspace);
+  if (step_gemm_ok(*cfg, *w, d_out, ws, batch))
+    return decode_step_gemm(*cfg, *w, plan, d_out, d_x, d_kv, rows, d_row, d_pos, batch, ws, off, s);
   float *q = reinterpret_cast<float *>(ws + off[0]);
   float *ka = reinterpret_cast<float *>(ws + off[1]);
   float *qabs = reinterpret_cast<float *>(ws + off[2]);

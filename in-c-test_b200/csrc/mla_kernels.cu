@@ -366,6 +366,81 @@ cudaError_t vup(float *ho, const float *mix, const uint16_t *kvb, int n, int NH,
   return cudaGetLastError();
 }
 
+// Tensor-core decode step helpers (batches of sequences).
+// q [t][h][DN + DR] fp32 -> qn [h][t][DN] bf16 (head-major: the A operand of
+// the per-head q_nope . W_UK product) and the rotated rope part of qabs
+// [t][h][R + DR] (the rope half of absorb_kernel, same arithmetic).
+__global__ void q_split_kernel(uint16_t *qn, float *qabs, const float *q, int NH, int DN, int DR, int R,
+                               float theta, const int *pos_of) {
+  const int h = blockIdx.x, t = blockIdx.y;
+  const float *qh = q + (static_cast<size_t>(t) * NH + h) * (DN + DR);
+  uint16_t *dn = qn + (static_cast<size_t>(h) * gridDim.y + t) * DN;
+  for (int d = threadIdx.x; d < DN; d += blockDim.x) dn[d] = __bfloat16_as_ushort(__float2bfloat16_rn(qh[d]));
+  float *dst = qabs + (static_cast<size_t>(t) * NH + h) * (R + DR);
+  const int half = DR / 2;
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    float lo, hi;
+    rope_pair(qh[DN + 2 * i], qh[DN + 2 * i + 1], i, DR, pos_of[t], theta, lo, hi);
+    dst[R + i] = lo;
+    dst[R + half + i] = hi;
+  }
+}
+
+cudaError_t q_split(uint16_t *qn, float *qabs, const float *q, int n, int NH, int DN, int DR, int R, float theta,
+                    const int *pos_of, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  ProfScope ps("q_split", s);
+  q_split_kernel<<<dim3(NH, n), 128, 0, s>>>(qn, qabs, q, NH, DN, DR, R, theta, pos_of);
+  return cudaGetLastError();
+}
+
+// mix [t][h][R] fp32 -> [h][t][R] bf16 (round to nearest even), the
+// head-major A operand of the per-head mix . W_UV^T product.
+__global__ void mix_heads_bf16_kernel(uint16_t *out, const float *mix, int n, int NH, int R) {
+  const long long total = static_cast<long long>(n) * NH * R;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const int r = static_cast<int>(i % R);
+    const long long tr = i / R;
+    const int h = static_cast<int>(tr % NH), t = static_cast<int>(tr / NH);
+    out[(static_cast<size_t>(h) * n + t) * R + r] = __bfloat16_as_ushort(__float2bfloat16_rn(mix[i]));
+  }
+}
+
+cudaError_t mix_heads_bf16(uint16_t *out, const float *mix, int n, int NH, int R, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const long long total = static_cast<long long>(n) * NH * R;
+  const int grid = static_cast<int>((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+  ProfScope ps("mix_heads_bf16", s);
+  mix_heads_bf16_kernel<<<grid, 256, 0, s>>>(out, mix, n, NH, R);
+  return cudaGetLastError();
+}
+
+// W_UK of every head (kv_b_proj rows h*(DN+DV) + d, d < DN: [d][R]) ->
+// wukT [h][R][DN], the K-major B operand of q_nope . W_UK.  32 x 32 tiles
+// through shared memory; grid (ceil(R/32), ceil(DN/32), NH), 32 x 8 threads.
+__global__ void wuk_transpose_kernel(uint16_t *wukT, const uint16_t *kvb, int DN, int DV, int R) {
+  __shared__ uint16_t tile[32][33];
+  const int h = blockIdx.z, r0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
+  const uint16_t *src = kvb + static_cast<size_t>(h) * (DN + DV) * R;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int d = d0 + i, r = r0 + threadIdx.x;
+    if (d < DN && r < R) tile[i][threadIdx.x] = src[static_cast<size_t>(d) * R + r];
+  }
+  __syncthreads();
+  uint16_t *dst = wukT + static_cast<size_t>(h) * R * DN;
+  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
+    const int r = r0 + i, d = d0 + threadIdx.x;
+    if (d < DN && r < R) dst[static_cast<size_t>(r) * DN + d] = tile[threadIdx.x][i];
+  }
+}
+
+cudaError_t wuk_transpose(uint16_t *wukT, const uint16_t *kvb, int NH, int DN, int DV, int R, cudaStream_t s) {
+  ProfScope ps("wuk_transpose", s);
+  wuk_transpose_kernel<<<dim3((R + 31) / 32, (DN + 31) / 32, NH), dim3(32, 8), 0, s>>>(wukT, kvb, DN, DV, R);
+  return cudaGetLastError();
+}
+
 // --------------------------------------------------------------------- Q8 helpers
 __global__ void quantize_rows_kernel(int8_t *q, float *scale, const float *x, int R) {
   extern __shared__ float sh[];
@@ -407,6 +482,7 @@ __global__ void bf16_rne_kernel(uint16_t *out, const float *x, long long n) {
 
 cudaError_t bf16_rne(uint16_t *out, const float *x, long long n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
+  ProfScope ps("bf16_rne", s);
   const int grid = static_cast<int>((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
   bf16_rne_kernel<<<grid, 256, 0, s>>>(out, x, n);
   return cudaGetLastError();

@@ -134,7 +134,11 @@ size_t kvl_mla_decode_step_workspace_bytes(const KvlMlaConfig *cfg, int batch);
 /* One absorbed decode step for `batch` sequences of a bf16 pool, all on the
  * device: projections, append of each token's row at d_row[b] (RoPE position
  * d_pos[b]), attend over the plan's ranges (which must already include the
- * appended rows), V up-projection and o_proj.  d_x/d_out [batch][H] fp32. */
+ * appended rows), V up-projection and o_proj.  d_x/d_out [batch][H] fp32.
+ * Batches of 16 or more with 16-byte aligned weights, d_out and workspace run
+ * the projections as tensor-core GEMMs on bf16-rounded activations; smaller
+ * batches use per-token matvecs.  A device-side error of any of the step's
+ * kernels is reported by kvl_mla_attend_check(plan, stream). */
 int kvl_mla_decode_step_bf16(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w,
                              const KvlMlaAttendPlan *plan, float *d_out, const float *d_x,
                              uint16_t *d_kv, int64_t rows, const int64_t *d_row,
