@@ -14,7 +14,10 @@
 //              float2 [rows][32] (position = row); stored bf16.
 // Batched mode (GemmParams::batch > 1): independent products over a third
 // tensor-map coordinate, e.g. the per-head absorbed-decode products
-// q_nope . W_UK and mix . W_UV^T for a batch of sequences.
+// q_nope . W_UK and mix . W_UV^T for a batch of sequences.  Split-K mode
+// (GemmParams::ksplit > 1): fp32 partial products of K ranges, summed by the
+// consumer (kv_a_proj, whose 576 output columns give too few tiles to fill
+// the SMs otherwise).
 //
 // Roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer,
 // warps 2-5 epilogue (TMEM subpartition = warp % 4).
@@ -153,8 +156,10 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
   const int tiles_n = (p.N + BN - 1) / BN;
   const int tiles_mn = tiles_m * tiles_n;
   const bool batched = p.batch > 1;
-  const int tiles = tiles_mn * (batched ? p.batch : 1);
+  const int nsplit = p.ksplit > 1 ? p.ksplit : 1;
+  const int tiles = tiles_mn * (batched ? p.batch : nsplit);
   const int ksteps = (p.K + kBK - 1) / kBK;
+  const int kc = ksteps / nsplit;  // K steps per split (the launcher checks divisibility)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -187,7 +192,8 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
       for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
         const int z = tile / tiles_mn, t = tile % tiles_mn;
         const int mb = t % tiles_m, nb = t / tiles_m;  // consecutive CTAs share the B tile
-        for (int ks = 0; ks < ksteps && ok; ++ks, ++it) {
+        const int kbeg = batched ? 0 : z * kc, kend = kbeg + kc;
+        for (int ks = kbeg; ks < kend && ok; ++ks, ++it) {
           const uint32_t s = it % kStages;
           ok = mbar_wait(&B->empty[s], ((it / kStages) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
           if (!ok) break;
@@ -219,7 +225,8 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
         ok = mbar_wait(&B->acc_empty[ab], ((lt >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
         if (!ok) break;
         tc_fence_after();
-        for (int ks = 0; ks < ksteps && ok; ++ks, ++it) {
+        const int kbeg = batched ? 0 : (tile / tiles_mn) * kc, kend = kbeg + kc;
+        for (int ks = kbeg; ks < kend && ok; ++ks, ++it) {
           const uint32_t s = it % kStages;
           ok = mbar_wait(&B->full[s], (it / kStages) & 1, abort, p.err, ERR_TIMEOUT_FULL);
           if (!ok) break;
@@ -229,7 +236,8 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
             mma_f16_ss(tmem + ab * 256, smem_desc(a_addr + kk * 32, 16, 1024, LAYOUT_SW128),
-                       smem_desc(b_addr + kk * 32, 16, 1024, LAYOUT_SW128), idesc, (ks | kk) ? 1u : 0u);
+                       smem_desc(b_addr + kk * 32, 16, 1024, LAYOUT_SW128), idesc,
+                       (ks != kbeg || kk) ? 1u : 0u);
           mma_commit(&B->empty[s]);
         }
         if (ok) mma_commit(&B->acc_full[ab]);
@@ -252,7 +260,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
       const int row = mb * kBM + 32 * sub + lane;
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem + ab * 256 + lane_base;
-      epilogue_tile<BN, EPI>(p, tbase, row, row_ok, nb, batched ? z * p.c_bstride : 0);
+      epilogue_tile<BN, EPI>(p, tbase, row, row_ok, nb, (batched || nsplit > 1) ? z * p.c_bstride : 0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&B->acc_empty[ab]);
@@ -426,7 +434,8 @@ static cudaError_t launch_gemm_t(const GemmParams &p, int sms, cudaStream_t stre
   cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        L::kSmem);
   if (e != cudaSuccess) return e;
-  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * (p.batch > 1 ? p.batch : 1);
+  const int tiles = ((p.M + kBM - 1) / kBM) * ((p.N + BN - 1) / BN) * (p.batch > 1 ? p.batch : 1) *
+                    (p.ksplit > 1 ? p.ksplit : 1);
   const int grid = tiles < sms ? tiles : sms;
   ProfScope ps(name, stream);
   gemm_bf16_tn_kernel<BN, EPI><<<grid, 192, L::kSmem, stream>>>(p);
@@ -435,6 +444,8 @@ static cudaError_t launch_gemm_t(const GemmParams &p, int sms, cudaStream_t stre
 
 cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream, const char *name) {
   if (!name) name = epi == EPI_QROPE ? "gemm_qrope" : "gemm_bf16";
+  if (p.ksplit > 1 && (p.batch > 1 || epi != EPI_F32 || ((p.K + kBK - 1) / kBK) % p.ksplit != 0))
+    return cudaErrorInvalidValue;
   if (epi == EPI_QROPE) {
     if (p.N % 192 != 0 || p.batch > 1) return cudaErrorInvalidValue;
     if (bn == 256) return launch_gemm_t<256, EPI_QROPE>(p, sms, stream, name);
@@ -472,7 +483,7 @@ static cudaError_t launch_gemm_pair_t(const GemmParams &p, int sms, cudaStream_t
 
 // B's tensor map box must be {64, bn / 2} rows for the pair form.
 cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream, const char *name) {
-  if (bn != 256 || p.batch > 1) return cudaErrorInvalidValue;
+  if (bn != 256 || p.batch > 1 || p.ksplit > 1) return cudaErrorInvalidValue;
   if (!name) name = epi == EPI_QROPE ? "gemm_qrope" : "gemm_bf16";
   if (epi == EPI_QROPE) {
     if (p.N % 192 != 0) return cudaErrorInvalidValue;
@@ -497,7 +508,9 @@ __global__ void rope_table_kernel(float2 *cs, int rows, int dim, float theta) {
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     const int pos = static_cast<int>(i / half), k = static_cast<int>(i % half);
     const double ang = static_cast<double>(pos) * inv_freq_s[k];
-    cs[i] = make_float2(static_cast<float>(cos(ang)), static_cast<float>(sin(ang)));
+    double sn, cn;
+    sincos(ang, &sn, &cn);
+    cs[i] = make_float2(static_cast<float>(cn), static_cast<float>(sn));
   }
 }
 

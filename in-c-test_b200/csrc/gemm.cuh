@@ -23,6 +23,9 @@ struct GemmParams {
   // writes c + z * c_bstride (elements).  batch <= 1: 2D maps, one product.
   int batch;
   long long c_bstride;
+  // ksplit > 1 (2D maps, EPI_F32, K steps divisible by ksplit): split-K, part z
+  // of the K range writes its fp32 partial product to c + z * c_bstride.
+  int ksplit;
 };
 
 // `name` labels the launch in the per-kernel profile (a string literal).

@@ -890,7 +890,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   GemmParams gq;
   memset(&gq, 0, sizeof gq);
   gq.err = err;
-  if (!bf16_map(&gq.tm_a, xb, H, s, H * 2, 128) || !bf16_map(&gq.tm_b, W.q, H, 16 * 192, H * 2, 256)) {
+  if (!bf16_map(&gq.tm_a, xb, H, s, H * 2, 128) || !bf16_map(&gq.tm_b, W.q, H, 16 * 192, H * 2, 128)) {
     set_err("prefill: tensor map (q_proj)");
     return -1;
   }
@@ -902,7 +902,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   gq.rope_cs = cs;
   CK(launch_rope_table(cs, S, 64, cfg.rope_theta, fk->s2));
   CK(cudaEventRecord(fk->rope, fk->s2));
-  CK(launch_gemm(gq, 256, EPI_QROPE, sms, fk->s2, "gemm_q"));
+  CK(launch_gemm_pair(gq, 256, EPI_QROPE, sms, fk->s2, "gemm_q"));
   CK(cudaEventRecord(fk->qdone, fk->s2));
 
   // caller's stream: kva = x Wkva^T, fp32 [S][576]
@@ -921,9 +921,9 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   CK(launch_gemm(g, 192, EPI_F32, sms, st, "gemm_kva"));
   // latent = rmsnorm(kva[:512]) * kv_a_norm, k_rope = rope(kva[512:]) -> pool [S][576] bf16
   CK(cudaStreamWaitEvent(st, fk->rope, 0));
-  CK(append_rows_bf16(pool, kva, W.kvan, cs, S, cfg.rms_eps, st));
+  CK(append_rows_bf16(pool, kva, 1, 0, W.kvan, cs, S, cfg.rms_eps, st));
   // kv = latent Wkvb^T, bf16 [S][16][256]
-  if (!bf16_map(&g.tm_a, pool, 512, s, 576 * 2, 128) || !bf16_map(&g.tm_b, W.kvb, 512, 4096, 512 * 2, 256)) {
+  if (!bf16_map(&g.tm_a, pool, 512, s, 576 * 2, 128) || !bf16_map(&g.tm_b, W.kvb, 512, 4096, 512 * 2, 128)) {
     set_err("prefill: tensor map (kv_b_proj)");
     return -1;
   }
@@ -931,7 +931,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   g.K = 512;
   g.c = kv;
   g.ldc = 4096;
-  CK(launch_gemm(g, 256, EPI_BF16, sms, st, "gemm_kvb"));
+  CK(launch_gemm_pair(g, 256, EPI_BF16, sms, st, "gemm_kvb"));
   CK(cudaStreamWaitEvent(st, fk->qdone, 0));  // join the second stream
   // causal attention -> o bf16 [S][16][128]
   FlashParams f;
@@ -1188,27 +1188,43 @@ KVL_EXPORT int kvl_mla_merge_partials(float *d_out, float *d_lse, const float *d
 }
 
 // =================================================================== batched decode step
-// Decode-step scratch: [0] q fp32 [B][NH][QD], [1] ka fp32 [B][R+DR], [2] qabs
-// fp32 [B][NH][R+DR], [3] mix fp32 [B][NH][R], [4] ho fp32 [B][NH*DV] (bf16 on
-// the tensor-core path), [5] x bf16 [B][H], [6] q_nope bf16 [NH][B][DN],
-// [7] W_UK^T bf16 [NH][R][DN], [8] mix bf16 [NH][B][R]; 256-byte aligned slots.
-static size_t step_ws_layout(const KvlMlaConfig &c, int B, size_t off[10]) {
+// Split-K parts of the decode-step projections on the tensor-core path: a
+// batch of B <= 256 tokens gives q_proj, kv_a_proj and o_proj only
+// 2 x (12, 3, 8) output tiles, so the K range is split to occupy the SMs.
+constexpr int kStepQSplit = 4, kStepKvaSplit = 8, kStepOSplit = 8;
+
+// Largest split <= want that divides ksteps.
+static int pick_split(int ksteps, int want) {
+  for (int s = want; s > 1; --s)
+    if (ksteps % s == 0) return s;
+  return 1;
+}
+
+// Decode-step scratch (256-byte aligned slots): [0] q fp32 [B][NH][QD]
+// (kStepQSplit partials on the tensor-core path), [1] ka fp32 [B][R+DR],
+// [2] qabs fp32 [B][NH][R+DR], [3] mix fp32 [B][NH][R], [4] ho fp32 [B][NH*DV]
+// (bf16 on the tensor-core path), [5] x bf16 [B][H], [6] q_nope bf16
+// [NH][B][DN], [7] W_UK^T bf16 [NH][R][DN], [8] mix bf16 [NH][B][R],
+// [9] kv_a partials [kStepKvaSplit][B][R+DR], [10] o_proj partials
+// [kStepOSplit][B][H].
+static size_t step_ws_layout(const KvlMlaConfig &c, int B, size_t off[12]) {
   const size_t NH = c.num_heads, QD = c.qk_nope_dim + c.qk_rope_dim, R = c.kv_lora_rank, DR = c.qk_rope_dim;
   const size_t DV = c.v_head_dim, DN = c.qk_nope_dim, H = c.hidden_size;
-  const size_t sz[9] = {B * NH * QD * 4, B * (R + DR) * 4, B * NH * (R + DR) * 4, B * NH * R * 4, B * NH * DV * 4,
-                        B * H * 2,       B * NH * DN * 2,  NH * R * DN * 2,        B * NH * R * 2};
+  const size_t sz[11] = {kStepQSplit * B * NH * QD * 4, B * (R + DR) * 4, B * NH * (R + DR) * 4, B * NH * R * 4,
+                         B * NH * DV * 4, B * H * 2, B * NH * DN * 2, NH * R * DN * 2, B * NH * R * 2,
+                         kStepKvaSplit * B * (R + DR) * 4, kStepOSplit * B * H * 4};
   size_t o = 0;
-  for (int i = 0; i < 9; ++i) {
+  for (int i = 0; i < 11; ++i) {
     off[i] = o;
     o += (sz[i] + 255) & ~size_t(255);
   }
-  off[9] = o;
+  off[11] = o;
   return o;
 }
 
 KVL_EXPORT size_t kvl_mla_decode_step_workspace_bytes(const KvlMlaConfig *cfg, int batch) {
   if (!cfg || batch <= 0) return 0;
-  size_t off[10];
+  size_t off[12];
   return step_ws_layout(*cfg, batch, off);
 }
 
@@ -1242,6 +1258,8 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   uint16_t *qn = reinterpret_cast<uint16_t *>(ws + off[6]);
   uint16_t *wukT = reinterpret_cast<uint16_t *>(ws + off[7]);
   uint16_t *mixb = reinterpret_cast<uint16_t *>(ws + off[8]);
+  float *ka_parts = reinterpret_cast<float *>(ws + off[9]);
+  float *o_parts = reinterpret_cast<float *>(ws + off[10]);
   int dev = 0, sms = 148;
   CK(cudaGetDevice(&dev));
   CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -1257,24 +1275,33 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
     set_err("decode step: tensor map (q_proj)");
     return -1;
   }
+  const int hsteps = static_cast<int>((H + 63) / 64);
   g.M = B;
   g.N = static_cast<int>(NH * QD);
   g.K = static_cast<int>(H);
   g.c = q;
   g.ldc = g.N;
+  g.ksplit = pick_split(hsteps, kStepQSplit);
+  g.c_bstride = static_cast<long long>(b * NH * QD);
+  const int q_parts = g.ksplit;
   CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_q"));
   if (!bf16_map(&g.tm_b, w.kv_a_proj, H, R + DR, H * 2, 192)) {
     set_err("decode step: tensor map (kv_a_proj)");
     return -1;
   }
   g.N = static_cast<int>(R + DR);
-  g.c = ka;
+  g.c = ka_parts;
   g.ldc = g.N;
+  g.ksplit = pick_split(hsteps, kStepKvaSplit);
+  g.c_bstride = static_cast<long long>(b * (R + DR));
   CK(launch_gemm(g, 192, EPI_F32, sms, s, "gemm_kva"));
+  CK(sum_parts(ka, ka_parts, g.ksplit, g.c_bstride, static_cast<long long>(b * (R + DR)), s));
+  g.ksplit = 0;
+  g.c_bstride = 0;
   CK(append_bf16(d_kv, 0, ka, w.kv_a_norm, B, static_cast<int>(R), static_cast<int>(DR), 0, cfg.rms_eps,
                  cfg.rope_theta, nullptr, s, reinterpret_cast<const long long *>(d_row), d_pos));
-  CK(q_split(qn, qabs, q, B, static_cast<int>(NH), static_cast<int>(DN), static_cast<int>(DR), static_cast<int>(R),
-             cfg.rope_theta, d_pos, s));
+  CK(q_split(qn, qabs, q, q_parts, static_cast<long long>(b * NH * QD), B, static_cast<int>(NH),
+             static_cast<int>(DN), static_cast<int>(DR), static_cast<int>(R), cfg.rope_theta, d_pos, s));
   // qabs[:, h, :R] = q_nope[:, h] . W_UK[h]   (NH products, M = B, N = R, K = DN)
   {
     const uint64_t ad[3] = {DN, b, NH}, as[2] = {DN * 2, b * DN * 2};
@@ -1332,9 +1359,12 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   }
   g.N = static_cast<int>(H);
   g.K = static_cast<int>(NH * DV);
-  g.c = d_out;
+  g.c = o_parts;
   g.ldc = static_cast<int>(H);
+  g.ksplit = pick_split(static_cast<int>((NH * DV + 63) / 64), kStepOSplit);
+  g.c_bstride = static_cast<long long>(b * H);
   CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_o"));
+  CK(sum_parts(d_out, o_parts, g.ksplit, g.c_bstride, static_cast<long long>(b * H), s));
   return 0;
 }
 
@@ -1350,7 +1380,7 @@ KVL_EXPORT int kvl_mla_decode_step_bf16(const KvlMlaConfig *cfg, const KvlMlaDev
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int H = cfg->hidden_size, NH = cfg->num_heads, DN = cfg->qk_nope_dim, DR = cfg->qk_rope_dim;
   const int DV = cfg->v_head_dim, R = cfg->kv_lora_rank, QD = DN + DR;
-  size_t off[10];
+  size_t off[12];
   step_ws_layout(*cfg, batch, off);
   uint8_t *ws = static_cast<uint8_t *>(d_workspace);
   if (step_gemm_ok(*cfg, *w, d_out, ws, batch))

@@ -125,14 +125,23 @@ cudaError_t gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int o
 // --------------------------------------------------------------------- rope / rmsnorm
 // src/mla_compressed_state.c:8-22: angle in double, cos/sin rounded to float,
 // rotation in float with separately rounded products.
-__device__ __forceinline__ void rope_pair(float a, float b, int i, int dim, int pos, float theta, float &lo,
-                                          float &hi) {
+__device__ __forceinline__ void rope_cos_sin(int i, int dim, int pos, float theta, float &c, float &s) {
   const double inv_freq = pow(static_cast<double>(theta), -(static_cast<double>(2 * i) / static_cast<double>(dim)));
   const double ang = static_cast<double>(pos) * inv_freq;
-  const float c = static_cast<float>(cos(ang));
-  const float s = static_cast<float>(sin(ang));
+  double sn, cn;
+  sincos(ang, &sn, &cn);
+  c = static_cast<float>(cn);
+  s = static_cast<float>(sn);
+}
+__device__ __forceinline__ void rope_rotate(float a, float b, float c, float s, float &lo, float &hi) {
   lo = __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
   hi = __fadd_rn(__fmul_rn(b, c), __fmul_rn(a, s));
+}
+__device__ __forceinline__ void rope_pair(float a, float b, int i, int dim, int pos, float theta, float &lo,
+                                          float &hi) {
+  float c, s;
+  rope_cos_sin(i, dim, pos, theta, c, s);
+  rope_rotate(a, b, c, s, lo, hi);
 }
 
 // RMSNorm of ka[0:R] into lat (shared memory), src/ops.c:76-83.
@@ -180,8 +189,10 @@ __global__ void append_bf16_kernel(uint16_t *kv, long long row0, const float *ka
 // rope_table_kernel with the same double-angle arithmetic as rope_pair.  The
 // same operations as append_bf16 (double sum of squares, float scale, float
 // rotation without contraction); only the order of the double sum differs.
-__global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, const uint16_t *norm_w,
-                                        const float2 *cs, int n, float eps) {
+// `ka` holds `parts` split-K partial rows (stride `part_stride` floats), added
+// in order 0, 1, ... to form the kv_a_proj row.
+__global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, int parts, long long part_stride,
+                                        const uint16_t *norm_w, const float2 *cs, int n, float eps) {
   constexpr int R = 512, DR = 64;
   const int warp = static_cast<int>((blockIdx.x * static_cast<unsigned>(blockDim.x) + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
@@ -192,6 +203,13 @@ __global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, const u
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     v[k] = reinterpret_cast<const float4 *>(kt)[lane + 32 * k];
+    for (int pp = 1; pp < parts; ++pp) {
+      const float4 u = reinterpret_cast<const float4 *>(kt + pp * part_stride)[lane + 32 * k];
+      v[k].x += u.x;
+      v[k].y += u.y;
+      v[k].z += u.z;
+      v[k].w += u.w;
+    }
     ss += static_cast<double>(v[k].x) * static_cast<double>(v[k].x);
     ss += static_cast<double>(v[k].y) * static_cast<double>(v[k].y);
     ss += static_cast<double>(v[k].z) * static_cast<double>(v[k].z);
@@ -217,7 +235,12 @@ __global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, const u
     *reinterpret_cast<uint2 *>(dst + c) = o;
   }
   // rope pair (2i, 2i+1) -> (i, 32 + i), i = lane
-  const float2 ab = reinterpret_cast<const float2 *>(kt + R)[lane];
+  float2 ab = reinterpret_cast<const float2 *>(kt + R)[lane];
+  for (int pp = 1; pp < parts; ++pp) {
+    const float2 u = reinterpret_cast<const float2 *>(kt + pp * part_stride + R)[lane];
+    ab.x += u.x;
+    ab.y += u.y;
+  }
   const float2 t = cs[static_cast<size_t>(warp) * (DR / 2) + lane];
   const float lo = __fsub_rn(__fmul_rn(ab.x, t.x), __fmul_rn(ab.y, t.y));
   const float hi = __fadd_rn(__fmul_rn(ab.y, t.x), __fmul_rn(ab.x, t.y));
@@ -225,11 +248,11 @@ __global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, const u
   dst[R + DR / 2 + lane] = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
 }
 
-cudaError_t append_rows_bf16(uint16_t *pool, const float *ka, const uint16_t *norm_w, const float2 *cs, int n,
-                             float eps, cudaStream_t s) {
+cudaError_t append_rows_bf16(uint16_t *pool, const float *ka, int parts, long long part_stride,
+                             const uint16_t *norm_w, const float2 *cs, int n, float eps, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   ProfScope ps("append_bf16", s);
-  append_rows_bf16_kernel<<<(n + 7) / 8, 256, 0, s>>>(pool, ka, norm_w, cs, n, eps);
+  append_rows_bf16_kernel<<<(n + 7) / 8, 256, 0, s>>>(pool, ka, parts, part_stride, norm_w, cs, n, eps);
   return cudaGetLastError();
 }
 
@@ -367,50 +390,114 @@ cudaError_t vup(float *ho, const float *mix, const uint16_t *kvb, int n, int NH,
 }
 
 // Tensor-core decode step helpers (batches of sequences).
-// q [t][h][DN + DR] fp32 -> qn [h][t][DN] bf16 (head-major: the A operand of
-// the per-head q_nope . W_UK product) and the rotated rope part of qabs
-// [t][h][R + DR] (the rope half of absorb_kernel, same arithmetic).
-__global__ void q_split_kernel(uint16_t *qn, float *qabs, const float *q, int NH, int DN, int DR, int R,
-                               float theta, const int *pos_of) {
-  const int h = blockIdx.x, t = blockIdx.y;
-  const float *qh = q + (static_cast<size_t>(t) * NH + h) * (DN + DR);
-  uint16_t *dn = qn + (static_cast<size_t>(h) * gridDim.y + t) * DN;
-  for (int d = threadIdx.x; d < DN; d += blockDim.x) dn[d] = __bfloat16_as_ushort(__float2bfloat16_rn(qh[d]));
-  float *dst = qabs + (static_cast<size_t>(t) * NH + h) * (R + DR);
-  const int half = DR / 2;
+// q: `parts` split-K partial products [part][t][h][DN + DR] fp32 (stride
+// part_stride floats), added in order -> qn [h][t][DN] bf16 (head-major: the A
+// operand of the per-head q_nope . W_UK product) and the rotated rope part of
+// qabs [t][h][R + DR] (the rope of absorb_kernel, same arithmetic; cos/sin
+// once per token).  One block per token.
+__global__ void q_split_kernel(uint16_t *qn, float *qabs, const float *q, int parts, long long part_stride, int n,
+                               int NH, int DN, int DR, int R, float theta, const int *pos_of) {
+  __shared__ float2 cs[128];
+  const int t = blockIdx.x, half = DR / 2, QD = DN + DR;
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    float c, sn;
+    rope_cos_sin(i, DR, pos_of[t], theta, c, sn);
+    cs[i] = make_float2(c, sn);
+  }
+  __syncthreads();
+  const float *qt = q + static_cast<size_t>(t) * NH * QD;
+  for (int idx = threadIdx.x; idx < NH * DN; idx += blockDim.x) {
+    const int h = idx / DN, d = idx % DN;
+    float v = qt[h * QD + d];
+    for (int pp = 1; pp < parts; ++pp) v += qt[pp * part_stride + h * QD + d];
+    qn[(static_cast<size_t>(h) * n + t) * DN + d] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  }
+  for (int idx = threadIdx.x; idx < NH * half; idx += blockDim.x) {
+    const int h = idx / half, i = idx % half;
+    const float *src = qt + h * QD + DN + 2 * i;
+    float a = src[0], b = src[1];
+    for (int pp = 1; pp < parts; ++pp) {
+      a += src[pp * part_stride];
+      b += src[pp * part_stride + 1];
+    }
     float lo, hi;
-    rope_pair(qh[DN + 2 * i], qh[DN + 2 * i + 1], i, DR, pos_of[t], theta, lo, hi);
+    rope_rotate(a, b, cs[i].x, cs[i].y, lo, hi);
+    float *dst = qabs + (static_cast<size_t>(t) * NH + h) * (R + DR);
     dst[R + i] = lo;
     dst[R + half + i] = hi;
   }
 }
 
-cudaError_t q_split(uint16_t *qn, float *qabs, const float *q, int n, int NH, int DN, int DR, int R, float theta,
-                    const int *pos_of, cudaStream_t s) {
+cudaError_t q_split(uint16_t *qn, float *qabs, const float *q, int parts, long long part_stride, int n, int NH,
+                    int DN, int DR, int R, float theta, const int *pos_of, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
+  if (DR / 2 > 128) return cudaErrorInvalidValue;
   ProfScope ps("q_split", s);
-  q_split_kernel<<<dim3(NH, n), 128, 0, s>>>(qn, qabs, q, NH, DN, DR, R, theta, pos_of);
+  q_split_kernel<<<n, 256, 0, s>>>(qn, qabs, q, parts, part_stride, n, NH, DN, DR, R, theta, pos_of);
+  return cudaGetLastError();
+}
+
+// dst[i] = src[i] + src[stride + i] + ... (parts terms, in order), fp32.
+__global__ void sum_parts_kernel(float *dst, const float *src, int parts, long long stride, long long n) {
+  const bool vec = ((n | stride) & 3) == 0 && ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) &
+                                               15) == 0;
+  const long long step = static_cast<long long>(gridDim.x) * blockDim.x;
+  if (vec) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n / 4; i += step) {
+      float4 v = reinterpret_cast<const float4 *>(src)[i];
+      for (int pp = 1; pp < parts; ++pp) {
+        const float4 u = reinterpret_cast<const float4 *>(src + pp * stride)[i];
+        v.x += u.x;
+        v.y += u.y;
+        v.z += u.z;
+        v.w += u.w;
+      }
+      reinterpret_cast<float4 *>(dst)[i] = v;
+    }
+  } else {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n; i += step) {
+      float v = src[i];
+      for (int pp = 1; pp < parts; ++pp) v += src[pp * stride + i];
+      dst[i] = v;
+    }
+  }
+}
+
+cudaError_t sum_parts(float *dst, const float *src, int parts, long long stride, long long n, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  const long long work = (n + 3) / 4;
+  const int grid = static_cast<int>((work + 255) / 256 < 148 * 8 ? (work + 255) / 256 : 148 * 8);
+  ProfScope ps("sum_parts", s);
+  sum_parts_kernel<<<grid, 256, 0, s>>>(dst, src, parts, stride, n);
   return cudaGetLastError();
 }
 
 // mix [t][h][R] fp32 -> [h][t][R] bf16 (round to nearest even), the
-// head-major A operand of the per-head mix . W_UV^T product.
+// head-major A operand of the per-head mix . W_UV^T product (R % 4 == 0).
 __global__ void mix_heads_bf16_kernel(uint16_t *out, const float *mix, int n, int NH, int R) {
-  const long long total = static_cast<long long>(n) * NH * R;
+  const int r4n = R / 4;
+  const long long total = static_cast<long long>(n) * NH * r4n;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int r = static_cast<int>(i % R);
-    const long long tr = i / R;
+    const int r4 = static_cast<int>(i % r4n);
+    const long long tr = i / r4n;
     const int h = static_cast<int>(tr % NH), t = static_cast<int>(tr / NH);
-    out[(static_cast<size_t>(h) * n + t) * R + r] = __bfloat16_as_ushort(__float2bfloat16_rn(mix[i]));
+    const float4 v = reinterpret_cast<const float4 *>(mix)[i];
+    uint2 o;
+    o.x = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v.x))) |
+          (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v.y))) << 16);
+    o.y = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v.z))) |
+          (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v.w))) << 16);
+    *reinterpret_cast<uint2 *>(out + (static_cast<size_t>(h) * n + t) * R + 4 * r4) = o;
   }
 }
 
 cudaError_t mix_heads_bf16(uint16_t *out, const float *mix, int n, int NH, int R, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
-  const long long total = static_cast<long long>(n) * NH * R;
-  const int grid = static_cast<int>((total + 255) / 256 < 148 * 16 ? (total + 255) / 256 : 148 * 16);
+  if (R % 4 != 0 || ((reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(mix)) & 15) != 0)
+    return cudaErrorInvalidValue;
+  const long long total = static_cast<long long>(n) * NH * (R / 4);
+  const int grid = static_cast<int>((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
   ProfScope ps("mix_heads_bf16", s);
   mix_heads_bf16_kernel<<<grid, 256, 0, s>>>(out, mix, n, NH, R);
   return cudaGetLastError();
@@ -475,15 +562,28 @@ cudaError_t dequant(float *out, const int8_t *q, const float *scale, long long r
 }
 
 __global__ void bf16_rne_kernel(uint16_t *out, const float *x, long long n) {
-  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
-       i += static_cast<long long>(gridDim.x) * blockDim.x)
-    out[i] = f32_to_bf16_rne_ref(x[i]);
+  const long long step = static_cast<long long>(gridDim.x) * blockDim.x;
+  const bool vec = (n & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out) & 7) == 0;
+  if (vec) {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n / 4; i += step) {
+      const float4 v = reinterpret_cast<const float4 *>(x)[i];
+      uint2 o;
+      o.x = static_cast<uint32_t>(f32_to_bf16_rne_ref(v.x)) | (static_cast<uint32_t>(f32_to_bf16_rne_ref(v.y)) << 16);
+      o.y = static_cast<uint32_t>(f32_to_bf16_rne_ref(v.z)) | (static_cast<uint32_t>(f32_to_bf16_rne_ref(v.w)) << 16);
+      reinterpret_cast<uint2 *>(out)[i] = o;
+    }
+  } else {
+    for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n; i += step)
+      out[i] = f32_to_bf16_rne_ref(x[i]);
+  }
 }
 
 cudaError_t bf16_rne(uint16_t *out, const float *x, long long n, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   ProfScope ps("bf16_rne", s);
-  const int grid = static_cast<int>((n + 255) / 256 < 148 * 16 ? (n + 255) / 256 : 148 * 16);
+  const long long work = (n + 3) / 4;
+  const int grid = static_cast<int>((work + 255) / 256 < 148 * 8 ? (work + 255) / 256 : 148 * 8);
   bf16_rne_kernel<<<grid, 256, 0, s>>>(out, x, n);
   return cudaGetLastError();
 }
