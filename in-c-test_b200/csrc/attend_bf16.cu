@@ -105,6 +105,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = B->tmem_base;
+  // Let a programmatically dependent merge grid get scheduled early (it waits
+  // for this grid's completion before reading anything).
+  asm volatile("griddepcontrol.launch_dependents;");
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer

@@ -122,9 +122,10 @@ int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long lo
 // first + p * step (each part is [16][R] floats and [16] lse values).
 // Grid (entry, head, 128-wide slice of R); each lane owns 4 consecutive output
 // elements and the block's warps split the entry's parts, so a part's slice is
-// one coalesced 512-byte read.  Every warp derives the normaliser itself from
-// the parts' lse values (few and cached), so the only block-wide step is the
-// final sum over warps.
+// one coalesced 512-byte read.  The block first turns the parts' lse values
+// into weights exp(lse - max) in shared memory (one pass of loads, block-wide
+// reductions); each warp then keeps four parts' slices in flight per step.
+constexpr int kMergeSmemParts = 256;
 __global__ void merge_partials_kernel(float *out, float *lse, const float *part_o,
                                       const float *part_lse, const MergeEntry *entries, int nh,
                                       int R, int uniform_parts) {
@@ -133,30 +134,67 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
                                : MergeEntry{(int)blockIdx.x, (int)blockIdx.x, uniform_parts, (int)gridDim.x};
   const int h = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  __shared__ float4 red[16][32];
+  __shared__ float4 red[8][32];
+  __shared__ float wts[kMergeSmemParts];
+  // Launched as a programmatic dependent of the attend kernel: wait until that
+  // grid has completed and its partials are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  __shared__ float rs[8];
   auto lse_of = [&](int q) { return part_lse[(size_t)(e.first + q * e.step) * nh + h]; };
   float m = -INFINITY;
-  for (int q = lane; q < e.count; q += 32) m = fmaxf(m, lse_of(q));
+  for (int q = threadIdx.x; q < e.count; q += blockDim.x) {
+    const float v = lse_of(q);
+    if (q < kMergeSmemParts) wts[q] = v;
+    m = fmaxf(m, v);
+  }
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  if (lane == 0) rs[warp] = m;
+  __syncthreads();
+  m = rs[0];
+  for (int i = 1; i < nw; ++i) m = fmaxf(m, rs[i]);
+  __syncthreads();
   float sum = 0.f;
-  for (int q = lane; q < e.count; q += 32) sum += expf(lse_of(q) - m);
+  for (int q = threadIdx.x; q < e.count; q += blockDim.x) {
+    const float w = expf((q < kMergeSmemParts ? wts[q] : lse_of(q)) - m);
+    if (q < kMergeSmemParts) wts[q] = w;
+    sum += w;
+  }
   for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  if (lane == 0) rs[warp] = sum;
+  __syncthreads();
+  sum = 0.f;
+  for (int i = 0; i < nw; ++i) sum += rs[i];
   if (lse && blockIdx.z == 0 && threadIdx.x == 0) lse[(size_t)e.seq * nh + h] = m + logf(sum);
   const int d0 = blockIdx.z * 128 + 4 * lane;
   const bool vec = (R & 3) == 0 && d0 + 3 < R &&
                    ((reinterpret_cast<uintptr_t>(part_o) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  auto weight = [&](int q) { return q < kMergeSmemParts ? wts[q] : expf(lse_of(q) - m); };
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-  for (int q = warp; q < e.count; q += nw) {
-    const float w = expf(lse_of(q) - m);
-    const float *src = part_o + ((size_t)(e.first + q * e.step) * nh + h) * R + d0;
-    if (vec) {
-      const float4 v = *reinterpret_cast<const float4 *>(src);
-      acc.x = fmaf(w, v.x, acc.x);
-      acc.y = fmaf(w, v.y, acc.y);
-      acc.z = fmaf(w, v.z, acc.z);
-      acc.w = fmaf(w, v.w, acc.w);
-    } else {
+  if (vec) {
+    for (int q0 = warp; q0 < e.count; q0 += 4 * nw) {
+      float4 v[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int q = q0 + j * nw;
+        v[j] = q < e.count ? *reinterpret_cast<const float4 *>(part_o + ((size_t)(e.first + q * e.step) * nh + h) * R + d0)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int q = q0 + j * nw;
+        if (q < e.count) {
+          const float w = weight(q);
+          acc.x = fmaf(w, v[j].x, acc.x);
+          acc.y = fmaf(w, v[j].y, acc.y);
+          acc.z = fmaf(w, v[j].z, acc.z);
+          acc.w = fmaf(w, v[j].w, acc.w);
+        }
+      }
+    }
+  } else {
+    for (int q = warp; q < e.count; q += nw) {
+      const float w = weight(q);
+      const float *src = part_o + ((size_t)(e.first + q * e.step) * nh + h) * R + d0;
       if (d0 < R) acc.x = fmaf(w, src[0], acc.x);
       if (d0 + 1 < R) acc.y = fmaf(w, src[1], acc.y);
       if (d0 + 2 < R) acc.z = fmaf(w, src[2], acc.z);
@@ -188,11 +226,32 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
 }
 
 // Warps per merge block: enough to split the largest part count (a few parts
-// per warp), at most 16.
+// per warp), at most 8, so that a merge block (~5 KB of shared memory) fits
+// beside a resident bf16 attend CTA and waits there for the attend grid to
+// complete.
 static int merge_warps(int max_count) {
   int w = 1;
-  while (w < 16 && 4 * w < max_count) w <<= 1;
+  while (w < 8 && 4 * w < max_count) w <<= 1;
   return w;
+}
+
+// Programmatic dependent launch: the merge grid may be scheduled while the
+// attend grid drains (its blocks wait in griddepcontrol.wait), which hides the
+// launch gap between the two.
+static cudaError_t merge_launch_pdl(float *out, float *lse, const float *part_o, const float *part_lse,
+                                    const MergeEntry *d_entries, int n_entries, int nh, int R,
+                                    cudaStream_t stream, int max_count) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(n_entries, nh, (R + 127) / 128);
+  cfg.blockDim = dim3(32 * merge_warps(max_count));
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, merge_partials_kernel, out, lse, part_o, part_lse, d_entries, nh, R, max_count);
 }
 
 cudaError_t launch_merge(float *out, float *lse, const float *part_o, const float *part_lse,
@@ -201,10 +260,7 @@ cudaError_t launch_merge(float *out, float *lse, const float *part_o, const floa
   // d_entries == nullptr selects the part-major layout with max_count parts per sequence.
   if (n_entries <= 0) return cudaSuccess;
   ProfScope ps("merge_partials", stream);
-  dim3 grid(n_entries, nh, (R + 127) / 128);
-  merge_partials_kernel<<<grid, 32 * merge_warps(max_count), 0, stream>>>(out, lse, part_o, part_lse, d_entries,
-                                                                          nh, R, max_count);
-  return cudaGetLastError();
+  return merge_launch_pdl(out, lse, part_o, part_lse, d_entries, n_entries, nh, R, stream, max_count);
 }
 
 // The merge launch without per-kernel timing (its events are created on
@@ -213,10 +269,7 @@ cudaError_t launch_merge_unprofiled(float *out, float *lse, const float *part_o,
                                    const MergeEntry *d_entries, int n_entries, int nh, int R,
                                    cudaStream_t stream, int max_count) {
   if (n_entries <= 0) return cudaSuccess;
-  dim3 grid(n_entries, nh, (R + 127) / 128);
-  merge_partials_kernel<<<grid, 32 * merge_warps(max_count), 0, stream>>>(out, lse, part_o, part_lse, d_entries,
-                                                                          nh, R, max_count);
-  return cudaGetLastError();
+  return merge_launch_pdl(out, lse, part_o, part_lse, d_entries, n_entries, nh, R, stream, max_count);
 }
 
 // ------------------------------------------------------------------ generic attend
