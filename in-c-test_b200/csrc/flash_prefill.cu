@@ -118,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int *abort = &B->abort;
   const int nq = (p.S + kT - 1) / kT;
-  const int n_items = nq * 16;
+  const int n_items = (nq - p.q_tile0) * 16;  // query tiles [q_tile0, nq), heaviest first
 
   if (threadIdx.x == 0) {
     mbar_init(&B->q_full, 1);
@@ -408,7 +408,8 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
 cudaError_t launch_flash_prefill(const FlashParams &p, int sms, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(flash_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) return e;
-  const int items = ((p.S + kT - 1) / kT) * 16;
+  const int items = ((p.S + kT - 1) / kT - p.q_tile0) * 16;
+  if (items <= 0 || p.q_tile0 < 0) return cudaErrorInvalidValue;
   const int grid = items < sms ? items : sms;
   ProfScope ps("flash_prefill", stream);
   flash_prefill_kernel<<<grid, kThreads, kSmem, stream>>>(p);

@@ -13,7 +13,8 @@ struct FlashParams {
   CUtensorMap tm_kv;   // kv [S][16][256] bf16 (k_nope 128 | v 128), 3-D box {64, 1, 128}
   CUtensorMap tm_kr;   // rotated k_rope: columns [kr_col, kr_col + 64) of a [S][ld] bf16 pool, box {64, 128}
   int kr_col;
-  int S;
+  int S;               // keys [0, S); queries [128 * q_tile0, S)
+  int q_tile0;
   float scale_log2;    // softmax scale * log2(e)
   __nv_bfloat16 *out;  // [S][16][128] bf16
   uint32_t *err;

@@ -12,6 +12,7 @@
 // GPU every compute call fails.
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <atomic>
 #include <cmath>
 #include <cstdarg>
@@ -114,10 +115,15 @@ struct DevW {
   const uint16_t *q, *kva, *kvan, *kvb, *o;
 };
 
+constexpr int kMaxPrefillChunks = 8;
+
 struct Ctx {
   int device = 0;
   int sms = 148;
   cudaStream_t stream = nullptr;
+  // host-buffer prefill: copy streams and per-chunk events (created on first use)
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  cudaEvent_t ev_in[kMaxPrefillChunks] = {}, ev_out[kMaxPrefillChunks] = {};
   std::mutex mu;
   DBuf x, q, ka, qabs, mix, ho, y, rowf, kvtmp;
   DBuf wq, wkva, wkvan, wkvb, wo;  // per-call weight upload
@@ -860,9 +866,18 @@ PrefillFork *get_fork(int device) {
 }
 
 // tcgen05 path; xb: bf16 tokens on the device.  Returns -1 with a message.
+// tcgen05 path over the query rows [r0, r1) of an S-row prompt (r0 % 128 == 0):
+// projections, append and kv_b of those rows, attention of those queries over
+// the keys [0, r1), o_proj into d_out rows [r0, r1).  xb: bf16 tokens on the
+// device; the RoPE table and the error word are set up by the call with
+// r0 == 0.  fork: run q_proj on a second stream beside the kv_a -> append ->
+// kv_b chain (whole-prompt calls); chunked calls stay on `st`.  Returns -1
+// with a message.
 int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, const uint16_t *xb, int S,
-                 uint8_t *ws, const PrefillWs &L, cudaStream_t st) {
-  const uint64_t H = cfg.hidden_size, s = S;
+                 uint8_t *ws, const PrefillWs &L, cudaStream_t st, int r0 = 0, int r1 = -1, bool fork = true) {
+  if (r1 < 0) r1 = S;
+  const uint64_t H = cfg.hidden_size, s = S, m = static_cast<uint64_t>(r1 - r0), R0 = static_cast<uint64_t>(r0);
+  const int M = r1 - r0;
   uint16_t *q = reinterpret_cast<uint16_t *>(ws + L.off[2]);
   float *kva = reinterpret_cast<float *>(ws + L.off[3]);
   uint16_t *pool = reinterpret_cast<uint16_t *>(ws + L.off[4]);
@@ -876,64 +891,72 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
     set_err("prefill: activations and weights must be 16-byte aligned");
     return -1;
   }
+  if (r0 < 0 || r0 % 128 != 0 || r1 <= r0 || r1 > S) {
+    set_err("prefill: invalid row range [%d, %d) of %d", r0, r1, S);
+    return -1;
+  }
   int dev = 0;
   CK(cudaGetDevice(&dev));
   PrefillFork *fk = get_fork(dev);
   if (!fk) return -1;
   std::lock_guard<std::mutex> lk(fk->mu);
-  CK(cudaMemsetAsync(err, 0, 4, st));
-  CK(cudaEventRecord(fk->fork, st));
-  CK(cudaStreamWaitEvent(fk->s2, fk->fork, 0));
+  cudaStream_t sq = fork ? fk->s2 : st;
+  if (r0 == 0) CK(cudaMemsetAsync(err, 0, 4, st));
+  if (fork) {
+    CK(cudaEventRecord(fk->fork, st));
+    CK(cudaStreamWaitEvent(fk->s2, fk->fork, 0));
+  }
 
-  // second stream: RoPE table, then q = x Wq^T with RoPE on each head's last
-  // 64 columns, bf16 [S][16][192]
+  // q = x Wq^T with RoPE on each head's last 64 columns, bf16 [S][16][192]
+  // (on the second stream when forked, after the RoPE table)
   GemmParams gq;
   memset(&gq, 0, sizeof gq);
   gq.err = err;
-  if (!bf16_map(&gq.tm_a, xb, H, s, H * 2, 128) || !bf16_map(&gq.tm_b, W.q, H, 16 * 192, H * 2, 128)) {
+  if (!bf16_map(&gq.tm_a, xb + R0 * H, H, m, H * 2, 128) || !bf16_map(&gq.tm_b, W.q, H, 16 * 192, H * 2, 128)) {
     set_err("prefill: tensor map (q_proj)");
     return -1;
   }
-  gq.M = S;
+  gq.M = M;
   gq.N = 16 * 192;
   gq.K = static_cast<int>(H);
-  gq.c = q;
+  gq.c = q + R0 * 16 * 192;
   gq.ldc = 16 * 192;
-  gq.rope_cs = cs;
-  CK(launch_rope_table(cs, S, 64, cfg.rope_theta, fk->s2));
-  CK(cudaEventRecord(fk->rope, fk->s2));
-  CK(launch_gemm_pair(gq, 256, EPI_QROPE, sms, fk->s2, "gemm_q"));
-  CK(cudaEventRecord(fk->qdone, fk->s2));
+  gq.rope_cs = cs + R0 * 32;
+  if (r0 == 0) CK(launch_rope_table(cs, S, 64, cfg.rope_theta, sq));
+  if (fork) CK(cudaEventRecord(fk->rope, sq));
+  CK(launch_gemm_pair(gq, 256, EPI_QROPE, sms, sq, "gemm_q"));
+  if (fork) CK(cudaEventRecord(fk->qdone, sq));
 
-  // caller's stream: kva = x Wkva^T, fp32 [S][576]
+  // kva = x Wkva^T, fp32 [S][576]
   GemmParams g;
   memset(&g, 0, sizeof g);
   g.err = err;
-  if (!bf16_map(&g.tm_a, xb, H, s, H * 2, 128) || !bf16_map(&g.tm_b, W.kva, H, 576, H * 2, 192)) {
+  if (!bf16_map(&g.tm_a, xb + R0 * H, H, m, H * 2, 128) || !bf16_map(&g.tm_b, W.kva, H, 576, H * 2, 192)) {
     set_err("prefill: tensor map (kv_a_proj)");
     return -1;
   }
-  g.M = S;
+  g.M = M;
   g.K = static_cast<int>(H);
   g.N = 576;
-  g.c = kva;
+  g.c = kva + R0 * 576;
   g.ldc = 576;
   CK(launch_gemm(g, 192, EPI_F32, sms, st, "gemm_kva"));
   // latent = rmsnorm(kva[:512]) * kv_a_norm, k_rope = rope(kva[512:]) -> pool [S][576] bf16
-  CK(cudaStreamWaitEvent(st, fk->rope, 0));
-  CK(append_rows_bf16(pool, kva, 1, 0, W.kvan, cs, S, cfg.rms_eps, st));
+  if (fork) CK(cudaStreamWaitEvent(st, fk->rope, 0));
+  CK(append_rows_bf16(pool + R0 * 576, kva + R0 * 576, 1, 0, W.kvan, cs + R0 * 32, M, cfg.rms_eps, st));
   // kv = latent Wkvb^T, bf16 [S][16][256]
-  if (!bf16_map(&g.tm_a, pool, 512, s, 576 * 2, 128) || !bf16_map(&g.tm_b, W.kvb, 512, 4096, 512 * 2, 128)) {
+  if (!bf16_map(&g.tm_a, pool + R0 * 576, 512, m, 576 * 2, 128) ||
+      !bf16_map(&g.tm_b, W.kvb, 512, 4096, 512 * 2, 128)) {
     set_err("prefill: tensor map (kv_b_proj)");
     return -1;
   }
   g.N = 4096;
   g.K = 512;
-  g.c = kv;
+  g.c = kv + R0 * 4096;
   g.ldc = 4096;
   CK(launch_gemm_pair(g, 256, EPI_BF16, sms, st, "gemm_kvb"));
-  CK(cudaStreamWaitEvent(st, fk->qdone, 0));  // join the second stream
-  // causal attention -> o bf16 [S][16][128]
+  if (fork) CK(cudaStreamWaitEvent(st, fk->qdone, 0));  // join the second stream
+  // causal attention of the queries [r0, r1) over the keys [0, r1) -> o bf16 [S][16][128]
   FlashParams f;
   memset(&f, 0, sizeof f);
   {
@@ -948,20 +971,22 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
     }
   }
   f.kr_col = 512;
-  f.S = S;
+  f.S = r1;
+  f.q_tile0 = r0 / 128;
   f.scale_log2 = (1.0f / sqrtf(192.0f)) * 1.4426950408889634f;
   f.out = reinterpret_cast<__nv_bfloat16 *>(o);
   f.err = err;
   CK(launch_flash_prefill(f, sms, st));
   // out = o Wo^T, fp32 [S][H]
   // (CTA-pair GEMM: 256 x 256 tiles, each CTA of a pair loads 128 rows of Wo)
-  if (!bf16_map(&g.tm_a, o, 2048, s, 2048 * 2, 128) || !bf16_map(&g.tm_b, W.o, 2048, H, 2048 * 2, 128)) {
+  if (!bf16_map(&g.tm_a, o + R0 * 2048, 2048, m, 2048 * 2, 128) ||
+      !bf16_map(&g.tm_b, W.o, 2048, H, 2048 * 2, 128)) {
     set_err("prefill: tensor map (o_proj)");
     return -1;
   }
   g.N = static_cast<int>(H);
   g.K = 2048;
-  g.c = d_out;
+  g.c = d_out + R0 * H;
   g.ldc = static_cast<int>(H);
   g.rope_cs = nullptr;
   CK(launch_gemm_pair(g, 256, EPI_F32, sms, st, "gemm_o"));
@@ -970,6 +995,17 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
 
 }  // namespace
 }  // namespace kvl
+
+// Chunks of the host-buffer prefill pipeline (whole multiples of 128 rows).
+// Measured at S = 4096 on one B200 (PCIe: 0.61 ms each way, full duplex):
+// 1 chunk 1.48 ms, 2 chunks 1.21 ms, 4 chunks 1.02 ms, 8 chunks 1.32 ms per
+// call -- smaller chunks overlap more copy time but run the GEMMs and the
+// causal attention on fewer SMs.
+static int prefill_chunks(int seq_len) {
+  if (seq_len >= 2048) return 4;
+  if (seq_len >= 1024) return 2;
+  return 1;
+}
 
 // Reference: src/mla_prefill_streaming.c:78-206 (validation :80-85).
 KVL_EXPORT int kvl_mla_prefill_bf16(float *out, const float *x, int seq_len, const KvlMlaConfig *cfg,
@@ -994,6 +1030,56 @@ KVL_EXPORT int kvl_mla_prefill_bf16(float *out, const float *x, int seq_len, con
   }
   uint8_t *ws = c->kvtmp.as<uint8_t>();
   float *xf = reinterpret_cast<float *>(ws + L.off[0]);
+  const int nch = fast_prefill_shape(*cfg) ? prefill_chunks(seq_len) : 1;
+  if (nch > 1) {
+    // Chunked pipeline: the H2D copy of chunk i+1 and the D2H copy of chunk
+    // i-1 run on their own streams while chunk i computes (its queries attend
+    // the keys of every chunk before it, which are already on the device).
+    if (!c->copy_in) {
+      if (cudaStreamCreateWithFlags(&c->copy_in, cudaStreamNonBlocking) != cudaSuccess ||
+          cudaStreamCreateWithFlags(&c->copy_out, cudaStreamNonBlocking) != cudaSuccess) {
+        set_err("prefill: cannot create copy streams");
+        return -1;
+      }
+      for (int i = 0; i < kMaxPrefillChunks; ++i)
+        if (cudaEventCreateWithFlags(&c->ev_in[i], cudaEventDisableTiming) != cudaSuccess ||
+            cudaEventCreateWithFlags(&c->ev_out[i], cudaEventDisableTiming) != cudaSuccess) {
+          set_err("prefill: cannot create copy events");
+          return -1;
+        }
+    }
+    const int rows = ((seq_len + nch - 1) / nch + 127) / 128 * 128;
+    uint16_t *xb = reinterpret_cast<uint16_t *>(ws + L.off[1]);
+    float *y = c->y.as<float>();
+    // the weights were staged on c->stream: the copies and kernels below follow it
+    CK(cudaEventRecord(c->ev_out[0], c->stream));
+    CK(cudaStreamWaitEvent(c->copy_in, c->ev_out[0], 0));
+    for (int i = 0, r0 = 0; r0 < seq_len; ++i, r0 += rows) {
+      const size_t n = static_cast<size_t>(std::min(seq_len, r0 + rows) - r0) * H;
+      CK(cudaMemcpyAsync(xf + static_cast<size_t>(r0) * H, x + static_cast<size_t>(r0) * H, n * 4,
+                         cudaMemcpyHostToDevice, c->copy_in));
+      CK(cudaEventRecord(c->ev_in[i], c->copy_in));
+    }
+    for (int i = 0, r0 = 0; r0 < seq_len; ++i, r0 += rows) {
+      const int r1 = std::min(seq_len, r0 + rows);
+      const size_t off = static_cast<size_t>(r0) * H, n = static_cast<size_t>(r1 - r0) * H;
+      CK(cudaStreamWaitEvent(c->stream, c->ev_in[i], 0));
+      CK(f32_to_bf16(xb + off, xf + off, static_cast<long long>(n), c->stream));
+      if (prefill_fast(c->sms, *cfg, W, y, xb, seq_len, ws, L, c->stream, r0, r1, false) != 0) return -1;
+      CK(cudaEventRecord(c->ev_out[i], c->stream));
+      CK(cudaStreamWaitEvent(c->copy_out, c->ev_out[i], 0));
+      CK(cudaMemcpyAsync(out + off, y + off, n * 4, cudaMemcpyDeviceToHost, c->copy_out));
+    }
+    uint32_t err = 0;
+    CK(cudaMemcpyAsync(&err, ws + L.off[8], 4, cudaMemcpyDeviceToHost, c->stream));
+    CK(cudaStreamSynchronize(c->stream));
+    CK(cudaStreamSynchronize(c->copy_out));
+    if (err != 0) {
+      set_err("prefill kernel reported device error 0x%x", err);
+      return -1;
+    }
+    return 0;
+  }
   CK(cudaMemcpyAsync(xf, x, s * H * 4, cudaMemcpyHostToDevice, c->stream));
   int rc;
   if (fast_prefill_shape(*cfg)) {

@@ -3,10 +3,12 @@ reference's own streaming prefill (src/mla_prefill_streaming.c:78-206, compiled
 from its sources into oracle/_ref) on seeded inputs.
 
 Covers the edges of the tiled path: a single token, lengths one short of / one
-past a 128-token tile, a length that is not a multiple of the tile, a hidden
-size whose K tail and output-column tail are not multiples of the 64-wide K
-step or the 256-wide N tile, and the device entry point (`kvl_mla_prefill_dev`)
-against the host one.  Tolerance: rel-L2 <= 1e-2, max-abs <= 2e-2.
+past a 128-token tile, a length that is not a multiple of the tile, the host
+entry's chunked copy/compute pipeline (2 and 4 chunks, a ragged last chunk),
+a hidden size whose K tail and output-column tail are not multiples of the
+64-wide K step or the 256-wide N tile, and the device entry point
+(`kvl_mla_prefill_dev`) against the host one.  Tolerance: rel-L2 <= 1e-2,
+max-abs <= 2e-2.
 """
 from __future__ import annotations
 
@@ -46,7 +48,7 @@ def _ref_prefill(ref, shape, x, w):
     return ref.prefill(x, cfg_of(*shape), w.arrays)
 
 
-@pytest.mark.parametrize("Sq", [1, 2, 127, 128, 129, 1000, 2048])
+@pytest.mark.parametrize("Sq", [1, 2, 127, 128, 129, 1000, 1100, 2048, 4100])
 def test_fast_prefill_lengths(K, S, ref, torch_cuda, Sq):
     shape = _shape()
     cfg, w, x = _setup(K, S, shape, Sq, 101 + Sq)
@@ -68,12 +70,14 @@ def test_fast_prefill_hidden_tails(K, S, ref, torch_cuda, H):
     assert_close(out, _ref_prefill(ref, shape, x, w), what=f"fast prefill H={H}")
 
 
-def test_device_entry_matches_host_entry(K, S, torch_cuda):
-    """kvl_mla_prefill_dev (device bf16 x, device weights, caller workspace) gives the
-    host entry's result on the same inputs: both run the same kernels."""
+@pytest.mark.parametrize("Sq", [513, 1100, 2048, 4100])
+def test_device_entry_matches_host_entry(K, S, torch_cuda, Sq):
+    """kvl_mla_prefill_dev (device bf16 x, device weights, caller workspace, one
+    pass over the prompt) gives the host entry's result on the same inputs, bit
+    for bit, also where the host entry pipelines its copies over 2 or 4 row
+    chunks (1100, 2048, 4100 tokens): the same kernels, per row, per query tile."""
     torch = torch_cuda
     shape = _shape()
-    Sq = 513
     cfg, w, x = _setup(K, S, shape, Sq, 55)
     lib = K.load()
     host = np.zeros_like(x)
