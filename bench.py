@@ -276,7 +276,7 @@ class Prefill:
     bound = "tensor"
     # dram__bytes_read.sum + dram__bytes_write.sum per launch, one ncu capture
     # (profiles/flash_prefill_config2.txt, profiles/gemm_prefill_config2.txt)
-    ncu_traffic = {"flash_prefill": 59.574528e6 + 3.482624e6, "gemm_q": 30.442752e6 + 0.157952e6}
+    ncu_traffic = {"flash_prefill": 59.550720e6 + 3.057408e6, "gemm_q": 30.439168e6 + 0.093440e6}
 
     def __init__(self, torch, K, lib, dist, S=4096, theta=50000.0):
         self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
@@ -362,7 +362,7 @@ class DecodeQ8:
     unit = "GB/s"
     bound = "hbm"
     # one ncu capture of the attend kernel (profiles/mla_attend_q8_config3.txt)
-    ncu_traffic = {"mla_attend_q8": 193.199872e6 + 5.985024e6}
+    ncu_traffic = {"mla_attend_q8": 193.175808e6 + 5.735936e6}
 
     def __init__(self, torch, K, lib, dist):
         import kvl_b200.synth as SY
@@ -408,7 +408,7 @@ class DecodeLong:
     unit = "GB/s"
     bound = "hbm"
     # one ncu capture of the attend kernel at world size 1 (profiles/mla_attend_bf16_config5.txt)
-    ncu_traffic = {"mla_attend_bf16": 151.11936e6 + 4.021504e6}
+    ncu_traffic = {"mla_attend_bf16": 151.119360e6 + 4.251904e6}
 
     def __init__(self, torch, K, lib, dist, L=131072):
         self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
@@ -508,6 +508,9 @@ class DecodeStack:
         self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         self.units = self.LAYERS * self.rows * 1152  # attend bytes this rank reads per step
         self.total_bytes = self.LAYERS * seqs * L * 1152
+        # per-launch DRAM traffic scaled from the config-5 capture of the same kernel
+        # (profiles/mla_attend_bf16_config5.txt: 155.37 MB for 131,072 rows) by rows
+        self.ncu_traffic = {"mla_attend_bf16": DecodeLong.ncu_traffic["mla_attend_bf16"] / 131072 * self.rows}
 
     def step(self):
         s = self.torch.cuda.current_stream().cuda_stream
@@ -623,6 +626,7 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="prefill")
     ap.add_argument("--no-extras", action="store_true", help="skip the decode sub-measurements")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the end-to-end (host buffer) leg")
     args = ap.parse_args()
     dist = Dist()
 
@@ -652,7 +656,7 @@ def main():
         "config": wl.config(), "roofline": roof, "gpu_launches": int(launches) * args.steps,
         "kernels": {k: {"ms_total": v[0], "launches": v[1]} for k, v in prof.items()}, "clocks": clk,
     }
-    if hasattr(wl, "e2e"):
+    if hasattr(wl, "e2e") and not args.no_e2e:
         line["e2e"] = wl.e2e(max(2, args.steps // 2), 1)
     if not args.no_extras and args.workload == "prefill":
         extras = {}

@@ -124,7 +124,7 @@ int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long lo
 // elements and the block's warps split the entry's parts, so a part's slice is
 // one coalesced 512-byte read.  The block first turns the parts' lse values
 // into weights exp(lse - max) in shared memory (one pass of loads, block-wide
-// reductions); each warp then keeps four parts' slices in flight per step.
+// reductions); each warp then keeps eight parts' slices in flight per step.
 constexpr int kMergeSmemParts = 256;
 __global__ void merge_partials_kernel(float *out, float *lse, const float *part_o,
                                       const float *part_lse, const MergeEntry *entries, int nh,
@@ -171,16 +171,16 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
   auto weight = [&](int q) { return q < kMergeSmemParts ? wts[q] : expf(lse_of(q) - m); };
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (vec) {
-    for (int q0 = warp; q0 < e.count; q0 += 4 * nw) {
-      float4 v[4];
+    for (int q0 = warp; q0 < e.count; q0 += 8 * nw) {
+      float4 v[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < 8; ++j) {
         const int q = q0 + j * nw;
         v[j] = q < e.count ? *reinterpret_cast<const float4 *>(part_o + ((size_t)(e.first + q * e.step) * nh + h) * R + d0)
                            : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < 8; ++j) {
         const int q = q0 + j * nw;
         if (q < e.count) {
           const float w = weight(q);
