@@ -473,7 +473,7 @@ class DecodeStack:
     bound = "hbm"
     LAYERS = 27
 
-    def __init__(self, torch, K, lib, dist, seqs=256, L=32768, mem_frac=0.7):
+    def __init__(self, torch, K, lib, dist, seqs=256, L=32768, mem_frac=0.85):
         import kvl_b200.parallel as PAR
         self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
         self.L = L
