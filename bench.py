@@ -424,12 +424,14 @@ class DecodeLong:
         gq = torch.Generator(device=dev)
         gq.manual_seed(55)
         self.q = dev_bf16(torch, (1, 16, 576), 0.1, gq, dev).float()
-        self.o = torch.empty((1, 16, 512), device=dev)
-        self.lse = torch.empty((1, 16), device=dev)
+        # this rank's (o, lse) as one packed record [16][512] ++ [16], so one
+        # all-gather moves both
+        self.rec = torch.empty((16 * 512 + 16,), device=dev)
+        self.o = self.rec[:16 * 512].view(1, 16, 512)
+        self.lse = self.rec[16 * 512:].view(1, 16)
         self.plan = K.AttendPlan([self.n], [0], 16, 512)
         if dist.world > 1:
-            self.go = torch.empty((dist.world, 1, 16, 512), device=dev)
-            self.gl = torch.empty((dist.world, 1, 16), device=dev)
+            self.grec = torch.empty((dist.world, 16 * 512 + 16), device=dev)
             self.final = torch.empty((1, 16, 512), device=dev)
             self.final_lse = torch.empty((1, 16), device=dev)
         self.units = self.n * 1152
@@ -442,11 +444,9 @@ class DecodeLong:
         if rc != 0:
             raise RuntimeError(self.K.last_error())
         if self.dist.world > 1:
-            d = self.dist.pg
-            d.all_gather_into_tensor(self.go, self.o)
-            d.all_gather_into_tensor(self.gl, self.lse)
-            rc = self.lib.kvl_mla_merge_partials(self.final.data_ptr(), self.final_lse.data_ptr(), self.go.data_ptr(),
-                                                 self.gl.data_ptr(), self.dist.world, 1, 16, 512, s)
+            self.dist.pg.all_gather_into_tensor(self.grec, self.rec)
+            rc = self.lib.kvl_mla_merge_packed(self.final.data_ptr(), self.final_lse.data_ptr(), self.grec.data_ptr(),
+                                               self.dist.world, 1, 16, 512, s)
             if rc != 0:
                 raise RuntimeError(self.K.last_error())
 
@@ -455,7 +455,7 @@ class DecodeLong:
 
     def config(self):
         return {"workload": "config 5: long-context decode attend, L=131072", "rows_per_rank": self.n,
-                "parallelism": f"split-KV x{self.dist.world} + NCCL all-gather merge"}
+                "parallelism": f"split-KV x{self.dist.world} + one NCCL all-gather of packed (o, lse) + merge"}
 
 
 class DecodeStack:

@@ -126,9 +126,12 @@ int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long lo
 // into weights exp(lse - max) in shared memory (one pass of loads, block-wide
 // reductions); each warp then keeps eight parts' slices in flight per step.
 constexpr int kMergeSmemParts = 256;
+// Part p lives at part_o + (p / pb) * rec_o + (p % pb) * nh * R (and the lse
+// likewise with rec_l, nh): pb = 1, rec_o = nh * R, rec_l = nh for the
+// part-major arrays; pb = batch for packed records [batch][nh][R] ++ [batch][nh].
 __global__ void merge_partials_kernel(float *out, float *lse, const float *part_o,
                                       const float *part_lse, const MergeEntry *entries, int nh,
-                                      int R, int uniform_parts) {
+                                      int R, int uniform_parts, int pb, long long rec_o, long long rec_l) {
   // entries == nullptr: sequence b combines parts b, b + B, b + 2B, ... (part-major layout)
   const MergeEntry e = entries ? entries[blockIdx.x]
                                : MergeEntry{(int)blockIdx.x, (int)blockIdx.x, uniform_parts, (int)gridDim.x};
@@ -140,7 +143,15 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
   // grid has completed and its partials are visible.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   __shared__ float rs[8];
-  auto lse_of = [&](int q) { return part_lse[(size_t)(e.first + q * e.step) * nh + h]; };
+  auto part_of = [&](int q) { return e.first + q * e.step; };
+  auto lse_of = [&](int q) {
+    const int p = part_of(q);
+    return part_lse[(p / pb) * rec_l + (size_t)(p % pb) * nh + h];
+  };
+  auto o_of = [&](int q) {
+    const int p = part_of(q);
+    return part_o + (p / pb) * rec_o + ((size_t)(p % pb) * nh + h) * R;
+  };
   float m = -INFINITY;
   for (int q = threadIdx.x; q < e.count; q += blockDim.x) {
     const float v = lse_of(q);
@@ -166,7 +177,7 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
   for (int i = 0; i < nw; ++i) sum += rs[i];
   if (lse && blockIdx.z == 0 && threadIdx.x == 0) lse[(size_t)e.seq * nh + h] = m + logf(sum);
   const int d0 = blockIdx.z * 128 + 4 * lane;
-  const bool vec = (R & 3) == 0 && d0 + 3 < R &&
+  const bool vec = (R & 3) == 0 && d0 + 3 < R && (rec_o & 3) == 0 &&
                    ((reinterpret_cast<uintptr_t>(part_o) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
   auto weight = [&](int q) { return q < kMergeSmemParts ? wts[q] : expf(lse_of(q) - m); };
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -176,8 +187,7 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const int q = q0 + j * nw;
-        v[j] = q < e.count ? *reinterpret_cast<const float4 *>(part_o + ((size_t)(e.first + q * e.step) * nh + h) * R + d0)
-                           : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[j] = q < e.count ? *reinterpret_cast<const float4 *>(o_of(q) + d0) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -194,7 +204,7 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
   } else {
     for (int q = warp; q < e.count; q += nw) {
       const float w = weight(q);
-      const float *src = part_o + ((size_t)(e.first + q * e.step) * nh + h) * R + d0;
+      const float *src = o_of(q) + d0;
       if (d0 < R) acc.x = fmaf(w, src[0], acc.x);
       if (d0 + 1 < R) acc.y = fmaf(w, src[1], acc.y);
       if (d0 + 2 < R) acc.z = fmaf(w, src[2], acc.z);
@@ -240,7 +250,10 @@ static int merge_warps(int max_count) {
 // launch gap between the two.
 static cudaError_t merge_launch_pdl(float *out, float *lse, const float *part_o, const float *part_lse,
                                     const MergeEntry *d_entries, int n_entries, int nh, int R,
-                                    cudaStream_t stream, int max_count) {
+                                    cudaStream_t stream, int max_count, int pb = 1, long long rec_o = -1,
+                                    long long rec_l = -1) {
+  if (rec_o < 0) rec_o = static_cast<long long>(nh) * R;
+  if (rec_l < 0) rec_l = nh;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(n_entries, nh, (R + 127) / 128);
   cfg.blockDim = dim3(32 * merge_warps(max_count));
@@ -251,7 +264,8 @@ static cudaError_t merge_launch_pdl(float *out, float *lse, const float *part_o,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, merge_partials_kernel, out, lse, part_o, part_lse, d_entries, nh, R, max_count);
+  return cudaLaunchKernelEx(&cfg, merge_partials_kernel, out, lse, part_o, part_lse, d_entries, nh, R, max_count,
+                            pb, rec_o, rec_l);
 }
 
 cudaError_t launch_merge(float *out, float *lse, const float *part_o, const float *part_lse,
@@ -261,6 +275,16 @@ cudaError_t launch_merge(float *out, float *lse, const float *part_o, const floa
   if (n_entries <= 0) return cudaSuccess;
   ProfScope ps("merge_partials", stream);
   return merge_launch_pdl(out, lse, part_o, part_lse, d_entries, n_entries, nh, R, stream, max_count);
+}
+
+// Packed records: part r of `parts` is [batch][nh][R] outputs followed by
+// [batch][nh] lse values (one all-gather of both per rank).
+cudaError_t launch_merge_packed(float *out, float *lse, const float *parts_base, int parts, int batch, int nh,
+                                int R, cudaStream_t stream) {
+  ProfScope ps("merge_partials", stream);
+  const long long rec = static_cast<long long>(batch) * nh * (R + 1);
+  return merge_launch_pdl(out, lse, parts_base, parts_base + static_cast<long long>(batch) * nh * R, nullptr,
+                          batch, nh, R, stream, parts, batch, rec, rec);
 }
 
 // The merge launch without per-kernel timing (its events are created on

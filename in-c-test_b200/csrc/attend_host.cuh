@@ -75,5 +75,7 @@ bool make_tmap_2d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, uint
 cudaError_t launch_merge(float *out, float *lse, const float *part_o, const float *part_lse,
                          const MergeEntry *d_entries, int n_entries, int nh, int R,
                          cudaStream_t stream, int max_count);
+cudaError_t launch_merge_packed(float *out, float *lse, const float *parts_base, int parts, int batch, int nh,
+                                int R, cudaStream_t stream);
 
 }  // namespace kvl

@@ -1493,6 +1493,18 @@ KVL_EXPORT int kvl_mla_decode_step_bf16(const KvlMlaConfig *cfg, const KvlMlaDev
   return 0;
 }
 
+KVL_EXPORT int kvl_mla_merge_packed(float *d_out, float *d_lse, const float *d_parts, int parts, int batch,
+                                    int num_heads, int kv_lora_rank, void *stream) {
+  if (!d_out || !d_parts || parts <= 0 || batch <= 0 || num_heads <= 0 || kv_lora_rank <= 0 ||
+      (reinterpret_cast<uintptr_t>(d_parts) & 3)) {
+    set_err("invalid merge arguments");
+    return -1;
+  }
+  CK(launch_merge_packed(d_out, d_lse, d_parts, parts, batch, num_heads, kv_lora_rank,
+                         static_cast<cudaStream_t>(stream)));
+  return 0;
+}
+
 // =================================================================== Q8 helpers
 KVL_EXPORT int kvl_mla_q8_quantize_rows(int8_t *d_q, float *d_scale, const float *d_x, int rows, int R, void *stream) {
   if (!d_q || !d_scale || !d_x || rows <= 0 || R <= 0) {

@@ -96,6 +96,8 @@ SIGNATURES = {
     "kvl_mla_attend_check": (C.c_int, [C.c_void_p, C.c_void_p]),
     "kvl_mla_merge_partials": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int,
                                          C.c_int, C.c_void_p]),
+    "kvl_mla_merge_packed": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
+                                       C.c_void_p]),
     "kvl_mla_decode_step_workspace_bytes": (C.c_size_t, [C.POINTER(KvlMlaConfig), C.c_int]),
     "kvl_mla_decode_step_bf16": (C.c_int, [C.POINTER(KvlMlaConfig), C.POINTER(KvlMlaDeviceWeights), C.c_void_p,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,

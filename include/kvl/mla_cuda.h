@@ -117,6 +117,13 @@ int kvl_mla_merge_partials(float *d_out, float *d_lse, const float *d_part_o,
                            const float *d_part_lse, int parts, int batch, int num_heads,
                            int kv_lora_rank, void *stream);
 
+/* Same combine over packed records, one per part: d_parts[p] is
+ * [batch][num_heads][R] outputs followed by [batch][num_heads] lse values
+ * (record stride batch * num_heads * (R + 1) floats), e.g. what one NCCL
+ * all-gather of each GPU's (o, lse) buffer produces. */
+int kvl_mla_merge_packed(float *d_out, float *d_lse, const float *d_parts, int parts, int batch,
+                         int num_heads, int kv_lora_rank, void *stream);
+
 /* ------------------------------------------------------------------ batched decode step */
 
 /* Device-resident layer weights (bf16, same shapes as KvlMlaBF16). */
