@@ -116,6 +116,41 @@ int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long lo
   return 0;
 }
 
+// The plans of `count` single sequences side by side: sequence t is cut into
+// exactly the segments, partial slots (in order) and merge entry that
+// build_attend_plan gives it alone, on CTAs of its own, so one launch computes
+// every sequence bit for bit as its own launch would (a block decode then
+// equals its serial decode).
+int build_concat_plan(HostPlan &hp, int count, const int *seq_len, const long long *seq_row0, int max_ctas) {
+  if (count <= 0 || !seq_len || !seq_row0) return -1;
+  hp = HostPlan();
+  hp.batch = count;
+  hp.seq_row0.assign(seq_row0, seq_row0 + count);
+  hp.seq_len.assign(seq_len, seq_len + count);
+  for (int t = 0; t < count; ++t) {
+    HostPlan one;
+    const long long r0 = seq_row0[t];
+    if (build_attend_plan(one, 1, &seq_len[t], &r0, max_ctas) != 0) return -1;
+    const int seg0 = static_cast<int>(hp.segs.size()), slot0 = hp.nparts;
+    for (AttendSegment sg : one.segs) {
+      sg.seq = t;
+      if (sg.slot >= 0) sg.slot += slot0;
+      hp.segs.push_back(sg);
+    }
+    for (int c = 0; c < one.grid; ++c) hp.cta_seg.push_back(seg0 + one.cta_seg[c]);
+    for (MergeEntry e : one.merges) {
+      e.seq = t;
+      e.first += slot0;
+      hp.merges.push_back(e);
+    }
+    hp.nparts += one.nparts;
+    hp.grid += one.grid;
+    hp.max_merge_count = std::max(hp.max_merge_count, one.max_merge_count);
+  }
+  hp.cta_seg.push_back(static_cast<int>(hp.segs.size()));
+  return 0;
+}
+
 // ------------------------------------------------------------------ merge
 // out[seq][h][:] = sum_p w_p o_p / sum_p w_p,  w_p = exp(lse_p - max_p lse_p);
 // lse[seq][h] = max + log(sum_p w_p).  Part p of an entry lives at part index
@@ -126,6 +161,18 @@ int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long lo
 // into weights exp(lse - max) in shared memory (one pass of loads, block-wide
 // reductions); each warp then keeps eight parts' slices in flight per step.
 constexpr int kMergeSmemParts = 256;
+// Warps that combine an entry of `count` parts: enough to split the parts (a
+// few per warp), at most 8, so that a merge block (~5 KB of shared memory) fits
+// beside a resident bf16 attend CTA and waits there for the attend grid to
+// complete.  A function of the entry alone, so an entry's summation order does
+// not depend on the other entries of the launch (a block decode merges each
+// token exactly as its serial decode does).
+__host__ __device__ inline int merge_warps(int count) {
+  int w = 1;
+  while (w < 8 && 4 * w < count) w <<= 1;
+  return w;
+}
+
 // Part p lives at part_o + (p / pb) * rec_o + (p % pb) * nh * R (and the lse
 // likewise with rec_l, nh): pb = 1, rec_o = nh * R, rec_l = nh for the
 // part-major arrays; pb = batch for packed records [batch][nh][R] ++ [batch][nh].
@@ -136,7 +183,9 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
   const MergeEntry e = entries ? entries[blockIdx.x]
                                : MergeEntry{(int)blockIdx.x, (int)blockIdx.x, uniform_parts, (int)gridDim.x};
   const int h = blockIdx.y;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nw = min(static_cast<int>(blockDim.x >> 5), merge_warps(e.count));  // warps >= nw only sync
+  const bool act = warp < nw;
   __shared__ float4 red[8][32];
   __shared__ float wts[kMergeSmemParts];
   // Launched as a programmatic dependent of the attend kernel: wait until that
@@ -153,25 +202,25 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
     return part_o + (p / pb) * rec_o + ((size_t)(p % pb) * nh + h) * R;
   };
   float m = -INFINITY;
-  for (int q = threadIdx.x; q < e.count; q += blockDim.x) {
+  for (int q = threadIdx.x; act && q < e.count; q += 32 * nw) {
     const float v = lse_of(q);
     if (q < kMergeSmemParts) wts[q] = v;
     m = fmaxf(m, v);
   }
   for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-  if (lane == 0) rs[warp] = m;
+  if (lane == 0 && act) rs[warp] = m;
   __syncthreads();
   m = rs[0];
   for (int i = 1; i < nw; ++i) m = fmaxf(m, rs[i]);
   __syncthreads();
   float sum = 0.f;
-  for (int q = threadIdx.x; q < e.count; q += blockDim.x) {
+  for (int q = threadIdx.x; act && q < e.count; q += 32 * nw) {
     const float w = expf((q < kMergeSmemParts ? wts[q] : lse_of(q)) - m);
     if (q < kMergeSmemParts) wts[q] = w;
     sum += w;
   }
   for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
-  if (lane == 0) rs[warp] = sum;
+  if (lane == 0 && act) rs[warp] = sum;
   __syncthreads();
   sum = 0.f;
   for (int i = 0; i < nw; ++i) sum += rs[i];
@@ -182,7 +231,7 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
   auto weight = [&](int q) { return q < kMergeSmemParts ? wts[q] : expf(lse_of(q) - m); };
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   if (vec) {
-    for (int q0 = warp; q0 < e.count; q0 += 8 * nw) {
+    for (int q0 = warp; act && q0 < e.count; q0 += 8 * nw) {
       float4 v[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -202,7 +251,7 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
       }
     }
   } else {
-    for (int q = warp; q < e.count; q += nw) {
+    for (int q = warp; act && q < e.count; q += nw) {
       const float w = weight(q);
       const float *src = o_of(q) + d0;
       if (d0 < R) acc.x = fmaf(w, src[0], acc.x);
@@ -211,7 +260,7 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
       if (d0 + 3 < R) acc.w = fmaf(w, src[3], acc.w);
     }
   }
-  red[warp][lane] = acc;
+  if (act) red[warp][lane] = acc;
   __syncthreads();
   if (warp == 0) {
     float4 t = red[0][lane];
@@ -235,15 +284,6 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
   }
 }
 
-// Warps per merge block: enough to split the largest part count (a few parts
-// per warp), at most 8, so that a merge block (~5 KB of shared memory) fits
-// beside a resident bf16 attend CTA and waits there for the attend grid to
-// complete.
-static int merge_warps(int max_count) {
-  int w = 1;
-  while (w < 8 && 4 * w < max_count) w <<= 1;
-  return w;
-}
 
 // Programmatic dependent launch: the merge grid may be scheduled while the
 // attend grid drains (its blocks wait in griddepcontrol.wait), which hides the

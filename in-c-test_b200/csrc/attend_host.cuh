@@ -34,6 +34,7 @@ struct HostPlan {
 
 int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long long *seq_row0,
                       int max_ctas);
+int build_concat_plan(HostPlan &hp, int count, const int *seq_len, const long long *seq_row0, int max_ctas);
 
 struct AttendLaunch {
   bool q8 = false;

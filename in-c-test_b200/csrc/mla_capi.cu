@@ -420,6 +420,73 @@ int decode_one(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, con
   return 0;
 }
 
+// `count` consecutive tokens of one bf16 state in one pass: projections,
+// appends of rows [position, position + count), attends (token t over rows
+// [0, position + t], each cut exactly as its own decode cuts it), V up and
+// o_proj.  Every kernel computes each token as decode_one does, so the outputs
+// and rows equal `count` serial decodes bit for bit.
+int decode_block(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, const float *x, float *out,
+                 int position, int count, float *mir_lat, float *mir_rope) {
+  const int H = cfg.hidden_size, NH = cfg.num_heads, DN = cfg.qk_nope_dim, DR = cfg.qk_rope_dim;
+  const int DV = cfg.v_head_dim, R = cfg.kv_lora_rank, QD = DN + DR;
+  const size_t n = count;
+  if (!c.x.ensure(n * H * 4) || !c.q.ensure(n * NH * QD * 4) || !c.ka.ensure(n * (R + DR) * 4) ||
+      !c.qabs.ensure(n * NH * (R + DR) * 4) || !c.mix.ensure(n * NH * R * 4) || !c.ho.ensure(n * NH * DV * 4) ||
+      !c.y.ensure(n * H * 4) || !c.rowf.ensure(n * (R + DR) * 4)) {
+    set_err("cudaMalloc of decode scratch failed");
+    return -1;
+  }
+  std::vector<int> lens(count);
+  std::vector<long long> row0(count, 0);
+  for (int t = 0; t < count; ++t) lens[t] = position + t + 1;
+  HostPlan hp;
+  if (build_concat_plan(hp, count, lens.data(), row0.data(), c.sms) != 0) {
+    set_err("block attend plan failed");
+    return -1;
+  }
+  if (!c.pin_plan.ensure(64 * 1024) || c.plan.upload(hp, NH, R, c.stream, c.pin_plan.p, c.pin_plan.n) != 0) {
+    set_err("attend plan upload failed");
+    return -1;
+  }
+  CK(cudaMemcpyAsync(c.x.p, x, n * H * 4, cudaMemcpyHostToDevice, c.stream));
+  CK(gemv_bf16(c.q.as<float>(), c.x.as<float>(), W.q, H, NH * QD, count, c.stream));
+  CK(gemv_bf16(c.ka.as<float>(), c.x.as<float>(), W.kva, H, R + DR, count, c.stream));
+  CK(append_bf16(ds.kv, 0, c.ka.as<float>(), W.kvan, count, R, DR, position, cfg.rms_eps, cfg.rope_theta,
+                 c.rowf.as<float>(), c.stream));
+  CK(absorb(c.qabs.as<float>(), c.q.as<float>(), W.kvb, count, NH, DN, DV, DR, R, position, cfg.rope_theta,
+            c.stream));
+  AttendLaunch a;
+  a.nh = NH;
+  a.R = R;
+  a.DR = DR;
+  a.rows = ds.cap_pad;
+  a.q = c.qabs.as<float>();
+  a.out = c.mix.as<float>();
+  a.kv = ds.kv;
+  a.softmax_scale = 1.0f / sqrtf(static_cast<float>(QD));
+  if (c.plan.launch(a, c.stream) != 0) {
+    set_err("attend launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return -1;
+  }
+  CK(vup(c.ho.as<float>(), c.mix.as<float>(), W.kvb, count, NH, DN, DV, R, c.stream));
+  CK(gemv_bf16(c.y.as<float>(), c.ho.as<float>(), W.o, NH * DV, H, count, c.stream));
+  uint32_t err = 0;
+  CK(cudaMemcpyAsync(&err, c.plan.err_word(), 4, cudaMemcpyDeviceToHost, c.stream));
+  CK(cudaStreamSynchronize(c.stream));
+  if (err != 0) {
+    set_err("attend kernel reported device error 0x%x", err);
+    return -1;
+  }
+  CK(cudaMemcpy(out, c.y.p, n * H * 4, cudaMemcpyDeviceToHost));
+  std::vector<float> rows(n * (R + DR));
+  CK(cudaMemcpy(rows.data(), c.rowf.p, rows.size() * 4, cudaMemcpyDeviceToHost));
+  for (size_t t = 0; t < n; ++t) {
+    memcpy(mir_lat + t * R, rows.data() + t * (R + DR), R * sizeof(float));
+    memcpy(mir_rope + t * DR, rows.data() + t * (R + DR) + R, DR * sizeof(float));
+  }
+  return 0;
+}
+
 // kv_a projection + append of rows 0..S-1 (state prefill, both formats).
 int prefill_state(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, const float *x, int S) {
   const int H = cfg.hidden_size, R = cfg.kv_lora_rank, DR = cfg.qk_rope_dim;
@@ -582,19 +649,35 @@ KVL_EXPORT int kvl_mla_decode_compressed_bf16(float *out, const float *x, int po
   return 0;
 }
 
-// Reference: src/mla_compressed_state.c:163-184 (serial steps).
+// Reference: src/mla_compressed_state.c:163-184 (serial steps; here one pass
+// over the block whose results equal the serial steps exactly).
 KVL_EXPORT int kvl_mla_decode_compressed_block_bf16(float *out, const float *x, int count, int start_position,
                                                     const KvlMlaConfig *cfg, const KvlMlaBF16 *w,
                                                     KvlMlaCompressedState *state) {
   if (!out || !x || !cfg || !w || !state || count <= 0 || start_position != state->len || start_position < 0 ||
       count > state->capacity - start_position)
     return -1;
-  const int H = cfg->hidden_size;
-  if (H <= 0) return -1;
-  for (int t = 0; t < count; ++t)
-    if (kvl_mla_decode_compressed_bf16(out + static_cast<size_t>(t) * H, x + static_cast<size_t>(t) * H,
-                                       start_position + t, cfg, w, state) != 0)
-      return -1;
+  if (!w->q_proj || !w->kv_a_proj || !w->kv_a_norm || !w->kv_b_proj || !w->o_proj ||
+      state->kv_lora_rank != cfg->kv_lora_rank || state->qk_rope_dim != cfg->qk_rope_dim || !cfg_dims_ok(*cfg))
+    return -1;
+  DevState *ds = find_state(state->latent);
+  if (!ds || ds->fmt != FMT_BF16) {
+    set_err("state was not created by kvl_mla_compressed_state_init");
+    return -1;
+  }
+  Ctx *c = get_ctx(ds->device);
+  if (!c) return -1;
+  std::lock_guard<std::mutex> lk(c->mu);
+  if (cudaSetDevice(ds->device) != cudaSuccess) return -1;
+  if (sync_bf16_state(*c, *ds, *state) != 0) return -1;
+  DevW W;
+  if (stage_weights(*c, *cfg, *w, W, true) != 0) return -1;
+  const size_t R = cfg->kv_lora_rank, DR = cfg->qk_rope_dim;
+  if (decode_block(*c, *ds, *cfg, W, x, out, start_position, count, state->latent + start_position * R,
+                   state->rope + start_position * DR) != 0)
+    return -1;
+  ds->dev_len = start_position + count;
+  state->len = start_position + count;
   return 0;
 }
 

@@ -214,3 +214,37 @@ def test_error_conventions(K, S, torch_cuda):
     lib.kvl_mla_compressed_state_free(C.byref(st))
     lib.kvl_mla_compressed_state_free(C.byref(st))  # double free is safe
     assert st.capacity == 0 and not st.latent
+
+
+@pytest.mark.parametrize("prefix,block", [(1020, 8), (3, 16), (20000, 4)])
+def test_block_decode_exact_kimi(K, S, torch_cuda, prefix, block):
+    """The one-pass block decode equals `block` serial decodes bit for bit (outputs
+    and the appended state rows) at the Kimi shape, where the attends are cut
+    into several KV splits: 1021..1028 rows cross a 128-row tile boundary (8 and
+    9 splits), 20001..20004 rows use every SM (148 splits), 4..19 rows one."""
+    shape = (2048, 16, 128, 64, 128, 512, 1e-5, 800000.0)
+    cfg, w = _weights(K, S, shape, 71, 0.02)
+    H = shape[0]
+    x = S.normal(71, S.S_X, (prefix + block) * H, 1.0).reshape(prefix + block, H)
+    lib = K.load()
+    outs, rows = [], []
+    for use_block in (False, True):
+        st = K.CompressedState(cfg, prefix + block)
+        assert st.prefill(x[:prefix], w) == 0, K.last_error()
+        out = np.zeros((block, H), np.float32)
+        if use_block:
+            xb = np.ascontiguousarray(x[prefix:])
+            assert lib.kvl_mla_decode_compressed_block_bf16(K.ptr(out, K.f32p), K.ptr(xb, K.f32p), block, prefix,
+                                                            C.byref(cfg), C.byref(w.c), C.byref(st.s)) == 0, \
+                K.last_error()
+        else:
+            for t in range(block):
+                rc, out[t] = st.decode(x[prefix + t], prefix + t, w)
+                assert rc == 0, K.last_error()
+        outs.append(out)
+        rows.append((st.latent()[prefix:].copy(), st.rope()[prefix:].copy()))
+        assert st.s.len == prefix + block
+        st.free()
+    np.testing.assert_array_equal(outs[1], outs[0])
+    np.testing.assert_array_equal(rows[1][0], rows[0][0])
+    np.testing.assert_array_equal(rows[1][1], rows[0][1])
