@@ -228,6 +228,13 @@ class Oracle:
         return outs, (lat, rope)
 
 
+class ExpandedState(C.Structure):
+    """KvlMlaState of the reference (include/kvl/mla_state.h:13-22): the expanded
+    fp32 K/V state of its V6a correctness oracle."""
+    _fields_ = [("capacity", C.c_int), ("len", C.c_int), ("num_heads", C.c_int), ("qk_nope_dim", C.c_int),
+                ("qk_rope_dim", C.c_int), ("v_head_dim", C.c_int), ("keys", f32p), ("values", f32p)]
+
+
 class Reference:
     """The reference runtime's own MLA functions, compiled from its sources."""
 
@@ -259,6 +266,27 @@ class Reference:
         L.kvl_mla_prefill_bf16.restype = C.c_int
         L.kvl_mla_prefill_materialized_bf16.argtypes = [f32p, f32p, C.c_int, C.POINTER(Cfg), C.POINTER(W)]
         L.kvl_mla_prefill_materialized_bf16.restype = C.c_int
+        L.kvl_mla_state_init.argtypes = [C.POINTER(ExpandedState), C.POINTER(Cfg), C.c_int]
+        L.kvl_mla_state_init.restype = C.c_int
+        L.kvl_mla_state_free.argtypes = [C.POINTER(ExpandedState)]
+        L.kvl_mla_decode_bf16.argtypes = [f32p, f32p, C.c_int, C.POINTER(Cfg), C.POINTER(W), C.POINTER(ExpandedState)]
+        L.kvl_mla_decode_bf16.restype = C.c_int
+
+    def decode_expanded(self, x, cfg, warrays):
+        """Every token of x decoded from position 0 through the reference's
+        expanded-K/V state (src/mla_state.c:66-149), the layer below the
+        compressed state in its oracle stack."""
+        x = np.ascontiguousarray(x, np.float32)
+        S = x.shape[0]
+        w = w_of(warrays)
+        st = ExpandedState()
+        assert self.lib.kvl_mla_state_init(C.byref(st), C.byref(cfg), S) == 0
+        outs = np.zeros((S, cfg.hidden_size), np.float32)
+        for t in range(S):
+            assert self.lib.kvl_mla_decode_bf16(_p(outs[t], f32p), _p(x[t], f32p), t, C.byref(cfg), C.byref(w),
+                                                C.byref(st)) == 0
+        self.lib.kvl_mla_state_free(C.byref(st))
+        return outs
 
     def prefill(self, x, cfg, warrays, materialized=False):
         x = np.ascontiguousarray(x, np.float32)

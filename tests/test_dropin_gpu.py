@@ -248,3 +248,24 @@ def test_block_decode_exact_kimi(K, S, torch_cuda, prefix, block):
     np.testing.assert_array_equal(outs[1], outs[0])
     np.testing.assert_array_equal(rows[1][0], rows[0][0])
     np.testing.assert_array_equal(rows[1][1], rows[0][1])
+
+
+@pytest.mark.parametrize("name", ["incremental_probe", "kimi"])
+def test_layered_oracles(K, S, ref, torch_cuda, name):
+    """The reference's lower oracle layers, run against the GPU path: its
+    expanded-K/V state decode (src/mla_state.c:66-149; the mla_incremental_probe
+    gate) against our compressed-state serial decode, and its materialised
+    prefill (src/ops.c:105-192) against our prefill."""
+    shape = SHAPES[name]
+    Sq = 24 if shape[0] >= 2048 else 13
+    cfg, w = _weights(K, S, shape, 31, 0.05 if shape[0] < 2048 else 0.02)
+    x = S.normal(31, S.S_X, Sq * shape[0], 1.0).reshape(Sq, shape[0])
+    got, st, lib, base = _decode_all(K, cfg, w, x, 0)
+    getattr(lib, base + "_free")(C.byref(st))
+    want = ref.decode_expanded(x, _ref_cfg(shape), w.arrays)
+    assert_close(got, want, what=f"compressed decode vs expanded-state decode ({name})")
+    out = np.zeros_like(x)
+    assert lib.kvl_mla_prefill_bf16(K.ptr(out, K.f32p), K.ptr(x, K.f32p), Sq, C.byref(cfg), C.byref(w.c)) == 0, \
+        K.last_error()
+    mat = ref.prefill(x, _ref_cfg(shape), w.arrays, materialized=True)
+    assert_close(out, mat, what=f"prefill vs materialised prefill ({name})")

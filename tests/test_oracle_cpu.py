@@ -72,6 +72,23 @@ def test_oracle_matches_live_reference(orc, ref_scalar, name):
     np.testing.assert_array_equal(got, want)
 
 
+@pytest.mark.parametrize("name", ["incremental", "spec_q8"])
+def test_oracle_against_reference_lower_layers(orc, ref_scalar, name):
+    """The restatement against the reference's lower oracle layers (its V6a
+    stack): the expanded-K/V state decode (src/mla_state.c:66-149, decoded from
+    position 0) within 2e-6, the gate of src/mla_incremental_probe.c:105, and the
+    materialised prefill (src/ops.c:105-192) within 2e-5
+    (src/mla_streaming_probe.c:90)."""
+    c = CASES[name]
+    w, x = case_inputs(c)
+    cfg = _cfg(c)
+    got, _ = orc.decode_sequence(x, cfg, w, prefix=0)
+    want = ref_scalar.decode_expanded(x, cfg, w)
+    assert np.max(np.abs(got - want)) <= 2e-6
+    mat = ref_scalar.prefill(x, cfg, w, materialized=True)
+    assert np.max(np.abs(orc.prefill(x, cfg, w) - mat)) <= 2e-5
+
+
 def test_attend_core_against_numpy(orc, S):
     L, NH, R, DR = 300, 4, 32, 8
     q = S.normal(7, 0, NH * (R + DR), 0.3).reshape(NH, R + DR)
