@@ -285,6 +285,67 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
 }
 
 
+// Entries of at most 4 parts (merge_warps == 1): one warp per (entry, head,
+// 128-wide slice), eight heads per block, so a batch of short-split sequences
+// does not launch one 32-thread block per head.  The arithmetic, including its
+// order, is that of merge_partials_kernel with one warp, so which of the two
+// runs never changes a result.
+__global__ void merge_small_kernel(float *out, float *lse, const float *part_o, const float *part_lse,
+                                   const MergeEntry *entries, int nh, int R, int uniform_parts, int pb,
+                                   long long rec_o, long long rec_l) {
+  const MergeEntry e = entries ? entries[blockIdx.x]
+                               : MergeEntry{(int)blockIdx.x, (int)blockIdx.x, uniform_parts, (int)gridDim.x};
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int h = blockIdx.y * 8 + warp;
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  if (h >= nh) return;
+  auto o_of = [&](int q) {
+    const int p = e.first + q * e.step;
+    return part_o + (p / pb) * rec_o + ((size_t)(p % pb) * nh + h) * R;
+  };
+  float m = -INFINITY, lv = -INFINITY;
+  if (lane < e.count) {
+    const int p = e.first + lane * e.step;
+    lv = part_lse[(p / pb) * rec_l + (size_t)(p % pb) * nh + h];
+    m = lv;
+  }
+  for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+  const float w = lane < e.count ? expf(lv - m) : 0.f;
+  float sum = w;
+  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  if (lse && blockIdx.z == 0 && lane == 0) lse[(size_t)e.seq * nh + h] = m + logf(sum);
+  const int d0 = blockIdx.z * 128 + 4 * lane;
+  const bool vec = (R & 3) == 0 && d0 + 3 < R && (rec_o & 3) == 0 &&
+                   ((reinterpret_cast<uintptr_t>(part_o) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int q = 0; q < e.count; ++q) {
+    const float wq = __shfl_sync(0xffffffffu, w, q);
+    const float *src = o_of(q) + d0;
+    if (vec) {
+      const float4 v = *reinterpret_cast<const float4 *>(src);
+      acc.x = fmaf(wq, v.x, acc.x);
+      acc.y = fmaf(wq, v.y, acc.y);
+      acc.z = fmaf(wq, v.z, acc.z);
+      acc.w = fmaf(wq, v.w, acc.w);
+    } else {
+      if (d0 < R) acc.x = fmaf(wq, src[0], acc.x);
+      if (d0 + 1 < R) acc.y = fmaf(wq, src[1], acc.y);
+      if (d0 + 2 < R) acc.z = fmaf(wq, src[2], acc.z);
+      if (d0 + 3 < R) acc.w = fmaf(wq, src[3], acc.w);
+    }
+  }
+  const float inv = 1.0f / sum;
+  float *dst = out + ((size_t)e.seq * nh + h) * R + d0;
+  if (vec) {
+    *reinterpret_cast<float4 *>(dst) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+  } else {
+    if (d0 < R) dst[0] = acc.x * inv;
+    if (d0 + 1 < R) dst[1] = acc.y * inv;
+    if (d0 + 2 < R) dst[2] = acc.z * inv;
+    if (d0 + 3 < R) dst[3] = acc.w * inv;
+  }
+}
+
 // Programmatic dependent launch: the merge grid may be scheduled while the
 // attend grid drains (its blocks wait in griddepcontrol.wait), which hides the
 // launch gap between the two.
@@ -294,9 +355,10 @@ static cudaError_t merge_launch_pdl(float *out, float *lse, const float *part_o,
                                     long long rec_l = -1) {
   if (rec_o < 0) rec_o = static_cast<long long>(nh) * R;
   if (rec_l < 0) rec_l = nh;
+  const bool small = merge_warps(max_count) == 1;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(n_entries, nh, (R + 127) / 128);
-  cfg.blockDim = dim3(32 * merge_warps(max_count));
+  cfg.gridDim = small ? dim3(n_entries, (nh + 7) / 8, (R + 127) / 128) : dim3(n_entries, nh, (R + 127) / 128);
+  cfg.blockDim = dim3(small ? 256 : 32 * merge_warps(max_count));
   cfg.dynamicSmemBytes = 0;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -304,6 +366,9 @@ static cudaError_t merge_launch_pdl(float *out, float *lse, const float *part_o,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (small)
+    return cudaLaunchKernelEx(&cfg, merge_small_kernel, out, lse, part_o, part_lse, d_entries, nh, R, max_count,
+                              pb, rec_o, rec_l);
   return cudaLaunchKernelEx(&cfg, merge_partials_kernel, out, lse, part_o, part_lse, d_entries, nh, R, max_count,
                             pb, rec_o, rec_l);
 }

@@ -1370,7 +1370,7 @@ static int pick_split(int ksteps, int want) {
 }
 
 // Decode-step scratch (256-byte aligned slots): [0] q fp32 [B][NH][QD]
-// (kStepQSplit partials on the tensor-core path), [1] ka fp32 [B][R+DR],
+// (kStepQSplit partials on the tensor-core path), [1] ka fp32 [B][R+DR] (matvec path),
 // [2] qabs fp32 [B][NH][R+DR], [3] mix fp32 [B][NH][R], [4] ho fp32 [B][NH*DV]
 // (bf16 on the tensor-core path), [5] x bf16 [B][H], [6] q_nope bf16
 // [NH][B][DN], [7] W_UK^T bf16 [NH][R][DN], [8] mix bf16 [NH][B][R],
@@ -1419,7 +1419,6 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   const uint64_t H = cfg.hidden_size, NH = cfg.num_heads, DN = cfg.qk_nope_dim, DR = cfg.qk_rope_dim;
   const uint64_t DV = cfg.v_head_dim, R = cfg.kv_lora_rank, QD = DN + DR, b = B;
   float *q = reinterpret_cast<float *>(ws + off[0]);
-  float *ka = reinterpret_cast<float *>(ws + off[1]);
   float *qabs = reinterpret_cast<float *>(ws + off[2]);
   float *mix = reinterpret_cast<float *>(ws + off[3]);
   uint16_t *hob = reinterpret_cast<uint16_t *>(ws + off[4]);
@@ -1464,11 +1463,12 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   g.ksplit = pick_split(hsteps, kStepKvaSplit);
   g.c_bstride = static_cast<long long>(b * (R + DR));
   CK(launch_gemm(g, 192, EPI_F32, sms, s, "gemm_kva"));
-  CK(sum_parts(ka, ka_parts, g.ksplit, g.c_bstride, static_cast<long long>(b * (R + DR)), s));
+  // the append sums the split-K partials of its row itself
+  CK(append_bf16(d_kv, 0, ka_parts, w.kv_a_norm, B, static_cast<int>(R), static_cast<int>(DR), 0, cfg.rms_eps,
+                 cfg.rope_theta, nullptr, s, reinterpret_cast<const long long *>(d_row), d_pos, g.ksplit,
+                 g.c_bstride));
   g.ksplit = 0;
   g.c_bstride = 0;
-  CK(append_bf16(d_kv, 0, ka, w.kv_a_norm, B, static_cast<int>(R), static_cast<int>(DR), 0, cfg.rms_eps,
-                 cfg.rope_theta, nullptr, s, reinterpret_cast<const long long *>(d_row), d_pos));
   CK(q_split(qn, qabs, q, q_parts, static_cast<long long>(b * NH * QD), B, static_cast<int>(NH),
              static_cast<int>(DN), static_cast<int>(DR), static_cast<int>(R), cfg.rope_theta, d_pos, s));
   // qabs[:, h, :R] = q_nope[:, h] . W_UK[h]   (NH products, M = B, N = R, K = DN)

@@ -155,16 +155,27 @@ __device__ void rmsnorm_row(float *lat, const float *ka, const uint16_t *w, int 
 }
 
 // bf16 state row [R latent | DR rope] at row (row0 + pos0 + t) of `kv` for each
-// of the n tokens; ka is [n][R + DR] (kv_a_proj output).  rows_f32 (optional)
-// receives the fp32 row before bf16 rounding.
+// of the n tokens; ka is [n][R + DR] (kv_a_proj output), or `parts` split-K
+// partials of it (stride part_stride floats) added in order 0, 1, ...
+// rows_f32 (optional) receives the fp32 row before bf16 rounding.
 __global__ void append_bf16_kernel(uint16_t *kv, long long row0, const float *ka, const uint16_t *norm_w, int R,
                                    int DR, int pos0, float eps, float theta, float *rows_f32,
-                                   const long long *row_of, const int *pos_of) {
+                                   const long long *row_of, const int *pos_of, int parts, long long part_stride) {
   extern __shared__ float sh[];
   float *lat = sh;
   double *dred = reinterpret_cast<double *>(sh + ((R + 1) & ~1));
+  float *ksum = reinterpret_cast<float *>(dred + 32) + 32;  // [R + DR] when parts > 1
   const int t = blockIdx.x;
   const float *kt = ka + static_cast<size_t>(t) * (R + DR);
+  if (parts > 1) {
+    for (int i = threadIdx.x; i < R + DR; i += blockDim.x) {
+      float v = kt[i];
+      for (int pp = 1; pp < parts; ++pp) v += kt[pp * part_stride + i];
+      ksum[i] = v;
+    }
+    __syncthreads();
+    kt = ksum;
+  }
   rmsnorm_row(lat, kt, norm_w, R, eps, dred);
   const int pos = pos_of ? pos_of[t] : pos0 + t;
   const long long row = row_of ? row_of[t] : row0 + pos0 + t;
@@ -300,14 +311,16 @@ __global__ void append_q8_kernel(int8_t *lat8, float *lscale, uint16_t *rope16, 
 }
 
 static size_t append_smem(int R) { return static_cast<size_t>((R + 1) & ~1) * 4 + 32 * 8 + 32 * 4; }
+static size_t append_smem_parts(int R, int DR) { return append_smem(R) + static_cast<size_t>(R + DR) * 4; }
 
 cudaError_t append_bf16(uint16_t *kv, long long row0, const float *ka, const uint16_t *norm_w, int n, int R,
                         int DR, int pos0, float eps, float theta, float *rows_f32, cudaStream_t s,
-                        const long long *row_of, const int *pos_of) {
+                        const long long *row_of, const int *pos_of, int parts, long long part_stride) {
   if (n <= 0) return cudaSuccess;
   ProfScope ps("append_bf16", s);
-  append_bf16_kernel<<<n, 128, append_smem(R), s>>>(kv, row0, ka, norm_w, R, DR, pos0, eps, theta, rows_f32,
-                                                    row_of, pos_of);
+  const size_t sm = parts > 1 ? append_smem_parts(R, DR) : append_smem(R);
+  append_bf16_kernel<<<n, 128, sm, s>>>(kv, row0, ka, norm_w, R, DR, pos0, eps, theta, rows_f32, row_of, pos_of,
+                                        parts, part_stride);
   return cudaGetLastError();
 }
 

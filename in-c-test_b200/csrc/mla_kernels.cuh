@@ -9,7 +9,8 @@ namespace kvl {
 cudaError_t gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int n, cudaStream_t s);
 cudaError_t append_bf16(uint16_t *kv, long long row0, const float *ka, const uint16_t *norm_w, int n, int R,
                         int DR, int pos0, float eps, float theta, float *rows_f32, cudaStream_t s,
-                        const long long *row_of = nullptr, const int *pos_of = nullptr);
+                        const long long *row_of = nullptr, const int *pos_of = nullptr, int parts = 1,
+                        long long part_stride = 0);
 cudaError_t append_q8(int8_t *lat8, float *lscale, uint16_t *rope16, long long row0, const float *ka,
                       const uint16_t *norm_w, int n, int R, int DR, int pos0, float eps, float theta,
                       cudaStream_t s, const long long *row_of = nullptr, const int *pos_of = nullptr);

@@ -216,12 +216,14 @@ def test_error_conventions(K, S, torch_cuda):
     assert st.capacity == 0 and not st.latent
 
 
-@pytest.mark.parametrize("prefix,block", [(1020, 8), (3, 16), (20000, 4)])
+@pytest.mark.parametrize("prefix,block", [(1020, 8), (509, 8), (3, 16), (20000, 4)])
 def test_block_decode_exact_kimi(K, S, torch_cuda, prefix, block):
     """The one-pass block decode equals `block` serial decodes bit for bit (outputs
     and the appended state rows) at the Kimi shape, where the attends are cut
     into several KV splits: 1021..1028 rows cross a 128-row tile boundary (8 and
-    9 splits), 20001..20004 rows use every SM (148 splits), 4..19 rows one."""
+    9 splits), 510..517 rows cross from 4 to 5 splits (the one-warp merge beside
+    the block-wide one), 20001..20004 rows use every SM (148 splits), 4..19 rows
+    one."""
     shape = (2048, 16, 128, 64, 128, 512, 1e-5, 800000.0)
     cfg, w = _weights(K, S, shape, 71, 0.02)
     H = shape[0]
