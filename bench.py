@@ -512,7 +512,8 @@ class DecodeStack:
         # (profiles/mla_attend_bf16_config5.txt: 155.37 MB for 131,072 rows) by rows
         self.ncu_traffic = {"mla_attend_bf16": DecodeLong.ncu_traffic["mla_attend_bf16"] / 131072 * self.rows}
 
-    def step(self):
+    def step_profiled(self):
+        """The 27 decode steps launched one by one (per-kernel CUDA events)."""
         s = self.torch.cuda.current_stream().cuda_stream
         for layer in range(self.LAYERS):
             kv = self.kv[layer % self.nbuf]
@@ -523,6 +524,30 @@ class DecodeStack:
             if rc != 0:
                 raise RuntimeError(self.K.last_error())
 
+    def step(self):
+        """One decode step of the stack as a CUDA graph of the 27 layer steps
+        (captured once; every replay runs every kernel of every layer)."""
+        torch = self.torch
+        if getattr(self, "graph", None) is None:
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(side):
+                self.step_profiled()
+            torch.cuda.current_stream().wait_stream(side)
+            torch.cuda.synchronize()
+            try:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    self.step_profiled()
+                self.graph = g
+            except RuntimeError as e:  # capture refused: launch the layers one by one
+                print(f"decode_stack: CUDA graph capture failed ({e}); launching per layer", file=sys.stderr)
+                self.graph = False
+        if self.graph:
+            self.graph.replay()
+        else:
+            self.step_profiled()
+
     def value(self, ms):
         return self.total_bytes / (ms * 1e-3) / 1e9
 
@@ -532,6 +557,8 @@ class DecodeStack:
                 "pool_note": "all 27 layers resident" if self.nbuf == self.LAYERS else
                 f"layer l reads pool l % {self.nbuf} (27 layers x 9.66 GB exceed one GPU)",
                 "kv_bytes_per_step": self.total_bytes, "weights": "27 distinct layers, bf16 ~N(0,0.02)",
+                "launch": ("the 27 layer steps captured once as a CUDA graph, replayed per step"
+                           if getattr(self, "graph", None) else "27 layer steps launched per step"),
                 "parallelism": f"sequence-sharded x{self.dist.world}"}
 
 
@@ -582,7 +609,7 @@ def measure(torch, K, lib, dist, wl, steps, warmup, flush, peaks):
     lib.kvl_mla_cuda_profile(1)
     for _ in range(steps):
         flush()
-        wl.step()
+        getattr(wl, "step_profiled", wl.step)()
     torch.cuda.synchronize()
     prof = profile_read(lib)
     lib.kvl_mla_cuda_profile(0)
