@@ -213,6 +213,31 @@ def device_weights(torch, K, cfg, gen, device, std=0.02):
     return t, w
 
 
+def replay_as_graph(torch, obj, raw, label):
+    """Runs raw() (a sequence of library launches on the current stream) as a
+    CUDA graph captured on first use; every replay launches every kernel again.
+    Falls back to raw() if the capture is refused."""
+    if getattr(obj, "_graph", None) is None:
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            raw()
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+        try:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                raw()
+            obj._graph = g
+        except RuntimeError as e:
+            print(f"{label}: CUDA graph capture failed ({e}); launching directly", file=sys.stderr)
+            obj._graph = False
+    if obj._graph:
+        obj._graph.replay()
+    else:
+        raw()
+
+
 # ----------------------------------------------------------------------------- CPU side (reference)
 _REF_INPUTS = {}
 
@@ -302,12 +327,17 @@ class Prefill:
                 "gemm_q": 2.0 * S * H * NH * QD, "gemm_kva": 2.0 * S * H * (R + DR),
                 "gemm_kvb": 2.0 * S * R * NH * (128 + DV), "gemm_o": 2.0 * S * NH * DV * H}
 
-    def step(self):
+    def step_profiled(self):
+        """kvl_mla_prefill_dev launched directly (per-kernel CUDA events)."""
         s = self.torch.cuda.current_stream().cuda_stream
         rc = self.lib.kvl_mla_prefill_dev(C.byref(self.cfg), C.byref(self.w), self.out.data_ptr(),
                                           self.x.data_ptr(), self.S, self.ws.data_ptr(), self.ws.numel(), s)
         if rc != 0:
             raise RuntimeError(self.K.last_error())
+
+    def step(self):
+        """The same launches (both streams of the fork) replayed as a CUDA graph."""
+        replay_as_graph(self.torch, self, self.step_profiled, "prefill")
 
     def value(self, ms_per_step):
         return self.dist.world * self.units / (ms_per_step * 1e-3) / 1e12
@@ -345,7 +375,9 @@ class Prefill:
                 "hidden": 2048, "heads": 16, "qk_nope": 128, "qk_rope": 64, "v_head": 128, "kv_lora_rank": 512,
                 "rope_theta": self.cfg.rope_theta, "x_dtype": "bf16", "weights": "bf16 ~N(0,0.02), kv_a_norm=1",
                 "flops_per_step_per_rank": self.units, "flops_projections": self.proj, "flops_attention": self.attn,
-                "l2": "flushed (256 MiB write) before every step", "parallelism": f"sequence-sharded x{self.dist.world}"}
+                "l2": "flushed (256 MiB write) before every step", "parallelism": f"sequence-sharded x{self.dist.world}",
+                "launch": ("kvl_mla_prefill_dev captured once as a CUDA graph (both streams), replayed per step"
+                           if getattr(self, "_graph", None) else "kvl_mla_prefill_dev launched per step")}
 
     def cpu_baseline(self):
         cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
@@ -527,26 +559,7 @@ class DecodeStack:
     def step(self):
         """One decode step of the stack as a CUDA graph of the 27 layer steps
         (captured once; every replay runs every kernel of every layer)."""
-        torch = self.torch
-        if getattr(self, "graph", None) is None:
-            side = torch.cuda.Stream()
-            side.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(side):
-                self.step_profiled()
-            torch.cuda.current_stream().wait_stream(side)
-            torch.cuda.synchronize()
-            try:
-                g = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(g):
-                    self.step_profiled()
-                self.graph = g
-            except RuntimeError as e:  # capture refused: launch the layers one by one
-                print(f"decode_stack: CUDA graph capture failed ({e}); launching per layer", file=sys.stderr)
-                self.graph = False
-        if self.graph:
-            self.graph.replay()
-        else:
-            self.step_profiled()
+        replay_as_graph(self.torch, self, self.step_profiled, "decode_stack")
 
     def value(self, ms):
         return self.total_bytes / (ms * 1e-3) / 1e9
@@ -558,7 +571,7 @@ class DecodeStack:
                 f"layer l reads pool l % {self.nbuf} (27 layers x 9.66 GB exceed one GPU)",
                 "kv_bytes_per_step": self.total_bytes, "weights": "27 distinct layers, bf16 ~N(0,0.02)",
                 "launch": ("the 27 layer steps captured once as a CUDA graph, replayed per step"
-                           if getattr(self, "graph", None) else "27 layer steps launched per step"),
+                           if getattr(self, "_graph", None) else "27 layer steps launched per step"),
                 "parallelism": f"sequence-sharded x{self.dist.world}"}
 
 
