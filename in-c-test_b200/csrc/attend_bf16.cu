@@ -256,10 +256,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&B->s_empty[sb]);
         const int tok = sg.tok_begin + kTileTok * t + tt;
         const bool valid = tok < sg.tok_end;
-        if (p.dbg_s != nullptr && blockIdx.x == 0 && static_cast<int>(g) < p.dbg_tiles) {
-#pragma unroll
-          for (int h = 0; h < kHeads; ++h) p.dbg_s[(static_cast<size_t>(g) * kTileTok + tt) * kHeads + h] = v[h];
-        }
         float s[kHeads];
         bool need = false;
 #pragma unroll

@@ -56,8 +56,6 @@ struct AttendParams {
   long long rows;            // rows in the pool
   float scale_log2;          // softmax scale * log2(e)
   uint32_t *err;             // error word (bit-or of kvl::ERR_*)
-  float *dbg_s;              // optional: raw scores of the first tiles, [tiles][64][16]
-  int dbg_tiles;
 };
 
 #ifdef __CUDACC__

@@ -603,8 +603,6 @@ int DevicePlan::launch(const AttendLaunch &a, cudaStream_t stream) const {
   p.rows = a.rows;
   p.scale_log2 = scale_log2;
   p.err = reinterpret_cast<uint32_t *>(const_cast<uint8_t *>(m + off_err));
-  p.dbg_s = a.dbg_s;
-  p.dbg_tiles = a.dbg_tiles;
   cudaError_t e = a.q8 ? launch_attend_q8(p, host.grid, stream) : launch_attend_bf16(p, host.grid, stream);
   if (e != cudaSuccess) return -1;
   if (!host.merges.empty()) {

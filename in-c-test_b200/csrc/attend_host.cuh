@@ -48,8 +48,6 @@ struct AttendLaunch {
   const float *lscale = nullptr;      // q8 pool [rows]
   const uint16_t *rope16 = nullptr;   // q8 pool [rows][DR]
   float softmax_scale = 0.f;
-  float *dbg_s = nullptr;
-  int dbg_tiles = 0;
 };
 
 // Device-resident copy of a plan plus the partial-output workspace.

@@ -1026,7 +1026,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   CK(launch_gemm(g, 192, EPI_F32, sms, st, "gemm_kva"));
   // latent = rmsnorm(kva[:512]) * kv_a_norm, k_rope = rope(kva[512:]) -> pool [S][576] bf16
   if (fork) CK(cudaStreamWaitEvent(st, fk->rope, 0));
-  CK(append_rows_bf16(pool + R0 * 576, kva + R0 * 576, 1, 0, W.kvan, cs + R0 * 32, M, cfg.rms_eps, st));
+  CK(append_rows_bf16(pool + R0 * 576, kva + R0 * 576, W.kvan, cs + R0 * 32, M, cfg.rms_eps, st));
   // kv = latent Wkvb^T, bf16 [S][16][256]
   if (!bf16_map(&g.tm_a, pool + R0 * 576, 512, m, 576 * 2, 128) ||
       !bf16_map(&g.tm_b, W.kvb, 512, 4096, 512 * 2, 128)) {

@@ -200,10 +200,8 @@ __global__ void append_bf16_kernel(uint16_t *kv, long long row0, const float *ka
 // rope_table_kernel with the same double-angle arithmetic as rope_pair.  The
 // same operations as append_bf16 (double sum of squares, float scale, float
 // rotation without contraction); only the order of the double sum differs.
-// `ka` holds `parts` split-K partial rows (stride `part_stride` floats), added
-// in order 0, 1, ... to form the kv_a_proj row.
-__global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, int parts, long long part_stride,
-                                        const uint16_t *norm_w, const float2 *cs, int n, float eps) {
+__global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, const uint16_t *norm_w,
+                                        const float2 *cs, int n, float eps) {
   constexpr int R = 512, DR = 64;
   const int warp = static_cast<int>((blockIdx.x * static_cast<unsigned>(blockDim.x) + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
@@ -214,13 +212,6 @@ __global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, int par
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     v[k] = reinterpret_cast<const float4 *>(kt)[lane + 32 * k];
-    for (int pp = 1; pp < parts; ++pp) {
-      const float4 u = reinterpret_cast<const float4 *>(kt + pp * part_stride)[lane + 32 * k];
-      v[k].x += u.x;
-      v[k].y += u.y;
-      v[k].z += u.z;
-      v[k].w += u.w;
-    }
     ss += static_cast<double>(v[k].x) * static_cast<double>(v[k].x);
     ss += static_cast<double>(v[k].y) * static_cast<double>(v[k].y);
     ss += static_cast<double>(v[k].z) * static_cast<double>(v[k].z);
@@ -246,12 +237,7 @@ __global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, int par
     *reinterpret_cast<uint2 *>(dst + c) = o;
   }
   // rope pair (2i, 2i+1) -> (i, 32 + i), i = lane
-  float2 ab = reinterpret_cast<const float2 *>(kt + R)[lane];
-  for (int pp = 1; pp < parts; ++pp) {
-    const float2 u = reinterpret_cast<const float2 *>(kt + pp * part_stride + R)[lane];
-    ab.x += u.x;
-    ab.y += u.y;
-  }
+  const float2 ab = reinterpret_cast<const float2 *>(kt + R)[lane];
   const float2 t = cs[static_cast<size_t>(warp) * (DR / 2) + lane];
   const float lo = __fsub_rn(__fmul_rn(ab.x, t.x), __fmul_rn(ab.y, t.y));
   const float hi = __fadd_rn(__fmul_rn(ab.y, t.x), __fmul_rn(ab.x, t.y));
@@ -259,11 +245,11 @@ __global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, int par
   dst[R + DR / 2 + lane] = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
 }
 
-cudaError_t append_rows_bf16(uint16_t *pool, const float *ka, int parts, long long part_stride,
-                             const uint16_t *norm_w, const float2 *cs, int n, float eps, cudaStream_t s) {
+cudaError_t append_rows_bf16(uint16_t *pool, const float *ka, const uint16_t *norm_w, const float2 *cs, int n,
+                             float eps, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   ProfScope ps("append_bf16", s);
-  append_rows_bf16_kernel<<<(n + 7) / 8, 256, 0, s>>>(pool, ka, parts, part_stride, norm_w, cs, n, eps);
+  append_rows_bf16_kernel<<<(n + 7) / 8, 256, 0, s>>>(pool, ka, norm_w, cs, n, eps);
   return cudaGetLastError();
 }
 
