@@ -462,10 +462,27 @@ class DecodeLong:
         self.o = self.rec[:16 * 512].view(1, 16, 512)
         self.lse = self.rec[16 * 512:].view(1, 16)
         self.plan = K.AttendPlan([self.n], [0], 16, 512)
+        self.peer = None
         if dist.world > 1:
             self.grec = torch.empty((dist.world, 16 * 512 + 16), device=dev)
             self.final = torch.empty((1, 16, 512), device=dev)
             self.final_lse = torch.empty((1, 16), device=dev)
+            # the records cross NVLink by peer stores inside one merge kernel;
+            # NCCL all-gather + merge where CUDA IPC is not available
+            ok = 1.0
+            try:
+                def gather(b):
+                    lst = [None] * dist.world
+                    dist.pg.all_gather_object(lst, b)
+                    return lst
+                self.peer = K.PeerGroup(dist.rank, dist.world, 1, gather)
+            except Exception as e:  # noqa: BLE001
+                print(f"decode_long: peer exchange unavailable ({e}); using NCCL", file=sys.stderr)
+                ok = 0.0
+            if dist.sum(torch, ok) < dist.world:  # every rank takes the same path
+                if self.peer is not None:
+                    self.peer.close()
+                self.peer = None
         self.units = self.n * 1152
         self.total_bytes = L * 1152
 
@@ -475,7 +492,9 @@ class DecodeLong:
         rc = self.plan.attend_bf16(self.o, self.lse, self.q, self.kv, self.n, stream=s)
         if rc != 0:
             raise RuntimeError(self.K.last_error())
-        if self.dist.world > 1:
+        if self.dist.world > 1 and self.peer is not None:
+            rc = self.peer.merge(self.final, self.final_lse, self.rec, stream=s)
+        elif self.dist.world > 1:
             self.dist.pg.all_gather_into_tensor(self.grec, self.rec)
             rc = self.lib.kvl_mla_merge_packed(self.final.data_ptr(), self.final_lse.data_ptr(), self.grec.data_ptr(),
                                                self.dist.world, 1, 16, 512, s)
@@ -487,7 +506,9 @@ class DecodeLong:
 
     def config(self):
         return {"workload": "config 5: long-context decode attend, L=131072", "rows_per_rank": self.n,
-                "parallelism": f"split-KV x{self.dist.world} + one NCCL all-gather of packed (o, lse) + merge"}
+                "parallelism": f"split-KV x{self.dist.world} + " + ("peer-store exchange and merge in one kernel (NVLink)"
+                                                                  if self.peer is not None else
+                                                                  "one NCCL all-gather of packed (o, lse) + merge")}
 
 
 class DecodeStack:

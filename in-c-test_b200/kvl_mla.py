@@ -98,6 +98,13 @@ SIGNATURES = {
                                          C.c_int, C.c_void_p]),
     "kvl_mla_merge_packed": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int,
                                        C.c_void_p]),
+    "kvl_mla_peer_handle_bytes": (C.c_size_t, []),
+    "kvl_mla_peer_group_create": (C.c_int, [C.POINTER(C.c_void_p), C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                            C.c_void_p]),
+    "kvl_mla_peer_group_connect": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "kvl_mla_merge_exchange": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "kvl_mla_peer_group_check": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "kvl_mla_peer_group_destroy": (None, [C.c_void_p]),
     "kvl_mla_decode_step_workspace_bytes": (C.c_size_t, [C.POINTER(KvlMlaConfig), C.c_int]),
     "kvl_mla_decode_step_bf16": (C.c_int, [C.POINTER(KvlMlaConfig), C.POINTER(KvlMlaDeviceWeights), C.c_void_p,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
@@ -233,6 +240,40 @@ class CompressedState:
 def t_ptr(t) -> int:
     """Device pointer of a torch tensor (0 for None)."""
     return 0 if t is None else int(t.data_ptr())
+
+
+class PeerGroup:
+    """kvl_mla_peer_group_*: the split-KV combine across the GPUs of one node.
+    `gather(bytes) -> list of bytes` gathers one byte string per rank in rank
+    order (e.g. torch.distributed.all_gather_object)."""
+
+    def __init__(self, rank, world, batch, gather, num_heads=16, kv_lora_rank=512, lib=None):
+        self.lib = lib or load()
+        n = self.lib.kvl_mla_peer_handle_bytes()
+        handle = C.create_string_buffer(n)
+        self.h = C.c_void_p()
+        check(self.lib.kvl_mla_peer_group_create(C.byref(self.h), rank, world, batch, num_heads, kv_lora_rank,
+                                                 handle), "peer group create")
+        handles = gather(handle.raw)
+        table = C.create_string_buffer(b"".join(handles), n * world)
+        check(self.lib.kvl_mla_peer_group_connect(self.h, table), "peer group connect")
+
+    def merge(self, out, lse, record, stream=0):
+        return self.lib.kvl_mla_merge_exchange(self.h, t_ptr(out), t_ptr(lse), t_ptr(record), stream)
+
+    def check(self, stream=0):
+        return self.lib.kvl_mla_peer_group_check(self.h, stream)
+
+    def close(self):
+        if self.h:
+            self.lib.kvl_mla_peer_group_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
 
 
 class AttendPlan:

@@ -124,6 +124,29 @@ int kvl_mla_merge_partials(float *d_out, float *d_lse, const float *d_part_o,
 int kvl_mla_merge_packed(float *d_out, float *d_lse, const float *d_parts, int parts, int batch,
                          int num_heads, int kv_lora_rank, void *stream);
 
+/* ------------------------------------------------------------------ split-KV across GPUs */
+
+/* The combine of a split-KV decode across the GPUs of one node in one launch
+ * (in place of an all-gather plus kvl_mla_merge_packed): each GPU stores its
+ * packed record (d_out-layout [batch][num_heads][R] then lse [batch][num_heads])
+ * into every GPU's exchange buffer over NVLink, raises a flag there and merges
+ * the world records once every flag of the call is up.  One process per GPU:
+ *   create (allocates this GPU's buffer; writes its CUDA IPC handle, of
+ *   kvl_mla_peer_handle_bytes() bytes, to handle_out) -> the caller gathers the
+ *   world handles in rank order (any host collective) -> connect -> per step
+ *   kvl_mla_merge_exchange on every rank, in the same order -> destroy.
+ * batch * num_heads <= 256, world <= 8.  Waits are bounded (2 s);
+ * kvl_mla_peer_group_check reports a record that did not arrive. */
+typedef struct KvlMlaPeerGroup KvlMlaPeerGroup;
+size_t kvl_mla_peer_handle_bytes(void);
+int kvl_mla_peer_group_create(KvlMlaPeerGroup **group, int rank, int world, int batch, int num_heads,
+                              int kv_lora_rank, void *handle_out);
+int kvl_mla_peer_group_connect(KvlMlaPeerGroup *group, const void *handles);
+int kvl_mla_merge_exchange(KvlMlaPeerGroup *group, float *d_out, float *d_lse, const float *d_record,
+                           void *stream);
+int kvl_mla_peer_group_check(KvlMlaPeerGroup *group, void *stream);
+void kvl_mla_peer_group_destroy(KvlMlaPeerGroup *group);
+
 /* ------------------------------------------------------------------ batched decode step */
 
 /* Device-resident layer weights (bf16, same shapes as KvlMlaBF16). */
