@@ -489,12 +489,16 @@ class DecodeLong:
     def step(self):
         torch = self.torch
         s = torch.cuda.current_stream().cuda_stream
+        if self.peer is not None:
+            # attend, then one kernel: local combine, peer stores, cross-GPU merge
+            rc = self.peer.attend_exchange(self.plan, self.final, self.final_lse, self.q, self.kv, self.n, stream=s)
+            if rc != 0:
+                raise RuntimeError(self.K.last_error())
+            return
         rc = self.plan.attend_bf16(self.o, self.lse, self.q, self.kv, self.n, stream=s)
         if rc != 0:
             raise RuntimeError(self.K.last_error())
-        if self.dist.world > 1 and self.peer is not None:
-            rc = self.peer.merge(self.final, self.final_lse, self.rec, stream=s)
-        elif self.dist.world > 1:
+        if self.dist.world > 1:
             self.dist.pg.all_gather_into_tensor(self.grec, self.rec)
             rc = self.lib.kvl_mla_merge_packed(self.final.data_ptr(), self.final_lse.data_ptr(), self.grec.data_ptr(),
                                                self.dist.world, 1, 16, 512, s)
@@ -505,10 +509,15 @@ class DecodeLong:
         return self.total_bytes / (ms * 1e-3) / 1e9
 
     def config(self):
+        if self.dist.world == 1:
+            par = "one GPU: attend + local combine"
+        elif self.peer is not None:
+            par = (f"split-KV x{self.dist.world} + local combine, peer-store exchange and merge in one kernel "
+                   "after the attend (NVLink)")
+        else:
+            par = f"split-KV x{self.dist.world} + one NCCL all-gather of packed (o, lse) + merge"
         return {"workload": "config 5: long-context decode attend, L=131072", "rows_per_rank": self.n,
-                "parallelism": f"split-KV x{self.dist.world} + " + ("peer-store exchange and merge in one kernel (NVLink)"
-                                                                  if self.peer is not None else
-                                                                  "one NCCL all-gather of packed (o, lse) + merge")}
+                "parallelism": par}
 
 
 class DecodeStack:

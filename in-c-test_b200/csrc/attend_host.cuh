@@ -48,6 +48,7 @@ struct AttendLaunch {
   const float *lscale = nullptr;      // q8 pool [rows]
   const uint16_t *rope16 = nullptr;   // q8 pool [rows][DR]
   float softmax_scale = 0.f;
+  bool skip_merge = false;            // leave split sequences as partials (a cross-GPU combine reads them)
 };
 
 // Device-resident copy of a plan plus the partial-output workspace.

@@ -31,6 +31,7 @@
 #include "flash_prefill.cuh"
 #include "gemm.cuh"
 #include "mla_kernels.cuh"
+#include "peer_merge.cuh"
 
 #define KVL_EXPORT extern "C" __attribute__((visibility("default")))
 
@@ -1309,6 +1310,36 @@ KVL_EXPORT int kvl_mla_attend_bf16(const KvlMlaAttendPlan *plan, float *d_out, f
   a.kv = d_kv;
   a.softmax_scale = softmax_scale;
   return attend_common(plan, a, num_heads, kv_lora_rank, rope_dim, stream);
+}
+
+KVL_EXPORT int kvl_mla_attend_bf16_exchange(const KvlMlaAttendPlan *plan, KvlMlaPeerGroup *group, float *d_out,
+                                            float *d_lse, const float *d_q, const uint16_t *d_kv, int64_t rows,
+                                            float softmax_scale, void *stream) {
+  if (!plan || !group || !group->connected || !d_kv || !d_out) {
+    set_err("invalid attend exchange arguments");
+    return -1;
+  }
+  if (plan->nh != kHeads || plan->R != kLatent || group->nh != plan->nh || group->R != plan->R ||
+      group->batch != plan->dp.host.batch || (reinterpret_cast<uintptr_t>(d_out) & 15) != 0) {
+    set_err("attend exchange: plan and group must both be %d heads x %d, the same batch, d_out 16-byte aligned",
+            kHeads, kLatent);
+    return -1;
+  }
+  AttendLaunch a;
+  a.q8 = false;
+  a.rows = rows;
+  a.q = d_q;
+  a.out = group->stage;  // unsplit sequences land here; split ones stay partials
+  a.lse = group->stage + static_cast<long long>(group->batch) * group->nh * group->R;
+  a.kv = d_kv;
+  a.softmax_scale = softmax_scale;
+  a.skip_merge = true;
+  if (attend_common(plan, a, kHeads, kLatent, kRope, stream) != 0) return -1;
+  if (launch_attend_exchange(group, plan->dp, d_out, d_lse, static_cast<cudaStream_t>(stream)) != cudaSuccess) {
+    set_err("attend exchange launch failed: %s", cudaGetErrorString(cudaGetLastError()));
+    return -1;
+  }
+  return 0;
 }
 
 KVL_EXPORT int kvl_mla_attend_q8(const KvlMlaAttendPlan *plan, float *d_out, float *d_lse, const float *d_q,

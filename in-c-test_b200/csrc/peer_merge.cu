@@ -1,25 +1,33 @@
-// peer_merge.cu -- split-KV combine across the GPUs of one node in one kernel:
-// every GPU stores its packed partial record (o [B][nh][R] ++ lse [B][nh]) into
-// slot `rank` of every GPU's exchange buffer over NVLink (plain peer stores,
-// no multicast), raises a flag in each, waits for the flags of all ranks in
-// its own buffer, and merges the `world` records -- the NCCL all-gather plus
-// merge launch of the split-KV decode (config 5) as one launch.
+// peer_merge.cu -- split-KV combine across the GPUs of one node in one kernel
+// per GPU (plain peer stores over NVLink, no multicast, no NCCL):
+//   kvl_mla_attend_bf16_exchange  attend this rank's KV range, then one kernel
+//                                 per (sequence, head, 128-wide slice) combines
+//                                 the attend's partials locally, exchanges the
+//                                 slice with every peer and merges the world
+//                                 slices;
+//   kvl_mla_merge_exchange        the same exchange and merge for a caller that
+//                                 already holds its packed (o, lse) record.
+// Values travel as tagged words: every value is one 64-bit store of
+// (call number << 32 | float bits), which a reader sees whole or not at all,
+// so a reader polls the words it needs in its own buffer until they carry the
+// current call's tag; no fence or flag round trip is needed.
 //
 // Exchange buffer of each GPU (cudaMalloc, shared with the peers through CUDA
-// IPC handles): 2 sets x world records of rec = B*nh*(R+1) floats, then flags
-// [2][world] uint32.  Call k uses set k & 1 and writes flag value k; a rank can
-// run at most one call ahead of a peer (call k + 1 waits for that peer's flag
-// of call k + 1, written only after the peer's call k has merged), so the set
-// it overwrites is never being read.  Every wait is bounded (2 s); a timeout
-// sets the group's error word (kvl_mla_peer_group_check) and skips the merge.
+// IPC handles; layout in peer_merge.cuh).  Call k uses set k & 1 and tag k; a
+// rank can run at most one call ahead of a peer (its call k + 1 ends only after
+// reading that peer's words of call k + 1, stored only after the peer's call k
+// has merged), so the set it overwrites is never being read.  Every wait is
+// bounded (2 s); a timeout sets the group's error word
+// (kvl_mla_peer_group_check) and skips the merge.
 #include <cuda_runtime.h>
 
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
-#include <vector>
 
 #include "kvl/mla_cuda.h"
+#include "merge_core.cuh"
+#include "peer_merge.cuh"
 #include "prof.cuh"
 #include "sm100.cuh"
 
@@ -30,129 +38,175 @@ void set_error_text(const char *msg);  // mla_capi.cu
 
 namespace {
 
-constexpr int kMaxWorld = 8;
-constexpr int kMaxRows = 256;  // batch * num_heads per record
-constexpr int kThreads = 1024;
+constexpr int kMaxWorld = kPeerMaxWorld;
+constexpr int kMaxRows = kPeerMaxRows;
 
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_tagged(unsigned long long *p, unsigned long long tag, float v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(tag | __float_as_uint(v)) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long *p) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+  return w;
 }
 
-struct PeerArgs {
-  float *bufs[kMaxWorld];  // every rank's exchange buffer (this rank's own included)
+// Grid (sequence b, head h, 128-wide slice z of R), 256 threads: combine this
+// GPU's partials of (b, h, z) exactly as merge_partials_kernel does (or, for a
+// sequence that is not split, read its result from the record), store the slice and the lse as
+// tagged words into slot (set, rank, b, h) of every other GPU's buffer, poll
+// this GPU's buffer until every peer's words of (b, h, z) carry the call's tag,
+// and combine the world slices in rank order (so every GPU computes the same
+// bits).  No block waits for another block of its own grid, only for its
+// counterparts on the peers, which store before they wait; where the grid
+// (up to 256 (b, h) pairs x 4 slices) exceeds what is resident at once, the
+// lowest-numbered blocks of every GPU are resident together and finish first.
+struct AttendExchangeArgs {
+  unsigned long long *bufs[kMaxWorld];
   int rank, world, set;
   uint32_t epoch;
-  long long rec;           // floats per record
   int batch, nh, R;
+  long long slot;                   // words per (set, rank, b, h) slot: R data + lse + pad
+  const float *part_o, *part_lse;   // the plan's partials [P][nh][R], [P][nh]
+  const MergeEntry *entries;        // split sequences (device), n_entries of them
+  int n_entries;
+  const float *rec_o, *rec_lse;     // the other sequences: [batch][nh][R], [batch][nh]
 };
 
-__global__ void __launch_bounds__(kThreads, 1)
-    peer_exchange_merge_kernel(const __grid_constant__ PeerArgs a, const float *record, float *out, float *lse,
-                               uint32_t *err) {
-  __shared__ int timed_out;
-  if (threadIdx.x == 0) timed_out = 0;
-  const long long rec = a.rec;
-  // 1. this rank's record into slot `rank` of every buffer
-  const bool vec = (rec & 3) == 0 && (reinterpret_cast<uintptr_t>(record) & 15) == 0;
+constexpr int kXThreads = 256;
+
+__global__ void __launch_bounds__(kXThreads)
+    attend_exchange_kernel(const __grid_constant__ AttendExchangeArgs a, float *out, float *lse, uint32_t *err) {
+  const int b = blockIdx.x, h = blockIdx.y, z = blockIdx.z, R = a.R;
+  const int lane = threadIdx.x & 31;
+  // the attend grid's partials must be complete (this kernel is its programmatic dependent)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  int ei = -1;
+  for (int i = 0; i < a.n_entries; ++i)
+    if (a.entries[i].seq == b) ei = i;
+  float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+  float row_lse;
+  const int d0 = z * 128 + 4 * lane;  // this lane's elements d0 .. d0 + 3 (R is a multiple of 128)
+  if (ei >= 0) {
+    const MergeSlice r = merge_slice(a.entries[ei], h, z, a.part_o, a.part_lse, a.nh, R, 1,
+                                     static_cast<long long>(a.nh) * R, a.nh, true);
+    const float inv = 1.0f / r.sum;
+    v = make_float4(r.t.x * inv, r.t.y * inv, r.t.z * inv, r.t.w * inv);
+    row_lse = r.m + logf(r.sum);
+  } else {
+    const long long bh = static_cast<long long>(b) * a.nh + h;
+    if (threadIdx.x < 32) v = *reinterpret_cast<const float4 *>(a.rec_o + bh * R + d0);
+    row_lse = a.rec_lse[bh];
+  }
+  if (threadIdx.x >= 32) return;
+  // Word j * 32 + lane of the slice holds element d0 + j, so each store
+  // instruction of the warp writes 256 contiguous bytes; word R holds the lse.
+  const unsigned long long tag = static_cast<unsigned long long>(a.epoch) << 32;
+  auto slot_of = [&](const unsigned long long *buf, int r) {
+    return buf + (((static_cast<long long>(a.set) * a.world + r) * a.batch + b) * a.nh + h) * a.slot;
+  };
   for (int p = 0; p < a.world; ++p) {
-    float *dst = a.bufs[p] + (static_cast<long long>(a.set) * a.world + a.rank) * rec;
-    if (vec) {
-      for (long long i = threadIdx.x; i < rec / 4; i += blockDim.x)
-        reinterpret_cast<float4 *>(dst)[i] = reinterpret_cast<const float4 *>(record)[i];
-    } else {
-      for (long long i = threadIdx.x; i < rec; i += blockDim.x) dst[i] = record[i];
-    }
+    if (p == a.rank) continue;
+    unsigned long long *dst = const_cast<unsigned long long *>(slot_of(a.bufs[p], a.rank));
+    st_tagged(dst + z * 128 + lane, tag, v.x);
+    st_tagged(dst + z * 128 + 32 + lane, tag, v.y);
+    st_tagged(dst + z * 128 + 64 + lane, tag, v.z);
+    st_tagged(dst + z * 128 + 96 + lane, tag, v.w);
+    if (lane == 0) st_tagged(dst + R, tag, row_lse);  // every slice stores the same value
   }
-  // 2. flag `rank` of the current set in every buffer: the barrier orders every
-  // thread's record stores before thread 0's system-scope fence, which orders
-  // them before the flag stores (release is cumulative)
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int p = 0; p < a.world; ++p) {
-      uint32_t *flags = reinterpret_cast<uint32_t *>(a.bufs[p] + 2LL * a.world * rec);
-      st_release_sys(flags + a.set * a.world + a.rank, a.epoch);
-    }
-  }
-  // 3. wait for every rank's flag in this buffer
-  if (threadIdx.x < a.world) {
-    const uint32_t *flags = reinterpret_cast<const uint32_t *>(a.bufs[a.rank] + 2LL * a.world * rec);
-    const uint32_t *f = flags + a.set * a.world + threadIdx.x;
+  // wait until every peer's words of this lane carry the tag
+  const unsigned long long *mine = a.bufs[a.rank];
+  bool ok = true;
+  for (int r = 0; r < a.world && ok; ++r) {
+    if (r == a.rank) continue;
+    const unsigned long long *src = slot_of(mine, r);
     const uint64_t t0 = globaltimer();
-    while (ld_acquire_sys(f) != a.epoch) {
+    while (true) {
+      const unsigned long long w0 = ld_tagged(src + z * 128 + lane), w1 = ld_tagged(src + z * 128 + 32 + lane),
+                               w2 = ld_tagged(src + z * 128 + 64 + lane), w3 = ld_tagged(src + z * 128 + 96 + lane),
+                               wl = ld_tagged(src + R);
+      if (((w0 & w1 & w2 & w3 & wl) >> 32) == a.epoch && ((w0 | w1 | w2 | w3 | wl) >> 32) == a.epoch) break;
       if (globaltimer() - t0 > KVL_WAIT_LIMIT_NS) {
         atomicOr(err, ERR_TIMEOUT_FULL);
-        timed_out = 1;
+        ok = false;
         break;
       }
     }
   }
-  // the waiting threads' acquire loads, then the barrier, order the records
-  // before every thread's reads below
-  __syncthreads();
-  if (timed_out) return;
-  // 4. combine the world records: o = sum_r w_r o_r / sum_r w_r, w_r = exp(lse_r - max),
-  // the weights once per (sequence, head) in shared memory, the outputs in float4
-  __shared__ float sw[kMaxWorld * kMaxRows];
-  __shared__ float sinv[kMaxRows];
-  const float *base = a.bufs[a.rank] + static_cast<long long>(a.set) * a.world * rec;
-  const int rows = a.batch * a.nh;  // (sequence, head) pairs, <= kMaxRows (checked at create)
-  const long long olen = static_cast<long long>(rows) * a.R;
-  for (int bh = threadIdx.x; bh < rows; bh += blockDim.x) {
-    float m = -INFINITY;
-    for (int r = 0; r < a.world; ++r) m = fmaxf(m, base[r * rec + olen + bh]);
-    float sum = 0.f;
-    for (int r = 0; r < a.world; ++r) {
-      const float w = expf(base[r * rec + olen + bh] - m);
-      sw[r * kMaxRows + bh] = w;
-      sum += w;
+  if (!__all_sync(0xffffffffu, ok)) return;
+  auto val = [](unsigned long long w) { return __uint_as_float(static_cast<uint32_t>(w)); };
+  float mm = -INFINITY;
+  for (int r = 0; r < a.world; ++r) mm = fmaxf(mm, r == a.rank ? row_lse : val(ld_tagged(slot_of(mine, r) + R)));
+  float ss = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int r = 0; r < a.world; ++r) {
+    float4 u = v;
+    float lr = row_lse;
+    if (r != a.rank) {
+      const unsigned long long *src = slot_of(mine, r);
+      u = make_float4(val(ld_tagged(src + z * 128 + lane)), val(ld_tagged(src + z * 128 + 32 + lane)),
+                      val(ld_tagged(src + z * 128 + 64 + lane)), val(ld_tagged(src + z * 128 + 96 + lane)));
+      lr = val(ld_tagged(src + R));
     }
-    sinv[bh] = 1.0f / sum;
-    if (lse) lse[bh] = m + logf(sum);
+    const float w = expf(lr - mm);
+    ss += w;
+    acc.x = fmaf(w, u.x, acc.x);
+    acc.y = fmaf(w, u.y, acc.y);
+    acc.z = fmaf(w, u.z, acc.z);
+    acc.w = fmaf(w, u.w, acc.w);
   }
-  __syncthreads();
-  if ((a.R & 3) == 0 && (rec & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0) {
-    for (long long i4 = threadIdx.x; i4 < olen / 4; i4 += blockDim.x) {
-      const int bh = static_cast<int>((4 * i4) / a.R);
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int r = 0; r < a.world; ++r) {
-        const float w = sw[r * kMaxRows + bh];
-        const float4 v = reinterpret_cast<const float4 *>(base + r * rec)[i4];
-        acc.x = fmaf(w, v.x, acc.x);
-        acc.y = fmaf(w, v.y, acc.y);
-        acc.z = fmaf(w, v.z, acc.z);
-        acc.w = fmaf(w, v.w, acc.w);
-      }
-      const float inv = sinv[bh];
-      reinterpret_cast<float4 *>(out)[i4] = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-    }
-  } else {
-    for (long long i = threadIdx.x; i < olen; i += blockDim.x) {
-      const int bh = static_cast<int>(i / a.R);
-      float acc = 0.f;
-      for (int r = 0; r < a.world; ++r) acc = fmaf(sw[r * kMaxRows + bh], base[r * rec + i], acc);
-      out[i] = acc * sinv[bh];
-    }
-  }
+  const float inv = 1.0f / ss;
+  *reinterpret_cast<float4 *>(out + (static_cast<long long>(b) * a.nh + h) * R + d0) =
+      make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+  if (lse && z == 0 && lane == 0) lse[b * a.nh + h] = mm + logf(ss);
 }
 
 }  // namespace
-}  // namespace kvl
 
-struct KvlMlaPeerGroup {
-  int device = 0, rank = 0, world = 0, batch = 0, nh = 0, R = 0;
-  long long rec = 0;
-  float *local = nullptr;
-  float *peers[kvl::kMaxWorld] = {};
-  uint32_t *err = nullptr;
-  uint32_t epoch = 0;
-  bool connected = false;
-};
+namespace {
+cudaError_t launch_exchange(KvlMlaPeerGroup *g, const MergeEntry *entries, int n_entries, const float *part_o,
+                            const float *part_lse, const float *rec_o, const float *rec_lse, float *d_out,
+                            float *d_lse, cudaStream_t stream) {
+  AttendExchangeArgs a;
+  memset(&a, 0, sizeof a);
+  for (int r = 0; r < g->world; ++r) a.bufs[r] = reinterpret_cast<unsigned long long *>(g->peers[r]);
+  ++g->epoch;
+  a.rank = g->rank;
+  a.world = g->world;
+  a.set = static_cast<int>(g->epoch & 1u);
+  a.epoch = g->epoch;
+  a.batch = g->batch;
+  a.nh = g->nh;
+  a.R = g->R;
+  a.slot = peer_tagged_slot_words(g->R);
+  a.part_o = part_o;
+  a.part_lse = part_lse;
+  a.entries = entries;
+  a.n_entries = n_entries;
+  a.rec_o = rec_o;
+  a.rec_lse = rec_lse;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(g->batch, g->nh, g->R / 128);
+  cfg.blockDim = dim3(kXThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ProfScope ps(n_entries ? "attend_exchange" : "merge_exchange", stream);
+  return cudaLaunchKernelEx(&cfg, attend_exchange_kernel, a, d_out, d_lse, g->err);
+}
+}  // namespace
+
+cudaError_t launch_attend_exchange(KvlMlaPeerGroup *g, const DevicePlan &dp, float *d_out, float *d_lse,
+                                   cudaStream_t stream) {
+  return launch_exchange(
+      g, reinterpret_cast<const MergeEntry *>(static_cast<const uint8_t *>(dp.d_meta) + dp.off_merge),
+      static_cast<int>(dp.host.merges.size()), dp.part_o, dp.part_lse, g->stage,
+      g->stage + static_cast<long long>(g->batch) * g->nh * g->R, d_out, d_lse, stream);
+}
+
+}  // namespace kvl
 
 namespace {
 void peer_err(const char *what, cudaError_t e) {
@@ -167,7 +221,7 @@ KVL_EXPORT size_t kvl_mla_peer_handle_bytes(void) { return sizeof(cudaIpcMemHand
 KVL_EXPORT int kvl_mla_peer_group_create(KvlMlaPeerGroup **group, int rank, int world, int batch, int num_heads,
                                          int kv_lora_rank, void *handle_out) {
   if (!group || !handle_out || world < 2 || world > kvl::kMaxWorld || rank < 0 || rank >= world || batch <= 0 ||
-      num_heads <= 0 || kv_lora_rank <= 0 || batch * num_heads > kvl::kMaxRows) {
+      num_heads <= 0 || kv_lora_rank <= 0 || kv_lora_rank % 128 != 0 || batch * num_heads > kvl::kMaxRows) {
     kvl::set_error_text("invalid peer group arguments");
     return -1;
   }
@@ -179,9 +233,10 @@ KVL_EXPORT int kvl_mla_peer_group_create(KvlMlaPeerGroup **group, int rank, int 
   g->nh = num_heads;
   g->R = kv_lora_rank;
   g->rec = static_cast<long long>(batch) * num_heads * (kv_lora_rank + 1);
-  const size_t bytes = (2ull * world * g->rec) * sizeof(float) + 2ull * world * sizeof(uint32_t);
+  const size_t bytes = kvl::peer_buffer_bytes(world, batch, num_heads, kv_lora_rank);
   cudaError_t e = cudaMalloc(&g->local, bytes);
   if (e == cudaSuccess) e = cudaMemset(g->local, 0, bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&g->stage, g->rec * sizeof(float));
   if (e == cudaSuccess) e = cudaMalloc(&g->err, sizeof(uint32_t));
   if (e == cudaSuccess) e = cudaMemset(g->err, 0, sizeof(uint32_t));
   cudaIpcMemHandle_t h;
@@ -189,6 +244,7 @@ KVL_EXPORT int kvl_mla_peer_group_create(KvlMlaPeerGroup **group, int rank, int 
   if (e != cudaSuccess) {
     peer_err("peer group create", e);
     cudaFree(g->local);
+    cudaFree(g->stage);
     cudaFree(g->err);
     delete g;
     return -1;
@@ -225,26 +281,15 @@ KVL_EXPORT int kvl_mla_peer_group_connect(KvlMlaPeerGroup *g, const void *handle
 
 KVL_EXPORT int kvl_mla_merge_exchange(KvlMlaPeerGroup *g, float *d_out, float *d_lse, const float *d_record,
                                       void *stream) {
-  if (!g || !g->connected || !d_out || !d_record) {
-    kvl::set_error_text("invalid merge exchange arguments");
+  if (!g || !g->connected || !d_out || !d_record ||
+      ((reinterpret_cast<uintptr_t>(d_out) | reinterpret_cast<uintptr_t>(d_record)) & 15) != 0) {
+    kvl::set_error_text("invalid merge exchange arguments (d_out and d_record 16-byte aligned)");
     return -1;
   }
-  kvl::PeerArgs a;
-  memset(&a, 0, sizeof a);
-  for (int r = 0; r < g->world; ++r) a.bufs[r] = g->peers[r];
-  ++g->epoch;
-  a.rank = g->rank;
-  a.world = g->world;
-  a.set = static_cast<int>(g->epoch & 1u);
-  a.epoch = g->epoch;
-  a.rec = g->rec;
-  a.batch = g->batch;
-  a.nh = g->nh;
-  a.R = g->R;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  kvl::ProfScope ps("merge_exchange", s);
-  kvl::peer_exchange_merge_kernel<<<1, kvl::kThreads, 0, s>>>(a, d_record, d_out, d_lse, g->err);
-  const cudaError_t e = cudaGetLastError();
+  const cudaError_t e =
+      kvl::launch_exchange(g, nullptr, 0, nullptr, nullptr, d_record,
+                           d_record + static_cast<long long>(g->batch) * g->nh * g->R, d_out, d_lse,
+                           static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) {
     peer_err("merge exchange launch", e);
     return -1;
@@ -273,6 +318,7 @@ KVL_EXPORT void kvl_mla_peer_group_destroy(KvlMlaPeerGroup *g) {
   for (int r = 0; r < g->world; ++r)
     if (r != g->rank && g->peers[r]) cudaIpcCloseMemHandle(g->peers[r]);
   cudaFree(g->local);
+  cudaFree(g->stage);
   cudaFree(g->err);
   delete g;
 }

@@ -105,6 +105,8 @@ SIGNATURES = {
     "kvl_mla_merge_exchange": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
     "kvl_mla_peer_group_check": (C.c_int, [C.c_void_p, C.c_void_p]),
     "kvl_mla_peer_group_destroy": (None, [C.c_void_p]),
+    "kvl_mla_attend_bf16_exchange": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                               C.c_void_p, C.c_int64, C.c_float, C.c_void_p]),
     "kvl_mla_decode_step_workspace_bytes": (C.c_size_t, [C.POINTER(KvlMlaConfig), C.c_int]),
     "kvl_mla_decode_step_bf16": (C.c_int, [C.POINTER(KvlMlaConfig), C.POINTER(KvlMlaDeviceWeights), C.c_void_p,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
@@ -260,6 +262,12 @@ class PeerGroup:
 
     def merge(self, out, lse, record, stream=0):
         return self.lib.kvl_mla_merge_exchange(self.h, t_ptr(out), t_ptr(lse), t_ptr(record), stream)
+
+    def attend_exchange(self, plan, out, lse, q, kv, rows, scale=1.0 / np.sqrt(192.0), stream=0):
+        """kvl_mla_attend_bf16_exchange: attend this rank's KV range with `plan`
+        and combine across the group in the same call."""
+        return self.lib.kvl_mla_attend_bf16_exchange(plan.h, self.h, t_ptr(out), t_ptr(lse), t_ptr(q), t_ptr(kv),
+                                                     rows, float(scale), stream)
 
     def check(self, stream=0):
         return self.lib.kvl_mla_peer_group_check(self.h, stream)

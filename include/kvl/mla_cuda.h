@@ -128,15 +128,18 @@ int kvl_mla_merge_packed(float *d_out, float *d_lse, const float *d_parts, int p
 
 /* The combine of a split-KV decode across the GPUs of one node in one launch
  * (in place of an all-gather plus kvl_mla_merge_packed): each GPU stores its
- * packed record (d_out-layout [batch][num_heads][R] then lse [batch][num_heads])
- * into every GPU's exchange buffer over NVLink, raises a flag there and merges
- * the world records once every flag of the call is up.  One process per GPU:
+ * (o, lse) values into every other GPU's exchange buffer over NVLink as tagged
+ * 64-bit words (call number and value in one store) and merges the world
+ * records once every word it needs carries the call's tag.  One process per GPU:
  *   create (allocates this GPU's buffer; writes its CUDA IPC handle, of
  *   kvl_mla_peer_handle_bytes() bytes, to handle_out) -> the caller gathers the
  *   world handles in rank order (any host collective) -> connect -> per step
- *   kvl_mla_merge_exchange on every rank, in the same order -> destroy.
- * batch * num_heads <= 256, world <= 8.  Waits are bounded (2 s);
- * kvl_mla_peer_group_check reports a record that did not arrive. */
+ *   kvl_mla_merge_exchange (packed record d_record = [batch][num_heads][R] then
+ *   lse [batch][num_heads]) or kvl_mla_attend_bf16_exchange on every rank, in
+ *   the same order -> destroy.
+ * batch * num_heads <= 256, world <= 8, kv_lora_rank a multiple of 128; d_out
+ * and d_record 16-byte aligned.  Waits are bounded (2 s);
+ * kvl_mla_peer_group_check reports a peer whose values did not arrive. */
 typedef struct KvlMlaPeerGroup KvlMlaPeerGroup;
 size_t kvl_mla_peer_handle_bytes(void);
 int kvl_mla_peer_group_create(KvlMlaPeerGroup **group, int rank, int world, int batch, int num_heads,
@@ -146,6 +149,17 @@ int kvl_mla_merge_exchange(KvlMlaPeerGroup *group, float *d_out, float *d_lse, c
                            void *stream);
 int kvl_mla_peer_group_check(KvlMlaPeerGroup *group, void *stream);
 void kvl_mla_peer_group_destroy(KvlMlaPeerGroup *group);
+/* The attend of this rank's KV range (plan of `batch` sequences, 16 heads,
+ * R = 512, rope 64) and the cross-GPU combine in two launches: the attend leaves
+ * split sequences as partials, and one kernel per (sequence, head, 128-wide
+ * slice) combines them locally (as kvl_mla_attend_bf16 would), exchanges the
+ * slice with every peer and merges the world slices into d_out [batch][16][512]
+ * and d_lse [batch][16] (NULL: not written).  Replaces kvl_mla_attend_bf16 +
+ * kvl_mla_merge_exchange; d_out 16-byte aligned; the plan's batch must equal the
+ * group's. */
+int kvl_mla_attend_bf16_exchange(const KvlMlaAttendPlan *plan, KvlMlaPeerGroup *group, float *d_out,
+                                 float *d_lse, const float *d_q, const uint16_t *d_kv, int64_t rows,
+                                 float softmax_scale, void *stream);
 
 /* ------------------------------------------------------------------ batched decode step */
 
