@@ -991,6 +991,21 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
     CK(cudaStreamWaitEvent(fk->s2, fk->fork, 0));
   }
 
+  // kva = x Wkva^T, fp32 [S][576], launched first: its 96 tiles (S = 4096) fill
+  // 96 SMs for one round, and the q GEMM's CTA pairs take the idle SMs meanwhile
+  GemmParams g;
+  memset(&g, 0, sizeof g);
+  g.err = err;
+  if (!bf16_map(&g.tm_a, xb + R0 * H, H, m, H * 2, 128) || !bf16_map(&g.tm_b, W.kva, H, 576, H * 2, 192)) {
+    set_err("prefill: tensor map (kv_a_proj)");
+    return -1;
+  }
+  g.M = M;
+  g.K = static_cast<int>(H);
+  g.N = 576;
+  g.c = kva + R0 * 576;
+  g.ldc = 576;
+  CK(launch_gemm(g, 192, EPI_F32, sms, st, "gemm_kva"));
   // q = x Wq^T with RoPE on each head's last 64 columns, bf16 [S][16][192]
   // (on the second stream when forked, after the RoPE table)
   GemmParams gq;
@@ -1011,20 +1026,6 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   CK(launch_gemm_pair(gq, 256, EPI_QROPE, sms, sq, "gemm_q"));
   if (fork) CK(cudaEventRecord(fk->qdone, sq));
 
-  // kva = x Wkva^T, fp32 [S][576]
-  GemmParams g;
-  memset(&g, 0, sizeof g);
-  g.err = err;
-  if (!bf16_map(&g.tm_a, xb + R0 * H, H, m, H * 2, 128) || !bf16_map(&g.tm_b, W.kva, H, 576, H * 2, 192)) {
-    set_err("prefill: tensor map (kv_a_proj)");
-    return -1;
-  }
-  g.M = M;
-  g.K = static_cast<int>(H);
-  g.N = 576;
-  g.c = kva + R0 * 576;
-  g.ldc = 576;
-  CK(launch_gemm(g, 192, EPI_F32, sms, st, "gemm_kva"));
   // latent = rmsnorm(kva[:512]) * kv_a_norm, k_rope = rope(kva[512:]) -> pool [S][576] bf16
   if (fork) CK(cudaStreamWaitEvent(st, fk->rope, 0));
   CK(append_rows_bf16(pool + R0 * 576, kva + R0 * 576, W.kvan, cs + R0 * 32, M, cfg.rms_eps, st));
