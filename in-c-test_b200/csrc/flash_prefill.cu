@@ -143,8 +143,6 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = B->tmem_base;
-  pdl_wait();  // q, k/v and the pool are complete from here on
-  pdl_trigger();
 
   if (warp == 8) {
     // ---------------------------------------------------------------- Q and K copies
@@ -414,7 +412,8 @@ cudaError_t launch_flash_prefill(const FlashParams &p, int sms, cudaStream_t str
   if (items <= 0 || p.q_tile0 < 0) return cudaErrorInvalidValue;
   const int grid = items < sms ? items : sms;
   ProfScope ps("flash_prefill", stream);
-  return launch_pdl(flash_prefill_kernel, dim3(grid), dim3(kThreads), kSmem, stream, p);
+  flash_prefill_kernel<<<grid, kThreads, kSmem, stream>>>(p);
+  return cudaGetLastError();
 }
 
 }  // namespace kvl

@@ -182,15 +182,11 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = B->tmem_base;
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&p.tm_a);
-    tma_prefetch_desc(&p.tm_b);
-  }
-  pdl_wait();  // the previous kernel's outputs (A) are complete from here on
-  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
+      tma_prefetch_desc(&p.tm_a);
+      tma_prefetch_desc(&p.tm_b);
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
@@ -350,15 +346,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem = B->tmem_base;
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&p.tm_a);
-    tma_prefetch_desc(&p.tm_b);
-  }
-  pdl_wait();  // the previous kernel's outputs (A) are complete from here on
-  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
+      tma_prefetch_desc(&p.tm_a);
+      tma_prefetch_desc(&p.tm_b);
       uint32_t it = 0;
       bool ok = true;
       for (int tile = pair; tile < tiles && ok; tile += npairs) {
@@ -446,7 +438,8 @@ static cudaError_t launch_gemm_t(const GemmParams &p, int sms, cudaStream_t stre
                     (p.ksplit > 1 ? p.ksplit : 1);
   const int grid = tiles < sms ? tiles : sms;
   ProfScope ps(name, stream);
-  return launch_pdl(gemm_bf16_tn_kernel<BN, EPI>, dim3(grid), dim3(192), L::kSmem, stream, p);
+  gemm_bf16_tn_kernel<BN, EPI><<<grid, 192, L::kSmem, stream>>>(p);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream, const char *name) {
@@ -484,7 +477,8 @@ static cudaError_t launch_gemm_pair_t(const GemmParams &p, int sms, cudaStream_t
   if (pairs > tiles) pairs = tiles;
   if (pairs < 1) pairs = 1;
   ProfScope ps(name, stream);
-  return launch_pdl(gemm_pair_bf16_tn_kernel<BN, EPI>, dim3(2 * pairs), dim3(192), L::kSmem, stream, p);
+  gemm_pair_bf16_tn_kernel<BN, EPI><<<2 * pairs, 192, L::kSmem, stream>>>(p);
+  return cudaGetLastError();
 }
 
 // B's tensor map box must be {64, bn / 2} rows for the pair form.
@@ -505,8 +499,6 @@ cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cuda
 __global__ void rope_table_kernel(float2 *cs, int rows, int dim, float theta) {
   __shared__ double inv_freq_s[128];
   const int half = dim / 2;
-  pdl_wait();
-  pdl_trigger();
   // theta^(-2k/dim) once per frequency (half <= 128 is checked by the launcher)
   for (int k = threadIdx.x; k < half; k += blockDim.x)
     inv_freq_s[k] = pow(static_cast<double>(theta), -(static_cast<double>(2 * k) / static_cast<double>(dim)));
@@ -527,7 +519,8 @@ cudaError_t launch_rope_table(float2 *cs, int rows, int dim, float theta, cudaSt
   const long long n = static_cast<long long>(rows) * (dim / 2);
   const int grid = static_cast<int>((n + 255) / 256 < 148 * 8 ? (n + 255) / 256 : 148 * 8);
   ProfScope ps("rope_table", stream);
-  return launch_pdl(rope_table_kernel, dim3(grid), dim3(256), 0, stream, cs, rows, dim, theta);
+  rope_table_kernel<<<grid, 256, 0, stream>>>(cs, rows, dim, theta);
+  return cudaGetLastError();
 }
 
 }  // namespace kvl

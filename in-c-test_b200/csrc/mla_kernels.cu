@@ -20,7 +20,6 @@
 
 #include "mla_kernels.cuh"
 #include "prof.cuh"
-#include "sm100.cuh"
 
 namespace kvl {
 
@@ -206,8 +205,6 @@ __global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, const u
   constexpr int R = 512, DR = 64;
   const int warp = static_cast<int>((blockIdx.x * static_cast<unsigned>(blockDim.x) + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
-  pdl_wait();
-  pdl_trigger();
   if (warp >= n) return;
   const float *kt = ka + static_cast<size_t>(warp) * (R + DR);
   float4 v[4];
@@ -252,7 +249,8 @@ cudaError_t append_rows_bf16(uint16_t *pool, const float *ka, const uint16_t *no
                              float eps, cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   ProfScope ps("append_bf16", s);
-  return launch_pdl(append_rows_bf16_kernel, dim3((n + 7) / 8), dim3(256), 0, s, pool, ka, norm_w, cs, n, eps);
+  append_rows_bf16_kernel<<<(n + 7) / 8, 256, 0, s>>>(pool, ka, norm_w, cs, n, eps);
+  return cudaGetLastError();
 }
 
 // src/mla_compressed_q8_state.c:34-55 for one row held in shared memory.
