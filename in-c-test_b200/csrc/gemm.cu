@@ -42,7 +42,11 @@ struct Layout {
   static constexpr uint32_t kStageBytes = kABytes + kBBytes;
   static constexpr uint32_t OFF_BAR = kStages * kStageBytes;
   static constexpr uint32_t kSmem = OFF_BAR + 256 + 1024;
-  static constexpr uint32_t kTmemCols = 512;
+  // two accumulators of kAccCols columns; narrow tiles take less tensor memory so
+  // that two CTAs that share an SM (BN = 64: 97 KB of shared memory each) do not
+  // wait for each other's allocation
+  static constexpr uint32_t kAccCols = BN <= 64 ? 64 : BN <= 128 ? 128 : 256;
+  static constexpr uint32_t kTmemCols = 2 * kAccCols;
 };
 
 struct Bars {
@@ -235,7 +239,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
           const uint32_t b_addr = a_addr + kABytes;
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_f16_ss(tmem + ab * 256, smem_desc(a_addr + kk * 32, 16, 1024, LAYOUT_SW128),
+            mma_f16_ss(tmem + ab * L::kAccCols, smem_desc(a_addr + kk * 32, 16, 1024, LAYOUT_SW128),
                        smem_desc(b_addr + kk * 32, 16, 1024, LAYOUT_SW128), idesc,
                        (ks != kbeg || kk) ? 1u : 0u);
           mma_commit(&B->empty[s]);
@@ -259,7 +263,7 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
       tc_fence_after();
       const int row = mb * kBM + 32 * sub + lane;
       const bool row_ok = row < p.M;
-      const uint32_t tbase = tmem + ab * 256 + lane_base;
+      const uint32_t tbase = tmem + ab * L::kAccCols + lane_base;
       epilogue_tile<BN, EPI>(p, tbase, row, row_ok, nb, (batched || nsplit > 1) ? z * p.c_bstride : 0);
       tc_fence_before();
       __syncwarp();
@@ -461,6 +465,8 @@ cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStrea
   } else if (bn == 128) {
     if (epi == EPI_F32) return launch_gemm_t<128, EPI_F32>(p, sms, stream, name);
     if (epi == EPI_BF16) return launch_gemm_t<128, EPI_BF16>(p, sms, stream, name);
+  } else if (bn == 64) {
+    if (epi == EPI_F32) return launch_gemm_t<64, EPI_F32>(p, sms, stream, name);
   }
   return cudaErrorInvalidValue;
 }

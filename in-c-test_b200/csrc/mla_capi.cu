@@ -992,11 +992,16 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   }
 
   // kva = x Wkva^T, fp32 [S][576], launched first: its 96 tiles (S = 4096) fill
-  // 96 SMs for one round, and the q GEMM's CTA pairs take the idle SMs meanwhile
+  // 96 SMs for one round, and the q GEMM's CTA pairs take the idle SMs meanwhile.
+  // When 3 tiles per 128 rows would leave more than half of the SMs idle (up to
+  // 3072 rows on 148 SMs: a chunk of the host-buffer pipeline, a short prompt),
+  // kv_a takes 64-column tiles, 9 per 128 rows (the same sums per element: the
+  // MMA accumulates each element over K in the same order whatever the width).
+  const int kva_bn = (M + 127) / 128 * 3 * 2 < sms ? 64 : 192;
   GemmParams g;
   memset(&g, 0, sizeof g);
   g.err = err;
-  if (!bf16_map(&g.tm_a, xb + R0 * H, H, m, H * 2, 128) || !bf16_map(&g.tm_b, W.kva, H, 576, H * 2, 192)) {
+  if (!bf16_map(&g.tm_a, xb + R0 * H, H, m, H * 2, 128) || !bf16_map(&g.tm_b, W.kva, H, 576, H * 2, kva_bn)) {
     set_err("prefill: tensor map (kv_a_proj)");
     return -1;
   }
@@ -1005,7 +1010,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   g.N = 576;
   g.c = kva + R0 * 576;
   g.ldc = 576;
-  CK(launch_gemm(g, 192, EPI_F32, sms, st, "gemm_kva"));
+  CK(launch_gemm(g, kva_bn, EPI_F32, sms, st, "gemm_kva"));
   // q = x Wq^T with RoPE on each head's last 64 columns, bf16 [S][16][192]
   // (on the second stream when forked, after the RoPE table)
   GemmParams gq;
@@ -1081,15 +1086,22 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
 }  // namespace
 }  // namespace kvl
 
-// Chunks of the host-buffer prefill pipeline (whole multiples of 128 rows).
-// Measured at S = 4096 on one B200 (PCIe: 0.61 ms each way, full duplex):
-// 1 chunk 1.48 ms, 2 chunks 1.21 ms, 4 chunks 1.02 ms, 8 chunks 1.32 ms per
-// call -- smaller chunks overlap more copy time but run the GEMMs and the
-// causal attention on fewer SMs.
-static int prefill_chunks(int seq_len) {
-  if (seq_len >= 2048) return 4;
-  if (seq_len >= 1024) return 2;
-  return 1;
+// Row boundaries of the host-buffer prefill pipeline: equal chunks of a
+// multiple of 128 rows; returns the chunk count, bounds[0..count] the
+// boundaries.  Measured at S = 4096 on one B200 (PCIe about 52 GB/s each way
+// alone, ~40 GB/s each way when both directions run; a 1024-row chunk computes
+// in ~140 us, mostly one round of each GEMM): 3 chunks 1.14 ms per call,
+// 4 chunks 1.01 ms, 4 chunks without the second stream or with 192-column kv_a
+// tiles 1.02-1.04 ms, 5 chunks with half-size end chunks 1.06-1.08 ms,
+// 8 chunks 1.32 ms -- smaller chunks overlap more copy time, but every chunk
+// pays the latency of its seven kernels.
+static int prefill_chunk_bounds(int seq_len, int *bounds) {
+  const int nch = seq_len >= 2048 ? 4 : seq_len >= 1024 ? 2 : 1;
+  const int rows = ((seq_len + nch - 1) / nch + 127) / 128 * 128;
+  int n = 0;
+  bounds[0] = 0;
+  for (int r0 = 0; r0 < seq_len; r0 += rows) bounds[++n] = std::min(seq_len, r0 + rows);
+  return n;
 }
 
 // Reference: src/mla_prefill_streaming.c:78-206 (validation :80-85).
@@ -1115,7 +1127,8 @@ KVL_EXPORT int kvl_mla_prefill_bf16(float *out, const float *x, int seq_len, con
   }
   uint8_t *ws = c->kvtmp.as<uint8_t>();
   float *xf = reinterpret_cast<float *>(ws + L.off[0]);
-  const int nch = fast_prefill_shape(*cfg) ? prefill_chunks(seq_len) : 1;
+  int bounds[kMaxPrefillChunks + 1];
+  const int nch = fast_prefill_shape(*cfg) ? prefill_chunk_bounds(seq_len, bounds) : 1;
   if (nch > 1) {
     // Chunked pipeline: the H2D copy of chunk i+1 and the D2H copy of chunk
     // i-1 run on their own streams while chunk i computes (its queries attend
@@ -1133,24 +1146,23 @@ KVL_EXPORT int kvl_mla_prefill_bf16(float *out, const float *x, int seq_len, con
           return -1;
         }
     }
-    const int rows = ((seq_len + nch - 1) / nch + 127) / 128 * 128;
     uint16_t *xb = reinterpret_cast<uint16_t *>(ws + L.off[1]);
     float *y = c->y.as<float>();
     // the weights were staged on c->stream: the copies and kernels below follow it
     CK(cudaEventRecord(c->ev_out[0], c->stream));
     CK(cudaStreamWaitEvent(c->copy_in, c->ev_out[0], 0));
-    for (int i = 0, r0 = 0; r0 < seq_len; ++i, r0 += rows) {
-      const size_t n = static_cast<size_t>(std::min(seq_len, r0 + rows) - r0) * H;
-      CK(cudaMemcpyAsync(xf + static_cast<size_t>(r0) * H, x + static_cast<size_t>(r0) * H, n * 4,
-                         cudaMemcpyHostToDevice, c->copy_in));
+    for (int i = 0; i < nch; ++i) {
+      const size_t off = static_cast<size_t>(bounds[i]) * H, n = static_cast<size_t>(bounds[i + 1] - bounds[i]) * H;
+      CK(cudaMemcpyAsync(xf + off, x + off, n * 4, cudaMemcpyHostToDevice, c->copy_in));
       CK(cudaEventRecord(c->ev_in[i], c->copy_in));
     }
-    for (int i = 0, r0 = 0; r0 < seq_len; ++i, r0 += rows) {
-      const int r1 = std::min(seq_len, r0 + rows);
+    for (int i = 0; i < nch; ++i) {
+      const int r0 = bounds[i], r1 = bounds[i + 1];
       const size_t off = static_cast<size_t>(r0) * H, n = static_cast<size_t>(r1 - r0) * H;
       CK(cudaStreamWaitEvent(c->stream, c->ev_in[i], 0));
       CK(f32_to_bf16(xb + off, xf + off, static_cast<long long>(n), c->stream));
-      if (prefill_fast(c->sms, *cfg, W, y, xb, seq_len, ws, L, c->stream, r0, r1, false) != 0) return -1;
+      // q_proj on the second stream beside the kv_a -> append -> kv_b chain
+      if (prefill_fast(c->sms, *cfg, W, y, xb, seq_len, ws, L, c->stream, r0, r1, true) != 0) return -1;
       CK(cudaEventRecord(c->ev_out[i], c->stream));
       CK(cudaStreamWaitEvent(c->copy_out, c->ev_out[i], 0));
       CK(cudaMemcpyAsync(out + off, y + off, n * 4, cudaMemcpyDeviceToHost, c->copy_out));
