@@ -1094,7 +1094,8 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
 // 4 chunks 1.01 ms, 4 chunks without the second stream or with 192-column kv_a
 // tiles 1.02-1.04 ms, 5 chunks with half-size end chunks 1.06-1.08 ms,
 // 8 chunks 1.32 ms -- smaller chunks overlap more copy time, but every chunk
-// pays the latency of its seven kernels.
+// pays the latency of its seven kernels.  Replaying each chunk as a recorded
+// CUDA graph was slower (1.09 ms).
 static int prefill_chunk_bounds(int seq_len, int *bounds) {
   const int nch = seq_len >= 2048 ? 4 : seq_len >= 1024 ? 2 : 1;
   const int rows = ((seq_len + nch - 1) / nch + 127) / 128 * 128;
