@@ -33,6 +33,7 @@ import os
 import pathlib
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -108,11 +109,13 @@ class ClockSampler:
     def __init__(self, gpu_index: int):
         self.proc = None
         self.gpu = gpu_index
-        self.path = ROOT / "gpurun_out" / f"clocks_rank{gpu_index}.csv"
+        # the raw samples go to $KVL_BENCH_OUT (default: the system temp directory)
+        out = os.environ.get("KVL_BENCH_OUT") or tempfile.gettempdir()
+        self.path = pathlib.Path(out) / f"kvl_bench_clocks_rank{gpu_index}.csv"
 
     def start(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
+            self.path.parent.mkdir(parents=True, exist_ok=True)
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-i", str(self.gpu), "-lms", "200"], stdout=self.f,
