@@ -771,8 +771,14 @@ def run_reference(args, dist):
     torchrun only rank 0 runs; the others exit without work."""
     if dist.rank != 0:
         return 0
-    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
-    cores = int(os.environ["OMP_NUM_THREADS"])
+    # every host thread this process may use (torchrun exports OMP_NUM_THREADS=1
+    # to each rank; here rank 0 runs alone), set before the reference library
+    # and its OpenMP runtime are loaded
+    try:
+        cores = len(os.sched_getaffinity(0))
+    except AttributeError:
+        cores = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(cores)
     from oracle.oracle import reference_available
     if not reference_available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref was not built (reference sources absent)"}))
