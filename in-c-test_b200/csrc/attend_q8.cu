@@ -3,24 +3,37 @@
 // reference's layout, include/kvl/mla_compressed_q8_state.h).
 //
 // Reference semantics: src/mla_compressed_q8_state.c:216-238, with the
-// dequantised row latent_j = (float)q_j * scale_j (:57-61).  The stored int8
-// values are exact in fp16, so the kernel feeds them to the tensor core
-// unscaled and applies the row scale outside the MMA:
-//     s_j  = scale_j * (q_lat . q_j) + (q_rope . rope_j)
-//     O    = sum_j (p_j * scale_j) q_j           (P' = p * scale in fp16)
-// which equals sum_j p_j * dequant(q_j) up to the rounding of P'.
+// dequantised row latent_j = (float)q_j * scale_j (:57-61).  Both contractions
+// run on the int8 tensor-core path (tcgen05 kind::i8, int32 accumulation)
+// straight from the int8 rows TMA brings in -- no conversion pass:
 //
-// Tiles of 128 KV rows (see attend_bf16.cu for the MMA cost model).  Shared
-// memory: int8 staging ring 2 x 16 KB (128 rows x 128 dims), fp16 ring 4 x
-// 32 KB (one tile; a slot is released when its P.V MMAs end), rope ring 2 x
-// 16 KB.
+//   scores  q_lat is split per head into two int8 parts, q ~ sq * (hi + lo/256)
+//           (sq = max|q_lat| / 127, so about 16 bits of precision); both parts
+//           go into one N = 32 MMA against the int8 rows (exact int32 sums), and
+//             s_j = scale_j * sq * (S_hi + S_lo / 256) + q_rope . rope_j
+//           with the rope term on the bf16 tensor core (fp32 accumulation).
+//   mix     P'_j = p_j * scale_j is split per head and tile the same way,
+//           P' ~ sp * (hi + lo/256) (sp = max_j |P'_j| / 127), and the P.V MMA
+//           reads the same int8 rows as an MN-major operand: per tile
+//             O += sp * (O_hi + O_lo / 256)
+//           folded into fp32 register accumulators by the softmax threads.
+// The int32 sums are exact; the only roundings are the two 16-bit splits and
+// fp32 arithmetic (the reference accumulates in double).
+//
+// Tiles of 128 KV rows.  Shared memory is one ring of 12 boxes of 16 KB
+// (128 rows x 128 B): a tile is five boxes -- the bf16 rope and four 128-dim
+// int8 chunks -- so the producer runs about two tiles ahead.  The rope box is
+// released when the tile's score MMAs end, a chunk when its P.V MMAs end.
+// Within a segment the issuer runs the scores of tile g+1 before the P.V of
+// tile g, so the tensor pipe works while the softmax of tile g runs.
 //
 // Roles (384 threads, one CTA per SM):
-//   warp 0      TMA producer (int8 staging + rope)
-//   warp 1      TMEM owner and tcgen05 issuer
-//   warps 4-7   query load per segment (q_lat -> fp16, q_rope -> bf16 SW128
-//               tiles), softmax and epilogue (TMEM subpartitions 0-3; thread = KV row)
-//   warps 8-11  converters: int8 staging -> fp16 SW128 ring
+//   warp 0       TMA producer
+//   warp 1       TMEM owner and tcgen05 issuer
+//   warps 4-11   two warpgroups of eight heads each: softmax, P' split, fold
+//                of the per-tile P.V sums, epilogue (thread = KV row of the
+//                tile for the scores, = latent dim of each 128-dim chunk for
+//                the mix); warpgroup 0 also splits the query of each segment
 #include "attend_common.cuh"
 #include "prof.cuh"
 #include "sm100.cuh"
@@ -28,58 +41,131 @@
 namespace kvl {
 namespace q8dec {
 
-constexpr int kStgSlots = 2;
-constexpr int kCvtSlots = 4;
-constexpr int kRopeSlots = 2;
+constexpr int kSlots = 12;
+constexpr int kBoxesPerTile = 5;               // rope + four int8 chunks
 constexpr uint32_t kBox = kTileTok * 128;      // 128 rows x 128 B = 16 KB
-constexpr uint32_t kStgBytes = kBox;           // int8: 128 rows x 128 dims
-constexpr uint32_t kCvtBytes = 2 * kBox;       // fp16: 128 rows x 128 dims (two 64-dim boxes)
-constexpr uint32_t kRopeBytes = kBox;          // bf16: 128 rows x 64 dims
-constexpr uint32_t kQBytes = 9 * 2048;
-constexpr uint32_t kPChunkSbo = (kTileTok / 8) * 128;
-constexpr uint32_t kPBytes = 2 * kPChunkSbo;
-constexpr uint32_t OFF_CVT = 0;
-constexpr uint32_t OFF_STG = OFF_CVT + kCvtSlots * kCvtBytes;
-constexpr uint32_t OFF_ROPE = OFF_STG + kStgSlots * kStgBytes;
-constexpr uint32_t OFF_Q = OFF_ROPE + kRopeSlots * kRopeBytes;
-constexpr uint32_t OFF_P = OFF_Q + kQBytes;
+constexpr uint32_t kQiBytes = 4 * 32 * 128;    // q parts [32][512] int8: four SW128 boxes of 32 rows
+constexpr uint32_t kQrBytes = kHeads * 128;    // q_rope [16][64] bf16: one SW128 box
+constexpr uint32_t kPBytes = 128 * 32;         // P' parts [128 KV rows][32] int8, MN-major, 32-byte swizzle
+constexpr uint32_t OFF_RING = 0;
+constexpr uint32_t OFF_QI = OFF_RING + kSlots * kBox;
+constexpr uint32_t OFF_QR = OFF_QI + kQiBytes;
+constexpr uint32_t OFF_P = OFF_QR + kQrBytes;
 constexpr uint32_t OFF_BAR = OFF_P + 2 * kPBytes;
 
 struct Bars {
-  uint64_t stg_full[kStgSlots], stg_empty[kStgSlots];
-  uint64_t cvt_full[kCvtSlots], cvt_empty[kCvtSlots];
-  uint64_t rope_full[kRopeSlots], rope_empty[kRopeSlots];
+  uint64_t full[kSlots], empty[kSlots];
   uint64_t q_full;
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full[2], p_empty[2];
-  uint64_t o_full, o_empty, drain;
+  uint64_t o_full[2], o_empty[2];
+  uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  float red[4][kHeads];
+  float qscale[kHeads];        // sq per head of the current segment
+  float red[2][4][8];          // per warpgroup: running-max / sum exchange
+  float pmax[2][2][4][8];      // per tile parity and warpgroup: max |P'| of each warp
 };
 
 constexpr uint32_t kSmemBytes = OFF_BAR + sizeof(Bars) + 1024;
-static_assert(OFF_STG % 1024 == 0 && OFF_ROPE % 1024 == 0 && OFF_Q % 1024 == 0 && OFF_P % 1024 == 0, "align");
+static_assert(OFF_QI % 1024 == 0 && OFF_QR % 1024 == 0 && OFF_P % 1024 == 0 && OFF_BAR % 8 == 0, "align");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-// TMEM columns: latent scores 2 buffers x 16 @0, rope scores 2 x 16 @32, O 4 x 16 @64.
-constexpr uint32_t kColRope = 32;
-constexpr uint32_t kColO = 64;
-constexpr uint32_t kTmemCols = 128;
+// TMEM columns: int32 scores 2 x 32 (heads hi | lo) @0, fp32 rope scores
+// 2 x 16 @64, int32 P.V sums 2 buffers x 4 chunks x 32 @128.
+constexpr uint32_t kColS = 0;
+constexpr uint32_t kColR = 64;
+constexpr uint32_t kColO = 128;
+constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kThreads = 384;
+constexpr uint32_t LAYOUT_SW32 = 6;  // tcgen05 shared-memory descriptor: 32-byte swizzle
 
-// Four signed bytes -> four fp16 values, exactly: bias each byte by 128 so it
-// becomes the low mantissa byte of 1024 + u (fp16 0x64uu), then subtract 1152.
-__device__ __forceinline__ void i8x4_to_f16x4(uint32_t w, uint32_t &lo, uint32_t &hi) {
-  const uint32_t u = w ^ 0x80808080u;
-  uint32_t a, b;
-  asm("prmt.b32 %0, %1, %2, 0x5140;" : "=r"(a) : "r"(u), "r"(0x64646464u));
-  asm("prmt.b32 %0, %1, %2, 0x5342;" : "=r"(b) : "r"(u), "r"(0x64646464u));
-  const __half2 bias = __half2half2(__ushort_as_half(0x6480));  // 1152.0
-  __half2 ha = __hsub2(*reinterpret_cast<__half2 *>(&a), bias);
-  __half2 hb = __hsub2(*reinterpret_cast<__half2 *>(&b), bias);
-  lo = *reinterpret_cast<uint32_t *>(&ha);
-  hi = *reinterpret_cast<uint32_t *>(&hb);
+// Byte offset of (row n, byte k) in an SW128 K-major box of 128-byte rows.
+__device__ __forceinline__ uint32_t sw128_byte(uint32_t n, uint32_t k) {
+  return (n >> 3) * 1024u + (n & 7u) * 128u + ((((k >> 4) ^ n) & 7u) << 4) + (k & 15u);
+}
+
+// v ~ s * (hi + lo / 256) with hi, lo int8; x = v / s in [-127, 127].
+__device__ __forceinline__ void split16(float x, int &hi, int &lo) {
+  const float h = rintf(x);
+  float l = rintf((x - h) * 256.0f);
+  l = fminf(fmaxf(l, -127.0f), 127.0f);
+  hi = static_cast<int>(h);
+  lo = static_cast<int>(l);
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 0xFFu) | ((static_cast<uint32_t>(b) & 0xFFu) << 8) |
+         ((static_cast<uint32_t>(c) & 0xFFu) << 16) | ((static_cast<uint32_t>(d) & 0xFFu) << 24);
+}
+
+// One unit of the absorbed query of a sequence ([16][576] fp32) as score
+// operands: q_lat split into int8 hi (rows 0-15) and lo (rows 16-31) parts,
+// K-major over four SW128 boxes of 128 dims, and q_rope as one bf16 SW128 box.
+// Unit u (0..127) is head u / 8, latent dims 64 * (u % 8) .. +63 and rope dims
+// 8 * (u % 8) .. +7; the eight units of a head are eight consecutive lanes.
+__device__ __forceinline__ void load_query_unit(uint8_t *qi, uint8_t *qr, float *qscale, const float *q, int u) {
+  const int h = u >> 3, j = u & 7;
+  const float *src = q + h * kRow + 64 * j;
+  float4 v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = *reinterpret_cast<const float4 *>(src + 4 * i);
+  const float4 r0 = *reinterpret_cast<const float4 *>(q + h * kRow + kLatent + 8 * j);
+  const float4 r1 = *reinterpret_cast<const float4 *>(q + h * kRow + kLatent + 8 * j + 4);
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
+#pragma unroll
+  for (int off = 1; off < 8; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  const float inv = amax > 0.f ? 127.0f / amax : 0.f;
+  if (j == 0) qscale[h] = amax / 127.0f;
+  // dims 64j + 16i .. +15: box j/2, 16-byte chunk 4 (j % 2) + i of the row
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t hw[4], lw[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float4 a = v[4 * i + e];
+      int h0, l0, h1, l1, h2, l2, h3, l3;
+      split16(a.x * inv, h0, l0);
+      split16(a.y * inv, h1, l1);
+      split16(a.z * inv, h2, l2);
+      split16(a.w * inv, h3, l3);
+      hw[e] = pack4(h0, h1, h2, h3);
+      lw[e] = pack4(l0, l1, l2, l3);
+    }
+    const uint32_t k = 16u * (4u * (j & 1) + i);
+    uint8_t *box = qi + (j >> 1) * 4096;
+    *reinterpret_cast<uint4 *>(box + sw128_byte(h, k)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    *reinterpret_cast<uint4 *>(box + sw128_byte(16 + h, k)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+  }
+  uint4 o;
+  o.x = pack2(r0.x, r0.y, false);
+  o.y = pack2(r0.z, r0.w, false);
+  o.z = pack2(r1.x, r1.y, false);
+  o.w = pack2(r1.z, r1.w, false);
+  *reinterpret_cast<uint4 *>(qr + (h >> 3) * 1024 + (h & 7) * 128 + ((j ^ (h & 7)) << 4)) = o;
+}
+
+// 8 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+// hi * 256 + lo of two int32 MMA sums (|hi| <= 512 * 127 * 127, so it fits).
+__device__ __forceinline__ float join16(uint32_t hi, uint32_t lo) {
+  return static_cast<float>(static_cast<int>(hi) * 256 + static_cast<int>(lo));
+}
+
+// Warp-wide maximum of 32-bit unsigned values (non-negative floats order like
+// their bit patterns).
+__device__ __forceinline__ uint32_t warp_max_u32(uint32_t v) {
+  uint32_t r;
+  asm volatile("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
+  return r;
 }
 
 }  // namespace q8dec
@@ -100,18 +186,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int *abort = &B->abort;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kStgSlots; ++i) { mbar_init(&B->stg_full[i], 1); mbar_init(&B->stg_empty[i], 4); }
-    for (int i = 0; i < kCvtSlots; ++i) { mbar_init(&B->cvt_full[i], 4); mbar_init(&B->cvt_empty[i], 1); }
-    for (int i = 0; i < kRopeSlots; ++i) { mbar_init(&B->rope_full[i], 1); mbar_init(&B->rope_empty[i], 1); }
+    for (int i = 0; i < kSlots; ++i) { mbar_init(&B->full[i], 1); mbar_init(&B->empty[i], 1); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&B->s_full[i], 1);
-      mbar_init(&B->s_empty[i], 4);
-      mbar_init(&B->p_full[i], 4);
+      mbar_init(&B->s_empty[i], 8);  // the eight softmax warps
+      mbar_init(&B->p_full[i], 8);
       mbar_init(&B->p_empty[i], 1);
+      mbar_init(&B->o_full[i], 1);
+      mbar_init(&B->o_empty[i], 8);
     }
-    mbar_init(&B->q_full, 4);
-    mbar_init(&B->o_full, 1);
-    mbar_init(&B->o_empty, 4);
+    mbar_init(&B->q_full, 4);  // warpgroup 0 writes the query operands
     mbar_init(&B->drain, 1);
     B->abort = 0;
     fence_barrier_init();
@@ -133,158 +217,119 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       tma_prefetch_desc(&p.tm_lat8);
       tma_prefetch_desc(&p.tm_rope);
-      uint32_t g = 0, n_stg = 0, n_rope = 0;
+      uint32_t ri = 0;  // boxes issued
       bool ok = true;
       for (int si = seg_lo; si < seg_hi && ok; ++si) {
         const AttendSegment sg = p.segs[si];
         const long long row0 = p.seq_row0[sg.seq] + sg.tok_begin;
         const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
-        for (int t = 0; t < nt && ok; ++t, ++g) {
+        for (int t = 0; t < nt && ok; ++t) {
           const int32_t y = static_cast<int32_t>(row0 + static_cast<long long>(kTileTok) * t);
-          for (int c = 0; c < 4 && ok; ++c) {
-            const uint32_t li = 4 * g + c, ls = li % kStgSlots;
-            ok = mbar_wait(&B->stg_empty[ls], ((li / kStgSlots) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+          for (int b = 0; b < kBoxesPerTile; ++b, ++ri) {
+            const uint32_t s = ri % kSlots;
+            ok = mbar_wait(&B->empty[s], ((ri / kSlots) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
             if (!ok) break;
-            mbar_arrive_expect_tx(&B->stg_full[ls], kStgBytes);
-            tma_load_2d(smem + OFF_STG + ls * kStgBytes, &p.tm_lat8, &B->stg_full[ls], 128 * c, y);
-            n_stg = li + 1;
-            if (c == 0) {
-              const uint32_t rs = g % kRopeSlots;
-              ok = mbar_wait(&B->rope_empty[rs], ((g / kRopeSlots) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
-              if (!ok) break;
-              mbar_arrive_expect_tx(&B->rope_full[rs], kRopeBytes);
-              tma_load_2d(smem + OFF_ROPE + rs * kRopeBytes, &p.tm_rope, &B->rope_full[rs], 0, y);
-              n_rope = g + 1;
-            }
+            uint8_t *dst = smem + OFF_RING + s * kBox;
+            mbar_arrive_expect_tx(&B->full[s], kBox);
+            if (b == 0)
+              tma_load_2d(dst, &p.tm_rope, &B->full[s], 0, y);
+            else
+              tma_load_2d(dst, &p.tm_lat8, &B->full[s], 128 * (b - 1), y);
           }
         }
       }
       if (!ok) {
-        for (uint32_t s = 0; s < kStgSlots && s < n_stg; ++s) {
-          const uint32_t last = s + kStgSlots * ((n_stg - 1 - s) / kStgSlots);
-          drain_wait(&B->stg_full[s], (last / kStgSlots) & 1, p.err);
-        }
-        for (uint32_t s = 0; s < kRopeSlots && s < n_rope; ++s) {
-          const uint32_t last = s + kRopeSlots * ((n_rope - 1 - s) / kRopeSlots);
-          drain_wait(&B->rope_full[s], (last / kRopeSlots) & 1, p.err);
+        // The most recent load issued into each slot must land before the CTA
+        // exits (earlier ones completed before the slot was reissued).
+        for (uint32_t s = 0; s < kSlots && s < ri; ++s) {
+          const uint32_t last = s + kSlots * ((ri - 1 - s) / kSlots);
+          drain_wait(&B->full[s], (last / kSlots) & 1, p.err);
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc_lat = idesc_f16(0, 0, 0, 0, 128, kHeads);   // fp16 x fp16
-      constexpr uint32_t idesc_rope = idesc_f16(1, 1, 0, 0, 128, kHeads);  // bf16 x bf16
-      constexpr uint32_t idesc_pv = idesc_f16(0, 0, 1, 0, 128, kHeads);    // fp16, A MN-major
+      constexpr uint32_t idesc_rope = idesc_f16(1, 1, 0, 0, 128, kHeads);  // bf16 rows x bf16 q_rope
+      constexpr uint32_t idesc_s = idesc_s8(0, 0, 128, 32);                // int8 rows x q parts
+      constexpr uint32_t idesc_pv = idesc_s8(1, 1, 128, 32);               // int8 rows^T x P' parts, both MN-major
+      const uint32_t ring = s_base + OFF_RING, qi = s_base + OFF_QI, qr = s_base + OFF_QR;
+      // scores of tile gg: rope (bf16) and the four int8 chunks
+      auto issue_scores = [&](uint32_t gg) -> bool {
+        const uint32_t sb = gg & 1, r0 = kBoxesPerTile * gg;
+        if (!mbar_wait(&B->s_empty[sb], ((gg >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY) ||
+            !mbar_wait(&B->full[r0 % kSlots], (r0 / kSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL))
+          return false;
+        tc_fence_after();
+        const uint32_t rope_box = ring + (r0 % kSlots) * kBox;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_ss(tmem + kColR + 16 * sb, smem_desc(rope_box + kk * 32, 16, 1024, LAYOUT_SW128),
+                     smem_desc(qr + kk * 32, 16, 1024, LAYOUT_SW128), idesc_rope, kk ? 1u : 0u);
+        mma_commit(&B->empty[r0 % kSlots]);
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t ri = r0 + 1 + c;
+          if (!mbar_wait(&B->full[ri % kSlots], (ri / kSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL)) return false;
+          tc_fence_after();
+          const uint32_t box = ring + (ri % kSlots) * kBox;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_s8_ss(tmem + kColS + 32 * sb, smem_desc(box + kk * 32, 16, 1024, LAYOUT_SW128),
+                      smem_desc(qi + c * 4096 + kk * 32, 16, 1024, LAYOUT_SW128), idesc_s, (c | kk) ? 1u : 0u);
+        }
+        mma_commit(&B->s_full[sb]);
+        return true;
+      };
+      // P'.V of tile gg into its own int32 buffer (folded by the softmax threads)
+      auto issue_pv = [&](uint32_t gg) -> bool {
+        const uint32_t pb = gg & 1;
+        if (!mbar_wait(&B->p_full[pb], (gg >> 1) & 1, abort, p.err, ERR_TIMEOUT_FULL) ||
+            !mbar_wait(&B->o_empty[pb], ((gg >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_FULL))
+          return false;
+        tc_fence_after();
+        const uint32_t pa = s_base + OFF_P + pb * kPBytes;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint32_t ri = kBoxesPerTile * gg + 1 + c;
+          const uint32_t box = ring + (ri % kSlots) * kBox;
+          // A = the chunk read MN-major: 128 dims (one 128-byte span) x 32 rows
+          // per MMA (four 8-row swizzle atoms, 1 KB apart); B = P' MN-major,
+          // 32 bytes per KV row, 8-row atoms of 256 bytes
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_s8_ss(tmem + kColO + 128 * pb + 32 * c, smem_desc(box + kk * 4096, kBox, 1024, LAYOUT_SW128),
+                      smem_desc(pa + kk * 1024, kPBytes, 256, LAYOUT_SW32), idesc_pv, kk ? 1u : 0u);
+          mma_commit(&B->empty[ri % kSlots]);
+        }
+        mma_commit(&B->p_empty[pb]);
+        mma_commit(&B->o_full[pb]);
+        return true;
+      };
       uint32_t g = 0;
       int seg_i = 0;
       bool ok = true;
       for (int si = seg_lo; si < seg_hi && ok; ++si, ++seg_i) {
         const AttendSegment sg = p.segs[si];
         const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
-        ok = mbar_wait(&B->q_full, seg_i & 1, abort, p.err, ERR_TIMEOUT_FULL);
-        const uint32_t q_addr = s_base + OFF_Q;
+        ok = mbar_wait(&B->q_full, seg_i & 1, abort, p.err, ERR_TIMEOUT_FULL) && issue_scores(g);
         for (int t = 0; t < nt && ok; ++t, ++g) {
-          const uint32_t sb = g & 1, rs = g % kRopeSlots;
-          ok = mbar_wait(&B->s_empty[sb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY) &&
-               mbar_wait(&B->rope_full[rs], (g / kRopeSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t rope_box = s_base + OFF_ROPE + rs * kRopeBytes;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_f16_ss(tmem + kColRope + sb * 16, smem_desc(rope_box + kk * 32, 16, 1024, LAYOUT_SW128),
-                       smem_desc(q_addr + 8 * 2048 + kk * 32, 16, 1024, LAYOUT_SW128), idesc_rope, kk ? 1u : 0u);
-          for (int c = 0; c < 4 && ok; ++c) {
-            const uint32_t li = 4 * g + c;
-            ok = mbar_wait(&B->cvt_full[li % kCvtSlots], (li / kCvtSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL);
-            if (!ok) break;
-            tc_fence_after();
-            const uint32_t slot = s_base + OFF_CVT + (li % kCvtSlots) * kCvtBytes;
-#pragma unroll
-            for (int half = 0; half < 2; ++half)
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk)
-                mma_f16_ss(tmem + sb * 16, smem_desc(slot + half * kBox + kk * 32, 16, 1024, LAYOUT_SW128),
-                           smem_desc(q_addr + (2 * c + half) * 2048 + kk * 32, 16, 1024, LAYOUT_SW128), idesc_lat,
-                           (c | half | kk) ? 1u : 0u);
-          }
-          if (!ok) break;
-          mma_commit(&B->s_full[sb]);
-          mma_commit(&B->rope_empty[rs]);
-          const bool first = (t == 0);
-          ok = mbar_wait(&B->p_full[sb], (g >> 1) & 1, abort, p.err, ERR_TIMEOUT_FULL);
-          if (ok && first && seg_i > 0) ok = mbar_wait(&B->o_empty, (seg_i - 1) & 1, abort, p.err, ERR_TIMEOUT_FULL);
-          if (!ok) break;
-          tc_fence_after();
-          const uint32_t p_addr = s_base + OFF_P + sb * kPBytes;
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const uint32_t li = 4 * g + c;
-            const uint32_t slot = s_base + OFF_CVT + (li % kCvtSlots) * kCvtBytes;
-#pragma unroll
-            for (int kk = 0; kk < kTileTok / 16; ++kk)
-              mma_f16_ss(tmem + kColO + 16 * c, smem_desc(slot + kk * 2048, kBox, 1024, LAYOUT_SW128),
-                         smem_desc(p_addr + kk * 256, 128, kPChunkSbo, LAYOUT_INTERLEAVE), idesc_pv,
-                         (first && kk == 0) ? 0u : 1u);
-            mma_commit(&B->cvt_empty[li % kCvtSlots]);
-          }
-          mma_commit(&B->p_empty[sb]);
+          // the next tile's scores go ahead of this tile's P.V (same segment:
+          // the next segment's query is written only after this one ends)
+          if (t + 1 < nt) ok = issue_scores(g + 1);
+          if (ok) ok = issue_pv(g);
         }
-        if (ok) mma_commit(&B->o_full);
       }
+      // All issued tensor-core work must finish before TMEM is released.
       mma_commit(&B->drain);
       drain_wait(&B->drain, 0, p.err);
     }
-  } else if (warp >= 8) {
-    // ------------------------------------------------------------ converters
-    const int ct = threadIdx.x - 256;  // 0..127
-    uint32_t g = 0;
-    bool ok = true;
-    for (int si = seg_lo; si < seg_hi && ok; ++si) {
-      const AttendSegment sg = p.segs[si];
-      const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
-      for (int t = 0; t < nt && ok; ++t, ++g) {
-        for (int c = 0; c < 4; ++c) {
-          const uint32_t li = 4 * g + c, ss = li % kStgSlots, cs = li % kCvtSlots;
-          int w_ok = 1;
-          if (lane == 0) {
-            w_ok = mbar_wait(&B->stg_full[ss], (li / kStgSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL) &&
-                   mbar_wait(&B->cvt_empty[cs], ((li / kCvtSlots) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
-          }
-          w_ok = __shfl_sync(0xffffffffu, w_ok, 0);
-          if (!w_ok) { ok = false; break; }
-          const uint8_t *src = smem + OFF_STG + ss * kStgBytes;
-          uint8_t *dst = smem + OFF_CVT + cs * kCvtBytes;
-#pragma unroll 4
-          for (int i = 0; i < 8; ++i) {
-            const int idx = ct + 128 * i;  // 1024 chunks of 16 int8 (128 rows x 8)
-            const int row = idx >> 3, k = idx & 7;
-            const uint4 v = *reinterpret_cast<const uint4 *>(src + row * 128 + ((k ^ (row & 7)) << 4));
-            uint4 o0, o1;
-            i8x4_to_f16x4(v.x, o0.x, o0.y);
-            i8x4_to_f16x4(v.y, o0.z, o0.w);
-            i8x4_to_f16x4(v.z, o1.x, o1.y);
-            i8x4_to_f16x4(v.w, o1.z, o1.w);
-            // dims 16k..16k+15 of this 128-dim chunk -> fp16 box (k >> 2), 16B chunks 2(k&3), 2(k&3)+1
-            uint8_t *box = dst + (k >> 2) * kBox;
-            const int fc = 2 * (k & 3);
-            *reinterpret_cast<uint4 *>(box + sw128_offset(row, fc * 8)) = o0;
-            *reinterpret_cast<uint4 *>(box + sw128_offset(row, fc * 8 + 8)) = o1;
-          }
-          fence_proxy_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            mbar_arrive(&B->stg_empty[ss]);
-            mbar_arrive(&B->cvt_full[cs]);
-          }
-        }
-      }
-    }
   } else if (warp >= 4) {
-    // ------------------------------------------------------------ softmax + epilogue
-    const int w = warp - 4;
+    // ------------------------------------------------------------ softmax, fold, epilogue
+    const int wg = (warp - 4) >> 2;  // warpgroup: heads 8 wg .. 8 wg + 7
+    const int w = (warp - 4) & 3;    // TMEM subpartition = rows / dims 32 w .. 32 w + 31
     const int tt = 32 * w + lane;
+    const int hb = 8 * wg;
+    const uint32_t bid = 1 + wg;     // this warpgroup's named barrier
     const uint32_t lane_base = static_cast<uint32_t>(32 * w) << 16;
     uint32_t g = 0;
     int seg_i = 0;
@@ -292,140 +337,194 @@ __global__ void __launch_bounds__(kThreads, 1)
       const AttendSegment sg = p.segs[si];
       const long long srow0 = p.seq_row0[sg.seq];
       const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
-      // The query tile is free here: every score MMA of the previous segment
-      // has completed (its scores were read above).
-      load_query_tile(smem + OFF_Q, p.q + static_cast<size_t>(sg.seq) * kHeads * kRow, tt, true);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&B->q_full);
-      float m_ref[kHeads], l_part[kHeads];
+      // row scales are read one tile ahead (global loads: their latency hides
+      // behind the previous tile)
+      float rs_next = sg.tok_begin + tt < sg.tok_end ? p.latent_scale[srow0 + sg.tok_begin + tt] : 0.f;
+      // The query operands are free here: every score MMA of the previous
+      // segment has completed (its scores were read below).
+      if (wg == 0) {
+        load_query_unit(smem + OFF_QI, smem + OFF_QR, B->qscale, p.q + static_cast<size_t>(sg.seq) * kHeads * kRow,
+                        tt);
+        fence_proxy_async_smem();
+      }
+      named_bar_sync(3, 256);
+      if (wg == 0 && lane == 0) mbar_arrive(&B->q_full);
+      float sq[8];  // sq / 256: the scores are read as S_hi * 256 + S_lo
 #pragma unroll
-      for (int h = 0; h < kHeads; ++h) { m_ref[h] = -INFINITY; l_part[h] = 0.f; }
+      for (int i = 0; i < 8; ++i) sq[i] = B->qscale[hb + i] * 0.00390625f;
+      float m_ref[8], l_part[8], sp_prev[8], acc[4][8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        m_ref[i] = -INFINITY;
+        l_part[i] = 0.f;
+        sp_prev[i] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[c][i] = 0.f;
+      }
+      // acc = (acc + sp * (O_hi * 256 + O_lo)) * alpha for tile gg (sp passed
+      // as the P' step / 256; alpha applied when resc)
+      auto fold = [&](uint32_t gg, const float (&sp)[8], bool resc, const float (&alpha)[8]) -> bool {
+        const uint32_t ob = gg & 1;
+        const bool bad = !mbar_wait(&B->o_full[ob], (gg >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
+        if (named_bar_or(bid, 128, bad)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t oh[8], ol[8];
+          const uint32_t col = tmem + kColO + 128 * ob + 32 * c + hb + lane_base;
+          tmem_ld8(col, oh);
+          tmem_ld8(col + 16, ol);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[c][i] = fmaf(sp[i], join16(oh[i], ol[i]), acc[c][i]);
+          if (resc)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[c][i] *= alpha[i];
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&B->o_empty[ob]);
+        return true;
+      };
       bool bad = false;
       for (int t = 0; t < nt; ++t, ++g) {
         const int tok = sg.tok_begin + kTileTok * t + tt;
         const bool valid = tok < sg.tok_end;
-        const float rs = valid ? p.latent_scale[srow0 + tok] : 0.f;
+        const float rs = rs_next;
+        if (t + 1 < nt) rs_next = tok + kTileTok < sg.tok_end ? p.latent_scale[srow0 + tok + kTileTok] : 0.f;
         const uint32_t sb = g & 1;
         bad = !mbar_wait(&B->s_full[sb], (g >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
-        if (named_bar_or(1, 128, bad)) { bad = true; break; }
+        if (named_bar_or(bid, 128, bad)) { bad = true; break; }
         tc_fence_after();
-        float vl[kHeads], vr[kHeads];
-        tmem_ld16(tmem + sb * 16 + lane_base, vl);
-        tmem_ld16(tmem + kColRope + sb * 16 + lane_base, vr);
+        uint32_t sh[8], sl[8], srp[8];
+        tmem_ld8(tmem + kColS + 32 * sb + hb + lane_base, sh);
+        tmem_ld8(tmem + kColS + 32 * sb + 16 + hb + lane_base, sl);
+        tmem_ld8(tmem + kColR + 16 * sb + hb + lane_base, srp);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&B->s_empty[sb]);
-        float s[kHeads];
+        float s[8];
         bool need = false;
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h) {
-          s[h] = valid ? fmaf(rs, vl[h], vr[h]) * p.scale_log2 : -INFINITY;
-          need |= s[h] > m_ref[h] + 8.0f;
+        for (int i = 0; i < 8; ++i) {
+          s[i] = valid ? fmaf(rs * sq[i], join16(sh[i], sl[i]), __uint_as_float(srp[i])) * p.scale_log2 : -INFINITY;
+          need |= s[i] > m_ref[i] + 8.0f;
         }
-        if (named_bar_or(1, 128, need)) {
-          float mx[kHeads];
+        // lazy rescale: the running maximum moves only by more than 2^8
+        bool resc = false;
+        float alpha[8];
 #pragma unroll
-          for (int h = 0; h < kHeads; ++h) mx[h] = s[h];
+        for (int i = 0; i < 8; ++i) alpha[i] = 1.f;
+        if (named_bar_or(bid, 128, need)) {
+          float mx[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) mx[i] = s[i];
 #pragma unroll
           for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
-            for (int h = 0; h < kHeads; ++h) mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], off));
+            for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], off));
           if (lane == 0)
 #pragma unroll
-            for (int h = 0; h < kHeads; ++h) B->red[w][h] = mx[h];
-          named_bar_sync(1, 128);
-          float alpha[kHeads];
+            for (int i = 0; i < 8; ++i) B->red[wg][w][i] = mx[i];
+          named_bar_sync(bid, 128);
 #pragma unroll
-          for (int h = 0; h < kHeads; ++h) {
-            const float tm = fmaxf(fmaxf(B->red[0][h], B->red[1][h]), fmaxf(B->red[2][h], B->red[3][h]));
-            const float mn = fmaxf(m_ref[h], tm);
-            alpha[h] = (m_ref[h] == -INFINITY) ? 0.f : exp2f(m_ref[h] - mn);
-            m_ref[h] = mn;
+          for (int i = 0; i < 8; ++i) {
+            const float tm = fmaxf(fmaxf(B->red[wg][0][i], B->red[wg][1][i]), fmaxf(B->red[wg][2][i], B->red[wg][3][i]));
+            const float mn = fmaxf(m_ref[i], tm);
+            alpha[i] = (m_ref[i] == -INFINITY) ? 0.f : exp2f(m_ref[i] - mn);
+            m_ref[i] = mn;
+            l_part[i] *= alpha[i];
           }
-          named_bar_sync(1, 128);
-          if (t > 0) {
-            bad = !mbar_wait(&B->p_empty[(g - 1) & 1], ((g - 1) >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
-            if (named_bar_or(1, 128, bad)) { bad = true; break; }
-            tc_fence_after();
-#pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              float o[kHeads];
-              tmem_ld16(tmem + kColO + 16 * c + lane_base, o);
-              tmem_wait_ld();
-#pragma unroll
-              for (int h = 0; h < kHeads; ++h) o[h] *= alpha[h];
-              tmem_st16(tmem + kColO + 16 * c + lane_base, o);
-            }
-            tmem_wait_st();
-          }
-#pragma unroll
-          for (int h = 0; h < kHeads; ++h) l_part[h] *= alpha[h];
+          named_bar_sync(bid, 128);
+          resc = true;
         }
-        float pr[kHeads];
+        // P'_j = p_j * scale_j, split per head against the tile's max |P'|
+        float pq[8];
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h) {
-          pr[h] = exp2f(s[h] - m_ref[h]);
-          l_part[h] += pr[h];
+        for (int i = 0; i < 8; ++i) {
+          const float pr = exp2f(s[i] - m_ref[i]);
+          l_part[i] += pr;
+          pq[i] = pr * rs;
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint32_t m = warp_max_u32(__float_as_uint(fabsf(pq[i])));
+          if (lane == 0) B->pmax[g & 1][wg][w][i] = __uint_as_float(m);
+        }
+        named_bar_sync(bid, 128);
+        float sp[8];
+        uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float m = fmaxf(fmaxf(B->pmax[g & 1][wg][0][i], B->pmax[g & 1][wg][1][i]),
+                                fmaxf(B->pmax[g & 1][wg][2][i], B->pmax[g & 1][wg][3][i]));
+          sp[i] = m * (1.0f / (127.0f * 256.0f));
+          int ph, pl;
+          split16(m > 0.f ? pq[i] * (127.0f * __frcp_rn(m)) : 0.f, ph, pl);
+          hw[i >> 2] |= (static_cast<uint32_t>(ph) & 0xFFu) << (8 * (i & 3));
+          lw[i >> 2] |= (static_cast<uint32_t>(pl) & 0xFFu) << (8 * (i & 3));
         }
         bad = !mbar_wait(&B->p_empty[sb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_MMA);
-        if (named_bar_or(1, 128, bad)) { bad = true; break; }
+        if (named_bar_or(bid, 128, bad)) { bad = true; break; }
         {
-          // Rows past the segment end carry rs = 0, so P' = 0; the converted
-          // int8 rows are always finite, so 0 * row is 0 in the P.V MMA.
-          uint8_t *pd = smem + OFF_P + sb * kPBytes + (tt >> 3) * 128 + (tt & 7) * 2;
-#pragma unroll
-          for (int h = 0; h < kHeads; ++h)
-            *reinterpret_cast<__half *>(pd + (h >> 3) * kPChunkSbo + (h & 7) * 16) = __float2half_rn(pr[h] * rs);
+          // P' parts as the MN-major B operand: KV row tt holds 32 bytes, hi of
+          // heads 0-15 then lo of heads 0-15, with the 32-byte swizzle (the
+          // 16-byte halves swap in rows with bit 2 set)
+          uint8_t *row = smem + OFF_P + sb * kPBytes + (tt >> 3) * 256 + (tt & 7) * 32;
+          const uint32_t swz = ((tt >> 2) & 1) << 4;
+          *reinterpret_cast<uint2 *>(row + (hb ^ swz)) = make_uint2(hw[0], hw[1]);
+          *reinterpret_cast<uint2 *>(row + ((16 + hb) ^ swz)) = make_uint2(lw[0], lw[1]);
         }
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&B->p_full[sb]);
+        // fold the previous tile's P'.V (its frame is rescaled with this tile's alpha)
+        if (t > 0 && !fold(g - 1, sp_prev, resc, alpha)) { bad = true; break; }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sp_prev[i] = sp[i];
       }
       if (bad) break;
-      bad = !mbar_wait(&B->o_full, seg_i & 1, abort, p.err, ERR_TIMEOUT_MMA);
-      if (named_bar_or(1, 128, bad)) break;
-      tc_fence_after();
-      float lt[kHeads];
+      // ---- epilogue: last tile's P'.V, then O / l and lse
+      {
+        float one[8];
 #pragma unroll
-      for (int h = 0; h < kHeads; ++h) {
-        float l = l_part[h];
+        for (int i = 0; i < 8; ++i) one[i] = 1.f;
+        if (!fold(g - 1, sp_prev, false, one)) break;
+      }
+      float lt[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float l = l_part[i];
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
-        lt[h] = l;
+        lt[i] = l;
       }
       if (lane == 0)
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h) B->red[w][h] = lt[h];
-      named_bar_sync(1, 128);
+        for (int i = 0; i < 8; ++i) B->red[wg][w][i] = lt[i];
+      named_bar_sync(bid, 128);
 #pragma unroll
-      for (int h = 0; h < kHeads; ++h) lt[h] = (B->red[0][h] + B->red[1][h]) + (B->red[2][h] + B->red[3][h]);
-      named_bar_sync(1, 128);
+      for (int i = 0; i < 8; ++i) lt[i] = (B->red[wg][0][i] + B->red[wg][1][i]) + (B->red[wg][2][i] + B->red[wg][3][i]);
+      named_bar_sync(bid, 128);
       float *dst = (sg.slot < 0) ? p.out + static_cast<size_t>(sg.seq) * kHeads * kLatent
                                  : p.part_o + static_cast<size_t>(sg.slot) * kHeads * kLatent;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        float o[kHeads];
-        tmem_ld16(tmem + kColO + 16 * c + lane_base, o);
-        tmem_wait_ld();
-        const int d = 128 * c + 32 * w + lane;
+        const int d = 128 * c + tt;
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h) dst[h * kLatent + d] = o[h] / lt[h];
+        for (int i = 0; i < 8; ++i) dst[(hb + i) * kLatent + d] = acc[c][i] / lt[i];
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&B->o_empty);
-      if (w == 0 && lane < kHeads) {
+      if (w == 0 && lane < 8) {
         float m = 0.f, l = 1.f;
 #pragma unroll
-        for (int h = 0; h < kHeads; ++h)
-          if (h == lane) { m = m_ref[h]; l = lt[h]; }
+        for (int i = 0; i < 8; ++i)
+          if (i == lane) { m = m_ref[i]; l = lt[i]; }
         const float lse = (m + log2f(l)) * 0.69314718055994531f;
         float *ldst = (sg.slot < 0) ? p.lse : p.part_lse;
         const int row = (sg.slot < 0) ? sg.seq : sg.slot;
-        if (ldst) ldst[row * kHeads + lane] = lse;
+        if (ldst) ldst[row * kHeads + hb + lane] = lse;
       }
     }
   }

@@ -196,6 +196,18 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc], kind::i8 (signed 8-bit operands,
+// int32 accumulation; K = 32 per instruction).
+__device__ __forceinline__ void mma_s8_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Same with A read from tensor memory: 128 lanes = rows of A, K packed two
 // 16-bit elements per 32-bit column (the even element in the low half).
 __device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
@@ -313,6 +325,14 @@ __host__ __device__ constexpr uint32_t idesc_f16(uint32_t a_fmt, uint32_t b_fmt,
   return (1u << 4)            // D = f32
          | (a_fmt << 7) | (b_fmt << 10) | (a_mn << 15) | (b_mn << 16) | ((N >> 3) << 17) |
          ((M >> 4) << 24);
+}
+
+// Instruction descriptor for kind::i8: both operands signed 8-bit, int32
+// accumulation; a_mn/b_mn: 1 = operand is MN-major.
+__host__ __device__ constexpr uint32_t idesc_s8(uint32_t a_mn, uint32_t b_mn, uint32_t M, uint32_t N) {
+  return (2u << 4)                 // D = s32
+         | (1u << 7) | (1u << 10)  // A, B = s8
+         | (a_mn << 15) | (b_mn << 16) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
 // Byte offset of element (row, col) of a bf16/fp16 tile stored K-major with the
