@@ -397,7 +397,7 @@ class DecodeQ8:
     unit = "GB/s"
     bound = "hbm"
     # one ncu capture of the attend kernel (profiles/mla_attend_q8_config3.txt)
-    ncu_traffic = {"mla_attend_q8": 193.175808e6 + 5.735936e6}
+    ncu_traffic = {"mla_attend_q8": 193.127424e6 + 5.535232e6}
 
     def __init__(self, torch, K, lib, dist):
         import kvl_b200.synth as SY
