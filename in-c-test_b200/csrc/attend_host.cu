@@ -472,6 +472,7 @@ int DevicePlan::launch(const AttendLaunch &a, cudaStream_t stream) const {
                : -1;
   }
   if (a.rows <= 0 || a.rows >= (1LL << 31)) return -1;
+  if ((reinterpret_cast<uintptr_t>(a.q) & 15) != 0) return -1;  // the kernels read q as float4
   AttendParams p;
   std::memset(&p, 0, sizeof(p));
   if (!a.q8) {

@@ -143,6 +143,10 @@ KVL_EXPORT int kvl_mla_attend_bf16_noalloc(float *d_out, float *d_lse, const flo
     fail("noalloc attend: kv pool must be 16-byte aligned");
     return -1;
   }
+  if ((reinterpret_cast<uintptr_t>(d_q) & 15) != 0) {
+    fail("noalloc attend: the absorbed query must be 16-byte aligned");
+    return -1;
+  }
   int dev = -1;
   if (cudaGetDevice(&dev) != cudaSuccess) {
     fail("noalloc attend: no CUDA device");

@@ -1293,6 +1293,10 @@ static int attend_common(const KvlMlaAttendPlan *plan, AttendLaunch &a, int num_
     set_err("invalid attend arguments");
     return -1;
   }
+  if ((reinterpret_cast<uintptr_t>(a.q) & 15) != 0) {
+    set_err("the absorbed query must be 16-byte aligned");
+    return -1;
+  }
   a.nh = num_heads;
   a.R = R;
   a.DR = DR;
