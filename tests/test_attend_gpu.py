@@ -164,3 +164,47 @@ def test_generic_shapes(K, S, orc, torch_cuda, nh, R, DR):
     mix1, _ = orc.attend_f32(q[1], lat[200:300], rope[200:300], SCALE)
     assert_close(out[0], mix0, what="generic seq0")
     assert_close(out[1], mix1, what="generic seq1")
+
+
+def test_q8_peaked_scores(K, S, orc, torch_cuda):
+    """Large scores move the running maximum often: the int8 kernel rescales
+    its folded P'.V sums and splits P' against small tile maxima."""
+    L = 2000
+    lat8, scale, rope = q8_pool(S, 7, L)
+    q = absorbed_q(S, 7, 1, std=1.5)
+    out, lse, _ = run_q8(K, torch_cuda, lat8, scale, rope, q, [L], [0], 4)
+    mix, lse_ref = orc.attend_q8(q[0], lat8, scale, rope, SCALE)
+    assert_close(out[0], mix, what="q8 peaked")
+    assert np.max(np.abs(lse[0] - lse_ref)) < 1e-2
+
+
+def test_q8_wide_scale_range(K, S, orc, torch_cuda):
+    """Row scales spanning four decades below the largest BASELINE scale (0.02,
+    so the outputs keep the magnitude the absolute tolerance is set for): the
+    per-tile split of P' = p * scale is taken against the largest |P'| of the
+    tile, so the small-scale rows get the fewest bits."""
+    L = 3000
+    lat8, _, rope = q8_pool(S, 8, L)
+    scale = (0.02 * 10.0 ** S.uniform_f32(8, S.S_SCALE, (L,), -4.0, 0.0)).astype(np.float32)
+    q = absorbed_q(S, 8, 1)
+    out, _, _ = run_q8(K, torch_cuda, lat8, scale, rope, q, [L], [0])
+    mix, _ = orc.attend_q8(q[0], lat8, scale, rope, SCALE)
+    assert_close(out[0], mix, what="q8 wide scale range")
+
+
+def test_attend_rejects_misaligned_query(K, S, torch_cuda):
+    """The decode kernels read the absorbed query as float4: a query that is
+    not 16-byte aligned is refused before anything is launched."""
+    dev = torch_cuda.device("cuda:0")
+    L = 256
+    kv, _, _ = bf16_pool(S, 9, L)
+    base = torch_cuda.zeros(NH * (R + DR) + 1, device=dev)
+    q_bad = base[1:].view(1, NH, R + DR)  # 4 bytes past a 16-byte boundary
+    out = torch_cuda.zeros((1, NH, R), device=dev)
+    plan = K.AttendPlan([L], [0], NH, R)
+    rc = plan.attend_bf16(out, None, q_bad, torch_cuda.from_numpy(kv.view(np.int16)).to(dev), L)
+    assert rc == -1 and "16-byte aligned" in K.last_error()
+    lat8, scale, rope = q8_pool(S, 9, L)
+    rc = plan.attend_q8(out, None, q_bad, torch_cuda.from_numpy(lat8).to(dev), torch_cuda.from_numpy(scale).to(dev),
+                        torch_cuda.from_numpy(rope.view(np.int16)).to(dev), L)
+    assert rc == -1 and "16-byte aligned" in K.last_error()
