@@ -396,6 +396,9 @@ class DecodeQ8:
     metric = "MLA Q8 decode KV GB/s (config 3: 64 seqs, L~U[512,8192])"
     unit = "GB/s"
     bound = "hbm"
+    # the attend's arithmetic: int8 rows x int8 query / softmax-weight parts on
+    # the tensor cores with int32 sums, the rope term bf16 with fp32 sums
+    dtype = "s8 (int32 accumulate; rope bf16)"
     # one ncu capture of the attend kernel (profiles/mla_attend_q8_config3.txt)
     ncu_traffic = {"mla_attend_q8": 193.127424e6 + 5.535232e6}
 
@@ -725,7 +728,8 @@ def main():
     line = {
         "metric": wl.metric, "value": wl.value(ms), "unit": wl.unit, "n_gpus": dist.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak"
-        if wl.name == "prefill" else "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded)",
+        if wl.name == "prefill" else "strong", "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"),
+        "data": "synthetic (seeded)",
         "config": wl.config(), "roofline": roof, "gpu_launches": int(launches) * args.steps,
         "kernels": {k: {"ms_total": v[0], "launches": v[1]} for k, v in prof.items()}, "clocks": clk,
     }
@@ -748,6 +752,7 @@ def main():
             ms2, prof2, l2 = measure(torch, K, lib, dist, w2, args.steps, args.warmup, flush, peaks)
             r2, _ = roofline_for(w2, prof2, peaks, peak_kind)
             extras[name] = {"metric": w2.metric, "value": w2.value(ms2), "unit": w2.unit, "ms_per_step": ms2,
+                            "dtype": getattr(w2, "dtype", "bf16"),
                             "frac_of_hbm": w2.value(ms2) / peaks["hbm_gbs"], "roofline": r2,
                             "config": w2.config(), "gpu_launches_per_step": int(l2),
                             "kernels": {k: {"ms_total": v[0], "launches": v[1]} for k, v in prof2.items()}}
