@@ -17,8 +17,9 @@
 //           reads the same int8 rows as an MN-major operand: per tile
 //             O += sp * (O_hi + O_lo / 256)
 //           folded into fp32 register accumulators by the softmax threads.
-// The int32 sums are exact; the only roundings are the two 16-bit splits and
-// fp32 arithmetic (the reference accumulates in double).
+// The int32 sums are exact; the roundings are the two 16-bit splits, q_rope
+// to bf16 for the rope term, and fp32 arithmetic (the reference accumulates in
+// double).
 //
 // Tiles of 128 KV rows.  Shared memory is one ring of 12 boxes of 16 KB
 // (128 rows x 128 B): a tile is five boxes -- the bf16 rope and four 128-dim
