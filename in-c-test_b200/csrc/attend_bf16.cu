@@ -235,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
       // The query tile is free here: every score MMA of the previous segment
       // has completed (its scores were read above).
-      load_query_tile(smem + OFF_Q, p.q + static_cast<size_t>(sg.seq) * kHeads * kRow, tt, false);
+      load_query_tile(smem + OFF_Q, p.q + static_cast<size_t>(sg.seq) * kHeads * kRow, tt);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&B->q_full);

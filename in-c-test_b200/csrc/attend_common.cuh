@@ -59,21 +59,18 @@ struct AttendParams {
 };
 
 #ifdef __CUDACC__
-// Loads the fp32 absorbed query [16][576] of one sequence into shared memory
-// as nine SW128 boxes (64 dims x 16 heads, 2 KB each): q_lat as bf16 (or fp16
-// when lat_f16), q_rope as bf16.  Run by 128 threads (tid 0..127) with every
-// global load in flight before the first store, so the tile costs one memory
-// round trip.
-__device__ __forceinline__ uint32_t pack2(float a, float b, bool f16) {
-  if (f16) {
-    __half2 v = __floats2half2_rn(a, b);
-    return *reinterpret_cast<uint32_t *>(&v);
-  }
+// Two floats as a packed bf16 pair (round to nearest even).
+__device__ __forceinline__ uint32_t pack2_bf16(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
-__device__ __forceinline__ void load_query_tile(uint8_t *qd, const float *qs, int tid, bool lat_f16) {
+// Loads the fp32 absorbed query [16][576] of one sequence into shared memory
+// as nine SW128 boxes of bf16 (64 dims x 16 heads, 2 KB each).  Run by 128
+// threads (tid 0..127) with every global load in flight before the first
+// store, so the tile costs one memory round trip.
+
+__device__ __forceinline__ void load_query_tile(uint8_t *qd, const float *qs, int tid) {
   constexpr int kChunks = kHeads * (kRow / 8);  // 1152 chunks of 8 values
   constexpr int kPer = kChunks / 128;           // 9 per thread
   float4 v[2 * kPer];
@@ -88,12 +85,11 @@ __device__ __forceinline__ void load_query_tile(uint8_t *qd, const float *qs, in
   for (int i = 0; i < kPer; ++i) {
     const int idx = tid + 128 * i;
     const int h = idx / (kRow / 8), c8 = idx % (kRow / 8);
-    const bool f16 = lat_f16 && c8 < kLatent / 8;
     uint4 o;
-    o.x = pack2(v[2 * i].x, v[2 * i].y, f16);
-    o.y = pack2(v[2 * i].z, v[2 * i].w, f16);
-    o.z = pack2(v[2 * i + 1].x, v[2 * i + 1].y, f16);
-    o.w = pack2(v[2 * i + 1].z, v[2 * i + 1].w, f16);
+    o.x = pack2_bf16(v[2 * i].x, v[2 * i].y);
+    o.y = pack2_bf16(v[2 * i].z, v[2 * i].w);
+    o.z = pack2_bf16(v[2 * i + 1].x, v[2 * i + 1].y);
+    o.w = pack2_bf16(v[2 * i + 1].z, v[2 * i + 1].w);
     const uint32_t chunk = (c8 & 7) ^ (h & 7);  // 128-byte swizzle within the 16-row box
     *reinterpret_cast<uint4 *>(qd + (c8 >> 3) * 2048 + (h >> 3) * 1024 + (h & 7) * 128 + chunk * 16) = o;
   }

@@ -142,10 +142,10 @@ __device__ __forceinline__ void load_query_unit(uint8_t *qi, uint8_t *qr, float 
     *reinterpret_cast<uint4 *>(box + sw128_byte(16 + h, k)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
   uint4 o;
-  o.x = pack2(r0.x, r0.y, false);
-  o.y = pack2(r0.z, r0.w, false);
-  o.z = pack2(r1.x, r1.y, false);
-  o.w = pack2(r1.z, r1.w, false);
+  o.x = pack2_bf16(r0.x, r0.y);
+  o.y = pack2_bf16(r0.z, r0.w);
+  o.z = pack2_bf16(r1.x, r1.y);
+  o.w = pack2_bf16(r1.z, r1.w);
   *reinterpret_cast<uint4 *>(qr + (h >> 3) * 1024 + (h & 7) * 128 + ((j ^ (h & 7)) << 4)) = o;
 }
 
