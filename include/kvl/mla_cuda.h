@@ -75,13 +75,17 @@ int kvl_mla_attend_plan_info(const KvlMlaAttendPlan *plan, int *ctas, int *parti
  * d_q [B][num_heads][kv_lora_rank + rope_dim] fp32 absorbed query,
  * d_out [B][num_heads][kv_lora_rank] fp32, d_lse [B][num_heads] (natural log;
  * may be NULL).  Production shape (16, 512, 64) runs the tcgen05 kernel; other
- * shapes run a CUDA-core kernel. */
+ * shapes run a CUDA-core kernel.  d_q and d_kv must be 16-byte aligned (the
+ * call returns -1 before launching anything otherwise). */
 int kvl_mla_attend_bf16(const KvlMlaAttendPlan *plan, float *d_out, float *d_lse,
                         const float *d_q, const uint16_t *d_kv, int64_t rows, int num_heads,
                         int kv_lora_rank, int rope_dim, float softmax_scale, void *stream);
 
 /* Q8 pool (reference layout): d_latent_q8 [rows][R] int8, d_latent_scale
- * [rows] fp32, d_rope_bf16 [rows][DR] bf16. */
+ * [rows] fp32, d_rope_bf16 [rows][DR] bf16, all 16-byte aligned, as d_q.  The
+ * production shape runs on the int8 tensor cores: the query and the softmax
+ * weights times the row scales enter as two int8 parts each (about 16 bits),
+ * against the stored int8 rows with exact int32 sums. */
 int kvl_mla_attend_q8(const KvlMlaAttendPlan *plan, float *d_out, float *d_lse,
                       const float *d_q, const int8_t *d_latent_q8, const float *d_latent_scale,
                       const uint16_t *d_rope_bf16, int64_t rows, int num_heads, int kv_lora_rank,
