@@ -270,10 +270,10 @@ def cpu_reference_prefill(S, theta=50000.0):
 
 
 def cpu_reference_decode_q8(lens, threads):
-    """Times the reference's attend work for a Q8 batch through its public
-    kvl_mla_decode_compressed_q8_bf16 call is not attend-only; the attend core
-    (src/mla_compressed_q8_state.c:216-238) is timed through the C restatement
-    with one worker per core.  Returns (seconds, bytes)."""
+    """Times the reference's attend work for a Q8 batch.  The reference's public
+    kvl_mla_decode_compressed_q8_bf16 call is not attend-only, so the attend core
+    (src/mla_compressed_q8_state.c:216-238) is timed through the C restatement,
+    one worker thread per sequence.  Returns (seconds, bytes)."""
     from concurrent.futures import ThreadPoolExecutor
 
     from oracle.oracle import Oracle
@@ -293,6 +293,21 @@ def cpu_reference_decode_q8(lens, threads):
     with ThreadPoolExecutor(max_workers=threads) as ex:
         list(ex.map(lambda j: orc.attend_q8(j[0], j[1], j[2], j[3], 1.0 / math.sqrt(192.0)), jobs))
     return time.perf_counter() - t0, sum(lens) * 644
+
+
+def decode_q8_cpu_baseline(lens):
+    """The config-3 attend on this host's cores, whole workload (about a
+    second): the C restatement of the reference attend core, one sequence per
+    worker thread."""
+    try:
+        cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+        secs, nbytes = cpu_reference_decode_q8(lens, cores)
+        return {"value": nbytes / secs / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+                "sample": f"all {len(lens)} sequences ({sum(lens)} rows) of the config-3 attend through the C "
+                          "restatement of src/mla_compressed_q8_state.c:216-238 (double accumulation, as the "
+                          f"reference), one sequence per thread, {secs:.2f} s"}
+    except Exception as e:  # noqa: BLE001 - report, keep the GPU numbers
+        return {"error": str(e)}
 
 
 # ----------------------------------------------------------------------------- workloads
@@ -756,6 +771,8 @@ def main():
                             "frac_of_hbm": w2.value(ms2) / peaks["hbm_gbs"], "roofline": r2,
                             "config": w2.config(), "gpu_launches_per_step": int(l2),
                             "kernels": {k: {"ms_total": v[0], "launches": v[1]} for k, v in prof2.items()}}
+            if name == "decode_q8" and dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+                extras[name]["cpu_baseline"] = decode_q8_cpu_baseline(w2.lens)
             del w2
             torch.cuda.empty_cache()
         line["decode"] = extras
