@@ -394,13 +394,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Host launcher.
 cudaError_t launch_attend_bf16(const AttendParams &p, int grid, cudaStream_t stream) {
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(mla_attend_bf16_kernel,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr_set = true;
-  }
+  static std::atomic<unsigned long long> opted{0};
+  cudaError_t e = smem_opt_in(reinterpret_cast<const void *>(mla_attend_bf16_kernel), kSmemBytes, opted);
+  if (e != cudaSuccess) return e;
   ProfScope ps("mla_attend_bf16", stream);
   mla_attend_bf16_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError();

@@ -21,8 +21,10 @@
 //     overlap on the GPU (different streams or host threads, same device) race
 //     on the array and must be serialised by the caller;
 //   * the first call on a device looks up the array's device address
-//     (cudaGetSymbolAddress, once per device, with that device current); make
-//     that first call before any stream capture.
+//     (cudaGetSymbolAddress, once per device, with that device current);
+//   * the call is synchronous: it returns once `stream` has finished the
+//     attend and the error word is back on the host, so it cannot be captured
+//     into a CUDA graph.
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -194,9 +196,12 @@ KVL_EXPORT int kvl_mla_attend_bf16_noalloc(float *d_out, float *d_lse, const flo
   if (e == cudaSuccess) e = launch_attend_bf16_unprofiled(p, splits, st);
   if (e == cudaSuccess && splits > 1)
     e = launch_merge_unprofiled(d_out, d_lse, part_o, part_lse, &plan->merge, 1, kHeads, kLatent, st, splits);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  // The error word comes back on the caller's stream, behind the kernels, so
+  // the call waits for that stream alone (not for the legacy default stream or
+  // other blocking streams of the device).
   uint32_t err = 0;
-  if (e == cudaSuccess) e = cudaMemcpy(&err, &plan->err, sizeof err, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(&err, &plan->err, sizeof err, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) {
     fail("noalloc attend: CUDA error %lld", static_cast<long long>(e));
     return -1;

@@ -169,7 +169,10 @@ cudaError_t launch_exchange(KvlMlaPeerGroup *g, const MergeEntry *entries, int n
   AttendExchangeArgs a;
   memset(&a, 0, sizeof a);
   for (int r = 0; r < g->world; ++r) a.bufs[r] = reinterpret_cast<unsigned long long *>(g->peers[r]);
-  ++g->epoch;
+  // The tag of a call is its 32-bit number.  Buffers start zeroed, so tag 0
+  // would match words nobody wrote: on wrap-around the count skips 0 and 1 and
+  // resumes at 2, which keeps the two buffer sets alternating (set = epoch & 1).
+  if (++g->epoch == 0u) g->epoch = 2u;
   a.rank = g->rank;
   a.world = g->world;
   a.set = static_cast<int>(g->epoch & 1u);

@@ -14,6 +14,18 @@
 #define KVL_EXPORT extern "C" __attribute__((visibility("default")))
 
 namespace kvl {
+
+cudaError_t smem_opt_in(const void *fn, int bytes, std::atomic<unsigned long long> &done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const unsigned long long bit = (dev >= 0 && dev < 64) ? (1ull << dev) : 0ull;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && bit) done.fetch_or(bit, std::memory_order_acq_rel);
+  return e;
+}
+
 namespace {
 
 struct Rec {

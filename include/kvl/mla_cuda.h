@@ -101,10 +101,11 @@ int kvl_mla_attend_q8(const KvlMlaAttendPlan *plan, float *d_out, float *d_lse,
  * (0 = one per SM), with its plan and partial outputs in a fixed 4.9 MB device
  * array that the library reserves on every GPU it is loaded on until the
  * process exits.  splits above 148 are rejected; only the (16, 512, 64) shape
- * is accepted.  The first call on a device looks up that array's address and
- * should come before any stream capture.  All calls share the array: calls
- * that overlap on the GPU race and must be serialised by the caller.  Returns
- * after the result is in d_out (it waits for `stream`). */
+ * is accepted.  The first call on a device looks up that array's address.  All
+ * calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  The call is synchronous: it returns after `stream`
+ * has finished and the result is in d_out, so it cannot be captured into a
+ * CUDA graph. */
 int kvl_mla_attend_bf16_noalloc(float *d_out, float *d_lse, const float *d_q, const uint16_t *d_kv,
                                 int64_t rows, int seq_len, int64_t seq_row0, int num_heads,
                                 int kv_lora_rank, int rope_dim, int splits, float softmax_scale,
@@ -143,7 +144,10 @@ int kvl_mla_merge_packed(float *d_out, float *d_lse, const float *d_parts, int p
  *   the same order -> destroy.
  * batch * num_heads <= 256, world <= 8, kv_lora_rank a multiple of 128; d_out
  * and d_record 16-byte aligned.  Waits are bounded (2 s);
- * kvl_mla_peer_group_check reports a peer whose values did not arrive. */
+ * kvl_mla_peer_group_check reports a peer whose values did not arrive.  After
+ * such a timeout the ranks' call counts no longer agree (the rank that timed
+ * out went on without the peer's values), so the group cannot be used again:
+ * destroy it on every rank and create and connect a new one. */
 typedef struct KvlMlaPeerGroup KvlMlaPeerGroup;
 size_t kvl_mla_peer_handle_bytes(void);
 int kvl_mla_peer_group_create(KvlMlaPeerGroup **group, int rank, int world, int batch, int num_heads,

@@ -4,7 +4,7 @@ runtime's own C code, compiled from its sources by oracle/Makefile into
 oracle/_ref/ (scalar build: double-accumulating matvec; AVX2 build: the CI
 configuration).  Run in a container where the reference sources exist:
 
-    make -f oracle/Makefile all && python tests/golden/make_golden.py
+    make -f oracle/Makefile all REF=<reference checkout> && python tests/golden/make_golden.py
 
 Inputs are regenerated from seeds by in-c-test_b200/synth.py; each fixture
 stores the seeds, a digest of the generated inputs (so a drifting generator is

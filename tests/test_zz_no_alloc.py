@@ -3,9 +3,10 @@ scratch lives in a fixed device array, for callers that cannot allocate
 device memory while they decode.
 
 It must give what the allocating entry point (kvl_mla_attend_bf16 with a
-plan) gives, within the parity tolerance of the other tests (rel-L2 <= 1e-2,
-max-abs <= 2e-2), on consecutive calls that share the array, and it must
-reject sizes its array cannot hold.  This file sorts last so that a failure
+plan) gives, and what the CPU restatement of the reference attend core
+(src/mla_compressed_state.c:132-148) gives, within the parity tolerance of the
+other tests (rel-L2 <= 1e-2, max-abs <= 2e-2), on consecutive calls that share
+the array, and it must reject sizes its array cannot hold.  This file sorts last so that a failure
 here comes after every other test has run; it also passes on its own in a
 fresh process.
 """
@@ -48,7 +49,7 @@ def _noalloc(K, torch, kv_t, q_t, rows, L, r0, splits=0):
     return rc, out.cpu().numpy()[0], lse.cpu().numpy()[0]
 
 
-def test_noalloc_matches_allocating_entry_point_on_consecutive_calls(K, S, torch_cuda):
+def test_noalloc_matches_allocating_entry_point_on_consecutive_calls(K, S, orc, torch_cuda):
     torch = torch_cuda
     rows = 20000
     kv, q = _inputs(S, 31, rows)
@@ -62,6 +63,12 @@ def test_noalloc_matches_allocating_entry_point_on_consecutive_calls(K, S, torch
         want, want_lse = _allocating(K, torch, kv_t, q_t, rows, L, r0)
         assert_close(got, want, what=f"noalloc L={L} splits={splits}")
         assert np.max(np.abs(got_lse - want_lse)) < 1e-2
+        # the same call against the oracle's restatement of the reference attend
+        lat = S.bf16_bits_to_f32(kv[r0:r0 + L, :R])
+        rope = S.bf16_bits_to_f32(kv[r0:r0 + L, R:])
+        ref_mix, ref_lse = orc.attend_f32(q[0], lat, rope, SCALE)
+        assert_close(got, ref_mix, what=f"noalloc vs oracle L={L} splits={splits}")
+        assert np.max(np.abs(got_lse - ref_lse)) < 2e-2, f"lse vs oracle L={L}"
 
 
 def test_noalloc_rejects_sizes_beyond_its_array(K, S, torch_cuda):
