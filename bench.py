@@ -241,32 +241,122 @@ def replay_as_graph(torch, obj, raw, label):
         raw()
 
 
+# ----------------------------------------------------------------------------- shared inputs
+_PREFILL_INPUTS = {}
+
+
+def prefill_inputs(S=4096):
+    """Host inputs of config 2, the same for both arms (synth.py, seed 2): bf16
+    bit patterns of [q_proj, kv_a_proj, kv_a_norm, kv_b_proj, o_proj] and of the
+    token activations x [S][2048]."""
+    if S not in _PREFILL_INPUTS:
+        import kvl_pkg
+        kvl_pkg.load()
+        import kvl_b200.synth as SY
+        H, NH, DN, DR, DV, R = 2048, 16, 128, 64, 128, 512
+        w = [SY.normal_bf16(2, SY.S_WQ, (NH * (DN + DR), H), 0.02), SY.normal_bf16(2, SY.S_WKVA, (R + DR, H), 0.02),
+             SY.f32_to_bf16_bits(np.ones(R, np.float32)), SY.normal_bf16(2, SY.S_WKVB, (NH * (DN + DV), R), 0.02),
+             SY.normal_bf16(2, SY.S_WO, (H, NH * DV), 0.02)]
+        x = SY.normal_bf16(2, SY.S_X, (S, H), 1.0)
+        _PREFILL_INPUTS[S] = (w, x)
+    return _PREFILL_INPUTS[S]
+
+
+def prefill_config(S, theta, world):
+    """The `config` of the prefill line, printed identically by both arms."""
+    proj, attn = prefill_flops(S)
+    return {"workload": f"config 2: causal MLA prefill, 1 sequence x {S} tokens per rank", "seq_len": S,
+            "hidden": 2048, "heads": 16, "qk_nope": 128, "qk_rope": 64, "v_head": 128, "kv_lora_rank": 512,
+            "rope_theta": theta, "x_dtype": "bf16", "weights": "bf16 ~N(0,0.02), kv_a_norm=1",
+            "inputs": "synth.py seed 2 (splitmix64 + Box-Muller), the same values in both arms",
+            "flops_per_step_per_rank": proj + attn, "flops_projections": proj, "flops_attention": attn,
+            "l2": "flushed (256 MiB write) before every step", "parallelism": f"sequence-sharded x{world}"}
+
+
 # ----------------------------------------------------------------------------- CPU side (reference)
-_REF_INPUTS = {}
+_REF = {}
+
+
+def _reference():
+    from oracle.oracle import REF_SO, Reference
+    if "ref" not in _REF:
+        _REF["ref"] = Reference(REF_SO)
+    return _REF["ref"]
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
 
 
 def cpu_reference_prefill(S, theta=50000.0):
     """Times the reference's own kvl_mla_prefill_bf16 (oracle/_ref, AVX2 + OpenMP)
-    on one S-token sequence at the config-2 head shapes.  Inputs are generated
-    once per S.  Returns (seconds, flops)."""
-    from oracle.oracle import REF_SO, Reference, cfg_of
-    import kvl_pkg
-    kvl_pkg.load()
+    on one S-token sequence at the config-2 head shapes, on the inputs the GPU
+    arm uses.  Returns (seconds, flops)."""
+    from oracle.oracle import cfg_of
     import kvl_b200.synth as SY
-    H, NH, DN, DR, DV, R = 2048, 16, 128, 64, 128, 512
-    if S not in _REF_INPUTS:
-        w = [SY.normal_bf16(2, SY.S_WQ, (NH * (DN + DR), H), 0.02), SY.normal_bf16(2, SY.S_WKVA, (R + DR, H), 0.02),
-             SY.f32_to_bf16_bits(np.ones(R, np.float32)), SY.normal_bf16(2, SY.S_WKVB, (NH * (DN + DV), R), 0.02),
-             SY.normal_bf16(2, SY.S_WO, (H, NH * DV), 0.02)]
-        x = SY.bf16_bits_to_f32(SY.normal_bf16(2, SY.S_X, (S, H), 1.0))
-        _REF_INPUTS[S] = (Reference(REF_SO), w, x)
-    ref, w, x = _REF_INPUTS[S]
-    cfg = cfg_of(H, NH, DN, DR, DV, R, 1e-5, theta)
+    w, xb = prefill_inputs(S)
+    if ("x", S) not in _REF:
+        _REF[("x", S)] = SY.bf16_bits_to_f32(xb)
+    cfg = cfg_of(2048, 16, 128, 64, 128, 512, 1e-5, theta)
+    ref = _reference()
     t0 = time.perf_counter()
-    ref.prefill(x, cfg, w)
+    ref.prefill(_REF[("x", S)], cfg, w)
     dt = time.perf_counter() - t0
     proj, attn = prefill_flops(S)
     return dt, proj + attn
+
+
+def cpu_reference_decode(L, nseq, threads, q8=False, theta=50000.0, seed=4):
+    """Times the reference's own decode call -- kvl_mla_decode_compressed_bf16,
+    or kvl_mla_decode_compressed_q8_bf16 with q8 (src/mla_compressed_state.c:86-161,
+    src/mla_compressed_q8_state.c:161-255; oracle/_ref, AVX2 + OpenMP) -- once
+    for each of `nseq` sequences of L cached rows (synthetic rows written into
+    the state, random config-2-shaped weights), `threads` sequences at a time.
+    The call is the whole decode of one token: projections, append and the
+    attention over L + 1 rows.  Returns seconds for all calls."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from oracle.oracle import cfg_of
+    import kvl_b200.kvl_mla as K
+    import kvl_b200.synth as SY
+    ref = _reference()
+    cfg = cfg_of(2048, 16, 128, 64, 128, 512, 1e-5, theta)
+    w = K.random_weights(K.make_config(2048, 16, 128, 64, 128, 512, 1e-5, theta), seed, 0.02)
+    xs = SY.bf16_bits_to_f32(SY.normal_bf16(seed, SY.S_X, (nseq, 2048), 1.0))
+    if q8:
+        rows = (SY.uniform_int8(seed, SY.S_LAT, (L, 512)), SY.uniform_f32(seed, SY.S_SCALE, (L,), 0.001, 0.02),
+                SY.normal_bf16(seed, SY.S_ROPE, (L, 64), 1.0))
+        call = lambda b: ref.decode_q8_from_rows(xs[b], cfg, w.arrays, *rows)  # noqa: E731
+    else:
+        kv = SY.bf16_bits_to_f32(SY.normal_bf16(seed, SY.S_LAT, (L, 576), 1.0))
+        lat, rope = np.ascontiguousarray(kv[:, :512]), np.ascontiguousarray(kv[:, 512:])
+        call = lambda b: ref.decode_from_rows(xs[b], cfg, w.arrays, lat, rope)  # noqa: E731
+    t0 = time.perf_counter()
+    if threads <= 1:
+        for b in range(nseq):
+            call(b)
+    else:
+        with ThreadPoolExecutor(max_workers=threads) as ex:
+            list(ex.map(call, range(nseq)))
+    return time.perf_counter() - t0
+
+
+def cpu_port_attend_bf16(L, threads=1):
+    """The attend core of the reference decode (src/mla_compressed_state.c:132-148)
+    through the C restatement (double accumulation, single-threaded as in the
+    reference) over L synthetic rows of one sequence.  Returns seconds."""
+    from oracle.oracle import Oracle
+    import kvl_b200.synth as SY
+    orc = Oracle()
+    kv = SY.bf16_bits_to_f32(SY.normal_bf16(5, SY.S_LAT, (L, 576), 1.0))
+    lat, rope = np.ascontiguousarray(kv[:, :512]), np.ascontiguousarray(kv[:, 512:])
+    q = SY.bf16_bits_to_f32(SY.normal_bf16(5, SY.S_Q, (16, 576), 0.1))
+    t0 = time.perf_counter()
+    orc.attend_f32(q, lat, rope, 1.0 / math.sqrt(192.0))
+    return time.perf_counter() - t0
 
 
 def cpu_reference_decode_q8(lens, threads):
@@ -277,8 +367,6 @@ def cpu_reference_decode_q8(lens, threads):
     from concurrent.futures import ThreadPoolExecutor
 
     from oracle.oracle import Oracle
-    import kvl_pkg
-    kvl_pkg.load()
     import kvl_b200.synth as SY
     orc = Oracle()
     R, DR, NH = 512, 64, 16
@@ -295,19 +383,78 @@ def cpu_reference_decode_q8(lens, threads):
     return time.perf_counter() - t0, sum(lens) * 644
 
 
-def decode_q8_cpu_baseline(lens):
-    """The config-3 attend on this host's cores, whole workload (about a
-    second): the C restatement of the reference attend core, one sequence per
-    worker thread."""
+def _cpu_guard(fn):
     try:
-        cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
-        secs, nbytes = cpu_reference_decode_q8(lens, cores)
-        return {"value": nbytes / secs / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
-                "sample": f"all {len(lens)} sequences ({sum(lens)} rows) of the config-3 attend through the C "
-                          "restatement of src/mla_compressed_q8_state.c:216-238 (double accumulation, as the "
-                          f"reference), one sequence per thread, {secs:.2f} s"}
+        return fn()
     except Exception as e:  # noqa: BLE001 - report, keep the GPU numbers
         return {"error": str(e)}
+
+
+def decode_cpu_baseline(name, wl):
+    """CPU figures of one decode sub-line, on this host's cores.  `cpu_baseline`
+    is the reference's own decode call where the line's workload allows it,
+    else the C restatement of the reference attend core (kind "port"); each
+    says what its sample was."""
+    cores = host_threads()
+    if name == "decode_parity":
+        def run():
+            reps = 5
+            dt = cpu_reference_decode(wl.L, reps, 1) / reps
+            port = cpu_port_attend_bf16(wl.L)
+            return {"value": wl.L * 1152 / dt / 1e9, "unit": "GB/s", "cores": cores, "kind": "reference",
+                    "sample": f"reference kvl_mla_decode_compressed_bf16 (AVX2 + OpenMP matvecs, serial attention) "
+                              f"at L={wl.L}, one call = the whole decode of a token (projections, append, "
+                              f"attention), {1e3 * dt:.1f} ms per call (mean of {reps}); KV bytes counted at "
+                              "1152 B per row as on the GPU line",
+                    "attend_core_port": {"value": wl.L * 1152 / port / 1e9, "unit": "GB/s", "cores": 1,
+                                         "sample": f"C restatement of src/mla_compressed_state.c:132-148 over "
+                                                   f"{wl.L} rows, {1e3 * port:.2f} ms"}}
+        return _cpu_guard(run)
+    if name == "decode_long":
+        def run():
+            n = 16384
+            dt = cpu_port_attend_bf16(n)
+            return {"value": n * 1152 / dt / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+                    "sample": f"C restatement of the reference attend core (src/mla_compressed_state.c:132-148, "
+                              f"single-threaded as the reference) over the first {n} of {wl.L} rows, "
+                              f"{dt:.2f} s; the rate is per row, so the whole sequence takes about "
+                              f"{dt * wl.L / n:.1f} s (extrapolated)"}
+        return _cpu_guard(run)
+    if name == "decode_stack":
+        def run():
+            nseq, thr = 8, min(8, cores)
+            dt = cpu_reference_decode(wl.L, nseq, thr)
+            nbytes = nseq * wl.L * 1152
+            step = dt * wl.LAYERS * (256 / nseq)
+            return {"value": nbytes / dt / 1e9, "unit": "GB/s", "cores": thr, "kind": "reference",
+                    "sample": f"subset: 1 layer x {nseq} sequences at L={wl.L} through the reference "
+                              f"kvl_mla_decode_compressed_bf16 (whole decode call), {thr} sequences in parallel, "
+                              f"{dt:.2f} s", "extrapolated": True,
+                    "extrapolated_step_s": step,
+                    "extrapolation": f"linear: x{wl.LAYERS} layers x {256 // nseq} sequence groups"}
+        return _cpu_guard(run)
+    if name == "decode_q8":
+        def run():
+            secs, nbytes = cpu_reference_decode_q8(wl.lens, cores)
+            res = {"value": nbytes / secs / 1e9, "unit": "GB/s", "cores": cores, "kind": "port",
+                   "sample": f"all {len(wl.lens)} sequences ({sum(wl.lens)} rows) of the config-3 attend through the "
+                             "C restatement of src/mla_compressed_q8_state.c:216-238 (double accumulation, as the "
+                             f"reference), one sequence per thread, {secs:.2f} s"}
+            sub = sorted(wl.lens)[len(wl.lens) // 2:len(wl.lens) // 2 + 8]
+            thr = min(8, cores)
+            t0 = time.perf_counter()
+            from concurrent.futures import ThreadPoolExecutor
+            with ThreadPoolExecutor(max_workers=thr) as ex:
+                times = list(ex.map(lambda L: cpu_reference_decode(L, 1, 1, q8=True), sub))
+            wall = time.perf_counter() - t0
+            res["reference_call"] = {
+                "value": sum(sub) * 644 / wall / 1e9, "unit": "GB/s", "cores": thr, "kind": "reference",
+                "sample": f"subset: 8 of the 64 config-3 lengths ({sum(sub)} rows) through the reference "
+                          f"kvl_mla_decode_compressed_q8_bf16 (whole decode call per sequence), {thr} in parallel, "
+                          f"{wall:.2f} s wall ({1e3 * sum(times) / len(times):.0f} ms per call)"}
+            return res
+        return _cpu_guard(run)
+    return None
 
 
 # ----------------------------------------------------------------------------- workloads
@@ -325,11 +472,14 @@ class Prefill:
         self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
         self.S = S
         dev = torch.device("cuda", torch.cuda.current_device())
-        g = torch.Generator(device=dev)
-        g.manual_seed(2 + 1000 * dist.rank)
         self.cfg = K.make_config(2048, 16, 128, 64, 128, 512, 1e-5, theta)
-        self.wt, self.w = device_weights(torch, K, self.cfg, g, dev)
-        self.x = dev_bf16(torch, (S, 2048), 1.0, g, dev)
+        # the same synthetic inputs as the reference arm (synth.py, seed 2)
+        w_host, x_host = prefill_inputs(S)
+        names = ("q_proj", "kv_a_proj", "kv_a_norm", "kv_b_proj", "o_proj")
+        self.w_host = w_host
+        self.wt = {k: torch.from_numpy(a.view(np.int16)).to(dev).view(torch.bfloat16) for k, a in zip(names, w_host)}
+        self.w = K.KvlMlaDeviceWeights(*[self.wt[k].data_ptr() for k in names])
+        self.x = torch.from_numpy(x_host.view(np.int16)).to(dev).view(torch.bfloat16)
         self.out = torch.empty((S, 2048), dtype=torch.float32, device=dev)
         nbytes = lib.kvl_mla_prefill_workspace_bytes(C.byref(self.cfg), S)
         self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
@@ -365,8 +515,7 @@ class Prefill:
         cached on the device, as with a full trunk cache)."""
         torch, K, lib = self.torch, self.K, self.lib
         lib.kvl_mla_cuda_weight_cache(1)
-        hw = K.Weights(*[self.wt[k].view(torch.int16).cpu().numpy().view(np.uint16)
-                         for k in ("q_proj", "kv_a_proj", "kv_a_norm", "kv_b_proj", "o_proj")])
+        hw = K.Weights(*self.w_host)
         x = self.x.float().cpu().numpy()
         x_pinned = torch.from_numpy(x).pin_memory().numpy()
         out = torch.empty((self.S, 2048), dtype=torch.float32).pin_memory().numpy()
@@ -389,16 +538,14 @@ class Prefill:
                 "path": "kvl_mla_prefill_bf16 (host fp32 in/out)"}
 
     def config(self):
-        return {"workload": "config 2: causal MLA prefill, 1 sequence x 4096 tokens per rank", "seq_len": self.S,
-                "hidden": 2048, "heads": 16, "qk_nope": 128, "qk_rope": 64, "v_head": 128, "kv_lora_rank": 512,
-                "rope_theta": self.cfg.rope_theta, "x_dtype": "bf16", "weights": "bf16 ~N(0,0.02), kv_a_norm=1",
-                "flops_per_step_per_rank": self.units, "flops_projections": self.proj, "flops_attention": self.attn,
-                "l2": "flushed (256 MiB write) before every step", "parallelism": f"sequence-sharded x{self.dist.world}",
-                "launch": ("kvl_mla_prefill_dev captured once as a CUDA graph (both streams), replayed per step"
-                           if getattr(self, "_graph", None) else "kvl_mla_prefill_dev launched per step")}
+        return prefill_config(self.S, self.cfg.rope_theta, self.dist.world)
+
+    def launch(self):
+        return ("kvl_mla_prefill_dev captured once as a CUDA graph (both streams), replayed per step"
+                if getattr(self, "_graph", None) else "kvl_mla_prefill_dev launched per step")
 
     def cpu_baseline(self):
-        cores = int(os.environ.get("OMP_NUM_THREADS", os.cpu_count() or 1))
+        cores = int(os.environ.get("OMP_NUM_THREADS", host_threads()))
         dt, fl = cpu_reference_prefill(self.S)
         return {"value": fl / dt / 1e12, "unit": self.unit, "cores": cores, "kind": "reference",
                 "sample": f"one full config-2 step: reference kvl_mla_prefill_bf16 (AVX2+OpenMP, oracle/_ref) on "
@@ -661,6 +808,73 @@ class DecodeParity:
                 "parallelism": f"replicas x{self.dist.world}"}
 
 
+def dropin_decode_line(K, lib, steps, warmup, cpu=True, lens=(1024, 8192)):
+    """The call the reference runtime makes once per layer per token
+    (src/generate.c:61): kvl_mla_decode_compressed_bf16 with host fp32 x and
+    out in pageable memory (malloc'd, as the runtime's), against a state of L
+    cached rows.  The call is synchronous, so each is timed on the host clock.
+    Two weight modes: cached on the device by host pointer (what a full trunk
+    cache allows, src/trunk_store.c:188-226) and uploaded on every call (the
+    ~27.5 MB of one layer's projections, what the runtime's per-call weight
+    reload implies otherwise, src/generate.c:40-76).  Beside each, the device
+    time of the call's kernels (per-kernel CUDA events) and the reference's own
+    call at the same L on this host's cores."""
+    import kvl_b200.synth as SY
+    cfg = K.make_config(2048, 16, 128, 64, 128, 512, 1e-5, 50000.0)
+    w = K.random_weights(cfg, 1, 0.02)
+    res = {"metric": "MLA drop-in decode latency (kvl_mla_decode_compressed_bf16, host fp32 x/out, pageable)",
+           "unit": "ms/call", "h2d_bytes_per_call": {"x": 2048 * 4, "weights_when_uploaded": int(
+               sum(a.nbytes for a in w.arrays))}, "d2h_bytes_per_call": {"out": 2048 * 4, "state_row_mirror": 576 * 4},
+           "lengths": {}}
+    prev = lib.kvl_mla_cuda_weight_cache(1)
+    n = warmup + steps
+    for L in lens:
+        st = K.CompressedState(cfg, L + n + 1, lib=lib)
+        x_pre = SY.bf16_bits_to_f32(SY.normal_bf16(11, SY.S_X, (L, 2048), 1.0))
+        if st.prefill(x_pre, w) != 0:
+            raise RuntimeError(K.last_error())
+        xs = SY.bf16_bits_to_f32(SY.normal_bf16(12, SY.S_X, (n, 2048), 1.0))
+        entry = {}
+        for mode, cache in (("weights_cached", 1), ("weights_uploaded", 0)):
+            lib.kvl_mla_cuda_weight_cache(cache)
+            times = []
+            for i in range(n):
+                t0 = time.perf_counter()
+                rc, _ = st.decode(xs[i], L + i, w)
+                dt = time.perf_counter() - t0
+                if rc != 0:
+                    raise RuntimeError(K.last_error())
+                if i >= warmup:
+                    times.append(dt)
+            if lib.kvl_mla_compressed_state_truncate(C.byref(st.s), L) != 0:
+                raise RuntimeError(K.last_error())
+            # device time of the same calls' kernels
+            lib.kvl_mla_cuda_profile(1)
+            for i in range(min(steps, 5)):
+                st.decode(xs[i], L + i, w)
+            prof = profile_read(lib)
+            lib.kvl_mla_cuda_profile(0)
+            if lib.kvl_mla_compressed_state_truncate(C.byref(st.s), L) != 0:
+                raise RuntimeError(K.last_error())
+            kern_ms = sum(v[0] for v in prof.values()) / max(1, min(steps, 5))
+            entry[mode] = {"ms_per_call": 1e3 * float(np.median(times)), "ms_min": 1e3 * float(min(times)),
+                           "kernel_ms_per_call": kern_ms,
+                           "kernels_per_call": int(sum(v[1] for v in prof.values()) // max(1, min(steps, 5))),
+                           "kv_gbs": L * 1152 / float(np.median(times)) / 1e9}
+        st.free()
+        if cpu:
+            reps = 3 if L <= 2048 else 1
+            dt = cpu_reference_decode(L, reps, 1) / reps
+            entry["cpu_reference"] = {"ms_per_call": 1e3 * dt, "cores": host_threads(), "kind": "reference",
+                                      "sample": f"reference kvl_mla_decode_compressed_bf16 (oracle/_ref, AVX2 + "
+                                                f"OpenMP matvecs) at L={L}, mean of {reps} call(s)"}
+            entry["speedup_vs_reference"] = {m: entry["cpu_reference"]["ms_per_call"] / entry[m]["ms_per_call"]
+                                             for m in ("weights_cached", "weights_uploaded")}
+        res["lengths"][str(L)] = entry
+    lib.kvl_mla_cuda_weight_cache(prev)
+    return res
+
+
 WORKLOADS = {"prefill": Prefill, "decode_q8": DecodeQ8, "decode_long": DecodeLong, "decode_stack": DecodeStack,
              "decode_parity": DecodeParity}
 
@@ -745,7 +959,8 @@ def main():
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak"
         if wl.name == "prefill" else "strong", "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"),
         "data": "synthetic (seeded)",
-        "config": wl.config(), "roofline": roof, "gpu_launches": int(launches) * args.steps,
+        "config": wl.config(), "launch": wl.launch() if hasattr(wl, "launch") else None,
+        "roofline": roof, "gpu_launches": int(launches) * args.steps,
         "kernels": {k: {"ms_total": v[0], "launches": v[1]} for k, v in prof.items()}, "clocks": clk,
     }
     if hasattr(wl, "e2e") and not args.no_e2e:
@@ -771,10 +986,17 @@ def main():
                             "frac_of_hbm": w2.value(ms2) / peaks["hbm_gbs"], "roofline": r2,
                             "config": w2.config(), "gpu_launches_per_step": int(l2),
                             "kernels": {k: {"ms_total": v[0], "launches": v[1]} for k, v in prof2.items()}}
-            if name == "decode_q8" and dist.rank == 0 and dist.world == 1 and not args.no_cpu:
-                extras[name]["cpu_baseline"] = decode_q8_cpu_baseline(w2.lens)
+            if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
+                cb = decode_cpu_baseline(name, w2)
+                if cb is not None:
+                    extras[name]["cpu_baseline"] = cb
             del w2
             torch.cuda.empty_cache()
+        if dist.rank == 0 and dist.world == 1:
+            try:
+                extras["decode_dropin"] = dropin_decode_line(K, lib, max(5, args.steps), 3, cpu=not args.no_cpu)
+            except Exception as e:  # noqa: BLE001
+                extras["decode_dropin"] = {"error": str(e)}
         line["decode"] = extras
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu and hasattr(wl, "cpu_baseline"):
         try:
@@ -809,6 +1031,7 @@ def run_reference(args, dist):
         print(json.dumps({"impl": "reference", "unavailable": f"reference arm implemented for prefill only"}))
         return 0
     S = 4096
+    prefill_inputs(S)
     for _ in range(max(0, min(args.warmup, 1))):
         cpu_reference_prefill(S)
     times, fl = [], 0
@@ -823,7 +1046,8 @@ def run_reference(args, dist):
         "impl": "reference", "metric": Prefill.metric, "value": value, "unit": Prefill.unit, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32 (bf16 weights)", "data": "synthetic (seeded)",
-        "config": {"workload": "config 2: causal MLA prefill, 1 sequence x 4096 tokens", "seq_len": S},
+        "config": prefill_config(S, 50000.0, args.gpus),
+        "launch": f"reference kvl_mla_prefill_bf16 on the host ({cores} threads), one call per step",
         "cpu_baseline": {"value": value, "unit": Prefill.unit, "cores": cores, "kind": "reference", "sample": sample},
         "e2e": {"value": value, "unit": Prefill.unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
     return 0

@@ -298,6 +298,53 @@ class Reference:
         assert rc == 0
         return out
 
+    def decode_from_rows(self, x, cfg, warrays, latent, rope):
+        """One kvl_mla_decode_compressed_bf16 call for token x at position L
+        against a state whose L cached rows are given (fp32 latent [L][R] and
+        rope [L][DR], written into the public state arrays as the reference's
+        lab tools do).  Returns (out [H], appended latent [R], appended rope [DR])."""
+        x = np.ascontiguousarray(x, np.float32)
+        L, R = latent.shape
+        DR = rope.shape[1]
+        w = w_of(warrays)
+        st = State()
+        assert self.lib.kvl_mla_compressed_state_init(C.byref(st), C.byref(cfg), L + 1) == 0
+        np.ctypeslib.as_array(st.latent, shape=((L + 1) * R,))[:L * R] = np.asarray(latent, np.float32).reshape(-1)
+        np.ctypeslib.as_array(st.rope, shape=((L + 1) * DR,))[:L * DR] = np.asarray(rope, np.float32).reshape(-1)
+        st.len = L
+        out = np.zeros(cfg.hidden_size, np.float32)
+        rc = self.lib.kvl_mla_decode_compressed_bf16(_p(out, f32p), _p(x, f32p), L, C.byref(cfg), C.byref(w),
+                                                     C.byref(st))
+        assert rc == 0
+        lat_new = np.ctypeslib.as_array(st.latent, shape=((L + 1) * R,))[L * R:].copy()
+        rope_new = np.ctypeslib.as_array(st.rope, shape=((L + 1) * DR,))[L * DR:].copy()
+        self.lib.kvl_mla_compressed_state_free(C.byref(st))
+        return out, lat_new, rope_new
+
+    def decode_q8_from_rows(self, x, cfg, warrays, lat8, lscale, rope16):
+        """kvl_mla_decode_compressed_q8_bf16 for token x at position L against a
+        Q8 state whose L cached rows are given (int8 [L][R], fp32 [L], bf16 bits
+        [L][DR]).  Returns (out [H], appended int8 [R], scale, bf16 rope [DR])."""
+        x = np.ascontiguousarray(x, np.float32)
+        L, R = lat8.shape
+        DR = rope16.shape[1]
+        w = w_of(warrays)
+        st = Q8State()
+        assert self.lib.kvl_mla_compressed_q8_state_init(C.byref(st), C.byref(cfg), L + 1) == 0
+        np.ctypeslib.as_array(st.latent_q8, shape=((L + 1) * R,))[:L * R] = np.asarray(lat8, np.int8).reshape(-1)
+        np.ctypeslib.as_array(st.latent_scale, shape=(L + 1,))[:L] = np.asarray(lscale, np.float32)
+        np.ctypeslib.as_array(st.rope_bf16, shape=((L + 1) * DR,))[:L * DR] = np.asarray(rope16, np.uint16).reshape(-1)
+        st.len = L
+        out = np.zeros(cfg.hidden_size, np.float32)
+        rc = self.lib.kvl_mla_decode_compressed_q8_bf16(_p(out, f32p), _p(x, f32p), L, C.byref(cfg), C.byref(w),
+                                                        C.byref(st))
+        assert rc == 0
+        q_new = np.ctypeslib.as_array(st.latent_q8, shape=((L + 1) * R,))[L * R:].copy()
+        s_new = float(np.ctypeslib.as_array(st.latent_scale, shape=(L + 1,))[L])
+        r_new = np.ctypeslib.as_array(st.rope_bf16, shape=((L + 1) * DR,))[L * DR:].copy()
+        self.lib.kvl_mla_compressed_q8_state_free(C.byref(st))
+        return out, q_new, s_new, r_new
+
     def decode_sequence(self, x, cfg, warrays, prefix=0, q8=False):
         """Prefill `prefix` rows then decode the remaining tokens one by one.
         Returns (outputs of the decoded tokens, final state arrays)."""
