@@ -3,7 +3,7 @@
 (% HBM peak) & prefill TFLOP/s at 1/2/4/8 B200").
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload prefill|decode_q8|decode_long|decode_stack|decode_parity]
+                    [--workload prefill|decode_q8|decode_q8_step|decode_long|decode_stack|decode_parity]
 
 Default workload: BASELINE config 2 (causal MLA prefill, one sequence of 4096
 tokens, H=2048, 16 heads; the configuration the metric's prefill half is quoted
@@ -216,11 +216,11 @@ def device_weights(torch, K, cfg, gen, device, std=0.02):
     return t, w
 
 
-def replay_as_graph(torch, obj, raw, label):
+def replay_as_graph(torch, obj, raw, label, attr="_graph"):
     """Runs raw() (a sequence of library launches on the current stream) as a
-    CUDA graph captured on first use; every replay launches every kernel again.
-    Falls back to raw() if the capture is refused."""
-    if getattr(obj, "_graph", None) is None:
+    CUDA graph captured on first use (kept in obj.<attr>); every replay launches
+    every kernel again.  Falls back to raw() if the capture is refused."""
+    if getattr(obj, attr, None) is None:
         side = torch.cuda.Stream()
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
@@ -231,12 +231,12 @@ def replay_as_graph(torch, obj, raw, label):
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 raw()
-            obj._graph = g
+            setattr(obj, attr, g)
         except RuntimeError as e:
             print(f"{label}: CUDA graph capture failed ({e}); launching directly", file=sys.stderr)
-            obj._graph = False
-    if obj._graph:
-        obj._graph.replay()
+            setattr(obj, attr, False)
+    if getattr(obj, attr):
+        getattr(obj, attr).replay()
     else:
         raw()
 
@@ -459,7 +459,11 @@ def decode_cpu_baseline(name, wl):
 
 # ----------------------------------------------------------------------------- workloads
 class Prefill:
-    """one 4096-token causal MLA prefill per rank."""
+    """one 4096-token causal MLA prefill.  On one GPU the
+    whole prompt; under torchrun (N > 1) the same prompt context-parallel over
+    the N GPUs (mode "cp": zigzag query chunks, one NCCL all-gather of the
+    compressed rows between kvl_mla_prefill_cp_begin and _end; strong scaling),
+    or one independent prompt per GPU (mode "independent"; weak scaling)."""
     name = "prefill"
     metric = "MLA prefill TFLOP/s (config 2: S=4096, H=2048, 16 heads, causal)"
     unit = "TFLOP/s"
@@ -468,9 +472,13 @@ class Prefill:
     # (profiles/flash_prefill_config2.txt, profiles/gemm_prefill_config2.txt)
     ncu_traffic = {"flash_prefill": 59.550720e6 + 3.057408e6, "gemm_q": 30.439168e6 + 0.093440e6}
 
-    def __init__(self, torch, K, lib, dist, S=4096, theta=50000.0):
+    def __init__(self, torch, K, lib, dist, S=4096, theta=50000.0, mode=None):
         self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
         self.S = S
+        self.mode = mode or ("cp" if dist.world > 1 else "single")
+        self.scaling = "strong" if self.mode == "cp" else "weak"
+        if self.mode == "independent":
+            self.name = "prefill_independent"
         dev = torch.device("cuda", torch.cuda.current_device())
         self.cfg = K.make_config(2048, 16, 128, 64, 128, 512, 1e-5, theta)
         # the same synthetic inputs as the reference arm (synth.py, seed 2)
@@ -485,18 +493,53 @@ class Prefill:
         self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         self.proj, self.attn = prefill_flops(S)
         self.units = self.proj + self.attn
+        if self.mode == "cp":
+            c = S // (2 * dist.world)
+            self.c = c
+            self.send = torch.empty((2 * c, 576), dtype=torch.int16, device=dev)
+            self.recv = torch.empty((dist.world * 2 * c, 576), dtype=torch.int16, device=dev)
 
     def kernel_flops(self):
-        """Algorithmic FLOPs per step of each library kernel of the prefill path."""
+        """Algorithmic FLOPs per step of each library kernel of the prefill path
+        (on this rank: in context-parallel mode its 2c query rows and the keys
+        its chunks see; the zigzag split gives every rank 1/N of the causal
+        pairs)."""
         S, H, NH, QD, DV, R, DR = self.S, 2048, 16, 192, 128, 512, 64
+        if self.mode == "cp":
+            rows, world = 2 * self.c, self.dist.world
+            kmax = (2 * world - self.dist.rank) * self.c
+            return {"flash_prefill": float(self.attn) / world, "gemm_q": 2.0 * rows * H * NH * QD,
+                    "gemm_kva": 2.0 * rows * H * (R + DR), "gemm_kvb": 2.0 * kmax * R * NH * (128 + DV),
+                    "gemm_o": 2.0 * rows * NH * DV * H}
         return {"gemv_bf16": 2.0 * S * (H * (NH * QD + R + DR) + NH * DV * H),
                 "vup": 2.0 * S * NH * DV * R, "absorb": 2.0 * S * NH * 128 * R,
                 "mla_attend_bf16": float(self.attn), "flash_prefill": float(self.attn),
                 "gemm_q": 2.0 * S * H * NH * QD, "gemm_kva": 2.0 * S * H * (R + DR),
                 "gemm_kvb": 2.0 * S * R * NH * (128 + DV), "gemm_o": 2.0 * S * NH * DV * H}
 
+    def _cp_begin(self):
+        s = self.torch.cuda.current_stream().cuda_stream
+        rc = self.lib.kvl_mla_prefill_cp_begin(C.byref(self.cfg), C.byref(self.w), self.x.data_ptr(), self.S,
+                                               self.dist.rank, self.dist.world, self.send.data_ptr(),
+                                               self.ws.data_ptr(), self.ws.numel(), s)
+        if rc != 0:
+            raise RuntimeError(self.K.last_error())
+
+    def _cp_end(self):
+        s = self.torch.cuda.current_stream().cuda_stream
+        rc = self.lib.kvl_mla_prefill_cp_end(C.byref(self.cfg), C.byref(self.w), self.out.data_ptr(), self.S,
+                                             self.dist.rank, self.dist.world, self.recv.data_ptr(),
+                                             self.ws.data_ptr(), self.ws.numel(), s)
+        if rc != 0:
+            raise RuntimeError(self.K.last_error())
+
     def step_profiled(self):
-        """kvl_mla_prefill_dev launched directly (per-kernel CUDA events)."""
+        """The launches of one step issued directly (per-kernel CUDA events)."""
+        if self.mode == "cp":
+            self._cp_begin()
+            self.dist.pg.all_gather_into_tensor(self.recv, self.send)
+            self._cp_end()
+            return
         s = self.torch.cuda.current_stream().cuda_stream
         rc = self.lib.kvl_mla_prefill_dev(C.byref(self.cfg), C.byref(self.w), self.out.data_ptr(),
                                           self.x.data_ptr(), self.S, self.ws.data_ptr(), self.ws.numel(), s)
@@ -504,15 +547,29 @@ class Prefill:
             raise RuntimeError(self.K.last_error())
 
     def step(self):
-        """The same launches (both streams of the fork) replayed as a CUDA graph."""
+        """The same launches replayed as CUDA graphs (both streams of the fork);
+        in context-parallel mode the two halves are graphs and the NCCL
+        all-gather between them is issued directly."""
+        if self.mode == "cp":
+            replay_as_graph(self.torch, self, self._cp_begin, "prefill cp begin", "_graph_begin")
+            self.dist.pg.all_gather_into_tensor(self.recv, self.send)
+            replay_as_graph(self.torch, self, self._cp_end, "prefill cp end", "_graph_end")
+            return
         replay_as_graph(self.torch, self, self.step_profiled, "prefill")
 
     def value(self, ms_per_step):
-        return self.dist.world * self.units / (ms_per_step * 1e-3) / 1e12
+        prompts = 1 if self.mode == "cp" else self.dist.world
+        return prompts * self.units / (ms_per_step * 1e-3) / 1e12
 
     def e2e(self, K_steps, W_steps):
         """Public host API kvl_mla_prefill_bf16 with host fp32 activations (weights
-        cached on the device, as with a full trunk cache)."""
+        cached on the device, as with a full trunk cache).  In context-parallel
+        mode: each rank copies its chunks' rows of the prompt (pinned fp32) to
+        the device, rounds them to bf16, runs kvl_mla_prefill_cp_begin, the
+        all-gather and kvl_mla_prefill_cp_end, and copies its rows of the output
+        back."""
+        if self.mode == "cp":
+            return self._e2e_cp(K_steps, W_steps)
         torch, K, lib = self.torch, self.K, self.lib
         lib.kvl_mla_cuda_weight_cache(1)
         hw = K.Weights(*self.w_host)
@@ -537,10 +594,56 @@ class Prefill:
                 "h2d_bytes_per_step": int(x.nbytes), "d2h_bytes_per_step": int(out.nbytes),
                 "path": "kvl_mla_prefill_bf16 (host fp32 in/out)"}
 
+    def _e2e_cp(self, K_steps, W_steps):
+        import kvl_b200.parallel as PAR
+        torch, lib = self.torch, self.lib
+        (a0, a1), (b0, b1) = PAR.zigzag_chunks(self.S, self.dist.world)[self.dist.rank]
+        x_host = torch.from_numpy(self.x.float().cpu().numpy()).pin_memory()
+        out_host = torch.empty((self.S, 2048), dtype=torch.float32).pin_memory()
+        xf = torch.empty((self.S, 2048), dtype=torch.float32, device=self.x.device)
+        xb16 = self.x.view(torch.int16)
+        stream = torch.cuda.current_stream()
+
+        def call():
+            for lo, hi in ((a0, a1), (b0, b1)):
+                xf[lo:hi].copy_(x_host[lo:hi], non_blocking=True)
+                rc = lib.kvl_mla_bf16_rne(xb16[lo:hi].data_ptr(), xf[lo:hi].data_ptr(), (hi - lo) * 2048,
+                                          stream.cuda_stream)
+                if rc != 0:
+                    raise RuntimeError(self.K.last_error())
+            self._cp_begin()
+            self.dist.pg.all_gather_into_tensor(self.recv, self.send)
+            self._cp_end()
+            for lo, hi in ((a0, a1), (b0, b1)):
+                out_host[lo:hi].copy_(self.out[lo:hi], non_blocking=True)
+            stream.synchronize()
+        for _ in range(W_steps):
+            call()
+        self.dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(K_steps):
+            call()
+        dt = (time.perf_counter() - t0) * 1e3 / K_steps
+        dt = self.dist.max(torch, dt)
+        rows = (a1 - a0) + (b1 - b0)
+        return {"value": self.value(dt), "unit": self.unit, "ms_per_step": dt,
+                "h2d_bytes_per_step": int(rows * 2048 * 4 * self.dist.world),
+                "d2h_bytes_per_step": int(rows * 2048 * 4 * self.dist.world),
+                "path": "per rank: its chunks' rows (pinned fp32) -> device, kvl_mla_bf16_rne, kvl_mla_prefill_cp_begin, "
+                        "NCCL all-gather, kvl_mla_prefill_cp_end, its rows of the output -> host; bytes summed "
+                        "over ranks"}
+
     def config(self):
-        return prefill_config(self.S, self.cfg.rope_theta, self.dist.world)
+        cfg = prefill_config(self.S, self.cfg.rope_theta, self.dist.world)
+        if self.mode == "cp":
+            cfg["parallelism"] = (f"context-parallel x{self.dist.world}: zigzag query chunks of {self.c} rows, one "
+                                  "NCCL all-gather of the compressed 576-wide rows per step")
+            cfg["workload"] = f"config 2: causal MLA prefill, 1 sequence x {self.S} tokens over all ranks"
+        return cfg
 
     def launch(self):
+        if self.mode == "cp":
+            return "kvl_mla_prefill_cp_begin / _end as two CUDA graphs with the NCCL all-gather issued between them"
         return ("kvl_mla_prefill_dev captured once as a CUDA graph (both streams), replayed per step"
                 if getattr(self, "_graph", None) else "kvl_mla_prefill_dev launched per step")
 
@@ -598,6 +701,72 @@ class DecodeQ8:
     def config(self):
         return {"workload": "config 3: Q8 batched decode attend, 64 seqs", "lens_sum": int(sum(self.lens)),
                 "bytes_per_token": 644, "parallelism": f"sequence-sharded x{self.dist.world}"}
+
+
+class DecodeQ8Step:
+    """BASELINE config 3 as a full decode step: for the 64 Q8 sequences, one
+    kvl_mla_decode_step_q8 (q/kv_a projections, the reference row quantiser
+    appending each token's row, the int8 attend over L + 1 rows, V
+    up-projection and o_proj) on random config-2-shaped weights; the
+    batched form of src/mla_compressed_q8_state.c:161-255."""
+    name = "decode_q8_step"
+    metric = "MLA Q8 decode step KV GB/s (config 3 full step: 64 seqs, L~U[512,8192])"
+    unit = "GB/s"
+    bound = "hbm"
+    dtype = DecodeQ8.dtype
+
+    def __init__(self, torch, K, lib, dist):
+        import kvl_b200.synth as SY
+        import kvl_b200.parallel as PAR
+        self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
+        lens_all = [int(v) for v in SY.uniform_ints(3, SY.S_LEN, 64, 512, 8192)]
+        mine = PAR.shard_sequences(lens_all, dist.world)[dist.rank]
+        self.lens = [lens_all[i] for i in mine]
+        self.total_bytes = sum(L + 1 for L in lens_all) * 644
+        rows_seq = [L + 1 for L in self.lens]
+        self.rows = sum(rows_seq)
+        row0 = np.concatenate([[0], np.cumsum(rows_seq)[:-1]]).astype(np.int64)
+        dev = torch.device("cuda", torch.cuda.current_device())
+        g = torch.Generator(device=dev)
+        g.manual_seed(33 + 1000 * dist.rank)
+        self.lat8 = torch.randint(-127, 128, (self.rows, 512), generator=g, device=dev, dtype=torch.int8)
+        self.scale = torch.rand((self.rows,), generator=g, device=dev) * 0.019 + 0.001
+        self.rope = dev_bf16(torch, (self.rows, 64), 1.0, g, dev)
+        self.cfg = K.make_config(2048, 16, 128, 64, 128, 512, 1e-5, 50000.0)
+        self.wt, self.w = device_weights(torch, K, self.cfg, g, dev)
+        self.n = len(self.lens)
+        self.x = dev_bf16(torch, (self.n, 2048), 1.0, g, dev).float()
+        self.out = torch.empty((self.n, 2048), dtype=torch.float32, device=dev)
+        self.plan = K.AttendPlan(rows_seq, row0, 16, 512)
+        self.d_row = torch.from_numpy(row0 + np.array(self.lens, np.int64)).to(dev)
+        self.d_pos = torch.tensor(self.lens, dtype=torch.int32, device=dev)
+        nbytes = lib.kvl_mla_decode_step_workspace_bytes(C.byref(self.cfg), self.n)
+        self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        self.units = self.rows * 644
+
+    def step_profiled(self):
+        s = self.torch.cuda.current_stream().cuda_stream
+        rc = self.lib.kvl_mla_decode_step_q8(
+            C.byref(self.cfg), C.byref(self.w), self.plan.h, self.out.data_ptr(), self.x.data_ptr(),
+            self.lat8.data_ptr(), self.scale.data_ptr(), self.rope.data_ptr(), self.rows, self.d_row.data_ptr(),
+            self.d_pos.data_ptr(), self.n, self.ws.data_ptr(), s)
+        if rc != 0:
+            raise RuntimeError(self.K.last_error())
+
+    def step(self):
+        """The step's launches captured once as a CUDA graph, replayed per step
+        (each replay appends at the same rows, as a re-run of the same token)."""
+        replay_as_graph(self.torch, self, self.step_profiled, "decode_q8_step")
+
+    def value(self, ms):
+        return self.total_bytes / (ms * 1e-3) / 1e9
+
+    def config(self):
+        return {"workload": "config 3 as a full Q8 decode step (one layer), 64 seqs", "lens_sum": int(sum(self.lens)),
+                "bytes_per_token": 644, "weights": "bf16 ~N(0,0.02), read once per step (27.5 MB, not counted)",
+                "launch": ("the step captured once as a CUDA graph, replayed per step"
+                           if getattr(self, "_graph", None) else "launched per step"),
+                "parallelism": f"sequence-sharded x{self.dist.world}"}
 
 
 class DecodeLong:
@@ -875,8 +1044,8 @@ def dropin_decode_line(K, lib, steps, warmup, cpu=True, lens=(1024, 8192)):
     return res
 
 
-WORKLOADS = {"prefill": Prefill, "decode_q8": DecodeQ8, "decode_long": DecodeLong, "decode_stack": DecodeStack,
-             "decode_parity": DecodeParity}
+WORKLOADS = {"prefill": Prefill, "decode_q8": DecodeQ8, "decode_q8_step": DecodeQ8Step, "decode_long": DecodeLong,
+             "decode_stack": DecodeStack, "decode_parity": DecodeParity}
 
 
 def measure(torch, K, lib, dist, wl, steps, warmup, flush, peaks):
@@ -956,8 +1125,8 @@ def main():
     roof, dom = roofline_for(wl, prof, peaks, peak_kind)
     line = {
         "metric": wl.metric, "value": wl.value(ms), "unit": wl.unit, "n_gpus": dist.world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak"
-        if wl.name == "prefill" else "strong", "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"),
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": getattr(wl, "scaling", "strong"), "vs_baseline": None, "dtype": getattr(wl, "dtype", "bf16"),
         "data": "synthetic (seeded)",
         "config": wl.config(), "launch": wl.launch() if hasattr(wl, "launch") else None,
         "roofline": roof, "gpu_launches": int(launches) * args.steps,
@@ -967,10 +1136,16 @@ def main():
         line["e2e"] = wl.e2e(max(2, args.steps // 2), 1)
     if not args.no_extras and args.workload == "prefill":
         extras = {}
-        for name in ("decode_parity", "decode_q8", "decode_long", "decode_stack"):
+        names = ("decode_parity", "decode_q8", "decode_q8_step", "decode_long", "decode_stack")
+        if dist.world > 1:  # beside the context-parallel headline: one independent prompt per GPU
+            names = ("prefill_independent",) + names
+        for name in names:
             w2, err = None, None
             try:
-                w2 = WORKLOADS[name](torch, K, lib, dist)
+                if name == "prefill_independent":
+                    w2 = Prefill(torch, K, lib, dist, mode="independent")
+                else:
+                    w2 = WORKLOADS[name](torch, K, lib, dist)
             except Exception as e:  # noqa: BLE001 - report, keep the headline
                 err = str(e)
             # every rank takes the same collective steps: skip on all ranks if any failed to set up
@@ -983,7 +1158,9 @@ def main():
             r2, _ = roofline_for(w2, prof2, peaks, peak_kind)
             extras[name] = {"metric": w2.metric, "value": w2.value(ms2), "unit": w2.unit, "ms_per_step": ms2,
                             "dtype": getattr(w2, "dtype", "bf16"),
-                            "frac_of_hbm": w2.value(ms2) / peaks["hbm_gbs"], "roofline": r2,
+                            "frac_of_peak": w2.value(ms2) / (peaks["hbm_gbs"] if w2.unit == "GB/s" else
+                                                             peaks["bf16_tflops"] * dist.world),
+                            "roofline": r2,
                             "config": w2.config(), "gpu_launches_per_step": int(l2),
                             "kernels": {k: {"ms_total": v[0], "launches": v[1]} for k, v in prof2.items()}}
             if dist.rank == 0 and dist.world == 1 and not args.no_cpu:

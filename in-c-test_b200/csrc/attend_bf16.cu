@@ -21,8 +21,9 @@
 // Roles (256 threads, one CTA per SM):
 //   warp 0      TMA producer
 //   warp 1      TMEM owner and tcgen05 issuer
-//   warps 4-7   query load per segment (fp32 -> bf16 SW128 tile), softmax and
-//               epilogue (TMEM subpartitions 0-3; thread = KV row)
+//   warp 2      query loader: one bulk copy per segment of the bf16 query tile
+//               that qprep_bf16_kernel writes before the attend
+//   warps 4-7   softmax and epilogue (TMEM subpartitions 0-3; thread = KV row)
 #include "attend_common.cuh"
 #include "prof.cuh"
 #include "sm100.cuh"
@@ -47,10 +48,10 @@ constexpr uint32_t OFF_BAR = OFF_P + 2 * kPBytes;
 struct Bars {
   uint64_t lat_full[kLatSlots], lat_empty[kLatSlots];
   uint64_t rope_full[kRopeSlots], rope_empty[kRopeSlots];
-  uint64_t q_full;
+  uint64_t q0_full, q_full, q_empty;
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full[2], p_empty[2];
-  uint64_t o_full, o_empty, drain;
+  uint64_t o_full[2], o_empty[2], drain;
   uint32_t tmem_base;
   int abort;
   float red[4][kHeads];
@@ -60,8 +61,16 @@ constexpr uint32_t kSmemBytes = OFF_BAR + sizeof(Bars) + 1024;  // + alignment s
 static_assert(OFF_ROPE % 1024 == 0 && OFF_Q % 1024 == 0 && OFF_P % 1024 == 0 && OFF_BAR % 8 == 0, "align");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
-constexpr uint32_t kTmemCols = 128;  // S: 2 buffers x 16 columns; O: 4 chunks x 16 columns
+// S: 2 buffers x 16 columns @0; O: kOBufs buffers (by segment index) x 4
+// chunks x 16 columns @32.  Two O buffers let a segment's first P.V skip the
+// wait for the previous segment's epilogue, but the 256-column allocation they
+// need measured 2 us slower on the single-sequence long decode (60.4 against
+// 58.4 us at L = 131072) for 1 % on batched decode, so one buffer it is.
+constexpr uint32_t kOBufs = 1;  // O accumulators (by segment index mod kOBufs)
+constexpr uint32_t kTmemCols = kOBufs == 2 ? 256 : 128;
 constexpr uint32_t kColO = 32;
+constexpr uint32_t kOCols = 64;
+constexpr int kLoaderWarp = 2;  // bulk-loads each segment's query image
 constexpr uint32_t kThreads = 256;
 
 }  // namespace bf16dec
@@ -90,9 +99,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&B->p_full[i], 4);
       mbar_init(&B->p_empty[i], 1);
     }
-    mbar_init(&B->q_full, 4);
-    mbar_init(&B->o_full, 1);
-    mbar_init(&B->o_empty, 4);
+    mbar_init(&B->q0_full, 4);  // the softmax warps write the first segment's query
+    mbar_init(&B->q_full, 1);   // the loader's expect-tx arrival (later segments)
+    mbar_init(&B->q_empty, 1);  // the issuer's commit after the segment's last scores
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&B->o_full[i], 1);
+      mbar_init(&B->o_empty[i], 4);
+    }
     mbar_init(&B->drain, 1);
     B->abort = 0;
     fence_barrier_init();
@@ -117,7 +130,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int si = seg_lo; si < seg_hi && ok; ++si) {
         const AttendSegment sg = p.segs[si];
-        const long long row0 = p.seq_row0[sg.seq] + sg.tok_begin;
+        const long long row0 = sg.row0 + sg.tok_begin;
         const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
         for (int t = 0; t < nt && ok; ++t, ++g) {
           const int32_t y = static_cast<int32_t>(row0 + static_cast<long long>(kTileTok) * t);
@@ -163,10 +176,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g = 0;
       int seg_i = 0;
       bool ok = true;
+      AttendSegment nx = p.segs[seg_lo];  // descriptors are read one segment ahead
       for (int si = seg_lo; si < seg_hi && ok; ++si, ++seg_i) {
-        const AttendSegment sg = p.segs[si];
+        const AttendSegment sg = nx;
+        if (si + 1 < seg_hi) nx = p.segs[si + 1];
         const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
-        ok = mbar_wait(&B->q_full, seg_i & 1, abort, p.err, ERR_TIMEOUT_FULL);
+        const uint32_t ob = seg_i % kOBufs;  // this segment's O buffer
+        ok = seg_i == 0 ? mbar_wait(&B->q0_full, 0, abort, p.err, ERR_TIMEOUT_FULL)
+                        : mbar_wait(&B->q_full, (seg_i - 1) & 1, abort, p.err, ERR_TIMEOUT_FULL);
         const uint32_t q_addr = s_base + OFF_Q;
         for (int t = 0; t < nt && ok; ++t, ++g) {
           // ---- scores S^T(g) = KV(g) . Q^T
@@ -197,10 +214,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           mma_commit(&B->s_full[sb]);
           mma_commit(&B->rope_empty[rs]);
+          // the query tile is free once the segment's last scores are done
+          if (t + 1 == nt) mma_commit(&B->q_empty);
           // ---- O^T += latent(g)^T . P^T(g), slot by slot
           const bool first = (t == 0);
           ok = mbar_wait(&B->p_full[sb], (g >> 1) & 1, abort, p.err, ERR_TIMEOUT_FULL);
-          if (ok && first && seg_i > 0) ok = mbar_wait(&B->o_empty, (seg_i - 1) & 1, abort, p.err, ERR_TIMEOUT_FULL);
+          // O buffer ob was last read by the epilogue of segment seg_i - kOBufs
+          if (ok && first && seg_i >= static_cast<int>(kOBufs))
+            ok = mbar_wait(&B->o_empty[ob], (seg_i / kOBufs - 1) & 1, abort, p.err, ERR_TIMEOUT_FULL);
           if (!ok) break;
           tc_fence_after();
           const uint32_t p_addr = s_base + OFF_P + sb * kPBytes;
@@ -210,18 +231,41 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t slot = s_base + OFF_LAT + (li % kLatSlots) * kLatSlotBytes;
 #pragma unroll
             for (int kk = 0; kk < kTileTok / 16; ++kk)
-              mma_f16_ss(tmem + kColO + 16 * c, smem_desc(slot + kk * 2048, kBox, 1024, LAYOUT_SW128),
+              mma_f16_ss(tmem + kColO + kOCols * ob + 16 * c, smem_desc(slot + kk * 2048, kBox, 1024, LAYOUT_SW128),
                          smem_desc(p_addr + kk * 256, 128, kPChunkSbo, LAYOUT_INTERLEAVE), idesc_pv,
                          (first && kk == 0) ? 0u : 1u);
             mma_commit(&B->lat_empty[li % kLatSlots]);
           }
           mma_commit(&B->p_empty[sb]);
         }
-        if (ok) mma_commit(&B->o_full);
+        if (ok) mma_commit(&B->o_full[ob]);
       }
       // All issued tensor-core work must finish before TMEM is released.
       mma_commit(&B->drain);
       drain_wait(&B->drain, 0, p.err);
+    }
+  } else if (warp == kLoaderWarp) {
+    // ------------------------------------------------------------ query loader
+    // From the CTA's second segment on: one bulk copy of the segment's query
+    // image (prepared by qprep_bf16_kernel, this grid's programmatic
+    // predecessor, launched when some CTA has more than one segment) once the
+    // previous segment's last score MMAs are done.  The first segment's query
+    // is converted by the softmax warps themselves, so no CTA waits for the
+    // prep kernel at its start.
+    if (lane == 0) {
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int si = seg_lo + 1, seg_i = 1; si < seg_hi; ++si, ++seg_i) {
+        const int seq = p.segs[si].seq;
+        ok = mbar_wait(&B->q_empty, (seg_i - 1) & 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+        if (!ok) break;
+        if (seg_i == 1) asm volatile("griddepcontrol.wait;" ::: "memory");
+        mbar_arrive_expect_tx(&B->q_full, kQImgBf16Bytes);
+        bulk_load(smem + OFF_Q, p.qimg + static_cast<size_t>(seq) * kQImgStride, kQImgBf16Bytes, &B->q_full);
+        ++issued;
+      }
+      // the last copy must land before the CTA exits
+      if (!ok && issued > 0) drain_wait(&B->q_full, (issued - 1) & 1, p.err);
     }
   } else if (warp >= 4) {
     // ------------------------------------------------------------ softmax + epilogue
@@ -230,15 +274,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t lane_base = static_cast<uint32_t>(32 * w) << 16;
     uint32_t g = 0;
     int seg_i = 0;
+    AttendSegment nx = p.segs[seg_lo];  // descriptors are read one segment ahead
     for (int si = seg_lo; si < seg_hi; ++si, ++seg_i) {
-      const AttendSegment sg = p.segs[si];
+      const AttendSegment sg = nx;
+      if (si + 1 < seg_hi) nx = p.segs[si + 1];
       const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
-      // The query tile is free here: every score MMA of the previous segment
-      // has completed (its scores were read above).
-      load_query_tile(smem + OFF_Q, p.q + static_cast<size_t>(sg.seq) * kHeads * kRow, tt);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&B->q_full);
+      const uint32_t ob = seg_i % kOBufs;  // this segment's O buffer
+      const uint32_t col_o = tmem + kColO + kOCols * ob;
+      if (seg_i == 0) {
+        load_query_tile(smem + OFF_Q, p.q + static_cast<size_t>(sg.seq) * kHeads * kRow, tt);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&B->q0_full);
+      }
       float m_ref[kHeads], l_part[kHeads];
 #pragma unroll
       for (int h = 0; h < kHeads; ++h) { m_ref[h] = -INFINITY; l_part[h] = 0.f; }
@@ -292,11 +340,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               float o[kHeads];
-              tmem_ld16(tmem + kColO + 16 * c + lane_base, o);
+              tmem_ld16(col_o + 16 * c + lane_base, o);
               tmem_wait_ld();
 #pragma unroll
               for (int h = 0; h < kHeads; ++h) o[h] *= alpha[h];
-              tmem_st16(tmem + kColO + 16 * c + lane_base, o);
+              tmem_st16(col_o + 16 * c + lane_base, o);
             }
             tmem_wait_st();
           }
@@ -339,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (bad) break;
       // ---- epilogue: O / l, lse
-      bad = !mbar_wait(&B->o_full, seg_i & 1, abort, p.err, ERR_TIMEOUT_MMA);
+      bad = !mbar_wait(&B->o_full[ob], (seg_i / kOBufs) & 1, abort, p.err, ERR_TIMEOUT_MMA);
       if (named_bar_or(1, 128, bad)) break;
       tc_fence_after();
       float lt[kHeads];
@@ -362,7 +410,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         float o[kHeads];
-        tmem_ld16(tmem + kColO + 16 * c + lane_base, o);
+        tmem_ld16(col_o + 16 * c + lane_base, o);
         tmem_wait_ld();
         const int d = 128 * c + 32 * w + lane;
 #pragma unroll
@@ -370,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&B->o_empty);
+      if (lane == 0) mbar_arrive(&B->o_empty[ob]);
       if (w == 0 && lane < kHeads) {
         float m = 0.f, l = 1.f;
 #pragma unroll
@@ -392,24 +440,48 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// Host launcher.
-cudaError_t launch_attend_bf16(const AttendParams &p, int grid, cudaStream_t stream) {
+// The query images of a launch: block b converts sequence b's absorbed query
+// ([16][576] fp32) into the bf16 SW128 tile the score MMAs read (128 threads).
+// The attend grid is its programmatic dependent and may start at once; only
+// the attend's loader waits for this grid.
+__global__ void __launch_bounds__(128) qprep_bf16_kernel(const float *q, uint8_t *img) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  load_query_tile(img + static_cast<size_t>(blockIdx.x) * kQImgStride,
+                  q + static_cast<size_t>(blockIdx.x) * kHeads * kRow, threadIdx.x);
+}
+
+static cudaError_t attend_bf16_launches(const AttendParams &p, int grid, int batch, bool qprep, cudaStream_t stream,
+                                        bool profiled) {
   static std::atomic<unsigned long long> opted{0};
   cudaError_t e = smem_opt_in(reinterpret_cast<const void *>(mla_attend_bf16_kernel), kSmemBytes, opted);
   if (e != cudaSuccess) return e;
-  ProfScope ps("mla_attend_bf16", stream);
+  if (qprep) {
+    ProfScope ps(profiled ? "qprep_bf16" : nullptr, stream);
+    qprep_bf16_kernel<<<batch, 128, 0, stream>>>(p.q, const_cast<uint8_t *>(p.qimg));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  ProfScope ps(profiled ? "mla_attend_bf16" : nullptr, stream);
+  // A programmatic dependent of the prep kernel only (its loader waits for the
+  // images); otherwise an ordinary launch, so every input the kernel reads
+  // directly was complete before it started.
+  if (qprep)
+    return launch_pdl(reinterpret_cast<const void *>(mla_attend_bf16_kernel), grid, kThreads, kSmemBytes, stream, p);
   mla_attend_bf16_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError();
 }
 
-// Same launch without the optional per-kernel timing, whose CUDA events are
+// Host launcher: the query prep for `batch` sequences (only when some CTA of
+// the plan has more than one segment: `qprep`), then the attend grid.
+cudaError_t launch_attend_bf16(const AttendParams &p, int grid, int batch, bool qprep, cudaStream_t stream) {
+  return attend_bf16_launches(p, grid, batch, qprep, stream, true);
+}
+
+// Same launches without the optional per-kernel timing, whose CUDA events are
 // created on demand: used by the entry point that must not allocate.
-cudaError_t launch_attend_bf16_unprofiled(const AttendParams &p, int grid, cudaStream_t stream) {
-  cudaError_t e = cudaFuncSetAttribute(mla_attend_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       kSmemBytes);
-  if (e != cudaSuccess) return e;
-  mla_attend_bf16_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
-  return cudaGetLastError();
+cudaError_t launch_attend_bf16_unprofiled(const AttendParams &p, int grid, int batch, bool qprep,
+                                         cudaStream_t stream) {
+  return attend_bf16_launches(p, grid, batch, qprep, stream, false);
 }
 
 }  // namespace kvl

@@ -9,7 +9,7 @@
 // with all heads sharing one 576-wide cached row (512 latent + 64 rope).
 //
 // Work decomposition ("stream-K" over KV tiles): the KV rows of every sequence
-// are cut into tiles of 64 rows; the concatenated tile list of the whole batch
+// are cut into tiles of 128 rows; the concatenated tile list of the whole batch
 // is split into equal contiguous ranges, one per CTA.  A CTA's range is a list
 // of segments (one sequence each).  A segment that covers a whole sequence
 // writes the normalised output directly; a piece of a split sequence writes a
@@ -17,6 +17,7 @@
 #pragma once
 #include <cstdint>
 #include <cuda.h>
+#include <cuda_runtime.h>
 #ifdef __CUDACC__
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
@@ -38,7 +39,21 @@ struct AttendSegment {
   int tok_begin;  // first KV row of the segment (tile aligned within the sequence)
   int tok_end;    // one past the last KV row
   int slot;       // partial slot, or -1 when the segment is the whole sequence
+  long long row0; // pool row of the sequence's row 0 (so no role reads seq_row0 at a boundary)
 };
+
+// Query images.  Before the attend, a small kernel writes the absorbed query of
+// every sequence in exactly the shared-memory layout the kernel's MMAs read;
+// a loader warp then brings a segment's query in with one bulk copy instead of
+// the softmax warps converting it at every segment start.
+//   bf16 kernel: nine SW128 boxes of 16 heads x 64 dims bf16 (18432 B)
+//   Q8 kernel:   int8 hi/lo parts [32][512] as four SW128 boxes (16384 B),
+//                q_rope [16][64] bf16 as one SW128 box (2048 B), then the
+//                per-head scale sq [16] fp32 (64 B)
+constexpr uint32_t kQImgBf16Bytes = 9 * 2048;
+constexpr uint32_t kQImgQ8Bytes = 4 * 4096 + 2048 + 64;
+constexpr uint32_t kQImgStride = 18688;  // per sequence, a multiple of 256
+static_assert(kQImgBf16Bytes <= kQImgStride && kQImgQ8Bytes <= kQImgStride, "query image stride");
 
 struct AttendParams {
   CUtensorMap tm_kv;         // bf16 layout: [rows][576] (latent | rope)
@@ -53,6 +68,7 @@ struct AttendParams {
   const AttendSegment *segs;
   const int *cta_seg;        // [grid + 1] segment ranges per CTA
   const long long *seq_row0; // [B] first pool row of each sequence
+  const uint8_t *qimg;       // [B][kQImgStride] query images (written by the prep kernel)
   long long rows;            // rows in the pool
   float scale_log2;          // softmax scale * log2(e)
   uint32_t *err;             // error word (bit-or of kvl::ERR_*)
@@ -95,5 +111,25 @@ __device__ __forceinline__ void load_query_tile(uint8_t *qd, const float *qs, in
   }
 }
 #endif
+
+// Launches fn(p) -- a kernel taking one parameter struct -- as a programmatic
+// dependent of the previous kernel on `stream`: it may start while that kernel
+// drains, and must order its reads of that kernel's results with
+// griddepcontrol.wait.
+template <typename P>
+inline cudaError_t launch_pdl(const void *fn, int grid, int threads, uint32_t smem, cudaStream_t stream, const P &p) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(threads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void *args[] = {const_cast<P *>(&p)};
+  return cudaLaunchKernelExC(&cfg, fn, args);
+}
 
 }  // namespace kvl

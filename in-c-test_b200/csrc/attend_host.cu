@@ -18,8 +18,8 @@
 
 namespace kvl {
 
-cudaError_t launch_attend_bf16(const AttendParams &p, int grid, cudaStream_t stream);
-cudaError_t launch_attend_q8(const AttendParams &p, int grid, cudaStream_t stream);
+cudaError_t launch_attend_bf16(const AttendParams &p, int grid, int batch, bool qprep, cudaStream_t stream);
+cudaError_t launch_attend_q8(const AttendParams &p, int grid, int batch, bool qprep, cudaStream_t stream);
 
 // ------------------------------------------------------------------ TMA maps
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -92,6 +92,7 @@ int build_attend_plan(HostPlan &hp, int batch, const int *seq_len, const long lo
       const long long take = std::min(remaining, tiles[b] - ob);
       AttendSegment s;
       s.seq = b;
+      s.row0 = seq_row0[b];
       s.tok_begin = static_cast<int>(ob * kTileTok);
       s.tok_end = static_cast<int>(std::min<long long>((ob + take) * kTileTok, seq_len[b]));
       const bool whole = (ob == 0 && take == tiles[b]);
@@ -431,7 +432,9 @@ int DevicePlan::upload(const HostPlan &hp, int nh, int R, cudaStream_t stream, v
     if (cudaMalloc(&d_meta, need) != cudaSuccess) { meta_bytes = 0; return -1; }
     meta_bytes = need;
   }
-  const size_t wneed = (size_t)std::max(hp.nparts, 1) * nh * (R + 1) * sizeof(float);
+  // partial outputs and lse values, then the query images (256-byte aligned)
+  const size_t part_bytes = ((size_t)std::max(hp.nparts, 1) * nh * (R + 1) * sizeof(float) + 255) & ~size_t(255);
+  const size_t wneed = part_bytes + (size_t)hp.batch * kQImgStride;
   if (wneed > work_bytes) {
     cudaFree(d_work);
     d_work = nullptr;
@@ -455,6 +458,7 @@ int DevicePlan::upload(const HostPlan &hp, int nh, int R, cudaStream_t stream, v
   if (stage == tmp.data()) cudaStreamSynchronize(stream);  // pageable staging must outlive the copy
   part_o = static_cast<float *>(d_work);
   part_lse = part_o + (size_t)std::max(hp.nparts, 1) * nh * R;
+  qimg = static_cast<uint8_t *>(d_work) + part_bytes;
   return 0;
 }
 
@@ -496,13 +500,18 @@ int DevicePlan::launch(const AttendLaunch &a, cudaStream_t stream) const {
   p.lse = a.lse;
   p.part_o = part_o;
   p.part_lse = part_lse;
+  p.qimg = qimg;
   p.segs = reinterpret_cast<const AttendSegment *>(m + off_segs);
   p.cta_seg = reinterpret_cast<const int *>(m + off_cta);
   p.seq_row0 = reinterpret_cast<const long long *>(m + off_row0);
   p.rows = a.rows;
   p.scale_log2 = scale_log2;
   p.err = reinterpret_cast<uint32_t *>(const_cast<uint8_t *>(m + off_err));
-  cudaError_t e = a.q8 ? launch_attend_q8(p, host.grid, stream) : launch_attend_bf16(p, host.grid, stream);
+  // query images are read only from a CTA's second segment on
+  bool multi = false;
+  for (int c = 0; c < host.grid && !multi; ++c) multi = host.cta_seg[c + 1] - host.cta_seg[c] > 1;
+  cudaError_t e = a.q8 ? launch_attend_q8(p, host.grid, host.batch, multi, stream)
+                       : launch_attend_bf16(p, host.grid, host.batch, multi, stream);
   if (e != cudaSuccess) return -1;
   if (!host.merges.empty() && !a.skip_merge) {
     e = launch_merge(a.out, a.lse, part_o, part_lse, reinterpret_cast<const MergeEntry *>(m + off_merge),

@@ -61,6 +61,7 @@ struct DevicePlan {
   size_t off_segs = 0, off_cta = 0, off_row0 = 0, off_merge = 0, off_len = 0, off_err = 0;
   float *part_o = nullptr;
   float *part_lse = nullptr;
+  uint8_t *qimg = nullptr;  // [batch][kQImgStride] query images
 
   int upload(const HostPlan &hp, int nh, int R, cudaStream_t stream, void *pinned, size_t pinned_bytes);
   int launch(const AttendLaunch &a, cudaStream_t stream) const;

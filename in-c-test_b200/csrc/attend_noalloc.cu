@@ -1,7 +1,8 @@
 // attend_noalloc.cu -- kvl_mla_attend_bf16_noalloc: the single-sequence
 // split-KV decode attend (the tcgen05 kernel of attend_bf16.cu plus the
 // partial merge) with every byte of its scratch -- the work plan, the
-// per-range partial outputs and the device error word -- in a file-scope
+// per-range partial outputs, the query image and the device error word -- in a
+// file-scope
 // device array instead of memory allocated at call time.
 //
 // It exists for callers that cannot allocate device memory when they decode:
@@ -39,7 +40,8 @@
 
 namespace kvl {
 
-cudaError_t launch_attend_bf16_unprofiled(const AttendParams &p, int grid, cudaStream_t stream);
+cudaError_t launch_attend_bf16_unprofiled(const AttendParams &p, int grid, int batch, bool qprep,
+                                         cudaStream_t stream);
 cudaError_t launch_merge_unprofiled(float *out, float *lse, const float *part_o, const float *part_lse,
                                    const MergeEntry *d_entries, int n_entries, int nh, int R,
                                    cudaStream_t stream, int max_count);
@@ -60,7 +62,7 @@ struct NoAllocPlan {
 constexpr size_t kPlanBytes = (sizeof(NoAllocPlan) + 255) & ~size_t(255);
 constexpr size_t kPartOBytes = size_t(kNoAllocMaxSplits) * kHeads * kLatent * sizeof(float);
 constexpr size_t kPartLseBytes = (size_t(kNoAllocMaxSplits) * kHeads * sizeof(float) + 255) & ~size_t(255);
-constexpr size_t kScratchBytes = kPlanBytes + kPartOBytes + kPartLseBytes;
+constexpr size_t kScratchBytes = kPlanBytes + kPartOBytes + kPartLseBytes + kQImgStride;
 
 }  // namespace
 
@@ -101,6 +103,7 @@ __global__ void noalloc_plan_kernel(NoAllocPlan *plan, int seq_len, long long ro
     const long long lo = tiles * c / splits, hi = tiles * (c + 1) / splits;
     AttendSegment s;
     s.seq = 0;
+    s.row0 = row0;
     s.tok_begin = static_cast<int>(lo * kTileTok);
     s.tok_end = static_cast<int>(hi * kTileTok < seq_len ? hi * kTileTok : seq_len);
     s.slot = splits > 1 ? c : -1;
@@ -170,6 +173,7 @@ KVL_EXPORT int kvl_mla_attend_bf16_noalloc(float *d_out, float *d_lse, const flo
   NoAllocPlan *plan = reinterpret_cast<NoAllocPlan *>(scratch);
   float *part_o = reinterpret_cast<float *>(scratch + kPlanBytes);
   float *part_lse = reinterpret_cast<float *>(scratch + kPlanBytes + kPartOBytes);
+  uint8_t *qimg = scratch + kPlanBytes + kPartOBytes + kPartLseBytes;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   AttendParams p;
@@ -184,6 +188,7 @@ KVL_EXPORT int kvl_mla_attend_bf16_noalloc(float *d_out, float *d_lse, const flo
   p.lse = d_lse;
   p.part_o = part_o;
   p.part_lse = part_lse;
+  p.qimg = qimg;
   p.segs = plan->segs;
   p.cta_seg = plan->cta_seg;
   p.seq_row0 = &plan->row0;
@@ -193,7 +198,8 @@ KVL_EXPORT int kvl_mla_attend_bf16_noalloc(float *d_out, float *d_lse, const flo
 
   noalloc_plan_kernel<<<1, 160, 0, st>>>(plan, seq_len, seq_row0, splits);
   cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess) e = launch_attend_bf16_unprofiled(p, splits, st);
+  // one segment per CTA: the kernel converts the query itself (no prep kernel)
+  if (e == cudaSuccess) e = launch_attend_bf16_unprofiled(p, splits, 1, false, st);
   if (e == cudaSuccess && splits > 1)
     e = launch_merge_unprofiled(d_out, d_lse, part_o, part_lse, &plan->merge, 1, kHeads, kLatent, st, splits);
   // The error word comes back on the caller's stream, behind the kernels, so

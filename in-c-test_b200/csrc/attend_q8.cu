@@ -28,13 +28,20 @@
 // Within a segment the issuer runs the scores of tile g+1 before the P.V of
 // tile g, so the tensor pipe works while the softmax of tile g runs.
 //
-// Roles (384 threads, one CTA per SM):
+// Roles (608 threads, one CTA per SM):
 //   warp 0       TMA producer
 //   warp 1       TMEM owner and tcgen05 issuer
-//   warps 4-11   two warpgroups of eight heads each: softmax, P' split, fold
+//   warps 2-17   four warpgroups of four heads each: softmax, P' split, fold
 //                of the per-tile P.V sums, epilogue (thread = KV row of the
 //                tile for the scores, = latent dim of each 128-dim chunk for
-//                the mix); warpgroup 0 also splits the query of each segment
+//                the mix).  Four heads per thread keep the per-tile softmax
+//                short enough to hide under the tile's HBM time (eight heads
+//                per thread took ~3k cycles per tile, close to the period).
+//   warp 18      query loader: one bulk copy per segment of the query image
+//                (int8 parts, bf16 q_rope and the per-head scale) that
+//                qprep_q8_kernel writes before the attend, so a segment
+//                boundary costs one copy latency instead of the softmax warps
+//                splitting the next query after their epilogue
 #include "attend_common.cuh"
 #include "prof.cuh"
 #include "sm100.cuh"
@@ -51,21 +58,22 @@ constexpr uint32_t kPBytes = 128 * 32;         // P' parts [128 KV rows][32] int
 constexpr uint32_t OFF_RING = 0;
 constexpr uint32_t OFF_QI = OFF_RING + kSlots * kBox;
 constexpr uint32_t OFF_QR = OFF_QI + kQiBytes;
-constexpr uint32_t OFF_P = OFF_QR + kQrBytes;
+constexpr uint32_t OFF_QS = OFF_QR + kQrBytes;  // sq [16] fp32, loaded with the query image
+constexpr uint32_t OFF_P = OFF_QS + 1024;
+static_assert(OFF_QS - OFF_QI + kHeads * 4 == kQImgQ8Bytes, "the query image is qi | qr | sq");
 constexpr uint32_t OFF_BAR = OFF_P + 2 * kPBytes;
 
 struct Bars {
   uint64_t full[kSlots], empty[kSlots];
-  uint64_t q_full;
+  uint64_t q0_full, q_full, q_empty;
   uint64_t s_full[2], s_empty[2];
   uint64_t p_full[2], p_empty[2];
   uint64_t o_full[2], o_empty[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
-  float qscale[kHeads];        // sq per head of the current segment
-  float red[2][4][8];          // per warpgroup: running-max / sum exchange
-  float pmax[2][2][4][8];      // per tile parity and warpgroup: max |P'| of each warp
+  float red[4][4][4];          // per warpgroup: running-max / sum exchange
+  float pmax[2][4][4][4];      // per tile parity and warpgroup: max |P'| of each warp
 };
 
 constexpr uint32_t kSmemBytes = OFF_BAR + sizeof(Bars) + 1024;
@@ -78,7 +86,13 @@ constexpr uint32_t kColS = 0;
 constexpr uint32_t kColR = 64;
 constexpr uint32_t kColO = 128;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kThreads = 384;
+// Softmax warpgroups: four groups of four heads.  A group is four
+// consecutive warps 2 + 4 wg .. 5 + 4 wg, which cover the four TMEM
+// subpartitions (warp w reads lanes 32 (w % 4) ..) in rotated order.
+constexpr int kWGs = 4;
+constexpr int kHPW = kHeads / kWGs;
+constexpr int kLoaderWarp = 2 + 4 * kWGs;  // bulk-loads each segment's query image
+constexpr uint32_t kThreads = 32 * (kLoaderWarp + 1);
 constexpr uint32_t LAYOUT_SW32 = 6;  // tcgen05 shared-memory descriptor: 32-byte swizzle
 
 // Byte offset of (row n, byte k) in an SW128 K-major box of 128-byte rows.
@@ -103,27 +117,27 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
 // One unit of the absorbed query of a sequence ([16][576] fp32) as score
 // operands: q_lat split into int8 hi (rows 0-15) and lo (rows 16-31) parts,
 // K-major over four SW128 boxes of 128 dims, and q_rope as one bf16 SW128 box.
-// Unit u (0..127) is head u / 8, latent dims 64 * (u % 8) .. +63 and rope dims
-// 8 * (u % 8) .. +7; the eight units of a head are eight consecutive lanes.
+// Unit u (0..255) is head u / 16, latent dims 32 * (u % 16) .. +31 and rope
+// dims 4 * (u % 16) .. +3; the sixteen units of a head are sixteen
+// consecutive lanes (one half-warp).
 __device__ __forceinline__ void load_query_unit(uint8_t *qi, uint8_t *qr, float *qscale, const float *q, int u) {
-  const int h = u >> 3, j = u & 7;
-  const float *src = q + h * kRow + 64 * j;
-  float4 v[16];
+  const int h = u >> 4, j = u & 15;
+  const float *src = q + h * kRow + 32 * j;
+  float4 v[8];
 #pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = *reinterpret_cast<const float4 *>(src + 4 * i);
-  const float4 r0 = *reinterpret_cast<const float4 *>(q + h * kRow + kLatent + 8 * j);
-  const float4 r1 = *reinterpret_cast<const float4 *>(q + h * kRow + kLatent + 8 * j + 4);
+  for (int i = 0; i < 8; ++i) v[i] = *reinterpret_cast<const float4 *>(src + 4 * i);
+  const float4 r0 = *reinterpret_cast<const float4 *>(q + h * kRow + kLatent + 4 * j);
   float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < 16; ++i)
+  for (int i = 0; i < 8; ++i)
     amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[i].x), fabsf(v[i].y)), fmaxf(fabsf(v[i].z), fabsf(v[i].w))));
 #pragma unroll
-  for (int off = 1; off < 8; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  for (int off = 1; off < 16; off <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
   const float inv = amax > 0.f ? 127.0f / amax : 0.f;
   if (j == 0) qscale[h] = amax / 127.0f;
-  // dims 64j + 16i .. +15: box j/2, 16-byte chunk 4 (j % 2) + i of the row
+  // dims 32j + 16i .. +15: box j/4, 16-byte chunk 2 (j % 4) + i of the row
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < 2; ++i) {
     uint32_t hw[4], lw[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -136,17 +150,21 @@ __device__ __forceinline__ void load_query_unit(uint8_t *qi, uint8_t *qr, float 
       hw[e] = pack4(h0, h1, h2, h3);
       lw[e] = pack4(l0, l1, l2, l3);
     }
-    const uint32_t k = 16u * (4u * (j & 1) + i);
-    uint8_t *box = qi + (j >> 1) * 4096;
+    const uint32_t k = 16u * (2u * (j & 3) + i);
+    uint8_t *box = qi + (j >> 2) * 4096;
     *reinterpret_cast<uint4 *>(box + sw128_byte(h, k)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
     *reinterpret_cast<uint4 *>(box + sw128_byte(16 + h, k)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
   }
-  uint4 o;
-  o.x = pack2_bf16(r0.x, r0.y);
-  o.y = pack2_bf16(r0.z, r0.w);
-  o.z = pack2_bf16(r1.x, r1.y);
-  o.w = pack2_bf16(r1.z, r1.w);
-  *reinterpret_cast<uint4 *>(qr + (h >> 3) * 1024 + (h & 7) * 128 + ((j ^ (h & 7)) << 4)) = o;
+  // rope dims 4j .. 4j + 3: bytes 8j .. 8j + 7 of head h's 128-byte row
+  *reinterpret_cast<uint2 *>(qr + (h >> 3) * 1024 + (h & 7) * 128 + (((j >> 1) ^ (h & 7)) << 4) + 8 * (j & 1)) =
+      make_uint2(pack2_bf16(r0.x, r0.y), pack2_bf16(r0.z, r0.w));
+}
+
+// 4 consecutive 32-bit TMEM columns of this thread's lane.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
 }
 
 // 8 consecutive 32-bit TMEM columns of this thread's lane.
@@ -190,13 +208,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < kSlots; ++i) { mbar_init(&B->full[i], 1); mbar_init(&B->empty[i], 1); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&B->s_full[i], 1);
-      mbar_init(&B->s_empty[i], 8);  // the eight softmax warps
-      mbar_init(&B->p_full[i], 8);
+      mbar_init(&B->s_empty[i], 4 * kWGs);  // every softmax warp
+      mbar_init(&B->p_full[i], 4 * kWGs);
       mbar_init(&B->p_empty[i], 1);
       mbar_init(&B->o_full[i], 1);
-      mbar_init(&B->o_empty[i], 8);
+      mbar_init(&B->o_empty[i], 4 * kWGs);
     }
-    mbar_init(&B->q_full, 4);  // warpgroup 0 writes the query operands
+    mbar_init(&B->q0_full, 8);                // warpgroups 0-1 split the first segment's query
+    mbar_init(&B->q_full, 1);                 // the loader's expect-tx arrival (later segments)
+    mbar_init(&B->q_empty, 1 + 4 * kWGs);     // the issuer's commit after the segment's last
+                                              // scores, and every softmax warp once it has read sq
     mbar_init(&B->drain, 1);
     B->abort = 0;
     fence_barrier_init();
@@ -222,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       for (int si = seg_lo; si < seg_hi && ok; ++si) {
         const AttendSegment sg = p.segs[si];
-        const long long row0 = p.seq_row0[sg.seq] + sg.tok_begin;
+        const long long row0 = sg.row0 + sg.tok_begin;
         const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
         for (int t = 0; t < nt && ok; ++t) {
           const int32_t y = static_cast<int32_t>(row0 + static_cast<long long>(kTileTok) * t);
@@ -256,7 +277,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_pv = idesc_s8(1, 1, 128, 32);               // int8 rows^T x P' parts, both MN-major
       const uint32_t ring = s_base + OFF_RING, qi = s_base + OFF_QI, qr = s_base + OFF_QR;
       // scores of tile gg: rope (bf16) and the four int8 chunks
-      auto issue_scores = [&](uint32_t gg) -> bool {
+      auto issue_scores = [&](uint32_t gg, bool last_of_segment) -> bool {
         const uint32_t sb = gg & 1, r0 = kBoxesPerTile * gg;
         if (!mbar_wait(&B->s_empty[sb], ((gg >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY) ||
             !mbar_wait(&B->full[r0 % kSlots], (r0 / kSlots) & 1, abort, p.err, ERR_TIMEOUT_FULL))
@@ -279,6 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                       smem_desc(qi + c * 4096 + kk * 32, 16, 1024, LAYOUT_SW128), idesc_s, (c | kk) ? 1u : 0u);
         }
         mma_commit(&B->s_full[sb]);
+        // the query operands are free once the segment's last scores are done
+        if (last_of_segment) mma_commit(&B->q_empty);
         return true;
       };
       // P'.V of tile gg into its own int32 buffer (folded by the softmax threads)
@@ -309,14 +332,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t g = 0;
       int seg_i = 0;
       bool ok = true;
+      AttendSegment nx = p.segs[seg_lo];  // descriptors are read one segment ahead
       for (int si = seg_lo; si < seg_hi && ok; ++si, ++seg_i) {
-        const AttendSegment sg = p.segs[si];
+        const AttendSegment sg = nx;
+        if (si + 1 < seg_hi) nx = p.segs[si + 1];
         const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
-        ok = mbar_wait(&B->q_full, seg_i & 1, abort, p.err, ERR_TIMEOUT_FULL) && issue_scores(g);
+        ok = (seg_i == 0 ? mbar_wait(&B->q0_full, 0, abort, p.err, ERR_TIMEOUT_FULL)
+                         : mbar_wait(&B->q_full, (seg_i - 1) & 1, abort, p.err, ERR_TIMEOUT_FULL)) &&
+             issue_scores(g, nt == 1);
         for (int t = 0; t < nt && ok; ++t, ++g) {
           // the next tile's scores go ahead of this tile's P.V (same segment:
-          // the next segment's query is written only after this one ends)
-          if (t + 1 < nt) ok = issue_scores(g + 1);
+          // the next segment's query lands only after this one's scores end)
+          if (t + 1 < nt) ok = issue_scores(g + 1, t + 2 == nt);
           if (ok) ok = issue_pv(g);
         }
       }
@@ -324,38 +351,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(&B->drain);
       drain_wait(&B->drain, 0, p.err);
     }
-  } else if (warp >= 4) {
+  } else if (warp < kLoaderWarp) {
     // ------------------------------------------------------------ softmax, fold, epilogue
-    const int wg = (warp - 4) >> 2;  // warpgroup: heads 8 wg .. 8 wg + 7
-    const int w = (warp - 4) & 3;    // TMEM subpartition = rows / dims 32 w .. 32 w + 31
+    const int wg = (warp - 2) >> 2;  // warpgroup: heads kHPW wg .. + kHPW - 1
+    const int w = warp & 3;          // TMEM subpartition = rows / dims 32 w .. 32 w + 31
     const int tt = 32 * w + lane;
-    const int hb = 8 * wg;
+    const int hb = kHPW * wg;
     const uint32_t bid = 1 + wg;     // this warpgroup's named barrier
     const uint32_t lane_base = static_cast<uint32_t>(32 * w) << 16;
     uint32_t g = 0;
     int seg_i = 0;
+    // The next segment's descriptor is read at the start of this one, and the
+    // row scales of its first tile during this one's last tile, so a segment
+    // boundary waits on no dependent global load.
+    AttendSegment nx = p.segs[seg_lo];
+    float rs_nx = nx.tok_begin + tt < nx.tok_end ? p.latent_scale[nx.row0 + nx.tok_begin + tt] : 0.f;
     for (int si = seg_lo; si < seg_hi; ++si, ++seg_i) {
-      const AttendSegment sg = p.segs[si];
-      const long long srow0 = p.seq_row0[sg.seq];
+      const AttendSegment sg = nx;
+      if (si + 1 < seg_hi) nx = p.segs[si + 1];
+      const long long srow0 = sg.row0;
       const int nt = (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
-      // row scales are read one tile ahead (global loads: their latency hides
-      // behind the previous tile)
-      float rs_next = sg.tok_begin + tt < sg.tok_end ? p.latent_scale[srow0 + sg.tok_begin + tt] : 0.f;
-      // The query operands are free here: every score MMA of the previous
-      // segment has completed (its scores were read below).
-      if (wg == 0) {
-        load_query_unit(smem + OFF_QI, smem + OFF_QR, B->qscale, p.q + static_cast<size_t>(sg.seq) * kHeads * kRow,
-                        tt);
-        fence_proxy_async_smem();
+      float rs_next = rs_nx;
+      if (seg_i == 0) {
+        // the first segment's query is split here (no wait for the prep kernel)
+        if (wg < 2) {
+          uint8_t *qi = smem + OFF_QI;
+          load_query_unit(qi, qi + kQiBytes, reinterpret_cast<float *>(smem + OFF_QS),
+                          p.q + static_cast<size_t>(sg.seq) * kHeads * kRow, 128 * wg + tt);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&B->q0_full);
+        }
+        named_bar_sync(1 + kWGs, 128 * kWGs);
+      } else {
+        // later segments: sq arrives with the query image
+        if (named_bar_or(bid, 128, !mbar_wait(&B->q_full, (seg_i - 1) & 1, abort, p.err, ERR_TIMEOUT_FULL))) break;
       }
-      named_bar_sync(3, 256);
-      if (wg == 0 && lane == 0) mbar_arrive(&B->q_full);
-      float sq[8];  // sq / 256: the scores are read as S_hi * 256 + S_lo
+      float sq[kHPW];  // sq / 256: the scores are read as S_hi * 256 + S_lo
+      const float *qs = reinterpret_cast<const float *>(smem + OFF_QS);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sq[i] = B->qscale[hb + i] * 0.00390625f;
-      float m_ref[8], l_part[8], sp_prev[8], acc[4][8];
+      for (int i = 0; i < kHPW; ++i) sq[i] = qs[hb + i] * 0.00390625f;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&B->q_empty);
+      float m_ref[kHPW], l_part[kHPW], sp_prev[kHPW], acc[4][kHPW];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < kHPW; ++i) {
         m_ref[i] = -INFINITY;
         l_part[i] = 0.f;
         sp_prev[i] = 0.f;
@@ -364,23 +404,26 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       // acc = (acc + sp * (O_hi * 256 + O_lo)) * alpha for tile gg (sp passed
       // as the P' step / 256; alpha applied when resc)
-      auto fold = [&](uint32_t gg, const float (&sp)[8], bool resc, const float (&alpha)[8]) -> bool {
+      auto fold = [&](uint32_t gg, const float (&sp)[kHPW], bool resc, const float (&alpha)[kHPW]) -> bool {
         const uint32_t ob = gg & 1;
         const bool bad = !mbar_wait(&B->o_full[ob], (gg >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
         if (named_bar_or(bid, 128, bad)) return false;
         tc_fence_after();
+        uint32_t oh[4][kHPW], ol[4][kHPW];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          uint32_t oh[8], ol[8];
           const uint32_t col = tmem + kColO + 128 * ob + 32 * c + hb + lane_base;
-          tmem_ld8(col, oh);
-          tmem_ld8(col + 16, ol);
-          tmem_wait_ld();
+          tmem_ld4(col, oh[c]);
+          tmem_ld4(col + 16, ol[c]);
+        }
+        tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[c][i] = fmaf(sp[i], join16(oh[i], ol[i]), acc[c][i]);
+        for (int c = 0; c < 4; ++c) {
+#pragma unroll
+          for (int i = 0; i < kHPW; ++i) acc[c][i] = fmaf(sp[i], join16(oh[c][i], ol[c][i]), acc[c][i]);
           if (resc)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[c][i] *= alpha[i];
+            for (int i = 0; i < kHPW; ++i) acc[c][i] *= alpha[i];
         }
         tc_fence_before();
         __syncwarp();
@@ -392,45 +435,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int tok = sg.tok_begin + kTileTok * t + tt;
         const bool valid = tok < sg.tok_end;
         const float rs = rs_next;
-        if (t + 1 < nt) rs_next = tok + kTileTok < sg.tok_end ? p.latent_scale[srow0 + tok + kTileTok] : 0.f;
+        if (t + 1 < nt)
+          rs_next = tok + kTileTok < sg.tok_end ? p.latent_scale[srow0 + tok + kTileTok] : 0.f;
+        else if (si + 1 < seg_hi)
+          rs_nx = nx.tok_begin + tt < nx.tok_end ? p.latent_scale[nx.row0 + nx.tok_begin + tt] : 0.f;
         const uint32_t sb = g & 1;
         bad = !mbar_wait(&B->s_full[sb], (g >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
         if (named_bar_or(bid, 128, bad)) { bad = true; break; }
         tc_fence_after();
-        uint32_t sh[8], sl[8], srp[8];
-        tmem_ld8(tmem + kColS + 32 * sb + hb + lane_base, sh);
-        tmem_ld8(tmem + kColS + 32 * sb + 16 + hb + lane_base, sl);
-        tmem_ld8(tmem + kColR + 16 * sb + hb + lane_base, srp);
+        uint32_t sh[kHPW], sl[kHPW], srp[kHPW];
+        tmem_ld4(tmem + kColS + 32 * sb + hb + lane_base, sh);
+        tmem_ld4(tmem + kColS + 32 * sb + 16 + hb + lane_base, sl);
+        tmem_ld4(tmem + kColR + 16 * sb + hb + lane_base, srp);
         tmem_wait_ld();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&B->s_empty[sb]);
-        float s[8];
+        float s[kHPW];
         bool need = false;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < kHPW; ++i) {
           s[i] = valid ? fmaf(rs * sq[i], join16(sh[i], sl[i]), __uint_as_float(srp[i])) * p.scale_log2 : -INFINITY;
           need |= s[i] > m_ref[i] + 8.0f;
         }
         // lazy rescale: the running maximum moves only by more than 2^8
         bool resc = false;
-        float alpha[8];
+        float alpha[kHPW];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) alpha[i] = 1.f;
+        for (int i = 0; i < kHPW; ++i) alpha[i] = 1.f;
         if (named_bar_or(bid, 128, need)) {
-          float mx[8];
+          float mx[kHPW];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) mx[i] = s[i];
+          for (int i = 0; i < kHPW; ++i) mx[i] = s[i];
 #pragma unroll
           for (int off = 16; off > 0; off >>= 1)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], off));
+            for (int i = 0; i < kHPW; ++i) mx[i] = fmaxf(mx[i], __shfl_xor_sync(0xffffffffu, mx[i], off));
           if (lane == 0)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) B->red[wg][w][i] = mx[i];
+            for (int i = 0; i < kHPW; ++i) B->red[wg][w][i] = mx[i];
           named_bar_sync(bid, 128);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
+          for (int i = 0; i < kHPW; ++i) {
             const float tm = fmaxf(fmaxf(B->red[wg][0][i], B->red[wg][1][i]), fmaxf(B->red[wg][2][i], B->red[wg][3][i]));
             const float mn = fmaxf(m_ref[i], tm);
             alpha[i] = (m_ref[i] == -INFINITY) ? 0.f : exp2f(m_ref[i] - mn);
@@ -441,30 +487,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           resc = true;
         }
         // P'_j = p_j * scale_j, split per head against the tile's max |P'|
-        float pq[8];
+        float pq[kHPW];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < kHPW; ++i) {
           const float pr = exp2f(s[i] - m_ref[i]);
           l_part[i] += pr;
           pq[i] = pr * rs;
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < kHPW; ++i) {
           const uint32_t m = warp_max_u32(__float_as_uint(fabsf(pq[i])));
           if (lane == 0) B->pmax[g & 1][wg][w][i] = __uint_as_float(m);
         }
         named_bar_sync(bid, 128);
-        float sp[8];
-        uint32_t hw[2] = {0u, 0u}, lw[2] = {0u, 0u};
+        float sp[kHPW];
+        uint32_t hw = 0u, lw = 0u;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < kHPW; ++i) {
           const float m = fmaxf(fmaxf(B->pmax[g & 1][wg][0][i], B->pmax[g & 1][wg][1][i]),
                                 fmaxf(B->pmax[g & 1][wg][2][i], B->pmax[g & 1][wg][3][i]));
           sp[i] = m * (1.0f / (127.0f * 256.0f));
           int ph, pl;
           split16(m > 0.f ? pq[i] * (127.0f * __frcp_rn(m)) : 0.f, ph, pl);
-          hw[i >> 2] |= (static_cast<uint32_t>(ph) & 0xFFu) << (8 * (i & 3));
-          lw[i >> 2] |= (static_cast<uint32_t>(pl) & 0xFFu) << (8 * (i & 3));
+          hw |= (static_cast<uint32_t>(ph) & 0xFFu) << (8 * i);
+          lw |= (static_cast<uint32_t>(pl) & 0xFFu) << (8 * i);
         }
         bad = !mbar_wait(&B->p_empty[sb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_MMA);
         if (named_bar_or(bid, 128, bad)) { bad = true; break; }
@@ -474,8 +520,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           // 16-byte halves swap in rows with bit 2 set)
           uint8_t *row = smem + OFF_P + sb * kPBytes + (tt >> 3) * 256 + (tt & 7) * 32;
           const uint32_t swz = ((tt >> 2) & 1) << 4;
-          *reinterpret_cast<uint2 *>(row + (hb ^ swz)) = make_uint2(hw[0], hw[1]);
-          *reinterpret_cast<uint2 *>(row + ((16 + hb) ^ swz)) = make_uint2(lw[0], lw[1]);
+          *reinterpret_cast<uint32_t *>(row + (hb ^ swz)) = hw;
+          *reinterpret_cast<uint32_t *>(row + ((16 + hb) ^ swz)) = lw;
         }
         fence_proxy_async_smem();
         tc_fence_before();
@@ -484,19 +530,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         // fold the previous tile's P'.V (its frame is rescaled with this tile's alpha)
         if (t > 0 && !fold(g - 1, sp_prev, resc, alpha)) { bad = true; break; }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sp_prev[i] = sp[i];
+        for (int i = 0; i < kHPW; ++i) sp_prev[i] = sp[i];
       }
       if (bad) break;
       // ---- epilogue: last tile's P'.V, then O / l and lse
       {
-        float one[8];
+        float one[kHPW];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) one[i] = 1.f;
+        for (int i = 0; i < kHPW; ++i) one[i] = 1.f;
         if (!fold(g - 1, sp_prev, false, one)) break;
       }
-      float lt[8];
+      float lt[kHPW];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
+      for (int i = 0; i < kHPW; ++i) {
         float l = l_part[i];
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
@@ -504,10 +550,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (lane == 0)
 #pragma unroll
-        for (int i = 0; i < 8; ++i) B->red[wg][w][i] = lt[i];
+        for (int i = 0; i < kHPW; ++i) B->red[wg][w][i] = lt[i];
       named_bar_sync(bid, 128);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) lt[i] = (B->red[wg][0][i] + B->red[wg][1][i]) + (B->red[wg][2][i] + B->red[wg][3][i]);
+      for (int i = 0; i < kHPW; ++i) lt[i] = (B->red[wg][0][i] + B->red[wg][1][i]) + (B->red[wg][2][i] + B->red[wg][3][i]);
       named_bar_sync(bid, 128);
       float *dst = (sg.slot < 0) ? p.out + static_cast<size_t>(sg.seq) * kHeads * kLatent
                                  : p.part_o + static_cast<size_t>(sg.slot) * kHeads * kLatent;
@@ -515,18 +561,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < 4; ++c) {
         const int d = 128 * c + tt;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) dst[(hb + i) * kLatent + d] = acc[c][i] / lt[i];
+        for (int i = 0; i < kHPW; ++i) dst[(hb + i) * kLatent + d] = acc[c][i] / lt[i];
       }
-      if (w == 0 && lane < 8) {
+      if (w == 0 && lane < kHPW) {
         float m = 0.f, l = 1.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < kHPW; ++i)
           if (i == lane) { m = m_ref[i]; l = lt[i]; }
         const float lse = (m + log2f(l)) * 0.69314718055994531f;
         float *ldst = (sg.slot < 0) ? p.lse : p.part_lse;
         const int row = (sg.slot < 0) ? sg.seq : sg.slot;
         if (ldst) ldst[row * kHeads + hb + lane] = lse;
       }
+    }
+  } else {
+    // ------------------------------------------------------------ query loader
+    // From the CTA's second segment on: one bulk copy of the segment's query
+    // image (prepared by qprep_q8_kernel, this grid's programmatic predecessor,
+    // launched when some CTA has more than one segment) once the previous
+    // segment's query is no longer read.  The first segment's query is split
+    // by the softmax warps, so no CTA waits for the prep kernel at its start.
+    if (lane == 0) {
+      uint32_t issued = 0;
+      bool ok = true;
+      for (int si = seg_lo + 1, seg_i = 1; si < seg_hi; ++si, ++seg_i) {
+        const int seq = p.segs[si].seq;
+        ok = mbar_wait(&B->q_empty, (seg_i - 1) & 1, abort, p.err, ERR_TIMEOUT_EMPTY);
+        if (!ok) break;
+        if (seg_i == 1) asm volatile("griddepcontrol.wait;" ::: "memory");
+        mbar_arrive_expect_tx(&B->q_full, kQImgQ8Bytes);
+        bulk_load(smem + OFF_QI, p.qimg + static_cast<size_t>(seq) * kQImgStride, kQImgQ8Bytes, &B->q_full);
+        ++issued;
+      }
+      // the last copy must land before the CTA exits
+      if (!ok && issued > 0) drain_wait(&B->q_full, (issued - 1) & 1, p.err);
     }
   }
 
@@ -538,11 +606,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-cudaError_t launch_attend_q8(const AttendParams &p, int grid, cudaStream_t stream) {
+// The query images of a launch: block b writes sequence b's q_lat parts, q_rope
+// and sq in the shared-memory layout of the kernel above (256 threads, one unit
+// each).  The attend grid is its programmatic dependent and may start at once;
+// only the attend's loader waits for this grid.
+__global__ void __launch_bounds__(256) qprep_q8_kernel(const float *q, uint8_t *img) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  uint8_t *base = img + static_cast<size_t>(blockIdx.x) * kQImgStride;
+  load_query_unit(base, base + kQiBytes, reinterpret_cast<float *>(base + kQiBytes + kQrBytes),
+                  q + static_cast<size_t>(blockIdx.x) * kHeads * kRow, threadIdx.x);
+}
+
+// The query prep for `batch` sequences (only when some CTA of the plan has
+// more than one segment: `qprep`), then the attend grid.
+cudaError_t launch_attend_q8(const AttendParams &p, int grid, int batch, bool qprep, cudaStream_t stream) {
   static std::atomic<unsigned long long> opted{0};
   cudaError_t e = smem_opt_in(reinterpret_cast<const void *>(mla_attend_q8_kernel), kSmemBytes, opted);
   if (e != cudaSuccess) return e;
+  if (qprep) {
+    ProfScope ps("qprep_q8", stream);
+    qprep_q8_kernel<<<batch, 256, 0, stream>>>(p.q, const_cast<uint8_t *>(p.qimg));
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
   ProfScope ps("mla_attend_q8", stream);
+  // A programmatic dependent of the prep kernel only (its loader waits for the
+  // images); otherwise an ordinary launch, so every input the kernel reads
+  // directly was complete before it started.
+  if (qprep)
+    return launch_pdl(reinterpret_cast<const void *>(mla_attend_q8_kernel), grid, kThreads, kSmemBytes, stream, p);
   mla_attend_q8_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError();
 }

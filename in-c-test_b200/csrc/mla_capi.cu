@@ -1083,6 +1083,116 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   return 0;
 }
 
+// ------------------------------------------------------------------ context-parallel prefill
+// One prompt of S rows over `world` GPUs: 2 * world chunks of c = S / (2 world)
+// rows; rank r owns chunk r (early keys) and chunk 2 world - 1 - r (late keys),
+// so every rank has the same causal attention work.  The only exchange is the
+// compressed 576-wide row of every token (latent | rotated k_rope, what the
+// reference's streaming prefill appends per token, src/mla_prefill_streaming.c:
+// 131-138): each rank projects and appends its own rows, the ranks all-gather
+// them (S x 1152 bytes in all), and each rank expands K/V with kv_b for the keys
+// its chunks see.  q_proj and o_proj stay with the rows' owner.
+struct CpChunks {
+  int c = 0;         // rows per chunk
+  int a0 = 0, b0 = 0;  // first rows of the rank's two chunks
+};
+
+bool cp_chunks(int S, int rank, int world, CpChunks &k) {
+  if (world <= 0 || rank < 0 || rank >= world || S <= 0 || S % (2 * world) != 0) return false;
+  k.c = S / (2 * world);
+  if (k.c % 128 != 0) return false;
+  k.a0 = rank * k.c;
+  k.b0 = (2 * world - 1 - rank) * k.c;
+  return true;
+}
+
+// kv_a projection of rows [r0, r0 + M) and their RMSNorm + RoPE into dst
+// [M][576] bf16; q_proj with RoPE of the same rows into the workspace q.
+int cp_project_rows(int sms, const KvlMlaConfig &cfg, const DevW &W, const uint16_t *xb, int r0, int M,
+                    uint16_t *dst, uint8_t *ws, const PrefillWs &L, cudaStream_t st) {
+  const uint64_t H = cfg.hidden_size, m = static_cast<uint64_t>(M), R0 = static_cast<uint64_t>(r0);
+  uint16_t *q = reinterpret_cast<uint16_t *>(ws + L.off[2]);
+  float *kva = reinterpret_cast<float *>(ws + L.off[3]);
+  float2 *cs = reinterpret_cast<float2 *>(ws + L.off[7]);
+  uint32_t *err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
+  const int kva_bn = (M + 127) / 128 * 3 * 2 < sms ? 64 : 192;
+  GemmParams g;
+  memset(&g, 0, sizeof g);
+  g.err = err;
+  if (!bf16_map(&g.tm_a, xb + R0 * H, H, m, H * 2, 128) || !bf16_map(&g.tm_b, W.kva, H, 576, H * 2, kva_bn)) {
+    set_err("prefill (context parallel): tensor map (kv_a_proj)");
+    return -1;
+  }
+  g.M = M;
+  g.K = static_cast<int>(H);
+  g.N = 576;
+  g.c = kva + R0 * 576;
+  g.ldc = 576;
+  CK(launch_gemm(g, kva_bn, EPI_F32, sms, st, "gemm_kva"));
+  CK(append_rows_bf16(dst, kva + R0 * 576, W.kvan, cs + R0 * 32, M, cfg.rms_eps, st));
+  GemmParams gq;
+  memset(&gq, 0, sizeof gq);
+  gq.err = err;
+  if (!bf16_map(&gq.tm_a, xb + R0 * H, H, m, H * 2, 128) || !bf16_map(&gq.tm_b, W.q, H, 16 * 192, H * 2, 128)) {
+    set_err("prefill (context parallel): tensor map (q_proj)");
+    return -1;
+  }
+  gq.M = M;
+  gq.N = 16 * 192;
+  gq.K = static_cast<int>(H);
+  gq.c = q + R0 * 16 * 192;
+  gq.ldc = 16 * 192;
+  gq.rope_cs = cs + R0 * 32;
+  CK(launch_gemm_pair(gq, 256, EPI_QROPE, sms, st, "gemm_q"));
+  return 0;
+}
+
+// Causal attention of the queries [r0, r0 + M) over the keys [0, r0 + M) and
+// o_proj of those rows (K/V of the keys already expanded in the workspace).
+int cp_attend_rows(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, int S, int r0, int M,
+                   uint8_t *ws, const PrefillWs &L, cudaStream_t st) {
+  const uint64_t H = cfg.hidden_size, s = S, m = static_cast<uint64_t>(M), R0 = static_cast<uint64_t>(r0);
+  uint16_t *q = reinterpret_cast<uint16_t *>(ws + L.off[2]);
+  uint16_t *pool = reinterpret_cast<uint16_t *>(ws + L.off[4]);
+  uint16_t *kv = reinterpret_cast<uint16_t *>(ws + L.off[5]);
+  uint16_t *o = reinterpret_cast<uint16_t *>(ws + L.off[6]);
+  uint32_t *err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
+  FlashParams f;
+  memset(&f, 0, sizeof f);
+  {
+    const uint64_t qd[3] = {192, 16, s}, qs[2] = {192 * 2, 16 * 192 * 2};
+    const uint64_t kd[3] = {256, 16, s}, ks[2] = {256 * 2, 16 * 256 * 2};
+    const uint32_t box[3] = {64, 1, 128};
+    if (!make_tmap_3d(&f.tm_q, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, qd, qs, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_3d(&f.tm_kv, kv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kd, ks, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !bf16_map(&f.tm_kr, pool, 576, s, 576 * 2, 128)) {
+      set_err("prefill (context parallel): tensor map (attention)");
+      return -1;
+    }
+  }
+  f.kr_col = 512;
+  f.S = r0 + M;
+  f.q_tile0 = r0 / 128;
+  f.scale_log2 = (1.0f / sqrtf(192.0f)) * 1.4426950408889634f;
+  f.out = reinterpret_cast<__nv_bfloat16 *>(o);
+  f.err = err;
+  CK(launch_flash_prefill(f, sms, st));
+  GemmParams g;
+  memset(&g, 0, sizeof g);
+  g.err = err;
+  if (!bf16_map(&g.tm_a, o + R0 * 2048, 2048, m, 2048 * 2, 128) || !bf16_map(&g.tm_b, W.o, 2048, H, 2048 * 2, 128)) {
+    set_err("prefill (context parallel): tensor map (o_proj)");
+    return -1;
+  }
+  g.M = M;
+  g.N = static_cast<int>(H);
+  g.K = 2048;
+  g.c = d_out + R0 * H;
+  g.ldc = static_cast<int>(H);
+  CK(launch_gemm_pair(g, 256, EPI_F32, sms, st, "gemm_o"));
+  return 0;
+}
+
 }  // namespace
 }  // namespace kvl
 
@@ -1233,6 +1343,101 @@ KVL_EXPORT int kvl_mla_prefill_dev(const KvlMlaConfig *cfg, const KvlMlaDeviceWe
   float *xf = reinterpret_cast<float *>(ws + L.off[0]);
   CK(bf16_to_f32(xf, d_x, static_cast<long long>(seq_len) * cfg->hidden_size, st));
   return prefill_absorbed(dev, sms, *cfg, W, d_out, xf, seq_len, ws, L, st);
+}
+
+// Checks shared by the two context-parallel calls; fills L, sms, the chunks.
+static int cp_setup(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, int seq_len, int rank, int world,
+                    void *d_workspace, size_t workspace_bytes, PrefillWs &L, int &sms, CpChunks &k) {
+  if (!cfg || !w || seq_len <= 0 || !d_workspace || !cfg_dims_ok(*cfg) || !fast_prefill_shape(*cfg) ||
+      !w->q_proj || !w->kv_a_proj || !w->kv_a_norm || !w->kv_b_proj || !w->o_proj) {
+    set_err("invalid context-parallel prefill arguments (production head shape required)");
+    return -1;
+  }
+  if (!cp_chunks(seq_len, rank, world, k)) {
+    set_err("context-parallel prefill: seq_len %d must split into %d chunks of a multiple of 128 rows "
+            "(rank %d of %d)", seq_len, 2 * world, rank, world);
+    return -1;
+  }
+  L = prefill_layout(*cfg, seq_len);
+  if (workspace_bytes < L.total || (reinterpret_cast<uintptr_t>(d_workspace) & 255)) {
+    set_err("context-parallel prefill: workspace too small or not 256-byte aligned (%zu < %zu)", workspace_bytes,
+            L.total);
+    return -1;
+  }
+  const int dev = current_device();
+  if (dev < 0) return -1;
+  sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return 0;
+}
+
+KVL_EXPORT int kvl_mla_prefill_cp_begin(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, const uint16_t *d_x,
+                                        int seq_len, int rank, int world, uint16_t *d_send, void *d_workspace,
+                                        size_t workspace_bytes, void *stream) {
+  PrefillWs L;
+  int sms = 0;
+  CpChunks k;
+  if (cp_setup(cfg, w, seq_len, rank, world, d_workspace, workspace_bytes, L, sms, k) != 0) return -1;
+  if (!d_x || !d_send || ((reinterpret_cast<uintptr_t>(d_x) | reinterpret_cast<uintptr_t>(d_send)) & 15)) {
+    set_err("context-parallel prefill: d_x and d_send must be 16-byte aligned device pointers");
+    return -1;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *ws = static_cast<uint8_t *>(d_workspace);
+  DevW W{w->q_proj, w->kv_a_proj, w->kv_a_norm, w->kv_b_proj, w->o_proj};
+  float2 *cs = reinterpret_cast<float2 *>(ws + L.off[7]);
+  CK(cudaMemsetAsync(ws + L.off[8], 0, 4, st));
+  CK(launch_rope_table(cs, seq_len, 64, cfg->rope_theta, st));
+  if (cp_project_rows(sms, *cfg, W, d_x, k.a0, k.c, d_send, ws, L, st) != 0) return -1;
+  return cp_project_rows(sms, *cfg, W, d_x, k.b0, k.c, d_send + static_cast<size_t>(k.c) * 576, ws, L, st);
+}
+
+KVL_EXPORT int kvl_mla_prefill_cp_end(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, float *d_out,
+                                      int seq_len, int rank, int world, const uint16_t *d_recv, void *d_workspace,
+                                      size_t workspace_bytes, void *stream) {
+  PrefillWs L;
+  int sms = 0;
+  CpChunks k;
+  if (cp_setup(cfg, w, seq_len, rank, world, d_workspace, workspace_bytes, L, sms, k) != 0) return -1;
+  if (!d_out || !d_recv || ((reinterpret_cast<uintptr_t>(d_out) | reinterpret_cast<uintptr_t>(d_recv)) & 15)) {
+    set_err("context-parallel prefill: d_out and d_recv must be 16-byte aligned device pointers");
+    return -1;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t *ws = static_cast<uint8_t *>(d_workspace);
+  DevW W{w->q_proj, w->kv_a_proj, w->kv_a_norm, w->kv_b_proj, w->o_proj};
+  uint16_t *pool = reinterpret_cast<uint16_t *>(ws + L.off[4]);
+  uint16_t *kv = reinterpret_cast<uint16_t *>(ws + L.off[5]);
+  // the keys this rank's chunks see: [0, end of its late chunk)
+  const int kmax = k.b0 + k.c;
+  const size_t row_b = 576 * 2, chunk_b = static_cast<size_t>(k.c) * row_b;
+  for (int p = 0; p < world; ++p) {
+    const uint8_t *src = reinterpret_cast<const uint8_t *>(d_recv) + 2 * static_cast<size_t>(p) * chunk_b;
+    const int pa = p * k.c, pb = (2 * world - 1 - p) * k.c;
+    if (pa < kmax)
+      CK(cudaMemcpyAsync(pool + static_cast<size_t>(pa) * 576, src, chunk_b, cudaMemcpyDeviceToDevice, st));
+    if (pb < kmax)
+      CK(cudaMemcpyAsync(pool + static_cast<size_t>(pb) * 576, src + chunk_b, chunk_b, cudaMemcpyDeviceToDevice,
+                         st));
+  }
+  // kv = latent Wkvb^T for the keys [0, kmax), bf16 [kmax][16][256]
+  GemmParams g;
+  memset(&g, 0, sizeof g);
+  g.err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
+  if (!bf16_map(&g.tm_a, pool, 512, static_cast<uint64_t>(kmax), 576 * 2, 128) ||
+      !bf16_map(&g.tm_b, W.kvb, 512, 4096, 512 * 2, 128)) {
+    set_err("prefill (context parallel): tensor map (kv_b_proj)");
+    return -1;
+  }
+  g.M = kmax;
+  g.N = 4096;
+  g.K = 512;
+  g.c = kv;
+  g.ldc = 4096;
+  CK(launch_gemm_pair(g, 256, EPI_BF16, sms, st, "gemm_kvb"));
+  // the late chunk first: its queries see the most keys
+  if (cp_attend_rows(sms, *cfg, W, d_out, seq_len, k.b0, k.c, ws, L, st) != 0) return -1;
+  return cp_attend_rows(sms, *cfg, W, d_out, seq_len, k.a0, k.c, ws, L, st);
 }
 
 // =================================================================== attend plans
@@ -1461,9 +1666,51 @@ static bool step_gemm_ok(const KvlMlaConfig &c, const KvlMlaDeviceWeights &w, co
          c.qk_rope_dim % 8 == 0 && c.kv_lora_rank % 8 == 0 && c.v_head_dim % 8 == 0;
 }
 
+// The KV pool a decode step appends to and attends over: a bf16 pool
+// [rows][R + DR], or a Q8 pool in the reference layout (int8 [rows][R], fp32
+// scale [rows], bf16 rope [rows][DR]).
+struct StepPool {
+  uint16_t *kv = nullptr;
+  int8_t *lat8 = nullptr;
+  float *lscale = nullptr;
+  uint16_t *rope16 = nullptr;
+  bool q8() const { return lat8 != nullptr; }
+};
+
+// Appends each token's row (kv_a output, or `parts` split-K partials of it) to
+// the pool at d_row[b], RoPE position d_pos[b]: bf16 rows, or the reference's
+// row quantiser for a Q8 pool (src/mla_compressed_q8_state.c:111-127).
+static cudaError_t step_append(const StepPool &pool, const KvlMlaConfig &cfg, const uint16_t *norm, const float *ka,
+                               int B, const int64_t *d_row, const int *d_pos, int parts, long long part_stride,
+                               cudaStream_t s) {
+  const int R = cfg.kv_lora_rank, DR = cfg.qk_rope_dim;
+  const long long *rows = reinterpret_cast<const long long *>(d_row);
+  if (pool.q8())
+    return append_q8(pool.lat8, pool.lscale, pool.rope16, 0, ka, norm, B, R, DR, 0, cfg.rms_eps, cfg.rope_theta, s,
+                     rows, d_pos, parts, part_stride);
+  return append_bf16(pool.kv, 0, ka, norm, B, R, DR, 0, cfg.rms_eps, cfg.rope_theta, nullptr, s, rows, d_pos, parts,
+                     part_stride);
+}
+
+// The attend of a decode step over its plan (bf16 or Q8 kernel).
+static int step_attend(const KvlMlaAttendPlan *plan, const StepPool &pool, const KvlMlaConfig &cfg, float *mix,
+                       const float *qabs, int64_t rows, cudaStream_t s) {
+  AttendLaunch a;
+  a.q8 = pool.q8();
+  a.rows = rows;
+  a.q = qabs;
+  a.out = mix;
+  a.kv = pool.kv;
+  a.lat8 = pool.lat8;
+  a.lscale = pool.lscale;
+  a.rope16 = pool.rope16;
+  a.softmax_scale = 1.0f / sqrtf(static_cast<float>(cfg.qk_nope_dim + cfg.qk_rope_dim));
+  return attend_common(plan, a, cfg.num_heads, cfg.kv_lora_rank, cfg.qk_rope_dim, s);
+}
+
 // Tensor-core projections of one decode step (batch >= kStepGemmBatch).
 static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &w, const KvlMlaAttendPlan *plan,
-                            float *d_out, const float *d_x, uint16_t *d_kv, int64_t rows, const int64_t *d_row,
+                            float *d_out, const float *d_x, const StepPool &pool, int64_t rows, const int64_t *d_row,
                             const int *d_pos, int B, uint8_t *ws, const size_t *off, cudaStream_t s) {
   const uint64_t H = cfg.hidden_size, NH = cfg.num_heads, DN = cfg.qk_nope_dim, DR = cfg.qk_rope_dim;
   const uint64_t DV = cfg.v_head_dim, R = cfg.kv_lora_rank, QD = DN + DR, b = B;
@@ -1513,9 +1760,7 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   g.c_bstride = static_cast<long long>(b * (R + DR));
   CK(launch_gemm(g, 192, EPI_F32, sms, s, "gemm_kva"));
   // the append sums the split-K partials of its row itself
-  CK(append_bf16(d_kv, 0, ka_parts, w.kv_a_norm, B, static_cast<int>(R), static_cast<int>(DR), 0, cfg.rms_eps,
-                 cfg.rope_theta, nullptr, s, reinterpret_cast<const long long *>(d_row), d_pos, g.ksplit,
-                 g.c_bstride));
+  CK(step_append(pool, cfg, w.kv_a_norm, ka_parts, B, d_row, d_pos, g.ksplit, g.c_bstride, s));
   g.ksplit = 0;
   g.c_bstride = 0;
   CK(q_split(qn, qabs, q, q_parts, static_cast<long long>(b * NH * QD), B, static_cast<int>(NH),
@@ -1539,13 +1784,7 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   g.c_bstride = static_cast<long long>(R + DR);
   CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_absorb"));
 
-  AttendLaunch a;
-  a.rows = rows;
-  a.q = qabs;
-  a.out = mix;
-  a.kv = d_kv;
-  a.softmax_scale = 1.0f / sqrtf(static_cast<float>(QD));
-  if (attend_common(plan, a, static_cast<int>(NH), static_cast<int>(R), static_cast<int>(DR), s) != 0) return -1;
+  if (step_attend(plan, pool, cfg, mix, qabs, rows, s) != 0) return -1;
 
   // ho[:, h, :] = mix[:, h] . W_UV[h]^T   (NH products, M = B, N = DV, K = R), bf16
   CK(mix_heads_bf16(mixb, mix, B, static_cast<int>(NH), static_cast<int>(R), s));
@@ -1586,6 +1825,34 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   return 0;
 }
 
+// One decode step over either pool format (the arguments are checked by the
+// entry points).
+static int decode_step(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, const KvlMlaAttendPlan *plan,
+                       float *d_out, const float *d_x, const StepPool &pool, int64_t rows, const int64_t *d_row,
+                       const int *d_pos, int batch, void *d_workspace, void *stream) {
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int H = cfg->hidden_size, NH = cfg->num_heads, DN = cfg->qk_nope_dim, DR = cfg->qk_rope_dim;
+  const int DV = cfg->v_head_dim, R = cfg->kv_lora_rank, QD = DN + DR;
+  size_t off[12];
+  step_ws_layout(*cfg, batch, off);
+  uint8_t *ws = static_cast<uint8_t *>(d_workspace);
+  if (step_gemm_ok(*cfg, *w, d_out, ws, batch))
+    return decode_step_gemm(*cfg, *w, plan, d_out, d_x, pool, rows, d_row, d_pos, batch, ws, off, s);
+  float *q = reinterpret_cast<float *>(ws + off[0]);
+  float *ka = reinterpret_cast<float *>(ws + off[1]);
+  float *qabs = reinterpret_cast<float *>(ws + off[2]);
+  float *mix = reinterpret_cast<float *>(ws + off[3]);
+  float *ho = reinterpret_cast<float *>(ws + off[4]);
+  CK(gemv_bf16(q, d_x, w->q_proj, H, NH * QD, batch, s));
+  CK(gemv_bf16(ka, d_x, w->kv_a_proj, H, R + DR, batch, s));
+  CK(step_append(pool, *cfg, w->kv_a_norm, ka, batch, d_row, d_pos, 1, 0, s));
+  CK(absorb(qabs, q, w->kv_b_proj, batch, NH, DN, DV, DR, R, 0, cfg->rope_theta, s, d_pos));
+  if (step_attend(plan, pool, *cfg, mix, qabs, rows, s) != 0) return -1;
+  CK(vup(ho, mix, w->kv_b_proj, batch, NH, DN, DV, R, s));
+  CK(gemv_bf16(d_out, ho, w->o_proj, NH * DV, H, batch, s));
+  return 0;
+}
+
 KVL_EXPORT int kvl_mla_decode_step_bf16(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w,
                                         const KvlMlaAttendPlan *plan, float *d_out, const float *d_x, uint16_t *d_kv,
                                         int64_t rows, const int64_t *d_row, const int *d_pos, int batch,
@@ -1595,34 +1862,28 @@ KVL_EXPORT int kvl_mla_decode_step_bf16(const KvlMlaConfig *cfg, const KvlMlaDev
     set_err("invalid decode step arguments");
     return -1;
   }
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int H = cfg->hidden_size, NH = cfg->num_heads, DN = cfg->qk_nope_dim, DR = cfg->qk_rope_dim;
-  const int DV = cfg->v_head_dim, R = cfg->kv_lora_rank, QD = DN + DR;
-  size_t off[12];
-  step_ws_layout(*cfg, batch, off);
-  uint8_t *ws = static_cast<uint8_t *>(d_workspace);
-  if (step_gemm_ok(*cfg, *w, d_out, ws, batch))
-    return decode_step_gemm(*cfg, *w, plan, d_out, d_x, d_kv, rows, d_row, d_pos, batch, ws, off, s);
-  float *q = reinterpret_cast<float *>(ws + off[0]);
-  float *ka = reinterpret_cast<float *>(ws + off[1]);
-  float *qabs = reinterpret_cast<float *>(ws + off[2]);
-  float *mix = reinterpret_cast<float *>(ws + off[3]);
-  float *ho = reinterpret_cast<float *>(ws + off[4]);
-  CK(gemv_bf16(q, d_x, w->q_proj, H, NH * QD, batch, s));
-  CK(gemv_bf16(ka, d_x, w->kv_a_proj, H, R + DR, batch, s));
-  CK(append_bf16(d_kv, 0, ka, w->kv_a_norm, batch, R, DR, 0, cfg->rms_eps, cfg->rope_theta, nullptr, s,
-                 reinterpret_cast<const long long *>(d_row), d_pos));
-  CK(absorb(qabs, q, w->kv_b_proj, batch, NH, DN, DV, DR, R, 0, cfg->rope_theta, s, d_pos));
-  AttendLaunch a;
-  a.rows = rows;
-  a.q = qabs;
-  a.out = mix;
-  a.kv = d_kv;
-  a.softmax_scale = 1.0f / sqrtf(static_cast<float>(QD));
-  if (attend_common(plan, a, NH, R, DR, stream) != 0) return -1;
-  CK(vup(ho, mix, w->kv_b_proj, batch, NH, DN, DV, R, s));
-  CK(gemv_bf16(d_out, ho, w->o_proj, NH * DV, H, batch, s));
-  return 0;
+  StepPool pool;
+  pool.kv = d_kv;
+  return decode_step(cfg, w, plan, d_out, d_x, pool, rows, d_row, d_pos, batch, d_workspace, stream);
+}
+
+// Reference: src/mla_compressed_q8_state.c:161-255 (one token of one state);
+// here a batch of states in one Q8 pool.
+KVL_EXPORT int kvl_mla_decode_step_q8(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w,
+                                      const KvlMlaAttendPlan *plan, float *d_out, const float *d_x,
+                                      int8_t *d_latent_q8, float *d_latent_scale, uint16_t *d_rope_bf16,
+                                      int64_t rows, const int64_t *d_row, const int *d_pos, int batch,
+                                      void *d_workspace, void *stream) {
+  if (!cfg || !w || !plan || !d_out || !d_x || !d_latent_q8 || !d_latent_scale || !d_rope_bf16 || !d_row ||
+      !d_pos || batch <= 0 || !d_workspace || !cfg_dims_ok(*cfg) || plan->dp.host.batch != batch) {
+    set_err("invalid Q8 decode step arguments");
+    return -1;
+  }
+  StepPool pool;
+  pool.lat8 = d_latent_q8;
+  pool.lscale = d_latent_scale;
+  pool.rope16 = d_rope_bf16;
+  return decode_step(cfg, w, plan, d_out, d_x, pool, rows, d_row, d_pos, batch, d_workspace, stream);
 }
 
 KVL_EXPORT int kvl_mla_merge_packed(float *d_out, float *d_lse, const float *d_parts, int parts, int batch,

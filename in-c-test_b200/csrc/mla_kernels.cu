@@ -274,17 +274,30 @@ __device__ void quantize_row(int8_t *q, float *scale_out, const float *lat, int 
   if (threadIdx.x == 0) *scale_out = scale;
 }
 
+// Q8 state row (int8 latent, fp32 scale, bf16 rope) for each of the n tokens,
+// at the rows append_bf16 would use; ka as for append_bf16 (optionally
+// `parts` split-K partials added in order).
 __global__ void append_q8_kernel(int8_t *lat8, float *lscale, uint16_t *rope16, long long row0, const float *ka,
                                  const uint16_t *norm_w, int R, int DR, int pos0, float eps, float theta,
-                                 const long long *row_of, const int *pos_of) {
+                                 const long long *row_of, const int *pos_of, int parts, long long part_stride) {
   extern __shared__ float sh[];
   float *lat = sh;
   double *dred = reinterpret_cast<double *>(sh + ((R + 1) & ~1));
   float *fred = reinterpret_cast<float *>(dred + 32);
+  float *ksum = fred + 32;  // [R + DR] when parts > 1
   const int t = blockIdx.x;
   const int pos = pos_of ? pos_of[t] : pos0 + t;
   const long long row = row_of ? row_of[t] : row0 + pos0 + t;
   const float *kt = ka + static_cast<size_t>(t) * (R + DR);
+  if (parts > 1) {
+    for (int i = threadIdx.x; i < R + DR; i += blockDim.x) {
+      float v = kt[i];
+      for (int pp = 1; pp < parts; ++pp) v += kt[pp * part_stride + i];
+      ksum[i] = v;
+    }
+    __syncthreads();
+    kt = ksum;
+  }
   rmsnorm_row(lat, kt, norm_w, R, eps, dred);
   quantize_row(lat8 + static_cast<size_t>(row) * R, lscale + row, lat, R, fred);
   const int half = DR / 2;
@@ -312,11 +325,12 @@ cudaError_t append_bf16(uint16_t *kv, long long row0, const float *ka, const uin
 
 cudaError_t append_q8(int8_t *lat8, float *lscale, uint16_t *rope16, long long row0, const float *ka,
                       const uint16_t *norm_w, int n, int R, int DR, int pos0, float eps, float theta,
-                      cudaStream_t s, const long long *row_of, const int *pos_of) {
+                      cudaStream_t s, const long long *row_of, const int *pos_of, int parts, long long part_stride) {
   if (n <= 0) return cudaSuccess;
   ProfScope ps("append_q8", s);
-  append_q8_kernel<<<n, 128, append_smem(R), s>>>(lat8, lscale, rope16, row0, ka, norm_w, R, DR, pos0, eps, theta,
-                                                  row_of, pos_of);
+  const size_t sm = parts > 1 ? append_smem_parts(R, DR) : append_smem(R);
+  append_q8_kernel<<<n, 128, sm, s>>>(lat8, lscale, rope16, row0, ka, norm_w, R, DR, pos0, eps, theta, row_of,
+                                      pos_of, parts, part_stride);
   return cudaGetLastError();
 }
 

@@ -13,7 +13,8 @@ cudaError_t append_bf16(uint16_t *kv, long long row0, const float *ka, const uin
                         long long part_stride = 0);
 cudaError_t append_q8(int8_t *lat8, float *lscale, uint16_t *rope16, long long row0, const float *ka,
                       const uint16_t *norm_w, int n, int R, int DR, int pos0, float eps, float theta,
-                      cudaStream_t s, const long long *row_of = nullptr, const int *pos_of = nullptr);
+                      cudaStream_t s, const long long *row_of = nullptr, const int *pos_of = nullptr,
+                      int parts = 1, long long part_stride = 0);
 // Prefill rows [0, n) of a bf16 [n][576] pool (Kimi shape), RoPE from a [n][32] cos/sin table.
 cudaError_t append_rows_bf16(uint16_t *pool, const float *ka, const uint16_t *norm_w, const float2 *cs, int n,
                              float eps, cudaStream_t s);

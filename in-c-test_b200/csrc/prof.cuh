@@ -22,7 +22,8 @@ cudaError_t smem_opt_in(const void *fn, int bytes, std::atomic<unsigned long lon
 struct ProfScope {
   int id;
   cudaStream_t s;
-  ProfScope(const char *name, cudaStream_t st) : id(prof_enabled() ? prof_begin(name, st) : -1), s(st) {}
+  // name == nullptr: never timed (launches that must not create events)
+  ProfScope(const char *name, cudaStream_t st) : id(name && prof_enabled() ? prof_begin(name, st) : -1), s(st) {}
   ~ProfScope() {
     if (id >= 0) prof_end(id, s);
   }

@@ -111,9 +111,18 @@ SIGNATURES = {
     "kvl_mla_decode_step_bf16": (C.c_int, [C.POINTER(KvlMlaConfig), C.POINTER(KvlMlaDeviceWeights), C.c_void_p,
                                            C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p,
                                            C.c_int, C.c_void_p, C.c_void_p]),
+    "kvl_mla_decode_step_q8": (C.c_int, [C.POINTER(KvlMlaConfig), C.POINTER(KvlMlaDeviceWeights), C.c_void_p,
+                                         C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64,
+                                         C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
     "kvl_mla_prefill_workspace_bytes": (C.c_size_t, [C.POINTER(KvlMlaConfig), C.c_int]),
     "kvl_mla_prefill_dev": (C.c_int, [C.POINTER(KvlMlaConfig), C.POINTER(KvlMlaDeviceWeights), C.c_void_p,
                                       C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
+    "kvl_mla_prefill_cp_begin": (C.c_int, [C.POINTER(KvlMlaConfig), C.POINTER(KvlMlaDeviceWeights), C.c_void_p,
+                                           C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_size_t,
+                                           C.c_void_p]),
+    "kvl_mla_prefill_cp_end": (C.c_int, [C.POINTER(KvlMlaConfig), C.POINTER(KvlMlaDeviceWeights), C.c_void_p,
+                                         C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_size_t,
+                                         C.c_void_p]),
     "kvl_mla_q8_quantize_rows": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "kvl_mla_q8_dequant": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int, C.c_void_p]),
     "kvl_mla_bf16_rne": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p]),

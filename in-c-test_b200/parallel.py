@@ -7,7 +7,12 @@ B200 build's multi-GPU layouts:
   * one long sequence is split into contiguous KV ranges, one per GPU; each GPU
     produces a normalised partial (o [16][512], lse [16]) that an all-gather
     plus the merge kernel (kvl_mla_merge_partials) combine:
-        M = max_g lse_g,  o = sum_g e^(lse_g - M) o_g / sum_g e^(lse_g - M).
+        M = max_g lse_g,  o = sum_g e^(lse_g - M) o_g / sum_g e^(lse_g - M);
+  * one prompt's causal prefill is context-parallel: 2 * world chunks of query
+    rows, rank r owning chunks r and 2 * world - 1 - r (zigzag: every rank gets
+    one early and one late chunk, so the causal work is even), with one
+    all-gather of the tokens' compressed 576-wide rows between the projection
+    of each rank's rows and the attention (kvl_mla_prefill_cp_begin / _end).
 """
 from __future__ import annotations
 
@@ -46,3 +51,19 @@ def merge_partials(o: np.ndarray, lse: np.ndarray):
     s = np.sum(w, axis=0)
     out = np.einsum("ph,phr->hr", w, o) / s[:, None]
     return out.astype(np.float32), (m + np.log(s)).astype(np.float32)
+
+
+def zigzag_chunks(seq_len: int, world: int) -> list[tuple[tuple[int, int], tuple[int, int]]]:
+    """Per rank, the [lo, hi) query rows of its early and late chunk in the
+    context-parallel prefill (the split kvl_mla_prefill_cp_begin uses)."""
+    if world <= 0 or seq_len % (2 * world):
+        raise ValueError(f"{seq_len} rows do not split into {2 * world} chunks")
+    c = seq_len // (2 * world)
+    return [((r * c, (r + 1) * c), ((2 * world - 1 - r) * c, (2 * world - r) * c)) for r in range(world)]
+
+
+def gathered_row_order(seq_len: int, world: int) -> np.ndarray:
+    """Prompt row held at each row of the all-gathered buffer [world][2c]: rank
+    order, each rank's early chunk then its late chunk."""
+    return np.concatenate([np.concatenate([np.arange(*a), np.arange(*b)])
+                           for a, b in zigzag_chunks(seq_len, world)])

@@ -57,7 +57,7 @@ size_t kvl_mla_cuda_state_device_bytes(const void *state);
 /* ------------------------------------------------------------------ attend */
 
 /* Work plan of one batch: cached lengths and the first pool row of every
- * sequence (host arrays), split into equal contiguous ranges of 64-row tiles,
+ * sequence (host arrays), split into equal contiguous ranges of 128-row tiles,
  * one per CTA (max_ctas = 0: one per SM).  Owns the partial-output workspace,
  * sized for num_heads x kv_lora_rank outputs per piece.  Created on, and used
  * with, the current CUDA device. */
@@ -196,6 +196,19 @@ int kvl_mla_decode_step_bf16(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights 
                              uint16_t *d_kv, int64_t rows, const int64_t *d_row,
                              const int *d_pos, int batch, void *d_workspace, void *stream);
 
+/* The same step over a Q8 pool in the reference layout (d_latent_q8 [rows][R]
+ * int8, d_latent_scale [rows] fp32, d_rope_bf16 [rows][DR] bf16; the layout of
+ * KvlMlaCompressedQ8State): each token's new row goes through the reference's
+ * row quantiser (src/mla_compressed_q8_state.c:34-55, 111-127) and the attend
+ * runs the int8 tensor-core kernel of kvl_mla_attend_q8.  Replaces one
+ * kvl_mla_decode_compressed_q8_bf16 call (src/mla_compressed_q8_state.c:161-255)
+ * per sequence.  Workspace as kvl_mla_decode_step_workspace_bytes. */
+int kvl_mla_decode_step_q8(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w,
+                           const KvlMlaAttendPlan *plan, float *d_out, const float *d_x,
+                           int8_t *d_latent_q8, float *d_latent_scale, uint16_t *d_rope_bf16,
+                           int64_t rows, const int64_t *d_row, const int *d_pos, int batch,
+                           void *d_workspace, void *stream);
+
 /* ------------------------------------------------------------------ prefill on device */
 
 /* Scratch bytes kvl_mla_prefill_dev needs for seq_len tokens. */
@@ -208,6 +221,32 @@ size_t kvl_mla_prefill_workspace_bytes(const KvlMlaConfig *cfg, int seq_len);
 int kvl_mla_prefill_dev(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, float *d_out,
                         const uint16_t *d_x, int seq_len, void *d_workspace, size_t workspace_bytes,
                         void *stream);
+
+/* Context-parallel causal prefill of one seq_len-token prompt over `world`
+ * GPUs, one process per GPU (the computation of kvl_mla_prefill_dev, split by
+ * query rows).  The prompt is cut into 2 * world chunks of c = seq_len /
+ * (2 * world) rows (c a multiple of 128); rank r owns chunks r and
+ * 2 * world - 1 - r, so every rank has the same causal attention work.  Two
+ * calls, with one all-gather of the compressed rows between them:
+ *   kvl_mla_prefill_cp_begin: kv_a projection, RMSNorm and RoPE of the rank's
+ *     rows (the per-token append of src/mla_prefill_streaming.c:131-138) into
+ *     d_send [2c][576] bf16 (early chunk, then late chunk), and q_proj of those
+ *     rows into the workspace;
+ *   the caller all-gathers every rank's d_send into d_recv [world][2c][576] in
+ *     rank order (one all-gather of 2c * 1152 bytes per rank, e.g. NCCL);
+ *   kvl_mla_prefill_cp_end: places the gathered rows, expands K/V with kv_b for
+ *     the keys its chunks see, runs the causal attention of its queries and
+ *     o_proj into its rows of d_out.
+ * d_x [seq_len][H] bf16 (only the rank's rows are read), d_out [seq_len][H]
+ * fp32 (only the rank's rows are written); both calls take the same workspace
+ * of kvl_mla_prefill_workspace_bytes(cfg, seq_len) bytes (256-byte aligned),
+ * which must not be reused between them.  Production head shape only. */
+int kvl_mla_prefill_cp_begin(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, const uint16_t *d_x,
+                             int seq_len, int rank, int world, uint16_t *d_send, void *d_workspace,
+                             size_t workspace_bytes, void *stream);
+int kvl_mla_prefill_cp_end(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, float *d_out, int seq_len,
+                           int rank, int world, const uint16_t *d_recv, void *d_workspace,
+                           size_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------------------ Q8 helpers */
 int kvl_mla_q8_quantize_rows(int8_t *d_q, float *d_scale, const float *d_x, int rows, int R,

@@ -100,3 +100,104 @@ def test_split_kv_merge_over_gloo_world2():
         assert p.exitcode == 0
     for rank, err_o, err_l in res:
         assert err_o < 1e-5 and err_l < 1e-4, (rank, err_o, err_l)
+
+
+def test_zigzag_chunks_partition_and_balance():
+    from kvl_b200.parallel import gathered_row_order, zigzag_chunks
+    for S_len, world in [(4096, 1), (4096, 2), (4096, 4), (4096, 8), (48, 3)]:
+        ch = zigzag_chunks(S_len, world)
+        rows = sorted(r for a, b in ch for r in list(range(*a)) + list(range(*b)))
+        assert rows == list(range(S_len))
+        # causal work of a chunk [lo, hi): sum of (t + 1) over its query rows
+        work = [sum(t + 1 for t in range(*a)) + sum(t + 1 for t in range(*b)) for a, b in ch]
+        assert max(work) - min(work) <= (S_len // (2 * world)) ** 2
+        order = gathered_row_order(S_len, world)
+        assert sorted(order.tolist()) == list(range(S_len))
+    with pytest.raises(ValueError):
+        zigzag_chunks(100, 3)
+
+
+# A small attention shape of the reference's own probes (H, NH, DN, DR, DV, R, eps, theta).
+_CP_SHAPE = (64, 4, 8, 8, 8, 32, 1e-6, 10000.0)
+
+
+def _cp_rank_main(rank, world, port, seq_len, result_q):
+    """One rank of the context-parallel prefill protocol on CPU: append the
+    rank's rows (the oracle's restatement of the reference's per-token append),
+    all-gather them over gloo in rank order, place them by the gathered row
+    order, then compute the rank's queries (the reference's streaming prefill
+    attends row t over rows [0, t], which is the oracle's decode at t)."""
+    import sys
+    import pathlib
+    root = pathlib.Path(__file__).resolve().parents[1]
+    sys.path.insert(0, str(root))
+    import kvl_pkg
+    kvl_pkg.load()
+    import torch
+    import torch.distributed as dist
+    import kvl_b200.kvl_mla as K
+    import kvl_b200.synth as S
+    from kvl_b200.parallel import gathered_row_order, zigzag_chunks
+    from oracle.oracle import Oracle, cfg_of
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        H, NH, DN, DR, DV, R, eps, theta = _CP_SHAPE
+        cfg = cfg_of(*_CP_SHAPE)
+        w = K.random_weights(K.make_config(*_CP_SHAPE), 61, 0.05)
+        x = S.normal(61, S.S_X, seq_len * H, 1.0).reshape(seq_len, H)
+        orc = Oracle()
+        (a0, a1), (b0, b1) = zigzag_chunks(seq_len, world)[rank]
+        mine = list(range(a0, a1)) + list(range(b0, b1))
+        send = np.zeros((len(mine), R + DR), np.float32)
+        for i, t in enumerate(mine):
+            lat, rp = orc.append_f32(x[t], t, cfg, w.arrays[1], w.arrays[2])
+            send[i, :R], send[i, R:] = lat, rp
+        recv = [torch.zeros(send.shape) for _ in range(world)]
+        dist.all_gather(recv, torch.from_numpy(send))
+        rows = np.concatenate([t.numpy() for t in recv])
+        pool = np.zeros_like(rows)
+        pool[gathered_row_order(seq_len, world)] = rows
+        latent = np.ascontiguousarray(pool[:, :R])
+        rope = np.ascontiguousarray(pool[:, R:])
+        out = {t: orc.decode_f32(x[t], t, cfg, w.arrays, latent, rope) for t in mine}
+        result_q.put((rank, out))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_context_parallel_prefill_over_gloo(ref, world):
+    """Every rank's rows of the zigzag context-parallel prefill equal the
+    reference's own streaming prefill (src/mla_prefill_streaming.c:78-206) of
+    the whole prompt, within the reference's decode-vs-prefill gate (2e-5)."""
+    import multiprocessing as mp
+
+    import kvl_pkg
+    kvl_pkg.load()
+    import kvl_b200.kvl_mla as K
+    import kvl_b200.synth as S
+    from oracle.oracle import cfg_of
+    seq_len = 48
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_cp_rank_main, args=(r, world, port, seq_len, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=180) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    H = _CP_SHAPE[0]
+    w = K.random_weights(K.make_config(*_CP_SHAPE), 61, 0.05)
+    x = S.normal(61, S.S_X, seq_len * H, 1.0).reshape(seq_len, H)
+    want = ref.prefill(x, cfg_of(*_CP_SHAPE), w.arrays)
+    seen = set()
+    for rank, out in res:
+        for t, o in out.items():
+            assert t not in seen
+            seen.add(t)
+            assert np.max(np.abs(o - want[t])) < 2e-5, (rank, t)
+    assert seen == set(range(seq_len))
