@@ -496,8 +496,9 @@ class Prefill:
         if self.mode == "cp":
             c = S // (2 * dist.world)
             self.c = c
-            self.send = torch.empty((2 * c, 576), dtype=torch.int16, device=dev)
-            self.recv = torch.empty((dist.world * 2 * c, 576), dtype=torch.int16, device=dev)
+            # bf16 rows (NCCL has no 16-bit integer type)
+            self.send = torch.empty((2 * c, 576), dtype=torch.bfloat16, device=dev)
+            self.recv = torch.empty((dist.world * 2 * c, 576), dtype=torch.bfloat16, device=dev)
 
     def kernel_flops(self):
         """Algorithmic FLOPs per step of each library kernel of the prefill path

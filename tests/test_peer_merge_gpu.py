@@ -172,3 +172,73 @@ def test_merge_exchange_two_gpus(torch_cuda, B):
     if torch_cuda.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
     _run_two(_worker, (B, 6))
+
+
+def _timeout_worker(rank, world, port, q):
+    """Rank 1 skips one merge call.  Rank 0's kernel waits for rank 1's values,
+    gives up after its bounded wait (2 s) and records the timeout, which
+    kvl_mla_peer_group_check reports; rank 1 stays (launching nothing) until
+    rank 0 has read that status.  Then both ranks destroy the group and create
+    and connect a new one, whose merges are correct again -- the recovery the
+    library documents."""
+    try:
+        import sys
+        sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+        import torch
+        import torch.distributed as dist
+        import kvl_pkg
+        kvl_pkg.load()
+        import kvl_b200.kvl_mla as K
+        from kvl_b200.parallel import merge_partials
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world, init_method=f"tcp://127.0.0.1:{port}")
+
+        def gather(b):
+            lst = [None] * world
+            dist.all_gather_object(lst, b)
+            return lst
+
+        dev = torch.device("cuda", rank)
+        B = 2
+
+        def merge_once(pg, call):
+            recs = _records(call, world, B)
+            o, lse = recs[rank]
+            rec = torch.from_numpy(np.concatenate([o.ravel(), lse.ravel()])).to(dev)
+            out = torch.empty((B, NH, R), device=dev)
+            out_l = torch.empty((B, NH), device=dev)
+            assert pg.merge(out, out_l, rec) == 0, K.last_error()
+            return out, out_l, recs
+
+        pg = K.PeerGroup(rank, world, B, gather)
+        merge_once(pg, 0)
+        assert pg.check() == 0, K.last_error()
+        dist.barrier()
+        if rank == 0:
+            merge_once(pg, 1)  # rank 1 never joins this call
+            rc = pg.check()
+            msg = K.last_error()
+            assert rc == -1, "the wait for the absent rank did not run out"
+            assert "did not arrive in time" in msg, msg
+        dist.barrier()  # rank 1 leaves its buffer in place until rank 0 has read the status
+        pg.close()
+        pg = K.PeerGroup(rank, world, B, gather)
+        out, out_l, recs = merge_once(pg, 2)
+        assert pg.check() == 0, K.last_error()
+        for b in range(B):
+            wo, wl = merge_partials(np.stack([r[0][b] for r in recs]).astype(np.float64),
+                                    np.stack([r[1][b] for r in recs]).astype(np.float64))
+            np.testing.assert_allclose(out[b].cpu().numpy(), wo, rtol=1e-5, atol=1e-5)
+        dist.barrier()
+        pg.close()
+        dist.destroy_process_group()
+        q.put((rank, "ok", None))
+    except Exception as e:  # noqa: BLE001 - reported to the parent
+        q.put((rank, f"error: {e!r}", None))
+
+
+def test_merge_exchange_timeout_and_recreate_two_gpus(torch_cuda):
+    if torch_cuda.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    _run_two(_timeout_worker, ())
