@@ -302,11 +302,13 @@ cudaError_t launch_merge_unprofiled(float *out, float *lse, const float *part_o,
 
 // ------------------------------------------------------------------ generic attend
 // One CTA per (head, sequence); online softmax over chunks of 1024 rows in
-// fp32.  Used only when (NH, R, DR) is not the production (16, 512, 64).
+// fp32.  Used only when (NH, R, DR) is not the production (16, 512, 64); the
+// drop-in states of such shapes keep fp32 rows (kvf), the reference's own
+// state format.
 template <bool Q8>
 __global__ void attend_generic_kernel(float *out, float *lse, const float *q,
-                                      const uint16_t *kv, const int8_t *lat8, const float *lscale,
-                                      const uint16_t *rope16, const long long *row0,
+                                      const uint16_t *kv, const float *kvf, const int8_t *lat8,
+                                      const float *lscale, const uint16_t *rope16, const long long *row0,
                                       const int *len, int nh, int R, int DR, float scale_log2) {
   constexpr int kChunk = 1024;
   const int h = blockIdx.x, b = blockIdx.y;
@@ -323,10 +325,12 @@ __global__ void attend_generic_kernel(float *out, float *lse, const float *q,
   __syncthreads();
   auto lat = [&](long long row, int r) -> float {
     if (Q8) return __fmul_rn((float)lat8[row * R + r], lscale[row]);
+    if (kvf) return kvf[row * (R + DR) + r];
     return __bfloat162float(__ushort_as_bfloat16(kv[row * (R + DR) + r]));
   };
   auto rp = [&](long long row, int d) -> float {
     if (Q8) return __bfloat162float(__ushort_as_bfloat16(rope16[row * DR + d]));
+    if (kvf) return kvf[row * (R + DR) + R + d];
     return __bfloat162float(__ushort_as_bfloat16(kv[row * (R + DR) + R + d]));
   };
   auto block_reduce = [&](float v, bool is_max) -> float {
@@ -379,7 +383,7 @@ __global__ void attend_generic_kernel(float *out, float *lse, const float *q,
 }
 
 cudaError_t launch_attend_generic(bool q8, float *out, float *lse, const float *q, const uint16_t *kv,
-                                  const int8_t *lat8, const float *lscale, const uint16_t *rope16,
+                                  const float *kvf, const int8_t *lat8, const float *lscale, const uint16_t *rope16,
                                   const long long *d_row0, const int *d_len, int batch, int nh,
                                   int R, int DR, float scale_log2, cudaStream_t stream) {
   const size_t sm = (size_t)(R + DR + 1024 + R + 32) * sizeof(float);
@@ -391,10 +395,10 @@ cudaError_t launch_attend_generic(bool q8, float *out, float *lse, const float *
   dim3 grid(nh, batch);
   ProfScope ps("attend_generic", stream);
   if (q8)
-    attend_generic_kernel<true><<<grid, 128, sm, stream>>>(out, lse, q, kv, lat8, lscale, rope16, d_row0,
-                                                           d_len, nh, R, DR, scale_log2);
+    attend_generic_kernel<true><<<grid, 128, sm, stream>>>(out, lse, q, kv, nullptr, lat8, lscale, rope16,
+                                                           d_row0, d_len, nh, R, DR, scale_log2);
   else
-    attend_generic_kernel<false><<<grid, 128, sm, stream>>>(out, lse, q, kv, lat8, lscale, rope16, d_row0,
+    attend_generic_kernel<false><<<grid, 128, sm, stream>>>(out, lse, q, kv, kvf, lat8, lscale, rope16, d_row0,
                                                             d_len, nh, R, DR, scale_log2);
   return cudaGetLastError();
 }
@@ -468,7 +472,7 @@ int DevicePlan::launch(const AttendLaunch &a, cudaStream_t stream) const {
   const float scale_log2 = a.softmax_scale * 1.4426950408889634f;
   const bool fast = (nh == kHeads && R == kLatent && DR == kRope);
   if (!fast) {
-    return launch_attend_generic(a.q8, a.out, a.lse, a.q, a.kv, a.lat8, a.lscale, a.rope16,
+    return launch_attend_generic(a.q8, a.out, a.lse, a.q, a.kv, a.kvf, a.lat8, a.lscale, a.rope16,
                                  reinterpret_cast<const long long *>(m + off_row0),
                                  reinterpret_cast<const int *>(m + off_len), host.batch, nh, R, DR,
                                  scale_log2, stream) == cudaSuccess

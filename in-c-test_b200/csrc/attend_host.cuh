@@ -44,6 +44,8 @@ struct AttendLaunch {
   float *out = nullptr;
   float *lse = nullptr;
   const uint16_t *kv = nullptr;       // bf16 pool [rows][R + DR]
+  const float *kvf = nullptr;         // fp32 rows [rows][R + DR], read instead of kv by the
+                                      // CUDA-core kernel (shapes other than 16 x 512 x 64)
   const int8_t *lat8 = nullptr;       // q8 pool [rows][R]
   const float *lscale = nullptr;      // q8 pool [rows]
   const uint16_t *rope16 = nullptr;   // q8 pool [rows][DR]

@@ -212,16 +212,20 @@ struct DevState {
   int capacity = 0, cap_pad = 0, R = 0, DR = 0;
   int dev_len = 0;
   uint16_t *kv = nullptr;     // bf16 [cap_pad][R+DR]
+  float *kvf = nullptr;       // fp32 [cap_pad][R+DR]: the rows the attend reads for shapes other
+                              // than the production 16 x 512 x 64 (the reference's fp32 state)
   int8_t *lat8 = nullptr;     // q8 [cap_pad][R]
   float *lscale = nullptr;    // q8 [cap_pad]
   uint16_t *rope16 = nullptr; // q8 [cap_pad][DR]
   size_t bytes = 0;
   void release() {
     cudaFree(kv);
+    cudaFree(kvf);
     cudaFree(lat8);
     cudaFree(lscale);
     cudaFree(rope16);
     kv = nullptr;
+    kvf = nullptr;
     lat8 = nullptr;
     lscale = nullptr;
     rope16 = nullptr;
@@ -251,7 +255,7 @@ DevState *unregister_state(const void *key) {
   return ds;
 }
 
-int alloc_dev_state(DevState &ds, int fmt, int capacity, int R, int DR) {
+int alloc_dev_state(DevState &ds, int fmt, int capacity, int R, int DR, bool f32_rows = false) {
   ds.fmt = fmt;
   ds.capacity = capacity;
   ds.cap_pad = (capacity + kTileTok - 1) / kTileTok * kTileTok;
@@ -264,6 +268,12 @@ int alloc_dev_state(DevState &ds, int fmt, int capacity, int R, int DR) {
     ds.bytes = rows * (R + DR) * sizeof(uint16_t);
     CK(cudaMalloc(&ds.kv, ds.bytes));
     CK(cudaMemset(ds.kv, 0, ds.bytes));
+    if (f32_rows) {
+      const size_t fb = rows * (R + DR) * sizeof(float);
+      CK(cudaMalloc(&ds.kvf, fb));
+      CK(cudaMemset(ds.kvf, 0, fb));
+      ds.bytes += fb;
+    }
   } else {
     CK(cudaMalloc(&ds.lat8, rows * R));
     CK(cudaMalloc(&ds.lscale, rows * sizeof(float)));
@@ -297,6 +307,9 @@ int sync_bf16_state(Ctx &c, DevState &ds, const KvlMlaCompressedState &st) {
                        DR * sizeof(float), DR * sizeof(float), n, cudaMemcpyHostToDevice, c.stream));
   CK(f32_to_bf16(ds.kv + static_cast<size_t>(ds.dev_len) * (R + DR), tmp, static_cast<long long>(n) * (R + DR),
                  c.stream));
+  if (ds.kvf)
+    CK(cudaMemcpyAsync(ds.kvf + static_cast<size_t>(ds.dev_len) * (R + DR), tmp,
+                       static_cast<size_t>(n) * (R + DR) * sizeof(float), cudaMemcpyDeviceToDevice, c.stream));
   CK(cudaStreamSynchronize(c.stream));
   ds.dev_len = st.len;
   return 0;
@@ -345,6 +358,7 @@ int attend_state(Ctx &c, const DevState &ds, int L, int nh, float scale) {
   a.q = c.qabs.as<float>();
   a.out = c.mix.as<float>();
   a.kv = ds.kv;
+  a.kvf = ds.kvf;
   a.lat8 = ds.lat8;
   a.lscale = ds.lscale;
   a.rope16 = ds.rope16;
@@ -384,10 +398,13 @@ int decode_one(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, con
   CK(cudaMemcpyAsync(c.x.p, px, H * 4, cudaMemcpyHostToDevice, c.stream));
   CK(gemv_bf16(c.q.as<float>(), c.x.as<float>(), W.q, H, NH * QD, 1, c.stream));
   CK(gemv_bf16(c.ka.as<float>(), c.x.as<float>(), W.kva, H, R + DR, 1, c.stream));
-  if (ds.fmt == FMT_BF16)
+  if (ds.fmt == FMT_BF16) {
     CK(append_bf16(ds.kv, 0, c.ka.as<float>(), W.kvan, 1, R, DR, position, cfg.rms_eps, cfg.rope_theta,
                    c.rowf.as<float>(), c.stream));
-  else
+    if (ds.kvf)
+      CK(cudaMemcpyAsync(ds.kvf + static_cast<size_t>(position) * (R + DR), c.rowf.p, (R + DR) * sizeof(float),
+                         cudaMemcpyDeviceToDevice, c.stream));
+  } else
     CK(append_q8(ds.lat8, ds.lscale, ds.rope16, 0, c.ka.as<float>(), W.kvan, 1, R, DR, position, cfg.rms_eps,
                  cfg.rope_theta, c.stream));
   CK(absorb(c.qabs.as<float>(), c.q.as<float>(), W.kvb, 1, NH, DN, DV, DR, R, position, cfg.rope_theta, c.stream));
@@ -454,6 +471,9 @@ int decode_block(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, c
   CK(gemv_bf16(c.ka.as<float>(), c.x.as<float>(), W.kva, H, R + DR, count, c.stream));
   CK(append_bf16(ds.kv, 0, c.ka.as<float>(), W.kvan, count, R, DR, position, cfg.rms_eps, cfg.rope_theta,
                  c.rowf.as<float>(), c.stream));
+  if (ds.kvf)
+    CK(cudaMemcpyAsync(ds.kvf + static_cast<size_t>(position) * (R + DR), c.rowf.p, n * (R + DR) * sizeof(float),
+                       cudaMemcpyDeviceToDevice, c.stream));
   CK(absorb(c.qabs.as<float>(), c.q.as<float>(), W.kvb, count, NH, DN, DV, DR, R, position, cfg.rope_theta,
             c.stream));
   AttendLaunch a;
@@ -464,6 +484,7 @@ int decode_block(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, c
   a.q = c.qabs.as<float>();
   a.out = c.mix.as<float>();
   a.kv = ds.kv;
+  a.kvf = ds.kvf;
   a.softmax_scale = 1.0f / sqrtf(static_cast<float>(QD));
   if (c.plan.launch(a, c.stream) != 0) {
     set_err("attend launch failed: %s", cudaGetErrorString(cudaGetLastError()));
@@ -498,10 +519,13 @@ int prefill_state(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, 
   }
   CK(cudaMemcpyAsync(c.x.p, x, static_cast<size_t>(S) * H * 4, cudaMemcpyHostToDevice, c.stream));
   CK(gemv_bf16(c.ka.as<float>(), c.x.as<float>(), W.kva, H, R + DR, S, c.stream));
-  if (ds.fmt == FMT_BF16)
+  if (ds.fmt == FMT_BF16) {
     CK(append_bf16(ds.kv, 0, c.ka.as<float>(), W.kvan, S, R, DR, 0, cfg.rms_eps, cfg.rope_theta,
                    c.rowf.as<float>(), c.stream));
-  else
+    if (ds.kvf)
+      CK(cudaMemcpyAsync(ds.kvf, c.rowf.p, static_cast<size_t>(S) * (R + DR) * sizeof(float),
+                         cudaMemcpyDeviceToDevice, c.stream));
+  } else
     CK(append_q8(ds.lat8, ds.lscale, ds.rope16, 0, c.ka.as<float>(), W.kvan, S, R, DR, 0, cfg.rms_eps,
                  cfg.rope_theta, c.stream));
   return 0;
@@ -545,7 +569,10 @@ KVL_EXPORT int kvl_mla_compressed_state_init(KvlMlaCompressedState *state, const
   state->latent = static_cast<float *>(calloc(static_cast<size_t>(capacity) * R, sizeof(float)));
   state->rope = static_cast<float *>(calloc(static_cast<size_t>(capacity) * DR, sizeof(float)));
   DevState *ds = new DevState();
-  if (!state->latent || !state->rope || alloc_dev_state(*ds, FMT_BF16, capacity, R, DR) != 0) {
+  // The production shape keeps bf16 rows for the tensor-core attend; other
+  // shapes (the reference's probes) keep fp32 rows as the reference does.
+  const bool f32_rows = !(cfg->num_heads == kHeads && R == kLatent && DR == kRope);
+  if (!state->latent || !state->rope || alloc_dev_state(*ds, FMT_BF16, capacity, R, DR, f32_rows) != 0) {
     ds->release();
     delete ds;
     free(state->latent);
@@ -835,11 +862,12 @@ PrefillWs prefill_layout(const KvlMlaConfig &c, int S) {
     for (int i = 0; i < 9; ++i) sz[i] = f[i];
     n = 9;
   } else {
-    // xf, q, kva, qabs, mix, head_out, pool
-    const size_t f[7] = {s * H * 4, s * NH * QD * 4, s * (R + DR) * 4, s * NH * (R + DR) * 4, s * NH * R * 4,
-                         s * NH * DV * 4, (s + kTileTok) * (R + DR) * 2};
-    for (int i = 0; i < 7; ++i) sz[i] = f[i];
-    n = 7;
+    // xf, q, kva, qabs, mix, head_out, pool (bf16), pool (fp32: what the
+    // CUDA-core attend reads for shapes other than 16 x 512 x 64)
+    const size_t f[8] = {s * H * 4, s * NH * QD * 4, s * (R + DR) * 4, s * NH * (R + DR) * 4, s * NH * R * 4,
+                         s * NH * DV * 4, (s + kTileTok) * (R + DR) * 2, (s + kTileTok) * (R + DR) * 4};
+    for (int i = 0; i < 8; ++i) sz[i] = f[i];
+    n = 8;
   }
   PrefillWs w;
   size_t o = 0;
@@ -888,9 +916,10 @@ int prefill_absorbed(int device, int sms, const KvlMlaConfig &cfg, const DevW &W
   float *mix = reinterpret_cast<float *>(ws + L.off[4]);
   float *ho = reinterpret_cast<float *>(ws + L.off[5]);
   uint16_t *pool = reinterpret_cast<uint16_t *>(ws + L.off[6]);
+  float *poolf = reinterpret_cast<float *>(ws + L.off[7]);
   CK(gemv_bf16(q, xf, W.q, H, NH * QD, S, st));
   CK(gemv_bf16(ka, xf, W.kva, H, R + DR, S, st));
-  CK(append_bf16(pool, 0, ka, W.kvan, S, R, DR, 0, cfg.rms_eps, cfg.rope_theta, nullptr, st));
+  CK(append_bf16(pool, 0, ka, W.kvan, S, R, DR, 0, cfg.rms_eps, cfg.rope_theta, poolf, st));
   CK(absorb(qabs, q, W.kvb, S, NH, DN, DV, DR, R, 0, cfg.rope_theta, st));
   const DevicePlan *dp = prefill_plan(device, S, NH, R, sms);
   if (!dp) {
@@ -905,6 +934,7 @@ int prefill_absorbed(int device, int sms, const KvlMlaConfig &cfg, const DevW &W
   a.q = qabs;
   a.out = mix;
   a.kv = pool;
+  a.kvf = poolf;
   a.softmax_scale = 1.0f / sqrtf(static_cast<float>(QD));
   if (dp->launch(a, st) != 0) {
     set_err("prefill attend launch failed");
