@@ -77,7 +77,15 @@ constexpr uint32_t kThreads = 256;
 
 using namespace bf16dec;
 
-__global__ void __launch_bounds__(kThreads, 1)
+// At most 192 registers: a merge block (256 threads x 64 registers) must fit
+// beside a resident attend CTA (256 x 192) in the 65,536 registers of an SM,
+// so that the merge grid, launched as the attend's programmatic dependent,
+// waits on the SMs and starts the moment the attend grid completes.  With 208
+// registers it did not fit, and config 5 (attend + merge) went from 58.4 to
+// 60.4 us, a 64 x 32768 batch from 478 to 484 us.  (A reciprocal per head in
+// the epilogue instead of a division per element took config 5 to 56.3 us
+// under this cap but the batch to 486 us, so the epilogue divides.)
+__global__ void __maxnreg__(192)
     mla_attend_bf16_kernel(const __grid_constant__ AttendParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>(

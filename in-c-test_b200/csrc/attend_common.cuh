@@ -81,24 +81,27 @@ __device__ __forceinline__ uint32_t pack2_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t *>(&v);
 }
 
-// Loads the fp32 absorbed query [16][576] of one sequence into shared memory
-// as nine SW128 boxes of bf16 (64 dims x 16 heads, 2 KB each).  Run by 128
-// threads (tid 0..127) with every global load in flight before the first
-// store, so the tile costs one memory round trip.
+// The fp32 absorbed query [16][576] of one sequence as nine SW128 boxes of
+// bf16 (64 dims x 16 heads, 2 KB each), in two phases so that a caller can
+// issue the loads, signal that they are in flight, and only then wait for
+// them: query_tile_load issues every global load of thread tid (0..127) into
+// v, query_tile_store converts and stores them.
 
-__device__ __forceinline__ void load_query_tile(uint8_t *qd, const float *qs, int tid) {
-  constexpr int kChunks = kHeads * (kRow / 8);  // 1152 chunks of 8 values
-  constexpr int kPer = kChunks / 128;           // 9 per thread
-  float4 v[2 * kPer];
+constexpr int kQueryPer = kHeads * (kRow / 8) / 128;  // 9 chunks of 8 values per thread
+
+__device__ __forceinline__ void query_tile_load(const float *qs, int tid, float4 (&v)[2 * kQueryPer]) {
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) {
+  for (int i = 0; i < kQueryPer; ++i) {
     const int idx = tid + 128 * i;
     const int h = idx / (kRow / 8), c8 = idx % (kRow / 8);
     v[2 * i] = *reinterpret_cast<const float4 *>(qs + h * kRow + c8 * 8);
     v[2 * i + 1] = *reinterpret_cast<const float4 *>(qs + h * kRow + c8 * 8 + 4);
   }
+}
+
+__device__ __forceinline__ void query_tile_store(uint8_t *qd, int tid, const float4 (&v)[2 * kQueryPer]) {
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) {
+  for (int i = 0; i < kQueryPer; ++i) {
     const int idx = tid + 128 * i;
     const int h = idx / (kRow / 8), c8 = idx % (kRow / 8);
     uint4 o;
@@ -109,6 +112,13 @@ __device__ __forceinline__ void load_query_tile(uint8_t *qd, const float *qs, in
     const uint32_t chunk = (c8 & 7) ^ (h & 7);  // 128-byte swizzle within the 16-row box
     *reinterpret_cast<uint4 *>(qd + (c8 >> 3) * 2048 + (h >> 3) * 1024 + (h & 7) * 128 + chunk * 16) = o;
   }
+}
+
+// Both phases at once.
+__device__ __forceinline__ void load_query_tile(uint8_t *qd, const float *qs, int tid) {
+  float4 v[2 * kQueryPer];
+  query_tile_load(qs, tid, v);
+  query_tile_store(qd, tid, v);
 }
 #endif
 

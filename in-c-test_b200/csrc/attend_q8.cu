@@ -120,13 +120,24 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
 // Unit u (0..255) is head u / 16, latent dims 32 * (u % 16) .. +31 and rope
 // dims 4 * (u % 16) .. +3; the sixteen units of a head are sixteen
 // consecutive lanes (one half-warp).
-__device__ __forceinline__ void load_query_unit(uint8_t *qi, uint8_t *qr, float *qscale, const float *q, int u) {
+// The loads of unit u, issued before any use so that a caller can signal
+// that they are in flight (query_unit_split below finishes the unit).
+struct QueryUnitLoads {
+  float4 v[8], r0;
+};
+__device__ __forceinline__ void query_unit_load(const float *q, int u, QueryUnitLoads &ld) {
   const int h = u >> 4, j = u & 15;
   const float *src = q + h * kRow + 32 * j;
-  float4 v[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) v[i] = *reinterpret_cast<const float4 *>(src + 4 * i);
-  const float4 r0 = *reinterpret_cast<const float4 *>(q + h * kRow + kLatent + 4 * j);
+  for (int i = 0; i < 8; ++i) ld.v[i] = *reinterpret_cast<const float4 *>(src + 4 * i);
+  ld.r0 = *reinterpret_cast<const float4 *>(q + h * kRow + kLatent + 4 * j);
+}
+
+__device__ __forceinline__ void query_unit_split(uint8_t *qi, uint8_t *qr, float *qscale, int u,
+                                                 const QueryUnitLoads &ld) {
+  const int h = u >> 4, j = u & 15;
+  const float4 *v = ld.v;
+  const float4 r0 = ld.r0;
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i)
@@ -158,6 +169,13 @@ __device__ __forceinline__ void load_query_unit(uint8_t *qi, uint8_t *qr, float 
   // rope dims 4j .. 4j + 3: bytes 8j .. 8j + 7 of head h's 128-byte row
   *reinterpret_cast<uint2 *>(qr + (h >> 3) * 1024 + (h & 7) * 128 + (((j >> 1) ^ (h & 7)) << 4) + 8 * (j & 1)) =
       make_uint2(pack2_bf16(r0.x, r0.y), pack2_bf16(r0.z, r0.w));
+}
+
+// Both phases at once.
+__device__ __forceinline__ void load_query_unit(uint8_t *qi, uint8_t *qr, float *qscale, const float *q, int u) {
+  QueryUnitLoads ld;
+  query_unit_load(q, u, ld);
+  query_unit_split(qi, qr, qscale, u, ld);
 }
 
 // 4 consecutive 32-bit TMEM columns of this thread's lane.
@@ -555,13 +573,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int i = 0; i < kHPW; ++i) lt[i] = (B->red[wg][0][i] + B->red[wg][1][i]) + (B->red[wg][2][i] + B->red[wg][3][i]);
       named_bar_sync(bid, 128);
+      float inv[kHPW];  // one division per head, not per element
+#pragma unroll
+      for (int i = 0; i < kHPW; ++i) inv[i] = 1.0f / lt[i];
       float *dst = (sg.slot < 0) ? p.out + static_cast<size_t>(sg.seq) * kHeads * kLatent
                                  : p.part_o + static_cast<size_t>(sg.slot) * kHeads * kLatent;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int d = 128 * c + tt;
 #pragma unroll
-        for (int i = 0; i < kHPW; ++i) dst[(hb + i) * kLatent + d] = acc[c][i] / lt[i];
+        for (int i = 0; i < kHPW; ++i) dst[(hb + i) * kLatent + d] = acc[c][i] * inv[i];
       }
       if (w == 0 && lane < kHPW) {
         float m = 0.f, l = 1.f;
