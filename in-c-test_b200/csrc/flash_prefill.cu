@@ -64,11 +64,15 @@ constexpr uint32_t kSmem = OFF_BAR + sizeof(Bars) + 1024;
 static_assert(kSmem <= 232448, "shared memory budget");
 constexpr uint32_t kTmemCols = 512;
 
-// Item k of the CTA: snake order over the items sorted by decreasing cost.
-__device__ __forceinline__ bool item_of(int k, int grid, int cta, int n_items, int nq, int &head, int &qt) {
+// Item k of the CTA: snake order over the items sorted by decreasing cost --
+// the query tiles of [q_tile0, nq) from the last down, then those of the
+// optional lower range [lo_t0, lo_t1) from its last down (n_hi tiles above it).
+__device__ __forceinline__ bool item_of(int k, int grid, int cta, int n_items, int nq, int n_hi, int lo_t1,
+                                        int &head, int &qt) {
   const int pos = (k & 1) ? (k + 1) * grid - 1 - cta : k * grid + cta;
   if (pos >= n_items) return false;
-  qt = nq - 1 - pos / 16;
+  const int t = pos / 16;
+  qt = t < n_hi ? nq - 1 - t : lo_t1 - 1 - (t - n_hi);
   head = pos % 16;
   return true;
 }
@@ -118,7 +122,8 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   volatile int *abort = &B->abort;
   const int nq = (p.S + kT - 1) / kT;
-  const int n_items = (nq - p.q_tile0) * 16;  // query tiles [q_tile0, nq), heaviest first
+  const int n_hi = nq - p.q_tile0;
+  const int n_items = (n_hi + p.lo_t1 - p.lo_t0) * 16;  // query tiles [q_tile0, nq) ++ [lo_t0, lo_t1)
 
   if (threadIdx.x == 0) {
     mbar_init(&B->q_full, 1);
@@ -157,7 +162,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
       uint32_t kc = 0, qc = 0;  // kc: key tiles issued = global S tile index
       bool ok = true;
       int head, qt;
-      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, head, qt); ++k) {
+      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, n_hi, p.lo_t1, head, qt); ++k) {
         if (kc > 0) {
           const uint32_t gl = kc - 1;  // last S of the previous item
           ok = mbar_wait(&B->s_full[gl % kSBuf], (gl / kSBuf) & 1, abort, p.err, ERR_TIMEOUT_EMPTY);
@@ -194,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
       uint32_t vc = 0;
       bool ok = true;
       int head, qt;
-      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, head, qt); ++k) {
+      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, n_hi, p.lo_t1, head, qt); ++k) {
         for (int j = 0; j <= qt && ok; ++j, ++vc) {
           // the V of tile g is free once P_g V_g has completed (pv_done of tile g)
           const uint32_t s = vc % kVSt;
@@ -229,7 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
       uint32_t tc = 0, kc = 0, vc = 0;  // S tiles, K stages, V stages consumed
       bool ok = true;
       int head, qt;
-      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, head, qt); ++k) {
+      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, n_hi, p.lo_t1, head, qt); ++k) {
         const int n = qt + 1;
         ok = mbar_wait(&B->q_full, k & 1, abort, p.err, ERR_TIMEOUT_FULL);
         auto issue_s = [&](int j) -> bool {
@@ -282,7 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
     uint32_t g = 0;  // S tiles consumed (same sequence as the MMA issuer's)
     int head, qt;
     bool bad = false;
-    for (int k = 0; !bad && item_of(k, gridDim.x, blockIdx.x, n_items, nq, head, qt); ++k) {
+    for (int k = 0; !bad && item_of(k, gridDim.x, blockIdx.x, n_items, nq, n_hi, p.lo_t1, head, qt); ++k) {
       const int n = qt + 1;
       const int qrow = qt * kT + r;
       float m = -INFINITY, l = 0.f;
@@ -408,8 +413,9 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
 cudaError_t launch_flash_prefill(const FlashParams &p, int sms, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(flash_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) return e;
-  const int items = ((p.S + kT - 1) / kT - p.q_tile0) * 16;
-  if (items <= 0 || p.q_tile0 < 0) return cudaErrorInvalidValue;
+  const int items = ((p.S + kT - 1) / kT - p.q_tile0 + p.lo_t1 - p.lo_t0) * 16;
+  if (items <= 0 || p.q_tile0 < 0 || p.lo_t0 < 0 || p.lo_t1 < p.lo_t0 || p.lo_t1 > p.q_tile0)
+    return cudaErrorInvalidValue;
   const int grid = items < sms ? items : sms;
   ProfScope ps("flash_prefill", stream);
   flash_prefill_kernel<<<grid, kThreads, kSmem, stream>>>(p);

@@ -15,6 +15,8 @@ struct FlashParams {
   int kr_col;
   int S;               // keys [0, S); queries [128 * q_tile0, S)
   int q_tile0;
+  int lo_t0, lo_t1;    // optional second query range: tiles [lo_t0, lo_t1), lo_t1 <= q_tile0
+                       // (0, 0: none); each of its tiles attends keys up to its own end
   float scale_log2;    // softmax scale * log2(e)
   __nv_bfloat16 *out;  // [S][16][128] bf16
   uint32_t *err;

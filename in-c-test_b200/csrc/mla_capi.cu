@@ -1177,16 +1177,38 @@ int cp_project_rows(int sms, const KvlMlaConfig &cfg, const DevW &W, const uint1
   return 0;
 }
 
-// Causal attention of the queries [r0, r0 + M) over the keys [0, r0 + M) and
-// o_proj of those rows (K/V of the keys already expanded in the workspace).
-int cp_attend_rows(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, int S, int r0, int M,
-                   uint8_t *ws, const PrefillWs &L, cudaStream_t st) {
-  const uint64_t H = cfg.hidden_size, s = S, m = static_cast<uint64_t>(M), R0 = static_cast<uint64_t>(r0);
+// o_proj of the rows [r0, r0 + M): out = o Wo^T, fp32.
+int cp_oproj_rows(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, int r0, int M, uint8_t *ws,
+                  const PrefillWs &L, cudaStream_t st) {
+  const uint64_t H = cfg.hidden_size, m = static_cast<uint64_t>(M), R0 = static_cast<uint64_t>(r0);
+  uint16_t *o = reinterpret_cast<uint16_t *>(ws + L.off[6]);
+  GemmParams g;
+  memset(&g, 0, sizeof g);
+  g.err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
+  if (!bf16_map(&g.tm_a, o + R0 * 2048, 2048, m, 2048 * 2, 128) || !bf16_map(&g.tm_b, W.o, 2048, H, 2048 * 2, 128)) {
+    set_err("prefill (context parallel): tensor map (o_proj)");
+    return -1;
+  }
+  g.M = M;
+  g.N = static_cast<int>(H);
+  g.K = 2048;
+  g.c = d_out + R0 * H;
+  g.ldc = static_cast<int>(H);
+  CK(launch_gemm_pair(g, 256, EPI_F32, sms, st, "gemm_o"));
+  return 0;
+}
+
+// Causal attention of a rank's two query chunks in one flash launch (the late
+// chunk as the kernel's main query range over keys [0, its end), the early one
+// as its second range), so both chunks' (head, query tile) items share the
+// CTAs; then o_proj of the two chunks, the early one on the second stream.
+int cp_attend(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, const CpChunks &k, uint8_t *ws,
+              const PrefillWs &L, cudaStream_t st, PrefillFork *fk) {
+  const uint64_t s = static_cast<uint64_t>(k.b0 + k.c);
   uint16_t *q = reinterpret_cast<uint16_t *>(ws + L.off[2]);
   uint16_t *pool = reinterpret_cast<uint16_t *>(ws + L.off[4]);
   uint16_t *kv = reinterpret_cast<uint16_t *>(ws + L.off[5]);
   uint16_t *o = reinterpret_cast<uint16_t *>(ws + L.off[6]);
-  uint32_t *err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
   FlashParams f;
   memset(&f, 0, sizeof f);
   {
@@ -1201,25 +1223,20 @@ int cp_attend_rows(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out
     }
   }
   f.kr_col = 512;
-  f.S = r0 + M;
-  f.q_tile0 = r0 / 128;
+  f.S = k.b0 + k.c;
+  f.q_tile0 = k.b0 / 128;
+  f.lo_t0 = k.a0 / 128;
+  f.lo_t1 = (k.a0 + k.c) / 128;
   f.scale_log2 = (1.0f / sqrtf(192.0f)) * 1.4426950408889634f;
   f.out = reinterpret_cast<__nv_bfloat16 *>(o);
-  f.err = err;
+  f.err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
   CK(launch_flash_prefill(f, sms, st));
-  GemmParams g;
-  memset(&g, 0, sizeof g);
-  g.err = err;
-  if (!bf16_map(&g.tm_a, o + R0 * 2048, 2048, m, 2048 * 2, 128) || !bf16_map(&g.tm_b, W.o, 2048, H, 2048 * 2, 128)) {
-    set_err("prefill (context parallel): tensor map (o_proj)");
-    return -1;
-  }
-  g.M = M;
-  g.N = static_cast<int>(H);
-  g.K = 2048;
-  g.c = d_out + R0 * H;
-  g.ldc = static_cast<int>(H);
-  CK(launch_gemm_pair(g, 256, EPI_F32, sms, st, "gemm_o"));
+  CK(cudaEventRecord(fk->fork, st));
+  CK(cudaStreamWaitEvent(fk->s2, fk->fork, 0));
+  if (cp_oproj_rows(sms, cfg, W, d_out, k.a0, k.c, ws, L, fk->s2) != 0) return -1;
+  CK(cudaEventRecord(fk->qdone, fk->s2));
+  if (cp_oproj_rows(sms, cfg, W, d_out, k.b0, k.c, ws, L, st) != 0) return -1;
+  CK(cudaStreamWaitEvent(st, fk->qdone, 0));
   return 0;
 }
 
@@ -1418,8 +1435,18 @@ KVL_EXPORT int kvl_mla_prefill_cp_begin(const KvlMlaConfig *cfg, const KvlMlaDev
   float2 *cs = reinterpret_cast<float2 *>(ws + L.off[7]);
   CK(cudaMemsetAsync(ws + L.off[8], 0, 4, st));
   CK(launch_rope_table(cs, seq_len, 64, cfg->rope_theta, st));
+  // the two chunks' projections run side by side, the late one on the second stream
+  PrefillFork *fk = get_fork(current_device());
+  if (!fk) return -1;
+  std::lock_guard<std::mutex> lk(fk->mu);
+  CK(cudaEventRecord(fk->fork, st));
+  CK(cudaStreamWaitEvent(fk->s2, fk->fork, 0));
+  if (cp_project_rows(sms, *cfg, W, d_x, k.b0, k.c, d_send + static_cast<size_t>(k.c) * 576, ws, L, fk->s2) != 0)
+    return -1;
+  CK(cudaEventRecord(fk->qdone, fk->s2));
   if (cp_project_rows(sms, *cfg, W, d_x, k.a0, k.c, d_send, ws, L, st) != 0) return -1;
-  return cp_project_rows(sms, *cfg, W, d_x, k.b0, k.c, d_send + static_cast<size_t>(k.c) * 576, ws, L, st);
+  CK(cudaStreamWaitEvent(st, fk->qdone, 0));
+  return 0;
 }
 
 KVL_EXPORT int kvl_mla_prefill_cp_end(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, float *d_out,
@@ -1465,9 +1492,10 @@ KVL_EXPORT int kvl_mla_prefill_cp_end(const KvlMlaConfig *cfg, const KvlMlaDevic
   g.c = kv;
   g.ldc = 4096;
   CK(launch_gemm_pair(g, 256, EPI_BF16, sms, st, "gemm_kvb"));
-  // the late chunk first: its queries see the most keys
-  if (cp_attend_rows(sms, *cfg, W, d_out, seq_len, k.b0, k.c, ws, L, st) != 0) return -1;
-  return cp_attend_rows(sms, *cfg, W, d_out, seq_len, k.a0, k.c, ws, L, st);
+  PrefillFork *fk = get_fork(current_device());
+  if (!fk) return -1;
+  std::lock_guard<std::mutex> lk(fk->mu);
+  return cp_attend(sms, *cfg, W, d_out, k, ws, L, st, fk);
 }
 
 // =================================================================== attend plans
