@@ -494,8 +494,13 @@ class Prefill:
         self.proj, self.attn = prefill_flops(S)
         self.units = self.proj + self.attn
         if self.mode == "cp":
+            import kvl_b200.parallel as PAR
             c = S // (2 * dist.world)
             self.c = c
+            # the rank holds only its own rows: early chunk, then late chunk
+            self.rows = PAR.rank_rows(S, dist.world, dist.rank)
+            self.xr = self.x[torch.from_numpy(self.rows).to(dev)].contiguous()
+            self.out = torch.empty((2 * c, 2048), dtype=torch.float32, device=dev)
             # bf16 rows (NCCL has no 16-bit integer type)
             self.send = torch.empty((2 * c, 576), dtype=torch.bfloat16, device=dev)
             self.recv = torch.empty((dist.world * 2 * c, 576), dtype=torch.bfloat16, device=dev)
@@ -520,11 +525,18 @@ class Prefill:
 
     def _cp_begin(self):
         s = self.torch.cuda.current_stream().cuda_stream
-        rc = self.lib.kvl_mla_prefill_cp_begin(C.byref(self.cfg), C.byref(self.w), self.x.data_ptr(), self.S,
+        rc = self.lib.kvl_mla_prefill_cp_begin(C.byref(self.cfg), C.byref(self.w), self.xr.data_ptr(), self.S,
                                                self.dist.rank, self.dist.world, self.send.data_ptr(),
                                                self.ws.data_ptr(), self.ws.numel(), s)
         if rc != 0:
             raise RuntimeError(self.K.last_error())
+
+    def _gather(self):
+        """The all-gather of the compressed rows (NCCL; a copy on one rank)."""
+        if self.dist.pg:
+            self.dist.pg.all_gather_into_tensor(self.recv, self.send)
+        else:
+            self.recv.copy_(self.send)
 
     def _cp_end(self):
         s = self.torch.cuda.current_stream().cuda_stream
@@ -538,7 +550,7 @@ class Prefill:
         """The launches of one step issued directly (per-kernel CUDA events)."""
         if self.mode == "cp":
             self._cp_begin()
-            self.dist.pg.all_gather_into_tensor(self.recv, self.send)
+            self._gather()
             self._cp_end()
             return
         s = self.torch.cuda.current_stream().cuda_stream
@@ -553,7 +565,7 @@ class Prefill:
         all-gather between them is issued directly."""
         if self.mode == "cp":
             replay_as_graph(self.torch, self, self._cp_begin, "prefill cp begin", "_graph_begin")
-            self.dist.pg.all_gather_into_tensor(self.recv, self.send)
+            self._gather()
             replay_as_graph(self.torch, self, self._cp_end, "prefill cp end", "_graph_end")
             return
         replay_as_graph(self.torch, self, self.step_profiled, "prefill")
@@ -599,24 +611,24 @@ class Prefill:
         import kvl_b200.parallel as PAR
         torch, lib = self.torch, self.lib
         (a0, a1), (b0, b1) = PAR.zigzag_chunks(self.S, self.dist.world)[self.dist.rank]
+        c = self.c
         x_host = torch.from_numpy(self.x.float().cpu().numpy()).pin_memory()
         out_host = torch.empty((self.S, 2048), dtype=torch.float32).pin_memory()
-        xf = torch.empty((self.S, 2048), dtype=torch.float32, device=self.x.device)
-        xb16 = self.x.view(torch.int16)
+        xf = torch.empty((2 * c, 2048), dtype=torch.float32, device=self.x.device)
+        xb16 = self.xr.view(torch.int16)
         stream = torch.cuda.current_stream()
 
         def call():
-            for lo, hi in ((a0, a1), (b0, b1)):
-                xf[lo:hi].copy_(x_host[lo:hi], non_blocking=True)
-                rc = lib.kvl_mla_bf16_rne(xb16[lo:hi].data_ptr(), xf[lo:hi].data_ptr(), (hi - lo) * 2048,
-                                          stream.cuda_stream)
-                if rc != 0:
-                    raise RuntimeError(self.K.last_error())
+            xf[:c].copy_(x_host[a0:a1], non_blocking=True)
+            xf[c:].copy_(x_host[b0:b1], non_blocking=True)
+            rc = lib.kvl_mla_bf16_rne(xb16.data_ptr(), xf.data_ptr(), 2 * c * 2048, stream.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(self.K.last_error())
             self._cp_begin()
-            self.dist.pg.all_gather_into_tensor(self.recv, self.send)
+            self._gather()
             self._cp_end()
-            for lo, hi in ((a0, a1), (b0, b1)):
-                out_host[lo:hi].copy_(self.out[lo:hi], non_blocking=True)
+            out_host[a0:a1].copy_(self.out[:c], non_blocking=True)
+            out_host[b0:b1].copy_(self.out[c:], non_blocking=True)
             stream.synchronize()
         for _ in range(W_steps):
             call()
@@ -1045,8 +1057,13 @@ def dropin_decode_line(K, lib, steps, warmup, cpu=True, lens=(1024, 8192)):
     return res
 
 
-WORKLOADS = {"prefill": Prefill, "decode_q8": DecodeQ8, "decode_q8_step": DecodeQ8Step, "decode_long": DecodeLong,
-             "decode_stack": DecodeStack, "decode_parity": DecodeParity}
+def PrefillCP(torch, K, lib, dist):
+    """Config 2 context-parallel at any N (N = 1: one rank holds both chunks)."""
+    return Prefill(torch, K, lib, dist, mode="cp")
+
+
+WORKLOADS = {"prefill": Prefill, "prefill_cp": PrefillCP, "decode_q8": DecodeQ8, "decode_q8_step": DecodeQ8Step,
+             "decode_long": DecodeLong, "decode_stack": DecodeStack, "decode_parity": DecodeParity}
 
 
 def measure(torch, K, lib, dist, wl, steps, warmup, flush, peaks):

@@ -107,6 +107,12 @@ __device__ __forceinline__ void fadd2(float &a0, float &a1, float b0, float b1) 
   asm("mov.b64 {%0, %1}, %2;" : "=f"(a0), "=f"(a1) : "l"(d));
 }
 
+// Row tile of tm_q and out that holds query tile qt.
+__device__ __forceinline__ int q_slot(const FlashParams &p, int qt) {
+  if (!p.q_compact) return qt;
+  return qt >= p.q_tile0 ? p.lo_t1 - p.lo_t0 + qt - p.q_tile0 : qt - p.lo_t0;
+}
+
 }  // namespace fpre
 
 using namespace fpre;
@@ -170,7 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
         }
         ++qc;
         mbar_arrive_expect_tx(&B->q_full, 3 * kBox);
-        for (int b = 0; b < 3; ++b) tma_load_3d(smem + OFF_Q + b * kBox, &p.tm_q, &B->q_full, 64 * b, head, qt * kT);
+        for (int b = 0; b < 3; ++b) tma_load_3d(smem + OFF_Q + b * kBox, &p.tm_q, &B->q_full, 64 * b, head, q_slot(p, qt) * kT);
         for (int j = 0; j <= qt && ok; ++j, ++kc) {
           const uint32_t s = kc % kKSt;
           if (kc >= static_cast<uint32_t>(kKSt)) {
@@ -378,7 +384,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
       if (named_bar_or(2, 256, bad)) break;
       tc_fence_after();
       const float inv = 1.0f / (xl[r] + xl[128 + r]);
-      __nv_bfloat16 *dst = p.out + (static_cast<size_t>(qrow) * 16 + head) * 128 + 64 * w;
+      __nv_bfloat16 *dst = p.out + (static_cast<size_t>(q_slot(p, qt) * kT + r) * 16 + head) * 128 + 64 * w;
 #pragma unroll 1
       for (int c = 0; c < 2; ++c) {
         float o[32];

@@ -17,8 +17,10 @@ struct FlashParams {
   int q_tile0;
   int lo_t0, lo_t1;    // optional second query range: tiles [lo_t0, lo_t1), lo_t1 <= q_tile0
                        // (0, 0: none); each of its tiles attends keys up to its own end
+  int q_compact;       // 0: query tile t is rows [128 t, 128 t + 128) of tm_q and out;
+                       // 1: tm_q and out hold only the queried tiles, [lo_t0, lo_t1) then [q_tile0, nq)
   float scale_log2;    // softmax scale * log2(e)
-  __nv_bfloat16 *out;  // [S][16][128] bf16
+  __nv_bfloat16 *out;  // [S][16][128] bf16 (q_compact: [queried rows][16][128])
   uint32_t *err;
 };
 

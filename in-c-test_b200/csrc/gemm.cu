@@ -24,6 +24,8 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
+
 #include "gemm.cuh"
 #include "prof.cuh"
 #include "sm100.cuh"
@@ -500,33 +502,45 @@ cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cuda
   return cudaErrorInvalidValue;
 }
 
-// cos/sin of pos * theta^(-2i/dim) for i < dim/2 and pos < rows: the angle
-// arithmetic of src/mla_compressed_state.c:8-22 (double angle, float result).
-__global__ void rope_table_kernel(float2 *cs, int rows, int dim, float theta) {
-  __shared__ double inv_freq_s[128];
-  const int half = dim / 2;
-  // theta^(-2k/dim) once per frequency (half <= 128 is checked by the launcher)
-  for (int k = threadIdx.x; k < half; k += blockDim.x)
-    inv_freq_s[k] = pow(static_cast<double>(theta), -(static_cast<double>(2 * k) / static_cast<double>(dim)));
-  __syncthreads();
+// Inverse frequencies theta^(-2i/dim), i < dim/2, computed on the host (the
+// reference's own expression, src/mla_compressed_state.c:12-13).
+struct RopeFreqs {
+  double inv[128];
+};
+
+// cos/sin of pos * inv_freq[i], one table row per position: row j < split is
+// position pos_a + j, row j >= split position pos_b + j - split (double angle,
+// float result, as src/mla_compressed_state.c:14-16).
+__global__ void rope_table_kernel(float2 *cs, int rows, int half, const __grid_constant__ RopeFreqs fr, int split,
+                                  int pos_a, int pos_b) {
   const long long n = static_cast<long long>(rows) * half;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
-    const int pos = static_cast<int>(i / half), k = static_cast<int>(i % half);
-    const double ang = static_cast<double>(pos) * inv_freq_s[k];
+    const int j = static_cast<int>(i / half), k = static_cast<int>(i % half);
+    const int pos = j < split ? pos_a + j : pos_b + (j - split);
+    const double ang = static_cast<double>(pos) * fr.inv[k];
     double sn, cn;
     sincos(ang, &sn, &cn);
     cs[i] = make_float2(static_cast<float>(cn), static_cast<float>(sn));
   }
 }
 
-cudaError_t launch_rope_table(float2 *cs, int rows, int dim, float theta, cudaStream_t stream) {
-  if (dim <= 0 || dim > 256 || (dim & 1)) return cudaErrorInvalidValue;
-  const long long n = static_cast<long long>(rows) * (dim / 2);
+cudaError_t launch_rope_table_rows(float2 *cs, int rows, int dim, float theta, int split, int pos_a, int pos_b,
+                                   cudaStream_t stream) {
+  if (dim <= 0 || dim > 256 || (dim & 1) || rows <= 0 || pos_a < 0 || pos_b < 0) return cudaErrorInvalidValue;
+  const int half = dim / 2;
+  RopeFreqs fr;
+  for (int k = 0; k < half; ++k)
+    fr.inv[k] = std::pow(static_cast<double>(theta), -(static_cast<double>(2 * k) / static_cast<double>(dim)));
+  const long long n = static_cast<long long>(rows) * half;
   const int grid = static_cast<int>((n + 255) / 256 < 148 * 8 ? (n + 255) / 256 : 148 * 8);
   ProfScope ps("rope_table", stream);
-  rope_table_kernel<<<grid, 256, 0, stream>>>(cs, rows, dim, theta);
+  rope_table_kernel<<<grid, 256, 0, stream>>>(cs, rows, half, fr, split, pos_a, pos_b);
   return cudaGetLastError();
+}
+
+cudaError_t launch_rope_table(float2 *cs, int rows, int dim, float theta, cudaStream_t stream) {
+  return launch_rope_table_rows(cs, rows, dim, theta, rows, 0, 0, stream);
 }
 
 }  // namespace kvl

@@ -35,5 +35,9 @@ cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStrea
 cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream,
                              const char *name = nullptr);
 cudaError_t launch_rope_table(float2 *cs, int rows, int dim, float theta, cudaStream_t stream);
+// Table rows of two position ranges: row j < split is position pos_a + j, row
+// j >= split position pos_b + j - split.
+cudaError_t launch_rope_table_rows(float2 *cs, int rows, int dim, float theta, int split, int pos_a, int pos_b,
+                                   cudaStream_t stream);
 
 }  // namespace kvl

@@ -1136,83 +1136,91 @@ bool cp_chunks(int S, int rank, int world, CpChunks &k) {
   return true;
 }
 
-// kv_a projection of rows [r0, r0 + M) and their RMSNorm + RoPE into dst
-// [M][576] bf16; q_proj with RoPE of the same rows into the workspace q.
-int cp_project_rows(int sms, const KvlMlaConfig &cfg, const DevW &W, const uint16_t *xb, int r0, int M,
-                    uint16_t *dst, uint8_t *ws, const PrefillWs &L, cudaStream_t st) {
-  const uint64_t H = cfg.hidden_size, m = static_cast<uint64_t>(M), R0 = static_cast<uint64_t>(r0);
+// Projections of the rank's 2c rows, held compact (early chunk, then late
+// chunk): the RoPE table of their positions; kv_a, RMSNorm and RoPE into d_send
+// [2c][576] bf16; q_proj with RoPE into the workspace q [2c][16][192].  q_proj
+// runs on the second stream beside the kv_a -> append chain.
+int cp_project(int sms, const KvlMlaConfig &cfg, const DevW &W, const uint16_t *xb, const CpChunks &k,
+               uint16_t *d_send, uint8_t *ws, const PrefillWs &L, cudaStream_t st, PrefillFork *fk) {
+  const int M = 2 * k.c;
+  const uint64_t H = cfg.hidden_size, m = static_cast<uint64_t>(M);
   uint16_t *q = reinterpret_cast<uint16_t *>(ws + L.off[2]);
   float *kva = reinterpret_cast<float *>(ws + L.off[3]);
   float2 *cs = reinterpret_cast<float2 *>(ws + L.off[7]);
   uint32_t *err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
+  CK(cudaMemsetAsync(err, 0, 4, st));
+  CK(cudaEventRecord(fk->fork, st));
+  CK(cudaStreamWaitEvent(fk->s2, fk->fork, 0));
   const int kva_bn = (M + 127) / 128 * 3 * 2 < sms ? 64 : 192;
   GemmParams g;
   memset(&g, 0, sizeof g);
   g.err = err;
-  if (!bf16_map(&g.tm_a, xb + R0 * H, H, m, H * 2, 128) || !bf16_map(&g.tm_b, W.kva, H, 576, H * 2, kva_bn)) {
+  if (!bf16_map(&g.tm_a, xb, H, m, H * 2, 128) || !bf16_map(&g.tm_b, W.kva, H, 576, H * 2, kva_bn)) {
     set_err("prefill (context parallel): tensor map (kv_a_proj)");
     return -1;
   }
   g.M = M;
   g.K = static_cast<int>(H);
   g.N = 576;
-  g.c = kva + R0 * 576;
+  g.c = kva;
   g.ldc = 576;
   CK(launch_gemm(g, kva_bn, EPI_F32, sms, st, "gemm_kva"));
-  CK(append_rows_bf16(dst, kva + R0 * 576, W.kvan, cs + R0 * 32, M, cfg.rms_eps, st));
   GemmParams gq;
   memset(&gq, 0, sizeof gq);
   gq.err = err;
-  if (!bf16_map(&gq.tm_a, xb + R0 * H, H, m, H * 2, 128) || !bf16_map(&gq.tm_b, W.q, H, 16 * 192, H * 2, 128)) {
+  if (!bf16_map(&gq.tm_a, xb, H, m, H * 2, 128) || !bf16_map(&gq.tm_b, W.q, H, 16 * 192, H * 2, 128)) {
     set_err("prefill (context parallel): tensor map (q_proj)");
     return -1;
   }
   gq.M = M;
   gq.N = 16 * 192;
   gq.K = static_cast<int>(H);
-  gq.c = q + R0 * 16 * 192;
+  gq.c = q;
   gq.ldc = 16 * 192;
-  gq.rope_cs = cs + R0 * 32;
-  CK(launch_gemm_pair(gq, 256, EPI_QROPE, sms, st, "gemm_q"));
+  gq.rope_cs = cs;
+  CK(launch_rope_table_rows(cs, M, 64, cfg.rope_theta, k.c, k.a0, k.b0, fk->s2));
+  CK(cudaEventRecord(fk->rope, fk->s2));
+  CK(launch_gemm_pair(gq, 256, EPI_QROPE, sms, fk->s2, "gemm_q"));
+  CK(cudaEventRecord(fk->qdone, fk->s2));
+  CK(cudaStreamWaitEvent(st, fk->rope, 0));
+  CK(append_rows_bf16(d_send, kva, W.kvan, cs, M, cfg.rms_eps, st));
+  CK(cudaStreamWaitEvent(st, fk->qdone, 0));
   return 0;
 }
 
-// o_proj of the rows [r0, r0 + M): out = o Wo^T, fp32.
-int cp_oproj_rows(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, int r0, int M, uint8_t *ws,
-                  const PrefillWs &L, cudaStream_t st) {
-  const uint64_t H = cfg.hidden_size, m = static_cast<uint64_t>(M), R0 = static_cast<uint64_t>(r0);
-  uint16_t *o = reinterpret_cast<uint16_t *>(ws + L.off[6]);
-  GemmParams g;
-  memset(&g, 0, sizeof g);
-  g.err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
-  if (!bf16_map(&g.tm_a, o + R0 * 2048, 2048, m, 2048 * 2, 128) || !bf16_map(&g.tm_b, W.o, 2048, H, 2048 * 2, 128)) {
-    set_err("prefill (context parallel): tensor map (o_proj)");
-    return -1;
-  }
-  g.M = M;
-  g.N = static_cast<int>(H);
-  g.K = 2048;
-  g.c = d_out + R0 * H;
-  g.ldc = static_cast<int>(H);
-  CK(launch_gemm_pair(g, 256, EPI_F32, sms, st, "gemm_o"));
-  return 0;
-}
-
-// Causal attention of a rank's two query chunks in one flash launch (the late
-// chunk as the kernel's main query range over keys [0, its end), the early one
-// as its second range), so both chunks' (head, query tile) items share the
-// CTAs; then o_proj of the two chunks, the early one on the second stream.
-int cp_attend(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, const CpChunks &k, uint8_t *ws,
-              const PrefillWs &L, cudaStream_t st, PrefillFork *fk) {
-  const uint64_t s = static_cast<uint64_t>(k.b0 + k.c);
+// The gathered rows placed in prompt order for the keys the rank's chunks see
+// ([0, end of its late chunk)), K/V expanded with kv_b, the causal attention
+// of both chunks in one flash launch (the late chunk as the kernel's main query
+// range, the early one as its second range, queries and output compact), and
+// o_proj of the 2c rows into d_out [2c][H] fp32.
+int cp_attend(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, const uint16_t *d_recv, int world,
+              const CpChunks &k, uint8_t *ws, const PrefillWs &L, cudaStream_t st) {
+  const int kmax = k.b0 + k.c, M = 2 * k.c;
+  const uint64_t H = cfg.hidden_size, s = static_cast<uint64_t>(kmax), m = static_cast<uint64_t>(M);
   uint16_t *q = reinterpret_cast<uint16_t *>(ws + L.off[2]);
   uint16_t *pool = reinterpret_cast<uint16_t *>(ws + L.off[4]);
   uint16_t *kv = reinterpret_cast<uint16_t *>(ws + L.off[5]);
   uint16_t *o = reinterpret_cast<uint16_t *>(ws + L.off[6]);
+  uint32_t *err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
+  CK(cp_place_rows(pool, d_recv, k.c, world, kmax, st));
+  // kv = latent Wkvb^T for the keys [0, kmax), bf16 [kmax][16][256]
+  GemmParams g;
+  memset(&g, 0, sizeof g);
+  g.err = err;
+  if (!bf16_map(&g.tm_a, pool, 512, s, 576 * 2, 128) || !bf16_map(&g.tm_b, W.kvb, 512, 4096, 512 * 2, 128)) {
+    set_err("prefill (context parallel): tensor map (kv_b_proj)");
+    return -1;
+  }
+  g.M = kmax;
+  g.N = 4096;
+  g.K = 512;
+  g.c = kv;
+  g.ldc = 4096;
+  CK(launch_gemm_pair(g, 256, EPI_BF16, sms, st, "gemm_kvb"));
   FlashParams f;
   memset(&f, 0, sizeof f);
   {
-    const uint64_t qd[3] = {192, 16, s}, qs[2] = {192 * 2, 16 * 192 * 2};
+    const uint64_t qd[3] = {192, 16, m}, qs[2] = {192 * 2, 16 * 192 * 2};
     const uint64_t kd[3] = {256, 16, s}, ks[2] = {256 * 2, 16 * 256 * 2};
     const uint32_t box[3] = {64, 1, 128};
     if (!make_tmap_3d(&f.tm_q, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, qd, qs, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
@@ -1223,20 +1231,26 @@ int cp_attend(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, con
     }
   }
   f.kr_col = 512;
-  f.S = k.b0 + k.c;
+  f.S = kmax;
   f.q_tile0 = k.b0 / 128;
   f.lo_t0 = k.a0 / 128;
   f.lo_t1 = (k.a0 + k.c) / 128;
+  f.q_compact = 1;
   f.scale_log2 = (1.0f / sqrtf(192.0f)) * 1.4426950408889634f;
   f.out = reinterpret_cast<__nv_bfloat16 *>(o);
-  f.err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
+  f.err = err;
   CK(launch_flash_prefill(f, sms, st));
-  CK(cudaEventRecord(fk->fork, st));
-  CK(cudaStreamWaitEvent(fk->s2, fk->fork, 0));
-  if (cp_oproj_rows(sms, cfg, W, d_out, k.a0, k.c, ws, L, fk->s2) != 0) return -1;
-  CK(cudaEventRecord(fk->qdone, fk->s2));
-  if (cp_oproj_rows(sms, cfg, W, d_out, k.b0, k.c, ws, L, st) != 0) return -1;
-  CK(cudaStreamWaitEvent(st, fk->qdone, 0));
+  // out = o Wo^T, fp32 [2c][H]
+  if (!bf16_map(&g.tm_a, o, 2048, m, 2048 * 2, 128) || !bf16_map(&g.tm_b, W.o, 2048, H, 2048 * 2, 128)) {
+    set_err("prefill (context parallel): tensor map (o_proj)");
+    return -1;
+  }
+  g.M = M;
+  g.N = static_cast<int>(H);
+  g.K = 2048;
+  g.c = d_out;
+  g.ldc = static_cast<int>(H);
+  CK(launch_gemm_pair(g, 256, EPI_F32, sms, st, "gemm_o"));
   return 0;
 }
 
@@ -1429,24 +1443,12 @@ KVL_EXPORT int kvl_mla_prefill_cp_begin(const KvlMlaConfig *cfg, const KvlMlaDev
     set_err("context-parallel prefill: d_x and d_send must be 16-byte aligned device pointers");
     return -1;
   }
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  uint8_t *ws = static_cast<uint8_t *>(d_workspace);
   DevW W{w->q_proj, w->kv_a_proj, w->kv_a_norm, w->kv_b_proj, w->o_proj};
-  float2 *cs = reinterpret_cast<float2 *>(ws + L.off[7]);
-  CK(cudaMemsetAsync(ws + L.off[8], 0, 4, st));
-  CK(launch_rope_table(cs, seq_len, 64, cfg->rope_theta, st));
-  // the two chunks' projections run side by side, the late one on the second stream
   PrefillFork *fk = get_fork(current_device());
   if (!fk) return -1;
   std::lock_guard<std::mutex> lk(fk->mu);
-  CK(cudaEventRecord(fk->fork, st));
-  CK(cudaStreamWaitEvent(fk->s2, fk->fork, 0));
-  if (cp_project_rows(sms, *cfg, W, d_x, k.b0, k.c, d_send + static_cast<size_t>(k.c) * 576, ws, L, fk->s2) != 0)
-    return -1;
-  CK(cudaEventRecord(fk->qdone, fk->s2));
-  if (cp_project_rows(sms, *cfg, W, d_x, k.a0, k.c, d_send, ws, L, st) != 0) return -1;
-  CK(cudaStreamWaitEvent(st, fk->qdone, 0));
-  return 0;
+  return cp_project(sms, *cfg, W, d_x, k, d_send, static_cast<uint8_t *>(d_workspace), L,
+                    static_cast<cudaStream_t>(stream), fk);
 }
 
 KVL_EXPORT int kvl_mla_prefill_cp_end(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, float *d_out,
@@ -1460,42 +1462,9 @@ KVL_EXPORT int kvl_mla_prefill_cp_end(const KvlMlaConfig *cfg, const KvlMlaDevic
     set_err("context-parallel prefill: d_out and d_recv must be 16-byte aligned device pointers");
     return -1;
   }
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  uint8_t *ws = static_cast<uint8_t *>(d_workspace);
   DevW W{w->q_proj, w->kv_a_proj, w->kv_a_norm, w->kv_b_proj, w->o_proj};
-  uint16_t *pool = reinterpret_cast<uint16_t *>(ws + L.off[4]);
-  uint16_t *kv = reinterpret_cast<uint16_t *>(ws + L.off[5]);
-  // the keys this rank's chunks see: [0, end of its late chunk)
-  const int kmax = k.b0 + k.c;
-  const size_t row_b = 576 * 2, chunk_b = static_cast<size_t>(k.c) * row_b;
-  for (int p = 0; p < world; ++p) {
-    const uint8_t *src = reinterpret_cast<const uint8_t *>(d_recv) + 2 * static_cast<size_t>(p) * chunk_b;
-    const int pa = p * k.c, pb = (2 * world - 1 - p) * k.c;
-    if (pa < kmax)
-      CK(cudaMemcpyAsync(pool + static_cast<size_t>(pa) * 576, src, chunk_b, cudaMemcpyDeviceToDevice, st));
-    if (pb < kmax)
-      CK(cudaMemcpyAsync(pool + static_cast<size_t>(pb) * 576, src + chunk_b, chunk_b, cudaMemcpyDeviceToDevice,
-                         st));
-  }
-  // kv = latent Wkvb^T for the keys [0, kmax), bf16 [kmax][16][256]
-  GemmParams g;
-  memset(&g, 0, sizeof g);
-  g.err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
-  if (!bf16_map(&g.tm_a, pool, 512, static_cast<uint64_t>(kmax), 576 * 2, 128) ||
-      !bf16_map(&g.tm_b, W.kvb, 512, 4096, 512 * 2, 128)) {
-    set_err("prefill (context parallel): tensor map (kv_b_proj)");
-    return -1;
-  }
-  g.M = kmax;
-  g.N = 4096;
-  g.K = 512;
-  g.c = kv;
-  g.ldc = 4096;
-  CK(launch_gemm_pair(g, 256, EPI_BF16, sms, st, "gemm_kvb"));
-  PrefillFork *fk = get_fork(current_device());
-  if (!fk) return -1;
-  std::lock_guard<std::mutex> lk(fk->mu);
-  return cp_attend(sms, *cfg, W, d_out, k, ws, L, st, fk);
+  return cp_attend(sms, *cfg, W, d_out, d_recv, world, k, static_cast<uint8_t *>(d_workspace), L,
+                   static_cast<cudaStream_t>(stream));
 }
 
 // =================================================================== attend plans

@@ -18,6 +18,10 @@ cudaError_t append_q8(int8_t *lat8, float *lscale, uint16_t *rope16, long long r
 // Prefill rows [0, n) of a bf16 [n][576] pool (Kimi shape), RoPE from a [n][32] cos/sin table.
 cudaError_t append_rows_bf16(uint16_t *pool, const float *ka, const uint16_t *norm_w, const float2 *cs, int n,
                              float eps, cudaStream_t s);
+// Context-parallel prefill: gathered compressed rows [world][2][c][576] bf16
+// (rank p: chunk p, then chunk 2 world - 1 - p) -> pool rows [0, kmax) in prompt
+// order; both 16-byte aligned.
+cudaError_t cp_place_rows(uint16_t *pool, const uint16_t *recv, int c, int world, int kmax, cudaStream_t s);
 cudaError_t absorb(float *qabs, const float *q, const uint16_t *kvb, int n, int NH, int DN, int DV, int DR, int R,
                    int pos0, float theta, cudaStream_t s, const int *pos_of = nullptr);
 cudaError_t vup(float *ho, const float *mix, const uint16_t *kvb, int n, int NH, int DN, int DV, int R,

@@ -62,8 +62,15 @@ def zigzag_chunks(seq_len: int, world: int) -> list[tuple[tuple[int, int], tuple
     return [((r * c, (r + 1) * c), ((2 * world - 1 - r) * c, (2 * world - r) * c)) for r in range(world)]
 
 
+def rank_rows(seq_len: int, world: int, rank: int) -> np.ndarray:
+    """Prompt rows a rank holds, in the order of its compact buffers (the d_x
+    and d_out of kvl_mla_prefill_cp_begin / _end): its early chunk, then its
+    late chunk."""
+    (a0, a1), (b0, b1) = zigzag_chunks(seq_len, world)[rank]
+    return np.concatenate([np.arange(a0, a1), np.arange(b0, b1)])
+
+
 def gathered_row_order(seq_len: int, world: int) -> np.ndarray:
     """Prompt row held at each row of the all-gathered buffer [world][2c]: rank
     order, each rank's early chunk then its late chunk."""
-    return np.concatenate([np.concatenate([np.arange(*a), np.arange(*b)])
-                           for a, b in zigzag_chunks(seq_len, world)])
+    return np.concatenate([rank_rows(seq_len, world, r) for r in range(world)])

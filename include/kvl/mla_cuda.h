@@ -234,13 +234,14 @@ int kvl_mla_prefill_dev(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, f
  *     rows into the workspace;
  *   the caller all-gathers every rank's d_send into d_recv [world][2c][576] in
  *     rank order (one all-gather of 2c * 1152 bytes per rank, e.g. NCCL);
- *   kvl_mla_prefill_cp_end: places the gathered rows, expands K/V with kv_b for
- *     the keys its chunks see, runs the causal attention of its queries and
- *     o_proj into its rows of d_out.
- * d_x [seq_len][H] bf16 (only the rank's rows are read), d_out [seq_len][H]
- * fp32 (only the rank's rows are written); both calls take the same workspace
- * of kvl_mla_prefill_workspace_bytes(cfg, seq_len) bytes (256-byte aligned),
- * which must not be reused between them.  Production head shape only. */
+ *   kvl_mla_prefill_cp_end: places the gathered rows in prompt order, expands
+ *     K/V with kv_b for the keys its chunks see, runs the causal attention of
+ *     its queries (both chunks in one launch) and o_proj into d_out.
+ * A rank holds only its own rows: d_x [2c][H] bf16 is the rank's tokens (chunk
+ * rank, then chunk 2 * world - 1 - rank) and d_out [2c][H] fp32 receives their
+ * outputs in the same order.  Both calls take the same workspace of
+ * kvl_mla_prefill_workspace_bytes(cfg, seq_len) bytes (256-byte aligned), which
+ * must not be reused between them.  Production head shape only. */
 int kvl_mla_prefill_cp_begin(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, const uint16_t *d_x,
                              int seq_len, int rank, int world, uint16_t *d_send, void *d_workspace,
                              size_t workspace_bytes, void *stream);

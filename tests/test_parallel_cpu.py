@@ -113,6 +113,13 @@ def test_zigzag_chunks_partition_and_balance():
         assert max(work) - min(work) <= (S_len // (2 * world)) ** 2
         order = gathered_row_order(S_len, world)
         assert sorted(order.tolist()) == list(range(S_len))
+        # the row map of the device placement (cp_place_rows): prompt row t of
+        # chunk j = t // c sits at gathered row 2j c + t % c (j < world) or
+        # (2 (2 world - 1 - j) + 1) c + t % c
+        c = S_len // (2 * world)
+        src = [(2 * (t // c) if t // c < world else 2 * (2 * world - 1 - t // c) + 1) * c + t % c
+               for t in range(S_len)]
+        assert (order[src] == np.arange(S_len)).all()
     with pytest.raises(ValueError):
         zigzag_chunks(100, 3)
 
@@ -137,7 +144,7 @@ def _cp_rank_main(rank, world, port, seq_len, result_q):
     import torch.distributed as dist
     import kvl_b200.kvl_mla as K
     import kvl_b200.synth as S
-    from kvl_b200.parallel import gathered_row_order, zigzag_chunks
+    from kvl_b200.parallel import gathered_row_order, rank_rows
     from oracle.oracle import Oracle, cfg_of
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
@@ -148,8 +155,7 @@ def _cp_rank_main(rank, world, port, seq_len, result_q):
         w = K.random_weights(K.make_config(*_CP_SHAPE), 61, 0.05)
         x = S.normal(61, S.S_X, seq_len * H, 1.0).reshape(seq_len, H)
         orc = Oracle()
-        (a0, a1), (b0, b1) = zigzag_chunks(seq_len, world)[rank]
-        mine = list(range(a0, a1)) + list(range(b0, b1))
+        mine = [int(t) for t in rank_rows(seq_len, world, rank)]
         send = np.zeros((len(mine), R + DR), np.float32)
         for i, t in enumerate(mine):
             lat, rp = orc.append_f32(x[t], t, cfg, w.arrays[1], w.arrays[2])

@@ -1,8 +1,9 @@
 """Context-parallel prefill (kvl_mla_prefill_cp_begin / kvl_mla_prefill_cp_end)
 on one GPU: every rank of a world of 2, 4 or 8 runs in turn with its own
-workspace, the ranks' compressed rows are concatenated in rank order (what the
-all-gather between the two calls produces), and the rows each rank writes
-together form the prompt's output.  Checked against the reference's own
+workspace and only its own rows (chunk r, then chunk 2 world - 1 - r), the
+ranks' compressed rows are concatenated in rank order (what the all-gather
+between the two calls produces), and the output rows each rank returns,
+scattered back to their prompt positions, form the prompt's output.  Checked against the reference's own
 streaming prefill (src/mla_prefill_streaming.c:78-206, oracle/_ref) within
 rel-L2 <= 1e-2 and max-abs <= 2e-2, and against the single-GPU device prefill
 (kvl_mla_prefill_dev), which uses the same kernels over other row ranges.
@@ -22,24 +23,32 @@ SHAPE = (2048, 16, 128, 64, 128, 512, 1e-5, 50000.0)
 
 
 def _cp_prefill(K, torch, cfg, dw, xb, Sq, world):
+    from kvl_b200.parallel import zigzag_chunks
     lib = K.load()
     dev = xb.device
     nbytes = lib.kvl_mla_prefill_workspace_bytes(C.byref(cfg), Sq)
     c = Sq // (2 * world)
-    out = torch.full((Sq, cfg.hidden_size), float("nan"), dtype=torch.float32, device=dev)
+    chunks = zigzag_chunks(Sq, world)
+    xs = [torch.cat([xb[a0:a1], xb[b0:b1]]).contiguous() for (a0, a1), (b0, b1) in chunks]
+    outs = [torch.full((2 * c, cfg.hidden_size), float("nan"), dtype=torch.float32, device=dev) for _ in range(world)]
     wss = [torch.empty(nbytes, dtype=torch.uint8, device=dev) for _ in range(world)]
     sends = [torch.empty((2 * c, 576), dtype=torch.int16, device=dev) for _ in range(world)]
     for r in range(world):
-        rc = lib.kvl_mla_prefill_cp_begin(C.byref(cfg), C.byref(dw), xb.data_ptr(), Sq, r, world, sends[r].data_ptr(),
-                                          wss[r].data_ptr(), nbytes, None)
+        rc = lib.kvl_mla_prefill_cp_begin(C.byref(cfg), C.byref(dw), xs[r].data_ptr(), Sq, r, world,
+                                          sends[r].data_ptr(), wss[r].data_ptr(), nbytes, None)
         assert rc == 0, K.last_error()
     recv = torch.cat(sends)
     for r in range(world):
-        rc = lib.kvl_mla_prefill_cp_end(C.byref(cfg), C.byref(dw), out.data_ptr(), Sq, r, world, recv.data_ptr(),
-                                        wss[r].data_ptr(), nbytes, None)
+        rc = lib.kvl_mla_prefill_cp_end(C.byref(cfg), C.byref(dw), outs[r].data_ptr(), Sq, r, world,
+                                        recv.data_ptr(), wss[r].data_ptr(), nbytes, None)
         assert rc == 0, K.last_error()
     torch.cuda.synchronize()
-    return out.cpu().numpy()
+    out = np.full((Sq, cfg.hidden_size), np.nan, dtype=np.float32)
+    for ((a0, a1), (b0, b1)), o in zip(chunks, outs):
+        o = o.cpu().numpy()
+        out[a0:a1] = o[:c]
+        out[b0:b1] = o[c:]
+    return out
 
 
 @pytest.mark.parametrize("Sq,world", [(1024, 2), (1024, 4), (4096, 8)])
