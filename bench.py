@@ -1176,8 +1176,8 @@ def main():
             r2, _ = roofline_for(w2, prof2, peaks, peak_kind)
             extras[name] = {"metric": w2.metric, "value": w2.value(ms2), "unit": w2.unit, "ms_per_step": ms2,
                             "dtype": getattr(w2, "dtype", "bf16"),
-                            "frac_of_peak": w2.value(ms2) / (peaks["hbm_gbs"] if w2.unit == "GB/s" else
-                                                             peaks["bf16_tflops"] * dist.world),
+                            "frac_of_peak": w2.value(ms2) / ((peaks["hbm_gbs"] if w2.unit == "GB/s" else
+                                                              peaks["bf16_tflops"]) * dist.world),
                             "roofline": r2,
                             "config": w2.config(), "gpu_launches_per_step": int(l2),
                             "kernels": {k: {"ms_total": v[0], "launches": v[1]} for k, v in prof2.items()}}
