@@ -31,6 +31,9 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
+#include <vector>
+
 #include "flash_prefill.cuh"
 #include "prof.cuh"
 #include "sm100.cuh"
@@ -64,16 +67,68 @@ constexpr uint32_t kSmem = OFF_BAR + sizeof(Bars) + 1024;
 static_assert(kSmem <= 232448, "shared memory budget");
 constexpr uint32_t kTmemCols = 512;
 
-// Item k of the CTA: snake order over the items sorted by decreasing cost --
-// the query tiles of [q_tile0, nq) from the last down, then those of the
-// optional lower range [lo_t0, lo_t1) from its last down (n_hi tiles above it).
-__device__ __forceinline__ bool item_of(int k, int grid, int cta, int n_items, int nq, int n_hi, int lo_t1,
-                                        int &head, int &qt) {
+// A work unit: key tiles [k0, k1) of query tile qt and one head; pos is its
+// index in the unit order (the slot of its partial result when cut).
+struct Unit {
+  int head, qt, k0, k1, pos;
+  bool cut;
+};
+
+// Query tile groups in the unit order: the tiles of [q_tile0, nq) from the
+// last down, then those of the optional lower range [lo_t0, lo_t1) from its
+// last down (n_hi tiles above it) -- decreasing key counts within each range.
+__host__ __device__ __forceinline__ int group_tile(const FlashParams &p, int nq, int n_hi, int t) {
+  return t < n_hi ? nq - 1 - t : p.lo_t1 - 1 - (t - n_hi);
+}
+
+// Pieces of an item with n key tiles.
+__host__ __device__ __forceinline__ int pieces_of(int n, int kpiece) {
+  return kpiece > 0 ? (n + kpiece - 1) / kpiece : 1;
+}
+
+__host__ __device__ __forceinline__ int unit_count(const FlashParams &p, int nq, int n_hi, int kpiece) {
+  const int groups = n_hi + p.lo_t1 - p.lo_t0;
+  if (kpiece <= 0) return groups * 16;
+  int n = 0;
+  for (int t = 0; t < groups; ++t) n += 16 * pieces_of(group_tile(p, nq, n_hi, t) + 1, kpiece);
+  return n;
+}
+
+// Unit pos: within a query tile group the units are piece-major (piece, head).
+__device__ __forceinline__ void unit_at(const FlashParams &p, int nq, int n_hi, int pos, Unit &u) {
+  u.pos = pos;
+  if (p.kpiece <= 0) {
+    u.qt = group_tile(p, nq, n_hi, pos / 16);
+    u.head = pos % 16;
+    u.k0 = 0;
+    u.k1 = u.qt + 1;
+    u.cut = false;
+    return;
+  }
+  int base = 0;
+  for (int t = 0;; ++t) {
+    const int qt = group_tile(p, nq, n_hi, t), np = pieces_of(qt + 1, p.kpiece);
+    if (pos < base + 16 * np) {
+      const int in = pos - base, piece = in / 16;
+      u.qt = qt;
+      u.head = in % 16;
+      u.k0 = piece * p.kpiece;
+      u.k1 = np > 1 ? min(qt + 1, u.k0 + p.kpiece) : qt + 1;
+      if (np == 1) u.k0 = 0;
+      u.cut = np > 1;
+      return;
+    }
+    base += 16 * np;
+  }
+}
+
+// Unit k of the CTA: snake order over the units (sorted by decreasing cost
+// within each range).
+__device__ __forceinline__ bool item_of(const FlashParams &p, int k, int nq, int n_hi, int n_units, Unit &u) {
+  const int grid = gridDim.x, cta = blockIdx.x;
   const int pos = (k & 1) ? (k + 1) * grid - 1 - cta : k * grid + cta;
-  if (pos >= n_items) return false;
-  const int t = pos / 16;
-  qt = t < n_hi ? nq - 1 - t : lo_t1 - 1 - (t - n_hi);
-  head = pos % 16;
+  if (pos >= n_units) return false;
+  unit_at(p, nq, n_hi, pos, u);
   return true;
 }
 
@@ -129,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
   volatile int *abort = &B->abort;
   const int nq = (p.S + kT - 1) / kT;
   const int n_hi = nq - p.q_tile0;
-  const int n_items = (n_hi + p.lo_t1 - p.lo_t0) * 16;  // query tiles [q_tile0, nq) ++ [lo_t0, lo_t1)
+  const int n_units = unit_count(p, nq, n_hi, p.kpiece);  // query tiles [q_tile0, nq) ++ [lo_t0, lo_t1)
 
   if (threadIdx.x == 0) {
     mbar_init(&B->q_full, 1);
@@ -167,8 +222,8 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
       // later, and S_{g-3} completed before S_{g-2}, which was waited for.
       uint32_t kc = 0, qc = 0;  // kc: key tiles issued = global S tile index
       bool ok = true;
-      int head, qt;
-      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, n_hi, p.lo_t1, head, qt); ++k) {
+      Unit u;
+      for (int k = 0; ok && item_of(p, k, nq, n_hi, n_units, u); ++k) {
         if (kc > 0) {
           const uint32_t gl = kc - 1;  // last S of the previous item
           ok = mbar_wait(&B->s_full[gl % kSBuf], (gl / kSBuf) & 1, abort, p.err, ERR_TIMEOUT_EMPTY);
@@ -176,8 +231,9 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
         }
         ++qc;
         mbar_arrive_expect_tx(&B->q_full, 3 * kBox);
-        for (int b = 0; b < 3; ++b) tma_load_3d(smem + OFF_Q + b * kBox, &p.tm_q, &B->q_full, 64 * b, head, q_slot(p, qt) * kT);
-        for (int j = 0; j <= qt && ok; ++j, ++kc) {
+        for (int b = 0; b < 3; ++b)
+          tma_load_3d(smem + OFF_Q + b * kBox, &p.tm_q, &B->q_full, 64 * b, u.head, q_slot(p, u.qt) * kT);
+        for (int j = u.k0; j < u.k1 && ok; ++j, ++kc) {
           const uint32_t s = kc % kKSt;
           if (kc >= static_cast<uint32_t>(kKSt)) {
             const uint32_t gp = kc - kKSt;  // the tile that last used this stage
@@ -186,8 +242,8 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
           }
           uint8_t *kd = smem + OFF_K + s * 3 * kBox;
           mbar_arrive_expect_tx(&B->k_full[s], 3 * kBox);
-          tma_load_3d(kd, &p.tm_kv, &B->k_full[s], 0, head, j * kT);
-          tma_load_3d(kd + kBox, &p.tm_kv, &B->k_full[s], 64, head, j * kT);
+          tma_load_3d(kd, &p.tm_kv, &B->k_full[s], 0, u.head, j * kT);
+          tma_load_3d(kd + kBox, &p.tm_kv, &B->k_full[s], 64, u.head, j * kT);
           tma_load_2d(kd + 2 * kBox, &p.tm_kr, &B->k_full[s], p.kr_col, j * kT);
         }
       }
@@ -204,9 +260,9 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
     if (lane == 0) {
       uint32_t vc = 0;
       bool ok = true;
-      int head, qt;
-      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, n_hi, p.lo_t1, head, qt); ++k) {
-        for (int j = 0; j <= qt && ok; ++j, ++vc) {
+      Unit u;
+      for (int k = 0; ok && item_of(p, k, nq, n_hi, n_units, u); ++k) {
+        for (int j = u.k0; j < u.k1 && ok; ++j, ++vc) {
           // the V of tile g is free once P_g V_g has completed (pv_done of tile g)
           const uint32_t s = vc % kVSt;
           if (vc >= static_cast<uint32_t>(kVSt)) {
@@ -216,8 +272,8 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
           }
           uint8_t *vd = smem + OFF_V + s * 2 * kBox;
           mbar_arrive_expect_tx(&B->v_full[s], 2 * kBox);
-          tma_load_3d(vd, &p.tm_kv, &B->v_full[s], 128, head, j * kT);
-          tma_load_3d(vd + kBox, &p.tm_kv, &B->v_full[s], 192, head, j * kT);
+          tma_load_3d(vd, &p.tm_kv, &B->v_full[s], 128, u.head, j * kT);
+          tma_load_3d(vd + kBox, &p.tm_kv, &B->v_full[s], 192, u.head, j * kT);
         }
       }
       if (!ok) {
@@ -239,9 +295,9 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
       const uint64_t v_desc = smem_desc(s_base + OFF_V, kBox, 1024, LAYOUT_SW128);
       uint32_t tc = 0, kc = 0, vc = 0;  // S tiles, K stages, V stages consumed
       bool ok = true;
-      int head, qt;
-      for (int k = 0; ok && item_of(k, gridDim.x, blockIdx.x, n_items, nq, n_hi, p.lo_t1, head, qt); ++k) {
-        const int n = qt + 1;
+      Unit u;
+      for (int k = 0; ok && item_of(p, k, nq, n_hi, n_units, u); ++k) {
+        const int n = u.k1 - u.k0;
         ok = mbar_wait(&B->q_full, k & 1, abort, p.err, ERR_TIMEOUT_FULL);
         auto issue_s = [&](int j) -> bool {
           // S_j = Q K_j^T into buffer (tc + j) % 3
@@ -291,13 +347,14 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
     const uint32_t o_col = tmem + lane_base + kColO + 64 * w;
     const float sl = p.scale_log2;
     uint32_t g = 0;  // S tiles consumed (same sequence as the MMA issuer's)
-    int head, qt;
+    Unit u;
     bool bad = false;
-    for (int k = 0; !bad && item_of(k, gridDim.x, blockIdx.x, n_items, nq, n_hi, p.lo_t1, head, qt); ++k) {
-      const int n = qt + 1;
-      const int qrow = qt * kT + r;
+    for (int k = 0; !bad && item_of(p, k, nq, n_hi, n_units, u); ++k) {
+      const int n = u.k1 - u.k0;
+      const int qrow = u.qt * kT + r;
       float m = -INFINITY, l = 0.f;
-      for (int j = 0; j < n; ++j, ++g) {
+      for (int jj = 0; jj < n; ++jj, ++g) {
+        const int j = u.k0 + jj;  // key tile
         const uint32_t b = g % kSBuf;
         const uint32_t s_col = tmem + lane_base + 128 * b;
         bad = !mbar_wait(&B->s_full[b], (g / kSBuf) & 1, abort, p.err, ERR_TIMEOUT_MMA);
@@ -308,7 +365,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
           tmem_ld32(s_col + 64 * w + 32, s + 32);
           tmem_wait_ld();
         }
-        if (j == n - 1) {
+        if (j == u.qt) {
           // diagonal tile and sequence end: key j*128 + 64w + c is visible iff c <= lim
           const int lim = min(qrow, p.S - 1) - j * kT - 64 * w;
 #pragma unroll
@@ -331,7 +388,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
         if (__any_sync(0xffffffffu, need)) {
           const float mn = fmaxf(m, mx);
           const float alpha = (m == -INFINITY) ? 0.f : ex2((m - mn) * sl);
-          if (j > 0) {
+          if (jj > 0) {
             // this group's half of the O row, once P_{j-1} V_{j-1} (and so every
             // earlier P V) has landed.  Per-buffer barriers keep the parity
             // unambiguous: s_full of tile g implies P V of tile g - 3 is done,
@@ -383,22 +440,40 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
       xl[w * 128 + r] = l;
       if (named_bar_or(2, 256, bad)) break;
       tc_fence_after();
-      const float inv = 1.0f / (xl[r] + xl[128 + r]);
-      __nv_bfloat16 *dst = p.out + (static_cast<size_t>(q_slot(p, qt) * kT + r) * 16 + head) * 128 + 64 * w;
+      const float lsum = xl[r] + xl[128 + r];
+      const float inv = 1.0f / lsum;
+      if (u.cut) {
+        // a piece of a cut item: O / l in fp32 and log2 of l at the exp2 scale
+        // of the scores, for the combine kernel
+        float *dst = p.part_o + (static_cast<size_t>(u.pos) * kT + r) * 128 + 64 * w;
 #pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        float o[32];
-        tmem_ld32(o_col + 32 * c, o);
-        tmem_wait_ld();
-        if (qrow < p.S) {
+        for (int c = 0; c < 2; ++c) {
+          float o[32];
+          tmem_ld32(o_col + 32 * c, o);
+          tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; i += 8) {
-            uint4 v;
-            v.x = pack_bf16(o[i] * inv, o[i + 1] * inv);
-            v.y = pack_bf16(o[i + 2] * inv, o[i + 3] * inv);
-            v.z = pack_bf16(o[i + 4] * inv, o[i + 5] * inv);
-            v.w = pack_bf16(o[i + 6] * inv, o[i + 7] * inv);
-            *reinterpret_cast<uint4 *>(dst + 32 * c + i) = v;
+          for (int i = 0; i < 32; i += 4)
+            *reinterpret_cast<float4 *>(dst + 32 * c + i) =
+                make_float4(o[i] * inv, o[i + 1] * inv, o[i + 2] * inv, o[i + 3] * inv);
+        }
+        if (w == 0) p.part_lse[static_cast<size_t>(u.pos) * kT + r] = m * sl + log2f(lsum);
+      } else {
+        __nv_bfloat16 *dst = p.out + (static_cast<size_t>(q_slot(p, u.qt) * kT + r) * 16 + u.head) * 128 + 64 * w;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          float o[32];
+          tmem_ld32(o_col + 32 * c, o);
+          tmem_wait_ld();
+          if (qrow < p.S) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 v;
+              v.x = pack_bf16(o[i] * inv, o[i + 1] * inv);
+              v.y = pack_bf16(o[i + 2] * inv, o[i + 3] * inv);
+              v.z = pack_bf16(o[i + 4] * inv, o[i + 5] * inv);
+              v.w = pack_bf16(o[i + 6] * inv, o[i + 7] * inv);
+              *reinterpret_cast<uint4 *>(dst + 32 * c + i) = v;
+            }
           }
         }
       }
@@ -416,16 +491,116 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
   }
 }
 
-cudaError_t launch_flash_prefill(const FlashParams &p, int sms, cudaStream_t stream) {
+// The cut items' pieces combined: block b takes rows 8 (b % 16) .. + 7 of the
+// (b / 16)-th cut item in unit order, 32 threads per row, four dimensions per
+// thread; o = sum_p w_p O_p / sum_p w_p with w_p = 2^(lse_p - max lse) (every
+// piece of a row has at least one visible key, so each lse is finite).
+__global__ void __launch_bounds__(256) flash_combine_kernel(const __grid_constant__ FlashParams p) {
+  const int nq = (p.S + kT - 1) / kT, n_hi = nq - p.q_tile0, groups = n_hi + p.lo_t1 - p.lo_t0;
+  int base = 0, item = blockIdx.x / 16, qt = -1, np = 0, head = 0;
+  for (int t = 0; t < groups; ++t) {
+    const int q = group_tile(p, nq, n_hi, t), n = pieces_of(q + 1, p.kpiece);
+    if (n > 1) {
+      if (item < 16) {
+        qt = q;
+        np = n;
+        head = item;
+        break;
+      }
+      item -= 16;
+    }
+    base += 16 * n;
+  }
+  const int r = 8 * (blockIdx.x % 16) + (threadIdx.x >> 5), d = 4 * (threadIdx.x & 31);
+  if (qt < 0 || qt * kT + r >= p.S) return;
+  float lmax = -INFINITY;
+  for (int i = 0; i < np; ++i) lmax = fmaxf(lmax, p.part_lse[static_cast<size_t>(base + 16 * i + head) * kT + r]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float wsum = 0.f;
+  for (int i = 0; i < np; ++i) {
+    const size_t u = static_cast<size_t>(base + 16 * i + head);
+    const float wt = exp2f(p.part_lse[u * kT + r] - lmax);
+    const float4 o = *reinterpret_cast<const float4 *>(p.part_o + (u * kT + r) * 128 + d);
+    acc.x += wt * o.x;
+    acc.y += wt * o.y;
+    acc.z += wt * o.z;
+    acc.w += wt * o.w;
+    wsum += wt;
+  }
+  const float inv = 1.0f / wsum;
+  uint2 v;
+  v.x = pack_bf16(acc.x * inv, acc.y * inv);
+  v.y = pack_bf16(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2 *>(p.out + (static_cast<size_t>(q_slot(p, qt) * kT + r) * 16 + head) * 128 + d) = v;
+}
+
+// Largest CTA load (key tiles, plus about 1.3 tiles of pipeline drain and
+// refill per unit) when the units of a launch cut at kpiece are dealt out in
+// snake order over `grid` CTAs.
+static double snake_max_load(const FlashParams &p, int nq, int n_hi, int kpiece, int units, int grid) {
+  std::vector<double> cost(units);
+  const int groups = n_hi + p.lo_t1 - p.lo_t0;
+  for (int t = 0, pos = 0; t < groups; ++t) {
+    const int n = group_tile(p, nq, n_hi, t) + 1, np = pieces_of(n, kpiece);
+    for (int i = 0; i < np; ++i) {
+      const int len = np > 1 ? std::min(n, (i + 1) * kpiece) - i * kpiece : n;
+      for (int h = 0; h < 16; ++h) cost[pos++] = len + 1.3;
+    }
+  }
+  std::vector<double> load(grid, 0.0);
+  for (int pos = 0; pos < units; ++pos) {
+    const int k = pos / grid, i = pos % grid;
+    load[(k & 1) ? grid - 1 - i : i] += cost[pos];
+  }
+  return *std::max_element(load.begin(), load.end());
+}
+
+cudaError_t launch_flash_prefill(const FlashParams &p_in, int sms, cudaStream_t stream) {
   cudaError_t e = cudaFuncSetAttribute(flash_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) return e;
-  const int items = ((p.S + kT - 1) / kT - p.q_tile0 + p.lo_t1 - p.lo_t0) * 16;
-  if (items <= 0 || p.q_tile0 < 0 || p.lo_t0 < 0 || p.lo_t1 < p.lo_t0 || p.lo_t1 > p.q_tile0)
+  FlashParams p = p_in;
+  const int nq = (p.S + kT - 1) / kT, n_hi = nq - p.q_tile0;
+  if (nq - p.q_tile0 + p.lo_t1 - p.lo_t0 <= 0 || p.q_tile0 < 0 || p.lo_t0 < 0 || p.lo_t1 < p.lo_t0 ||
+      p.lo_t1 > p.q_tile0)
     return cudaErrorInvalidValue;
-  const int grid = items < sms ? items : sms;
-  ProfScope ps("flash_prefill", stream);
-  flash_prefill_kernel<<<grid, kThreads, kSmem, stream>>>(p);
-  return cudaGetLastError();
+  if (p.kpiece < 0) {
+    // cut only when the items leave SMs idle, at the piece length whose snake
+    // deal has the smallest largest load (within the partial-result slots)
+    const int items = unit_count(p, nq, n_hi, 0);
+    p.kpiece = 0;
+    if (items < sms && p.part_o && p.part_lse) {
+      double best = snake_max_load(p, nq, n_hi, 0, items, items);
+      for (int kp = 2; kp <= nq; ++kp) {
+        const int units = unit_count(p, nq, n_hi, kp);
+        if (units > kFlashMaxUnits) continue;
+        const double ld = snake_max_load(p, nq, n_hi, kp, units, std::min(units, sms));
+        // a cut costs the combine launch: ask for two key tiles of gain
+        if (ld + 2.0 < best) {
+          best = ld;
+          p.kpiece = kp;
+        }
+      }
+    }
+  }
+  const int units = unit_count(p, nq, n_hi, p.kpiece);
+  if (p.kpiece > 0 && (units > kFlashMaxUnits || !p.part_o || !p.part_lse)) return cudaErrorInvalidValue;
+  const int grid = units < sms ? units : sms;
+  {
+    ProfScope ps("flash_prefill", stream);
+    flash_prefill_kernel<<<grid, kThreads, kSmem, stream>>>(p);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  if (p.kpiece > 0) {
+    int cut = 0;
+    for (int t = 0; t < n_hi + p.lo_t1 - p.lo_t0; ++t) cut += pieces_of(group_tile(p, nq, n_hi, t) + 1, p.kpiece) > 1;
+    if (cut > 0) {
+      ProfScope ps("flash_combine", stream);
+      flash_combine_kernel<<<16 * 16 * cut, 256, 0, stream>>>(p);
+      e = cudaGetLastError();
+    }
+  }
+  return e;
 }
 
 }  // namespace kvl

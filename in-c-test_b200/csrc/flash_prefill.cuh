@@ -22,7 +22,19 @@ struct FlashParams {
   float scale_log2;    // softmax scale * log2(e)
   __nv_bfloat16 *out;  // [S][16][128] bf16 (q_compact: [queried rows][16][128])
   uint32_t *err;
+  // Key-range pieces, for launches with fewer (head, query tile) items than
+  // SMs (the context-parallel prefill): kpiece > 0 cuts every item into pieces
+  // of at most kpiece key tiles; a cut item's pieces write their O (normalised
+  // by their own sum) and the log2 of that sum to part_o / part_lse at their
+  // unit index, and a second kernel combines them.  kpiece < 0: the launcher
+  // picks kpiece (or 0) from the items' key counts.  0: no cut.
+  int kpiece;
+  float *part_o;       // [kFlashMaxUnits][128 rows][128] fp32
+  float *part_lse;     // [kFlashMaxUnits][128 rows]
 };
+
+// Work units (pieces) a launch may hold when items are cut.
+constexpr int kFlashMaxUnits = 296;
 
 cudaError_t launch_flash_prefill(const FlashParams &p, int sms, cudaStream_t stream);
 

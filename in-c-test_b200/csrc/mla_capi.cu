@@ -846,21 +846,23 @@ bool fast_prefill_shape(const KvlMlaConfig &c) {
 }
 
 struct PrefillWs {
-  size_t off[10];
+  size_t off[11];
   size_t total;
 };
 
 PrefillWs prefill_layout(const KvlMlaConfig &c, int S) {
   const size_t s = S, H = c.hidden_size, NH = c.num_heads, QD = c.qk_nope_dim + c.qk_rope_dim;
   const size_t R = c.kv_lora_rank, DR = c.qk_rope_dim, DV = c.v_head_dim, DN = c.qk_nope_dim;
-  size_t sz[9];
+  size_t sz[10];
   int n;
   if (fast_prefill_shape(c)) {
-    // xf, xb, q (bf16, rope applied), kva (fp32), pool (bf16 latent|rope), kv (bf16), o (bf16), cos/sin, err
-    const size_t f[9] = {s * H * 4, s * H * 2, s * NH * QD * 2, s * (R + DR) * 4, s * (R + DR) * 2,
-                         s * NH * (DN + DV) * 2, s * NH * DV * 2, s * (DR / 2) * 8, 256};
-    for (int i = 0; i < 9; ++i) sz[i] = f[i];
-    n = 9;
+    // xf, xb, q (bf16, rope applied), kva (fp32), pool (bf16 latent|rope), kv (bf16), o (bf16), cos/sin, err,
+    // the flash kernel's key-range pieces (partial O and log-sum-exp; context-parallel launches)
+    const size_t f[10] = {s * H * 4, s * H * 2, s * NH * QD * 2, s * (R + DR) * 4, s * (R + DR) * 2,
+                          s * NH * (DN + DV) * 2, s * NH * DV * 2, s * (DR / 2) * 8, 256,
+                          static_cast<size_t>(kFlashMaxUnits) * 128 * (128 + 1) * 4};
+    for (int i = 0; i < 10; ++i) sz[i] = f[i];
+    n = 10;
   } else {
     // xf, q, kva, qabs, mix, head_out, pool (bf16), pool (fp32: what the
     // CUDA-core attend reads for shapes other than 16 x 512 x 64)
@@ -875,7 +877,7 @@ PrefillWs prefill_layout(const KvlMlaConfig &c, int S) {
     w.off[i] = o;
     o += (sz[i] + 255) & ~size_t(255);
   }
-  for (int i = n; i < 10; ++i) w.off[i] = o;
+  for (int i = n; i < 11; ++i) w.off[i] = o;
   w.total = o;
   return w;
 }
@@ -1140,7 +1142,7 @@ bool cp_chunks(int S, int rank, int world, CpChunks &k) {
 // chunk): the RoPE table of their positions; kv_a, RMSNorm and RoPE into d_send
 // [2c][576] bf16; q_proj with RoPE into the workspace q [2c][16][192].  q_proj
 // runs on the second stream beside the kv_a -> append chain.
-int cp_project(int sms, const KvlMlaConfig &cfg, const DevW &W, const uint16_t *xb, const CpChunks &k,
+int cp_project(int sms, const KvlMlaConfig &cfg, const DevW &W, const uint16_t *xb, int world, const CpChunks &k,
                uint16_t *d_send, uint8_t *ws, const PrefillWs &L, cudaStream_t st, PrefillFork *fk) {
   const int M = 2 * k.c;
   const uint64_t H = cfg.hidden_size, m = static_cast<uint64_t>(M);
@@ -1152,6 +1154,13 @@ int cp_project(int sms, const KvlMlaConfig &cfg, const DevW &W, const uint16_t *
   CK(cudaEventRecord(fk->fork, st));
   CK(cudaStreamWaitEvent(fk->s2, fk->fork, 0));
   const int kva_bn = (M + 127) / 128 * 3 * 2 < sms ? 64 : 192;
+  // kv_a over a few hundred rows fills a fraction of the SMs: split its K range
+  // (at most `world` parts of 2c rows fit the kva slot) and sum in the append
+  const int tiles_mn = (M / 128) * (576 / kva_bn), ksteps = static_cast<int>((H + 63) / 64);
+  int ks = 1;
+  if (2 * tiles_mn <= sms)
+    for (int want = std::min(world, sms / tiles_mn); want > 1 && ks == 1; --want)
+      if (ksteps % want == 0) ks = want;
   GemmParams g;
   memset(&g, 0, sizeof g);
   g.err = err;
@@ -1164,26 +1173,47 @@ int cp_project(int sms, const KvlMlaConfig &cfg, const DevW &W, const uint16_t *
   g.N = 576;
   g.c = kva;
   g.ldc = 576;
+  g.ksplit = ks;
+  g.c_bstride = static_cast<long long>(M) * 576;
   CK(launch_gemm(g, kva_bn, EPI_F32, sms, st, "gemm_kva"));
+  // q_proj: CTA-pair tiles with RoPE in the epilogue, or, when those fill a
+  // fraction of the SMs, a K split over 1-SM 192-wide tiles whose fp32
+  // partials (in the x slot, unused by this form) are summed with the RoPE
+  const int q_tiles = (M / 128) * (16 * 192 / 192);
+  int qks = 1;
+  if (2 * q_tiles <= sms)
+    for (int want = sms / q_tiles; want > 1 && qks == 1; --want)
+      if (ksteps % want == 0 && static_cast<size_t>(want) * M * 16 * 192 <= static_cast<size_t>(k.c) * 2 * world * H)
+        qks = want;
   GemmParams gq;
   memset(&gq, 0, sizeof gq);
   gq.err = err;
-  if (!bf16_map(&gq.tm_a, xb, H, m, H * 2, 128) || !bf16_map(&gq.tm_b, W.q, H, 16 * 192, H * 2, 128)) {
+  if (!bf16_map(&gq.tm_a, xb, H, m, H * 2, 128) ||
+      !bf16_map(&gq.tm_b, W.q, H, 16 * 192, H * 2, qks > 1 ? 192 : 128)) {
     set_err("prefill (context parallel): tensor map (q_proj)");
     return -1;
   }
   gq.M = M;
   gq.N = 16 * 192;
   gq.K = static_cast<int>(H);
-  gq.c = q;
   gq.ldc = 16 * 192;
-  gq.rope_cs = cs;
   CK(launch_rope_table_rows(cs, M, 64, cfg.rope_theta, k.c, k.a0, k.b0, fk->s2));
   CK(cudaEventRecord(fk->rope, fk->s2));
-  CK(launch_gemm_pair(gq, 256, EPI_QROPE, sms, fk->s2, "gemm_q"));
+  if (qks > 1) {
+    float *parts = reinterpret_cast<float *>(ws + L.off[0]);
+    gq.c = parts;
+    gq.ksplit = qks;
+    gq.c_bstride = static_cast<long long>(M) * 16 * 192;
+    CK(launch_gemm(gq, 192, EPI_F32, sms, fk->s2, "gemm_q"));
+    CK(sum_parts_qrope(q, parts, qks, gq.c_bstride, cs, M, fk->s2));
+  } else {
+    gq.c = q;
+    gq.rope_cs = cs;
+    CK(launch_gemm_pair(gq, 256, EPI_QROPE, sms, fk->s2, "gemm_q"));
+  }
   CK(cudaEventRecord(fk->qdone, fk->s2));
   CK(cudaStreamWaitEvent(st, fk->rope, 0));
-  CK(append_rows_bf16(d_send, kva, W.kvan, cs, M, cfg.rms_eps, st));
+  CK(append_rows_bf16(d_send, kva, W.kvan, cs, M, cfg.rms_eps, st, ks, g.c_bstride));
   CK(cudaStreamWaitEvent(st, fk->qdone, 0));
   return 0;
 }
@@ -1239,8 +1269,37 @@ int cp_attend(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, con
   f.scale_log2 = (1.0f / sqrtf(192.0f)) * 1.4426950408889634f;
   f.out = reinterpret_cast<__nv_bfloat16 *>(o);
   f.err = err;
+  // few items per rank at larger worlds: the launcher cuts the long ones by key range
+  f.kpiece = -1;
+  f.part_o = reinterpret_cast<float *>(ws + L.off[9]);
+  f.part_lse = f.part_o + static_cast<size_t>(kFlashMaxUnits) * 128 * 128;
   CK(launch_flash_prefill(f, sms, st));
-  // out = o Wo^T, fp32 [2c][H]
+  // out = o Wo^T, fp32 [2c][H].  At a few hundred rows the CTA-pair tiles
+  // would fill a fraction of the SMs, so the K range is split over 1-SM tiles
+  // (fp32 partials in the x slot, which this form does not use: at most
+  // `world` parts of 2c rows) and the partials summed.
+  const int tiles_mn = (M / 128) * static_cast<int>((H + 255) / 256);
+  int ks = 1;
+  if (2 * tiles_mn <= sms)
+    for (int want = std::min(world, sms / tiles_mn); want > 1 && ks == 1; --want)
+      if ((2048 / 64) % want == 0) ks = want;
+  if (ks > 1) {
+    float *parts = reinterpret_cast<float *>(ws + L.off[0]);
+    if (!bf16_map(&g.tm_a, o, 2048, m, 2048 * 2, 128) || !bf16_map(&g.tm_b, W.o, 2048, H, 2048 * 2, 256)) {
+      set_err("prefill (context parallel): tensor map (o_proj)");
+      return -1;
+    }
+    g.M = M;
+    g.N = static_cast<int>(H);
+    g.K = 2048;
+    g.c = parts;
+    g.ldc = static_cast<int>(H);
+    g.ksplit = ks;
+    g.c_bstride = static_cast<long long>(M) * static_cast<long long>(H);
+    CK(launch_gemm(g, 256, EPI_F32, sms, st, "gemm_o"));
+    CK(sum_parts(d_out, parts, ks, g.c_bstride, g.c_bstride, st));
+    return 0;
+  }
   if (!bf16_map(&g.tm_a, o, 2048, m, 2048 * 2, 128) || !bf16_map(&g.tm_b, W.o, 2048, H, 2048 * 2, 128)) {
     set_err("prefill (context parallel): tensor map (o_proj)");
     return -1;
@@ -1447,7 +1506,7 @@ KVL_EXPORT int kvl_mla_prefill_cp_begin(const KvlMlaConfig *cfg, const KvlMlaDev
   PrefillFork *fk = get_fork(current_device());
   if (!fk) return -1;
   std::lock_guard<std::mutex> lk(fk->mu);
-  return cp_project(sms, *cfg, W, d_x, k, d_send, static_cast<uint8_t *>(d_workspace), L,
+  return cp_project(sms, *cfg, W, d_x, world, k, d_send, static_cast<uint8_t *>(d_workspace), L,
                     static_cast<cudaStream_t>(stream), fk);
 }
 

@@ -201,7 +201,7 @@ __global__ void append_bf16_kernel(uint16_t *kv, long long row0, const float *ka
 // same operations as append_bf16 (double sum of squares, float scale, float
 // rotation without contraction); only the order of the double sum differs.
 __global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, const uint16_t *norm_w,
-                                        const float2 *cs, int n, float eps) {
+                                        const float2 *cs, int n, float eps, int parts, long long part_stride) {
   constexpr int R = 512, DR = 64;
   const int warp = static_cast<int>((blockIdx.x * static_cast<unsigned>(blockDim.x) + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
@@ -212,6 +212,13 @@ __global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, const u
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     v[k] = reinterpret_cast<const float4 *>(kt)[lane + 32 * k];
+    for (int z = 1; z < parts; ++z) {  // split-K partial products, summed in order
+      const float4 u = reinterpret_cast<const float4 *>(kt + z * part_stride)[lane + 32 * k];
+      v[k].x += u.x;
+      v[k].y += u.y;
+      v[k].z += u.z;
+      v[k].w += u.w;
+    }
     ss += static_cast<double>(v[k].x) * static_cast<double>(v[k].x);
     ss += static_cast<double>(v[k].y) * static_cast<double>(v[k].y);
     ss += static_cast<double>(v[k].z) * static_cast<double>(v[k].z);
@@ -237,7 +244,12 @@ __global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, const u
     *reinterpret_cast<uint2 *>(dst + c) = o;
   }
   // rope pair (2i, 2i+1) -> (i, 32 + i), i = lane
-  const float2 ab = reinterpret_cast<const float2 *>(kt + R)[lane];
+  float2 ab = reinterpret_cast<const float2 *>(kt + R)[lane];
+  for (int z = 1; z < parts; ++z) {
+    const float2 u = reinterpret_cast<const float2 *>(kt + z * part_stride + R)[lane];
+    ab.x += u.x;
+    ab.y += u.y;
+  }
   const float2 t = cs[static_cast<size_t>(warp) * (DR / 2) + lane];
   const float lo = __fsub_rn(__fmul_rn(ab.x, t.x), __fmul_rn(ab.y, t.y));
   const float hi = __fadd_rn(__fmul_rn(ab.y, t.x), __fmul_rn(ab.x, t.y));
@@ -246,10 +258,55 @@ __global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, const u
 }
 
 cudaError_t append_rows_bf16(uint16_t *pool, const float *ka, const uint16_t *norm_w, const float2 *cs, int n,
-                             float eps, cudaStream_t s) {
+                             float eps, cudaStream_t s, int parts, long long part_stride) {
   if (n <= 0) return cudaSuccess;
+  if (parts < 1) return cudaErrorInvalidValue;
   ProfScope ps("append_bf16", s);
-  append_rows_bf16_kernel<<<(n + 7) / 8, 256, 0, s>>>(pool, ka, norm_w, cs, n, eps);
+  append_rows_bf16_kernel<<<(n + 7) / 8, 256, 0, s>>>(pool, ka, norm_w, cs, n, eps, parts, part_stride);
+  return cudaGetLastError();
+}
+
+// q = sum of split-K partial products [parts][n][16 * 192] fp32 with RoPE on
+// each head's last 64 columns, bf16 [n][16][192]: the arithmetic of the
+// q_proj GEMM's EPI_QROPE epilogue (pair (2i, 2i + 1) -> (i, 32 + i)).  One
+// warp per (row, head): lane l sums nope columns 4l .. 4l + 3 and rope pair l.
+__global__ void sum_parts_qrope_kernel(uint16_t *q, const float *parts, int np, long long stride,
+                                       const float2 *cs, int n) {
+  const int wid = static_cast<int>((blockIdx.x * static_cast<unsigned>(blockDim.x) + threadIdx.x) >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wid >= n * 16) return;
+  const int row = wid >> 4, head = wid & 15;
+  const float *src = parts + static_cast<size_t>(row) * (16 * 192) + head * 192;
+  float4 a = *reinterpret_cast<const float4 *>(src + 4 * lane);
+  float2 r = *reinterpret_cast<const float2 *>(src + 128 + 2 * lane);
+  for (int z = 1; z < np; ++z) {
+    const float4 u = *reinterpret_cast<const float4 *>(src + z * stride + 4 * lane);
+    const float2 v = *reinterpret_cast<const float2 *>(src + z * stride + 128 + 2 * lane);
+    a.x += u.x;
+    a.y += u.y;
+    a.z += u.z;
+    a.w += u.w;
+    r.x += v.x;
+    r.y += v.y;
+  }
+  __nv_bfloat16 *dst = reinterpret_cast<__nv_bfloat16 *>(q) + static_cast<size_t>(row) * (16 * 192) + head * 192;
+  uint2 o;
+  o.x = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(a.x))) |
+        (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(a.y))) << 16);
+  o.y = static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(a.z))) |
+        (static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(a.w))) << 16);
+  *reinterpret_cast<uint2 *>(dst + 4 * lane) = o;
+  const float2 t = cs[static_cast<size_t>(row) * 32 + lane];
+  dst[128 + lane] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(r.x, t.x), __fmul_rn(r.y, t.y)));
+  dst[160 + lane] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(r.y, t.x), __fmul_rn(r.x, t.y)));
+}
+
+cudaError_t sum_parts_qrope(uint16_t *q, const float *parts, int np, long long stride, const float2 *cs, int n,
+                            cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  if (np < 1) return cudaErrorInvalidValue;
+  ProfScope ps("sum_qrope", s);
+  sum_parts_qrope_kernel<<<(n * 16 + 7) / 8, 256, 0, s>>>(q, parts, np, stride, cs, n);
   return cudaGetLastError();
 }
 

@@ -16,8 +16,15 @@ cudaError_t append_q8(int8_t *lat8, float *lscale, uint16_t *rope16, long long r
                       cudaStream_t s, const long long *row_of = nullptr, const int *pos_of = nullptr,
                       int parts = 1, long long part_stride = 0);
 // Prefill rows [0, n) of a bf16 [n][576] pool (Kimi shape), RoPE from a [n][32] cos/sin table.
+// parts > 1: ka holds split-K partial products `part_stride` floats apart,
+// summed in order before the normalisation.
 cudaError_t append_rows_bf16(uint16_t *pool, const float *ka, const uint16_t *norm_w, const float2 *cs, int n,
-                             float eps, cudaStream_t s);
+                             float eps, cudaStream_t s, int parts = 1, long long part_stride = 0);
+// q bf16 [n][16][192] = the sum of `np` fp32 partial products [n][16 * 192]
+// (`stride` floats apart) with RoPE (cos/sin cs [n][32]) on each head's last
+// 64 columns, as the q_proj GEMM's EPI_QROPE epilogue computes it.
+cudaError_t sum_parts_qrope(uint16_t *q, const float *parts, int np, long long stride, const float2 *cs, int n,
+                            cudaStream_t s);
 // Context-parallel prefill: gathered compressed rows [world][2][c][576] bf16
 // (rank p: chunk p, then chunk 2 world - 1 - p) -> pool rows [0, kmax) in prompt
 // order; both 16-byte aligned.

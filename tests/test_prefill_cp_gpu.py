@@ -6,7 +6,11 @@ between the two calls produces), and the output rows each rank returns,
 scattered back to their prompt positions, form the prompt's output.  Checked against the reference's own
 streaming prefill (src/mla_prefill_streaming.c:78-206, oracle/_ref) within
 rel-L2 <= 1e-2 and max-abs <= 2e-2, and against the single-GPU device prefill
-(kvl_mla_prefill_dev), which uses the same kernels over other row ranges.
+(kvl_mla_prefill_dev), which uses the same kernels over other row ranges.  A
+rank with fewer (head, query tile) items than SMs has its long items cut into
+key-range pieces whose softmax partials are combined afterwards (every shape
+below cuts on some rank; 2048 x 2 leaves rank 1 uncut), which re-associates
+the softmax sums: against the one-GPU prefill the bound is rel-L2 <= 5e-3.
 Bad splits are rejected."""
 from __future__ import annotations
 
@@ -51,7 +55,7 @@ def _cp_prefill(K, torch, cfg, dw, xb, Sq, world):
     return out
 
 
-@pytest.mark.parametrize("Sq,world", [(1024, 2), (1024, 4), (4096, 8)])
+@pytest.mark.parametrize("Sq,world", [(1024, 2), (1024, 4), (2048, 2), (4096, 8)])
 def test_context_parallel_prefill(K, S, ref, torch_cuda, Sq, world):
     from oracle.oracle import cfg_of
     torch = torch_cuda
@@ -72,7 +76,7 @@ def test_context_parallel_prefill(K, S, ref, torch_cuda, Sq, world):
     assert lib.kvl_mla_prefill_dev(C.byref(cfg), C.byref(dw), one.data_ptr(), xb.data_ptr(), Sq, ws.data_ptr(),
                                    nbytes, None) == 0, K.last_error()
     torch.cuda.synchronize()
-    assert_close(got, one.cpu().numpy(), rel=1e-4, mabs=1e-4, what=f"cp x{world} vs one-GPU prefill")
+    assert_close(got, one.cpu().numpy(), rel=5e-3, mabs=2e-2, what=f"cp x{world} vs one-GPU prefill")
     if Sq <= 1024:
         want = ref.prefill(S.bf16_bits_to_f32(xbits), cfg_of(*SHAPE), w.arrays)
         assert_close(got, want, what=f"cp x{world} vs reference prefill S={Sq}")
