@@ -3,19 +3,24 @@
 (% HBM peak) & prefill TFLOP/s at 1/2/4/8 B200").
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload prefill|decode_q8|decode_q8_step|decode_long|decode_stack|decode_parity]
+                    [--workload prefill|prefill_cp|decode_q8|decode_q8_step|decode_long|
+                                decode_long_stack|decode_stack|decode_parity]
 
 Default workload: BASELINE config 2 (causal MLA prefill, one sequence of 4096
 tokens, H=2048, 16 heads; the configuration the metric's prefill half is quoted
 on and the largest that fits one GPU).  The decode half of the metric is
 reported in the same JSON line under "decode" (config 1 single-sequence
-attend, config 3 Q8 batched decode, config 5 long-context decode and config 4
-27-layer batched decode step; KV GB/s against measured HBM bandwidth).
+attend, config 3 Q8 batched attend and full step, config 5 long-context
+decode and its 27-layer variant, config 4 27-layer batched decode step; KV
+GB/s against measured HBM bandwidth), beside the drop-in decode call.
 
-Multi-GPU (torchrun, one rank per GPU): prefill runs one independent sequence
-per rank (weak scaling); batched decode shards sequences across ranks; the
-long-context decode splits the KV range across ranks and merges the (o, lse)
-partials with an NCCL all-gather and the library's merge kernel.
+Multi-GPU (torchrun, one rank per GPU): the prefill headline is the one
+config-2 prompt context-parallel over the ranks (zigzag query chunks, one NCCL
+all-gather of the compressed rows; strong scaling), with one independent
+prompt per rank as a sub-line (weak scaling); batched decode shards sequences
+across ranks; the long-context decode splits the KV range across ranks and
+merges the (o, lse) partials with the library's peer-store exchange kernel
+over NVLink.
 
 Inputs are synthetic, seeded (seed = configuration index), created once on the
 device; every timed step is preceded by an untimed 256 MiB write that flushes
@@ -433,6 +438,32 @@ def decode_cpu_baseline(name, wl):
                     "extrapolated_step_s": step,
                     "extrapolation": f"linear: x{wl.LAYERS} layers x {256 // nseq} sequence groups"}
         return _cpu_guard(run)
+    if name == "decode_q8_step":
+        def run():
+            sub = sorted(wl.lens)[len(wl.lens) // 2:len(wl.lens) // 2 + 8]
+            thr = min(8, cores)
+            t0 = time.perf_counter()
+            from concurrent.futures import ThreadPoolExecutor
+            with ThreadPoolExecutor(max_workers=thr) as ex:
+                list(ex.map(lambda L: cpu_reference_decode(L, 1, 1, q8=True), sub))
+            wall = time.perf_counter() - t0
+            nbytes = sum(L + 1 for L in sub) * 644
+            return {"value": nbytes / wall / 1e9, "unit": "GB/s", "cores": thr, "kind": "reference",
+                    "sample": f"subset: 8 of the 64 config-3 sequences ({sum(sub)} rows) through the reference "
+                              f"kvl_mla_decode_compressed_q8_bf16 (the whole step of a token: projections, "
+                              f"quantised append, attention), {thr} in parallel, {wall:.2f} s wall",
+                    "extrapolated": True, "extrapolated_step_s": wall * len(wl.lens) / len(sub),
+                    "extrapolation": f"linear: x{len(wl.lens) // len(sub)} sequence groups"}
+        return _cpu_guard(run)
+    if name == "decode_long_stack":
+        def run():
+            dt = cpu_reference_decode(wl.L, 1, 1)
+            return {"value": wl.L * 1152 / dt / 1e9, "unit": "GB/s", "cores": cores, "kind": "reference",
+                    "sample": f"subset: 1 layer of the 27 through the reference kvl_mla_decode_compressed_bf16 "
+                              f"(whole decode call: projections, append, serial attention over {wl.L + 1} rows), "
+                              f"{dt:.2f} s", "extrapolated": True, "extrapolated_step_s": dt * wl.LAYERS,
+                    "extrapolation": f"linear: x{wl.LAYERS} layers"}
+        return _cpu_guard(run)
     if name == "decode_q8":
         def run():
             secs, nbytes = cpu_reference_decode_q8(wl.lens, cores)
@@ -711,6 +742,10 @@ class DecodeQ8:
     def value(self, ms):
         return self.total_bytes / (ms * 1e-3) / 1e9
 
+    def e2e_io(self):
+        """Per step: the absorbed queries in, the latent contexts out."""
+        return [self.q], [self.out]
+
     def config(self):
         return {"workload": "config 3: Q8 batched decode attend, 64 seqs", "lens_sum": int(sum(self.lens)),
                 "bytes_per_token": 644, "parallelism": f"sequence-sharded x{self.dist.world}"}
@@ -770,6 +805,10 @@ class DecodeQ8Step:
         """The step's launches captured once as a CUDA graph, replayed per step
         (each replay appends at the same rows, as a re-run of the same token)."""
         replay_as_graph(self.torch, self, self.step_profiled, "decode_q8_step")
+
+    def e2e_io(self):
+        """Per step: the tokens' hidden states in, the layer outputs out."""
+        return [self.x], [self.out]
 
     def value(self, ms):
         return self.total_bytes / (ms * 1e-3) / 1e9
@@ -858,6 +897,10 @@ class DecodeLong:
     def value(self, ms):
         return self.total_bytes / (ms * 1e-3) / 1e9
 
+    def e2e_io(self):
+        """Per step: the absorbed query in, the merged (o, lse) out."""
+        return [self.q], [self.final if self.dist.world > 1 else self.rec]
+
     def config(self):
         if self.dist.world == 1:
             par = "one GPU: attend + local combine"
@@ -941,6 +984,10 @@ class DecodeStack:
         (captured once; every replay runs every kernel of every layer)."""
         replay_as_graph(self.torch, self, self.step_profiled, "decode_stack")
 
+    def e2e_io(self):
+        """Per step: the first layer's hidden states in, the last layer's out."""
+        return [self.x[0]], [self.out[self.LAYERS - 1]]
+
     def value(self, ms):
         return self.total_bytes / (ms * 1e-3) / 1e9
 
@@ -953,6 +1000,25 @@ class DecodeStack:
                 "launch": ("the 27 layer steps captured once as a CUDA graph, replayed per step"
                            if getattr(self, "_graph", None) else "27 layer steps launched per step"),
                 "parallelism": f"sequence-sharded x{self.dist.world}"}
+
+
+class DecodeLongStack(DecodeStack):
+    """Config 5's 27-layer variant: one decode step of the 27-layer text stack
+    for one sequence at 131072 cached tokens (27 x 151 MB of bf16 KV, every
+    layer resident), each layer a full kvl_mla_decode_step_bf16 whose attend
+    splits the sequence over all SMs and merges the partials.  One GPU: the
+    split-KV exchange across GPUs is the single-layer decode_long line."""
+    name = "decode_long_stack"
+    metric = "MLA 27-layer decode KV GB/s (config 5 variant: 1 seq x 131072)"
+
+    def __init__(self, torch, K, lib, dist):
+        super().__init__(torch, K, lib, dist, seqs=1, L=131072)
+
+    def config(self):
+        cfg = super().config()
+        cfg["workload"] = "config 5, 27-layer variant: one decode step of the stack, 1 seq x 131072 cached tokens"
+        cfg["parallelism"] = "one GPU"
+        return cfg
 
 
 class DecodeParity:
@@ -985,9 +1051,44 @@ class DecodeParity:
     def value(self, ms):
         return self.total_bytes / (ms * 1e-3) / 1e9
 
+    def e2e_io(self):
+        return [self.q], [self.o]
+
     def config(self):
         return {"workload": "config 1: single-sequence decode attend, L=1024", "rows": self.L,
                 "parallelism": f"replicas x{self.dist.world}"}
+
+
+def decode_e2e(torch, dist, wl, steps, warmup):
+    """A decode sub-line end to end: every step copies the workload's inputs
+    (e2e_io) from pinned host buffers to the device, runs the step (the same
+    graph as the timed line) and reads its outputs back to pinned host
+    buffers; host clock around the synchronised steps, max over ranks.  The KV
+    state stays resident, as in a decoding runtime."""
+    ins, outs = wl.e2e_io()
+    h_in = [t.detach().cpu().pin_memory() for t in ins]
+    h_out = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outs]
+    stream = torch.cuda.current_stream()
+
+    def call():
+        for d, h in zip(ins, h_in):
+            d.copy_(h, non_blocking=True)
+        wl.step()
+        for d, h in zip(outs, h_out):
+            h.copy_(d, non_blocking=True)
+        stream.synchronize()
+    for _ in range(warmup):
+        call()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        call()
+    dt = dist.max(torch, (time.perf_counter() - t0) * 1e3 / steps)
+    nbytes = lambda ts: int(sum(t.numel() * t.element_size() for t in ts)) * dist.world  # noqa: E731
+    return {"value": wl.value(dt), "unit": wl.unit, "ms_per_step": dt, "h2d_bytes_per_step": nbytes(ins),
+            "d2h_bytes_per_step": nbytes(outs),
+            "path": "per rank: inputs pinned host -> device, the step's launches, outputs device -> pinned host, "
+                    "synchronised; bytes summed over ranks"}
 
 
 def dropin_decode_line(K, lib, steps, warmup, cpu=True, lens=(1024, 8192)):
@@ -1063,7 +1164,8 @@ def PrefillCP(torch, K, lib, dist):
 
 
 WORKLOADS = {"prefill": Prefill, "prefill_cp": PrefillCP, "decode_q8": DecodeQ8, "decode_q8_step": DecodeQ8Step,
-             "decode_long": DecodeLong, "decode_stack": DecodeStack, "decode_parity": DecodeParity}
+             "decode_long": DecodeLong, "decode_long_stack": DecodeLongStack, "decode_stack": DecodeStack,
+             "decode_parity": DecodeParity}
 
 
 def measure(torch, K, lib, dist, wl, steps, warmup, flush, peaks):
@@ -1157,6 +1259,8 @@ def main():
         names = ("decode_parity", "decode_q8", "decode_q8_step", "decode_long", "decode_stack")
         if dist.world > 1:  # beside the context-parallel headline: one independent prompt per GPU
             names = ("prefill_independent",) + names
+        else:  # config 5's 27-layer variant (one GPU)
+            names = names + ("decode_long_stack",)
         for name in names:
             w2, err = None, None
             try:
@@ -1181,6 +1285,8 @@ def main():
                             "roofline": r2,
                             "config": w2.config(), "gpu_launches_per_step": int(l2),
                             "kernels": {k: {"ms_total": v[0], "launches": v[1]} for k, v in prof2.items()}}
+            if hasattr(w2, "e2e_io") and not args.no_e2e:
+                extras[name]["e2e"] = decode_e2e(torch, dist, w2, max(2, args.steps // 2), 1)
             if dist.rank == 0 and dist.world == 1 and not args.no_cpu:
                 cb = decode_cpu_baseline(name, w2)
                 if cb is not None:

@@ -437,11 +437,58 @@ __global__ void absorb_kernel(float *qabs, const float *q, const uint16_t *kvb, 
   }
 }
 
+// The same product with R split into 64-wide blocks (grid NH x R/64 x n): warp
+// g of a block sums dims d in [g DN/8, (g + 1) DN/8) for two columns per lane
+// (one 4-byte load of a bf16 pair, 128 contiguous bytes per warp), and the
+// eight partial sums are added in warp order.  R % 64 == 0, DN % 8 == 0.
+__global__ void __launch_bounds__(256) absorb_r64_kernel(float *qabs, const float *q, const uint16_t *kvb, int NH,
+                                                         int DN, int DV, int DR, int R, int pos0, float theta,
+                                                         const int *pos_of) {
+  __shared__ float part[8][64];
+  const int h = blockIdx.x, rb = blockIdx.y, t = blockIdx.z;
+  const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float *qh = q + (static_cast<size_t>(t) * NH + h) * (DN + DR);
+  const uint16_t *wh = kvb + static_cast<size_t>(h) * (DN + DV) * R + 64 * rb + 2 * lane;
+  const int dpg = DN / 8;
+  float a0 = 0.f, a1 = 0.f;
+  for (int k = 0; k < dpg; ++k) {
+    const int d = g * dpg + k;
+    const uint32_t w2 = *reinterpret_cast<const uint32_t *>(wh + static_cast<size_t>(d) * R);
+    const float qd = qh[d];
+    a0 = fmaf(__uint_as_float(w2 << 16), qd, a0);
+    a1 = fmaf(__uint_as_float(w2 & 0xffff0000u), qd, a1);
+  }
+  part[g][2 * lane] = a0;
+  part[g][2 * lane + 1] = a1;
+  __syncthreads();
+  float *dst = qabs + (static_cast<size_t>(t) * NH + h) * (R + DR);
+  if (threadIdx.x < 64) {
+    float acc = part[0][threadIdx.x];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) acc += part[i][threadIdx.x];
+    dst[64 * rb + threadIdx.x] = acc;
+  }
+  if (rb == 0) {
+    const int half = DR / 2;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+      float lo, hi;
+      rope_pair(qh[DN + 2 * i], qh[DN + 2 * i + 1], i, DR, pos_of ? pos_of[t] : pos0 + t, theta, lo, hi);
+      dst[R + i] = lo;
+      dst[R + half + i] = hi;
+    }
+  }
+}
+
 cudaError_t absorb(float *qabs, const float *q, const uint16_t *kvb, int n, int NH, int DN, int DV, int DR, int R,
                    int pos0, float theta, cudaStream_t s, const int *pos_of) {
   if (n <= 0) return cudaSuccess;
   ProfScope ps("absorb", s);
-  absorb_kernel<<<dim3(NH, n), 256, DN * sizeof(float), s>>>(qabs, q, kvb, NH, DN, DV, DR, R, pos0, theta, pos_of);
+  if (R % 64 == 0 && DN % 8 == 0 && (reinterpret_cast<uintptr_t>(kvb) & 3) == 0) {
+    absorb_r64_kernel<<<dim3(NH, R / 64, n), 256, 0, s>>>(qabs, q, kvb, NH, DN, DV, DR, R, pos0, theta, pos_of);
+  } else {
+    absorb_kernel<<<dim3(NH, n), 256, DN * sizeof(float), s>>>(qabs, q, kvb, NH, DN, DV, DR, R, pos0, theta,
+                                                               pos_of);
+  }
   return cudaGetLastError();
 }
 
