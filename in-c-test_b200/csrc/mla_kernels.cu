@@ -73,21 +73,34 @@ __global__ void gemv_bf16_kernel(float *y, const float *x, const uint16_t *W, in
   for (int b = 0; b < NB; ++b) acc[b] = 0.f;
   const bool vec = ((in & 7) == 0) && ((reinterpret_cast<uintptr_t>(row) & 15) == 0);
   if (vec) {
-    for (int i8 = lane; i8 < (in >> 3); i8 += 32) {
-      const uint4 wv = *reinterpret_cast<const uint4 *>(row + i8 * 8);
-      const uint32_t wr[4] = {wv.x, wv.y, wv.z, wv.w};
-      float wf[8];
+    // eight 16-byte loads per lane in flight before their FMAs (the row is a
+    // few KB: one load at a time left each warp waiting on HBM latency); the
+    // lane still sums its words in the order i8 = lane, lane + 32, ...
+    const int n8 = in >> 3;
+    constexpr int kPre = 8;
+    for (int base = lane; base < n8; base += 32 * kPre) {
+      uint4 wv[kPre];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        wf[2 * k] = __uint_as_float(wr[k] << 16);
-        wf[2 * k + 1] = __uint_as_float(wr[k] & 0xffff0000u);
-      }
+      for (int j = 0; j < kPre; ++j)
+        if (base + 32 * j < n8) wv[j] = *reinterpret_cast<const uint4 *>(row + (base + 32 * j) * 8);
 #pragma unroll
-      for (int b = 0; b < NB; ++b) {
-        if (b < nb) {
-          const float *xb = xs + b * in + i8 * 8;
+      for (int j = 0; j < kPre; ++j) {
+        const int i8 = base + 32 * j;
+        if (i8 >= n8) break;
+        const uint32_t wr[4] = {wv[j].x, wv[j].y, wv[j].z, wv[j].w};
+        float wf[8];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) acc[b] = fmaf(wf[k], xb[k], acc[b]);
+        for (int k = 0; k < 4; ++k) {
+          wf[2 * k] = __uint_as_float(wr[k] << 16);
+          wf[2 * k + 1] = __uint_as_float(wr[k] & 0xffff0000u);
+        }
+#pragma unroll
+        for (int b = 0; b < NB; ++b) {
+          if (b < nb) {
+            const float *xb = xs + b * in + i8 * 8;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) acc[b] = fmaf(wf[k], xb[k], acc[b]);
+          }
         }
       }
     }
