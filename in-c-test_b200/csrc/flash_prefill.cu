@@ -35,6 +35,7 @@
 #include <vector>
 
 #include "flash_prefill.cuh"
+#include "gemm.cuh"
 #include "prof.cuh"
 #include "sm100.cuh"
 
@@ -244,7 +245,7 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
           mbar_arrive_expect_tx(&B->k_full[s], 3 * kBox);
           tma_load_3d(kd, &p.tm_kv, &B->k_full[s], 0, u.head, j * kT);
           tma_load_3d(kd + kBox, &p.tm_kv, &B->k_full[s], 64, u.head, j * kT);
-          tma_load_2d(kd + 2 * kBox, &p.tm_kr, &B->k_full[s], p.kr_col, j * kT);
+          tma_load_2d(kd + 2 * kBox, &p.tm_kr, &B->k_full[s], p.kr_col, zigzag_tile(j, p.zz_world, p.zz_c128) * kT);
         }
       }
       if (!ok) {

@@ -31,6 +31,9 @@ struct FlashParams {
   int kpiece;
   float *part_o;       // [kFlashMaxUnits][128 rows][128] fp32
   float *part_lse;     // [kFlashMaxUnits][128 rows]
+  // zz_world > 0: tm_kr's rows are the context-parallel all-gather (key tile j
+  // at zigzag_tile(j, zz_world, zz_c128), gemm.cuh); 0: prompt order.
+  int zz_world, zz_c128;
 };
 
 // Work units (pieces) a launch may hold when items are cut.

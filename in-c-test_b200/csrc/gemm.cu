@@ -368,7 +368,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           if (leader) mbar_arrive_expect_tx(&B->full[s], 2 * L::kStageBytes);
           const uint32_t full_l = mapa_shared(smem_u32(&B->full[s]), 0);
           uint8_t *st = smem + s * L::kStageBytes;
-          tma_load_2d_pair(st, &p.tm_a, full_l, ks * kBK, (2 * mb + static_cast<int>(rank)) * kBM);
+          tma_load_2d_pair(st, &p.tm_a, full_l, ks * kBK,
+                           zigzag_tile(2 * mb + static_cast<int>(rank), p.zz_world, p.zz_c128) * kBM);
           tma_load_2d_pair(st + kABytes, &p.tm_b, full_l, ks * kBK, nb * BN + static_cast<int>(rank) * (BN / 2));
         }
       }

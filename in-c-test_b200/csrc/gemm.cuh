@@ -26,7 +26,21 @@ struct GemmParams {
   // ksplit > 1 (2D maps, EPI_F32, K steps divisible by ksplit): split-K, part z
   // of the K range writes its fp32 partial product to c + z * c_bstride.
   int ksplit;
+  // zz_world > 0 (CTA-pair form): A's rows are the context-parallel all-gather
+  // [world][2][c][K] (rank p's chunks p and 2 world - 1 - p), read in prompt
+  // order: logical 128-row tile t of chunk j = t / zz_c128 is physical tile
+  // (j < world ? 2j : 2 (2 world - 1 - j) + 1) * zz_c128 + t % zz_c128.
+  int zz_world, zz_c128;
 };
+
+// The physical 128-row tile of logical tile t in the zigzag all-gather layout
+// (tiles past the 2 * world chunks map to themselves).
+__host__ __device__ __forceinline__ int zigzag_tile(int t, int world, int c128) {
+  if (world <= 0) return t;
+  const int j = t / c128;
+  if (j >= 2 * world) return t;
+  return (j < world ? 2 * j : 2 * (2 * world - 1 - j) + 1) * c128 + t % c128;
+}
 
 // `name` labels the launch in the per-kernel profile (a string literal).
 cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream,

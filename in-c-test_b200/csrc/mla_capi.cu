@@ -1218,8 +1218,8 @@ int cp_project(int sms, const KvlMlaConfig &cfg, const DevW &W, const uint16_t *
   return 0;
 }
 
-// The gathered rows placed in prompt order for the keys the rank's chunks see
-// ([0, end of its late chunk)), K/V expanded with kv_b, the causal attention
+// K/V expanded with kv_b from the gathered rows for the keys the rank's chunks
+// see ([0, end of its late chunk), read through the zigzag tile map), the causal attention
 // of both chunks in one flash launch (the late chunk as the kernel's main query
 // range, the early one as its second range, queries and output compact), and
 // o_proj of the 2c rows into d_out [2c][H] fp32.
@@ -1228,16 +1228,17 @@ int cp_attend(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, con
   const int kmax = k.b0 + k.c, M = 2 * k.c;
   const uint64_t H = cfg.hidden_size, s = static_cast<uint64_t>(kmax), m = static_cast<uint64_t>(M);
   uint16_t *q = reinterpret_cast<uint16_t *>(ws + L.off[2]);
-  uint16_t *pool = reinterpret_cast<uint16_t *>(ws + L.off[4]);
   uint16_t *kv = reinterpret_cast<uint16_t *>(ws + L.off[5]);
   uint16_t *o = reinterpret_cast<uint16_t *>(ws + L.off[6]);
   uint32_t *err = reinterpret_cast<uint32_t *>(ws + L.off[8]);
-  CK(cp_place_rows(pool, d_recv, k.c, world, kmax, st));
+  // the gathered rows are read in place, in prompt order through the zigzag
+  // tile map (kv_b's A rows and the flash kernel's k_rope rows)
+  const uint64_t S_all = static_cast<uint64_t>(2 * world) * k.c;
   // kv = latent Wkvb^T for the keys [0, kmax), bf16 [kmax][16][256]
   GemmParams g;
   memset(&g, 0, sizeof g);
   g.err = err;
-  if (!bf16_map(&g.tm_a, pool, 512, s, 576 * 2, 128) || !bf16_map(&g.tm_b, W.kvb, 512, 4096, 512 * 2, 128)) {
+  if (!bf16_map(&g.tm_a, d_recv, 512, S_all, 576 * 2, 128) || !bf16_map(&g.tm_b, W.kvb, 512, 4096, 512 * 2, 128)) {
     set_err("prefill (context parallel): tensor map (kv_b_proj)");
     return -1;
   }
@@ -1246,6 +1247,8 @@ int cp_attend(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, con
   g.K = 512;
   g.c = kv;
   g.ldc = 4096;
+  g.zz_world = world;
+  g.zz_c128 = k.c / 128;
   CK(launch_gemm_pair(g, 256, EPI_BF16, sms, st, "gemm_kvb"));
   FlashParams f;
   memset(&f, 0, sizeof f);
@@ -1255,7 +1258,7 @@ int cp_attend(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, con
     const uint32_t box[3] = {64, 1, 128};
     if (!make_tmap_3d(&f.tm_q, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, qd, qs, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
         !make_tmap_3d(&f.tm_kv, kv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, kd, ks, box, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !bf16_map(&f.tm_kr, pool, 576, s, 576 * 2, 128)) {
+        !bf16_map(&f.tm_kr, d_recv, 576, S_all, 576 * 2, 128)) {
       set_err("prefill (context parallel): tensor map (attention)");
       return -1;
     }
@@ -1273,6 +1276,8 @@ int cp_attend(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, con
   f.kpiece = -1;
   f.part_o = reinterpret_cast<float *>(ws + L.off[9]);
   f.part_lse = f.part_o + static_cast<size_t>(kFlashMaxUnits) * 128 * 128;
+  f.zz_world = world;
+  f.zz_c128 = k.c / 128;
   CK(launch_flash_prefill(f, sms, st));
   // out = o Wo^T, fp32 [2c][H].  At a few hundred rows the CTA-pair tiles
   // would fill a fraction of the SMs, so the K range is split over 1-SM tiles

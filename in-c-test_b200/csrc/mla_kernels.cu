@@ -323,27 +323,6 @@ cudaError_t sum_parts_qrope(uint16_t *q, const float *parts, int np, long long s
   return cudaGetLastError();
 }
 
-// Context-parallel prefill: the all-gathered compressed rows (rank p's block
-// holds its chunks p and 2 world - 1 - p, c rows each) placed in prompt order,
-// pool row t for t < kmax.  One 16-byte word per thread.
-__global__ void cp_place_rows_kernel(uint4 *pool, const uint4 *recv, int c, int world, int kmax) {
-  constexpr int kW = 576 * 2 / 16;  // words per row; a block moves 4 rows
-  const int t = blockIdx.x * 4 + threadIdx.x / kW, w = threadIdx.x % kW;
-  if (t >= kmax) return;
-  const int j = t / c, off = t % c;
-  const long long src_row = (j < world ? 2LL * j : 2LL * (2 * world - 1 - j) + 1) * c + off;
-  pool[static_cast<long long>(t) * kW + w] = recv[src_row * kW + w];
-}
-
-cudaError_t cp_place_rows(uint16_t *pool, const uint16_t *recv, int c, int world, int kmax, cudaStream_t s) {
-  if (kmax <= 0) return cudaSuccess;
-  if (c <= 0 || world <= 0 || kmax > 2 * world * c) return cudaErrorInvalidValue;
-  ProfScope ps("cp_place_rows", s);
-  cp_place_rows_kernel<<<(kmax + 3) / 4, 4 * 72, 0, s>>>(reinterpret_cast<uint4 *>(pool),
-                                                          reinterpret_cast<const uint4 *>(recv), c, world, kmax);
-  return cudaGetLastError();
-}
-
 // src/mla_compressed_q8_state.c:34-55 for one row held in shared memory.
 __device__ void quantize_row(int8_t *q, float *scale_out, const float *lat, int R, float *fred) {
   float amax = 0.f;

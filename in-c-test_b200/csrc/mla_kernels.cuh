@@ -25,10 +25,6 @@ cudaError_t append_rows_bf16(uint16_t *pool, const float *ka, const uint16_t *no
 // 64 columns, as the q_proj GEMM's EPI_QROPE epilogue computes it.
 cudaError_t sum_parts_qrope(uint16_t *q, const float *parts, int np, long long stride, const float2 *cs, int n,
                             cudaStream_t s);
-// Context-parallel prefill: gathered compressed rows [world][2][c][576] bf16
-// (rank p: chunk p, then chunk 2 world - 1 - p) -> pool rows [0, kmax) in prompt
-// order; both 16-byte aligned.
-cudaError_t cp_place_rows(uint16_t *pool, const uint16_t *recv, int c, int world, int kmax, cudaStream_t s);
 cudaError_t absorb(float *qabs, const float *q, const uint16_t *kvb, int n, int NH, int DN, int DV, int DR, int R,
                    int pos0, float theta, cudaStream_t s, const int *pos_of = nullptr);
 cudaError_t vup(float *ho, const float *mix, const uint16_t *kvb, int n, int NH, int DN, int DV, int R,

@@ -113,9 +113,9 @@ def test_zigzag_chunks_partition_and_balance():
         assert max(work) - min(work) <= (S_len // (2 * world)) ** 2
         order = gathered_row_order(S_len, world)
         assert sorted(order.tolist()) == list(range(S_len))
-        # the row map of the device placement (cp_place_rows): prompt row t of
-        # chunk j = t // c sits at gathered row 2j c + t % c (j < world) or
-        # (2 (2 world - 1 - j) + 1) c + t % c
+        # the row map the device reads the all-gather through (zigzag_tile,
+        # gemm.cuh, per 128-row tile): prompt row t of chunk j = t // c sits at
+        # gathered row 2j c + t % c (j < world) or (2 (2 world - 1 - j) + 1) c + t % c
         c = S_len // (2 * world)
         src = [(2 * (t // c) if t // c < world else 2 * (2 * world - 1 - t // c) + 1) * c + t % c
                for t in range(S_len)]
