@@ -302,7 +302,10 @@ __global__ void __maxnreg__(192)
       for (int t = 0; t < nt; ++t, ++g) {
         const uint32_t sb = g & 1;
         bad = !mbar_wait(&B->s_full[sb], (g >> 1) & 1, abort, p.err, ERR_TIMEOUT_MMA);
-        if (named_bar_or(1, 128, bad)) { bad = true; break; }
+        // the P buffer of this tile is free by now (P.V of tile g - 2 ended
+        // before the scores of tile g - 1 started); its wait rides on the
+        // same barrier as the scores' wait and the rescale vote
+        bad |= !mbar_wait(&B->p_empty[sb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_MMA);
         tc_fence_after();
         float v[kHeads];
         tmem_ld16(tmem + sb * 16 + lane_base, v);
@@ -319,7 +322,8 @@ __global__ void __maxnreg__(192)
           s[h] = valid ? v[h] * p.scale_log2 : -INFINITY;
           need |= s[h] > m_ref[h] + 8.0f;
         }
-        if (named_bar_or(1, 128, need)) {
+        if (named_bar_or(1, 128, need || bad)) {
+          if (named_bar_or(1, 128, bad)) { bad = true; break; }
           float mx[kHeads];
 #pragma unroll
           for (int h = 0; h < kHeads; ++h) mx[h] = s[h];
@@ -365,8 +369,6 @@ __global__ void __maxnreg__(192)
           pr[h] = exp2f(s[h] - m_ref[h]);
           l_part[h] += pr[h];
         }
-        bad = !mbar_wait(&B->p_empty[sb], ((g >> 1) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_MMA);
-        if (named_bar_or(1, 128, bad)) { bad = true; break; }
         if (!valid) {
           // Rows past the segment end get p = 0, but 0 * (NaN/Inf garbage) is
           // NaN in the P.V MMA: clear their latent rows (the score MMAs of this
