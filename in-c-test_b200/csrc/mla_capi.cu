@@ -397,7 +397,7 @@ int decode_one(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, con
   memcpy(px, x, H * sizeof(float));
   CK(cudaMemcpyAsync(c.x.p, px, H * 4, cudaMemcpyHostToDevice, c.stream));
   CK(gemv_bf16(c.q.as<float>(), c.x.as<float>(), W.q, H, NH * QD, 1, c.stream));
-  CK(gemv_bf16(c.ka.as<float>(), c.x.as<float>(), W.kva, H, R + DR, 1, c.stream));
+  CK(gemv_bf16(c.ka.as<float>(), c.x.as<float>(), W.kva, H, R + DR, 1, c.stream, true));
   if (ds.fmt == FMT_BF16) {
     CK(append_bf16(ds.kv, 0, c.ka.as<float>(), W.kvan, 1, R, DR, position, cfg.rms_eps, cfg.rope_theta,
                    c.rowf.as<float>(), c.stream));
@@ -468,7 +468,7 @@ int decode_block(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, c
   }
   CK(cudaMemcpyAsync(c.x.p, x, n * H * 4, cudaMemcpyHostToDevice, c.stream));
   CK(gemv_bf16(c.q.as<float>(), c.x.as<float>(), W.q, H, NH * QD, count, c.stream));
-  CK(gemv_bf16(c.ka.as<float>(), c.x.as<float>(), W.kva, H, R + DR, count, c.stream));
+  CK(gemv_bf16(c.ka.as<float>(), c.x.as<float>(), W.kva, H, R + DR, count, c.stream, true));
   CK(append_bf16(ds.kv, 0, c.ka.as<float>(), W.kvan, count, R, DR, position, cfg.rms_eps, cfg.rope_theta,
                  c.rowf.as<float>(), c.stream));
   if (ds.kvf)
@@ -518,7 +518,7 @@ int prefill_state(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, 
     return -1;
   }
   CK(cudaMemcpyAsync(c.x.p, x, static_cast<size_t>(S) * H * 4, cudaMemcpyHostToDevice, c.stream));
-  CK(gemv_bf16(c.ka.as<float>(), c.x.as<float>(), W.kva, H, R + DR, S, c.stream));
+  CK(gemv_bf16(c.ka.as<float>(), c.x.as<float>(), W.kva, H, R + DR, S, c.stream, true));
   if (ds.fmt == FMT_BF16) {
     CK(append_bf16(ds.kv, 0, c.ka.as<float>(), W.kvan, S, R, DR, 0, cfg.rms_eps, cfg.rope_theta,
                    c.rowf.as<float>(), c.stream));
@@ -920,7 +920,7 @@ int prefill_absorbed(int device, int sms, const KvlMlaConfig &cfg, const DevW &W
   uint16_t *pool = reinterpret_cast<uint16_t *>(ws + L.off[6]);
   float *poolf = reinterpret_cast<float *>(ws + L.off[7]);
   CK(gemv_bf16(q, xf, W.q, H, NH * QD, S, st));
-  CK(gemv_bf16(ka, xf, W.kva, H, R + DR, S, st));
+  CK(gemv_bf16(ka, xf, W.kva, H, R + DR, S, st, true));
   CK(append_bf16(pool, 0, ka, W.kvan, S, R, DR, 0, cfg.rms_eps, cfg.rope_theta, poolf, st));
   CK(absorb(qabs, q, W.kvb, S, NH, DN, DV, DR, R, 0, cfg.rope_theta, st));
   const DevicePlan *dp = prefill_plan(device, S, NH, R, sms);
@@ -1935,7 +1935,7 @@ static int decode_step(const KvlMlaConfig *cfg, const KvlMlaDeviceWeights *w, co
   float *mix = reinterpret_cast<float *>(ws + off[3]);
   float *ho = reinterpret_cast<float *>(ws + off[4]);
   CK(gemv_bf16(q, d_x, w->q_proj, H, NH * QD, batch, s));
-  CK(gemv_bf16(ka, d_x, w->kv_a_proj, H, R + DR, batch, s));
+  CK(gemv_bf16(ka, d_x, w->kv_a_proj, H, R + DR, batch, s, true));
   CK(step_append(pool, *cfg, w->kv_a_norm, ka, batch, d_row, d_pos, 1, 0, s));
   CK(absorb(qabs, q, w->kv_b_proj, batch, NH, DN, DV, DR, R, 0, cfg->rope_theta, s, d_pos));
   if (step_attend(plan, pool, *cfg, mix, qabs, rows, s) != 0) return -1;

@@ -1,7 +1,8 @@
 // mla_kernels.cu -- the small kernels around the attend core of one absorbed
 // MLA decode step (src/mla_compressed_state.c:86-161):
 //   gemv_bf16      y = W x for the q_proj / kv_a_proj / o_proj projections
-//                  (src/ops.c:53-66; fp32 accumulation like the AVX2 build)
+//                  (src/ops.c:53-66; fp32 accumulation; kv_a_proj in the AVX2
+//                  build's exact summation order, src/ops.c:31-50)
 //   append_*       RMSNorm of the latent (src/ops.c:76-83) and interleaved
 //                  RoPE of the rope slice (src/mla_compressed_state.c:8-22),
 //                  stored as a bf16 state row or quantised into the Q8 state
@@ -120,8 +121,84 @@ __global__ void gemv_bf16_kernel(float *y, const float *x, const uint16_t *W, in
   }
 }
 
-cudaError_t gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int n, cudaStream_t s) {
+// The kv_a_proj rows become state rows, so that product follows the
+// summation order of the reference's AVX2 matvec (src/ops.c:31-50) and a
+// stored row is the reference's bit for bit: eight fp32 accumulators, the one
+// for i = l (mod 8) adding the rounded products w_i * x_i (a multiply, then an
+// add: that build has no FMA) in increasing i; then
+// ((a0 + a4) + (a1 + a5)) + ((a2 + a6) + (a3 + a7)); then the products of a
+// tail past the last multiple of 8, added in order.  A warp per output row: it
+// copies the row to shared memory with coalesced 16-byte loads, then lane
+// 8 b + l runs accumulator l of token b of the block.
+constexpr int kExactTok = 4;
+constexpr int kExactWarps = 8;
+
+__global__ void __launch_bounds__(32 * kExactWarps) gemv_bf16_exact_kernel(float *y, const float *x,
+                                                                           const uint16_t *W, int in, int out,
+                                                                           int n) {
+  extern __shared__ float xs[];                                       // [kExactTok][in]
+  uint16_t *rows = reinterpret_cast<uint16_t *>(xs + kExactTok * in);  // [kExactWarps][in]
+  const int t0 = blockIdx.y * kExactTok;
+  const int nb = min(kExactTok, n - t0);
+  for (int i = threadIdx.x; i < nb * in; i += blockDim.x) xs[i] = x[static_cast<size_t>(t0) * in + i];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int o = blockIdx.x * kExactWarps + warp;
+  uint16_t *wr = rows + static_cast<size_t>(warp) * in;
+  if (o < out) {
+    const uint16_t *row = W + static_cast<size_t>(o) * in;
+    if ((in & 7) == 0 && ((reinterpret_cast<uintptr_t>(row) | reinterpret_cast<uintptr_t>(wr)) & 15) == 0) {
+      const int n8 = in >> 3;
+      constexpr int kPre = 8;
+      for (int base = lane; base < n8; base += 32 * kPre) {
+        uint4 v[kPre];
+#pragma unroll
+        for (int j = 0; j < kPre; ++j)
+          if (base + 32 * j < n8) v[j] = *reinterpret_cast<const uint4 *>(row + (base + 32 * j) * 8);
+#pragma unroll
+        for (int j = 0; j < kPre; ++j)
+          if (base + 32 * j < n8) *reinterpret_cast<uint4 *>(wr + (base + 32 * j) * 8) = v[j];
+      }
+    } else {
+      for (int i = lane; i < in; i += 32) wr[i] = row[i];
+    }
+  }
+  __syncthreads();
+  if (o >= out) return;
+  const int b = lane >> 3, l = lane & 7;
+  const int n8 = in >> 3;
+  const float *xb = xs + min(b, kExactTok - 1) * in;
+  float a = 0.f;
+  if (b < nb) {
+#pragma unroll 8
+    for (int k = 0; k < n8; ++k) a = __fadd_rn(a, __fmul_rn(bf16f(wr[8 * k + l]), xb[8 * k + l]));
+  }
+  // the horizontal sum within each group of eight lanes (lane l of the group
+  // holds accumulator l)
+  const float s1 = __fadd_rn(a, __shfl_down_sync(0xffffffffu, a, 4));    // l < 4: a_l + a_{l+4}
+  const float s2 = __fadd_rn(s1, __shfl_down_sync(0xffffffffu, s1, 1));  // l = 0, 2: pairs of those
+  float tot = __fadd_rn(s2, __shfl_down_sync(0xffffffffu, s2, 2));       // l = 0: the total
+  if (l == 0 && b < nb) {
+    for (int i = 8 * n8; i < in; ++i) tot = __fadd_rn(tot, __fmul_rn(bf16f(wr[i]), xb[i]));
+    y[static_cast<size_t>(t0 + b) * out + o] = tot;
+  }
+}
+
+cudaError_t gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int n, cudaStream_t s,
+                      bool ref_order) {
   if (n <= 0) return cudaSuccess;
+  if (ref_order) {
+    const size_t sm = static_cast<size_t>(in) * (kExactTok * sizeof(float) + kExactWarps * sizeof(uint16_t));
+    if (sm > 227 * 1024) return cudaErrorInvalidValue;
+    if (sm > 48 * 1024) {
+      cudaError_t e = cudaFuncSetAttribute(gemv_bf16_exact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(sm));
+      if (e != cudaSuccess) return e;
+    }
+    dim3 grid((out + kExactWarps - 1) / kExactWarps, (n + kExactTok - 1) / kExactTok);
+    ProfScope ps("gemv_bf16", s);
+    gemv_bf16_exact_kernel<<<grid, 32 * kExactWarps, sm, s>>>(y, x, W, in, out, n);
+    return cudaGetLastError();
+  }
   constexpr int NB = 4;
   const size_t sm = static_cast<size_t>(NB) * in * sizeof(float);
   if (sm > 48 * 1024) {

@@ -6,7 +6,10 @@
 
 namespace kvl {
 
-cudaError_t gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int n, cudaStream_t s);
+// ref_order: sum in the reference AVX2 matvec's order (bit-identical rows;
+// used for kv_a_proj, whose output becomes the stored state row).
+cudaError_t gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int out, int n, cudaStream_t s,
+                      bool ref_order = false);
 cudaError_t append_bf16(uint16_t *kv, long long row0, const float *ka, const uint16_t *norm_w, int n, int R,
                         int DR, int pos0, float eps, float theta, float *rows_f32, cudaStream_t s,
                         const long long *row_of = nullptr, const int *pos_of = nullptr, int parts = 1,
