@@ -709,7 +709,7 @@ class DecodeQ8:
     # the tensor cores with int32 sums, the rope term bf16 with fp32 sums
     dtype = "s8 (int32 accumulate; rope bf16)"
     # one ncu capture of the attend kernel (profiles/mla_attend_q8_config3.txt)
-    ncu_traffic = {"mla_attend_q8": 193.127424e6 + 5.535232e6}
+    ncu_traffic = {"mla_attend_q8": 192.881408e6 + 4.977152e6}
 
     def __init__(self, torch, K, lib, dist):
         import kvl_b200.synth as SY
@@ -829,7 +829,7 @@ class DecodeLong:
     unit = "GB/s"
     bound = "hbm"
     # one ncu capture of the attend kernel at world size 1 (profiles/mla_attend_bf16_config5.txt)
-    ncu_traffic = {"mla_attend_bf16": 151.119360e6 + 4.251904e6}
+    ncu_traffic = {"mla_attend_bf16": 151.122944e6 + 4.220672e6}
 
     def __init__(self, torch, K, lib, dist, L=131072):
         self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
