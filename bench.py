@@ -928,7 +928,7 @@ class DecodeStack:
     bound = "hbm"
     LAYERS = 27
 
-    def __init__(self, torch, K, lib, dist, seqs=256, L=32768, mem_frac=0.85):
+    def __init__(self, torch, K, lib, dist, seqs=256, L=32768, mem_frac=0.85, max_pools=27):
         import kvl_b200.parallel as PAR
         self.torch, self.K, self.lib, self.dist = torch, K, lib, dist
         self.L = L
@@ -939,7 +939,7 @@ class DecodeStack:
         dev = torch.device("cuda", torch.cuda.current_device())
         layer_bytes = self.rows * 1152
         free, _ = torch.cuda.mem_get_info(dev)
-        self.nbuf = int(max(1, min(self.LAYERS, (free * mem_frac) // layer_bytes)))
+        self.nbuf = int(max(1, min(self.LAYERS, max_pools, (free * mem_frac) // layer_bytes)))
         if self.nbuf < min(4, self.LAYERS):
             raise RuntimeError(f"config 4 needs 4 layer pools of {layer_bytes / 1e9:.1f} GB; "
                                f"{free / 1e9:.1f} GB free")
@@ -963,9 +963,10 @@ class DecodeStack:
         self.ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         self.units = self.LAYERS * self.rows * 1152  # attend bytes this rank reads per step
         self.total_bytes = self.LAYERS * seqs * L * 1152
-        # per-launch DRAM traffic scaled from the config-5 capture of the same kernel
-        # (profiles/mla_attend_bf16_config5.txt: 155.37 MB for 131,072 rows) by rows
-        self.ncu_traffic = {"mla_attend_bf16": DecodeLong.ncu_traffic["mla_attend_bf16"] / 131072 * self.rows}
+        # per-launch DRAM traffic: the capture of one attend launch of the 16-sequence
+        # slice of this step (profiles/mla_attend_bf16_config4.txt: 605.60 + 3.49 MB
+        # for 524,304 rows), scaled by rows -- the kernel reads each row once
+        self.ncu_traffic = {"mla_attend_bf16": (605.596928e6 + 3.485440e6) / 524304 * self.rows}
 
     def step_profiled(self):
         """The 27 decode steps launched one by one (per-kernel CUDA events)."""
@@ -1000,6 +1001,24 @@ class DecodeStack:
                 "launch": ("the 27 layer steps captured once as a CUDA graph, replayed per step"
                            if getattr(self, "_graph", None) else "27 layer steps launched per step"),
                 "parallelism": f"sequence-sharded x{self.dist.world}"}
+
+
+class DecodeStackSlice(DecodeStack):
+    """Config 4's decode step on 16 of its 256 sequences (the same 27 layers,
+    shapes and kernels; a few GB on the device): the case whose attend launch
+    is captured with ncu for config 4's DRAM traffic per row
+    (profiles/mla_attend_bf16_config4.txt)."""
+    name = "decode_stack_slice"
+    metric = "MLA 27-layer decode KV GB/s (config 4 slice: 16 seqs x 32768)"
+
+    def __init__(self, torch, K, lib, dist):
+        # four layer pools of 0.6 GB (each far larger than L2), cycled by the 27 layers
+        super().__init__(torch, K, lib, dist, seqs=16, max_pools=4)
+
+    def config(self):
+        cfg = super().config()
+        cfg["workload"] = "config 4 slice: 27-layer decode step, 16 seqs x 32768 cached tokens"
+        return cfg
 
 
 class DecodeLongStack(DecodeStack):
@@ -1165,7 +1184,7 @@ def PrefillCP(torch, K, lib, dist):
 
 WORKLOADS = {"prefill": Prefill, "prefill_cp": PrefillCP, "decode_q8": DecodeQ8, "decode_q8_step": DecodeQ8Step,
              "decode_long": DecodeLong, "decode_long_stack": DecodeLongStack, "decode_stack": DecodeStack,
-             "decode_parity": DecodeParity}
+             "decode_parity": DecodeParity, "decode_stack_slice": DecodeStackSlice}
 
 
 def measure(torch, K, lib, dist, wl, steps, warmup, flush, peaks):
