@@ -85,6 +85,10 @@ using namespace bf16dec;
 // 60.4 us, a 64 x 32768 batch from 478 to 484 us.  (A reciprocal per head in
 // the epilogue instead of a division per element took config 5 to 56.3 us
 // under this cap but the batch to 486 us, so the epilogue divides.)
+// kFirstAlone (launches of few tiles per CTA, p.first_tile_alone): the copies
+// beyond a CTA's first tile wait for that tile to land.  A separate
+// instantiation, so that long batches run exactly the code without it.
+template <bool kFirstAlone>
 __global__ void __maxnreg__(192)
     mla_attend_bf16_kernel(const __grid_constant__ AttendParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -144,6 +148,12 @@ __global__ void __maxnreg__(192)
           const int32_t y = static_cast<int32_t>(row0 + static_cast<long long>(kTileTok) * t);
           for (int c = 0; c < 4 && ok; ++c) {
             const uint32_t li = 4 * g + c, ls = li % kLatSlots;
+            // With few tiles per CTA, the copies beyond the first tile wait for
+            // it to land, so the whole grid's first tiles are not queued behind
+            // the prefetch of second ones (config 5: 58.4 -> 56.3 us; with ~57
+            // tiles per CTA it cost 1 %, so the plan turns it off there).
+            if (kFirstAlone && li == 4 && !(ok = mbar_wait(&B->lat_full[3], 0, abort, p.err, ERR_TIMEOUT_FULL)))
+              break;
             ok = mbar_wait(&B->lat_empty[ls], ((li / kLatSlots) & 1) ^ 1, abort, p.err, ERR_TIMEOUT_EMPTY);
             if (!ok) break;
             uint8_t *dst = smem + OFF_LAT + ls * kLatSlotBytes;
@@ -460,11 +470,23 @@ __global__ void __launch_bounds__(128) qprep_bf16_kernel(const float *q, uint8_t
                   q + static_cast<size_t>(blockIdx.x) * kHeads * kRow, threadIdx.x);
 }
 
+template <bool kFirstAlone>
+static cudaError_t attend_bf16_grid(const AttendParams &p, int grid, bool qprep, cudaStream_t stream) {
+  static std::atomic<unsigned long long> opted{0};
+  const void *fn = reinterpret_cast<const void *>(mla_attend_bf16_kernel<kFirstAlone>);
+  cudaError_t e = smem_opt_in(fn, kSmemBytes, opted);
+  if (e != cudaSuccess) return e;
+  // A programmatic dependent of the prep kernel only (its loader waits for the
+  // images); otherwise an ordinary launch, so every input the kernel reads
+  // directly was complete before it started.
+  if (qprep) return launch_pdl(fn, grid, kThreads, kSmemBytes, stream, p);
+  mla_attend_bf16_kernel<kFirstAlone><<<grid, kThreads, kSmemBytes, stream>>>(p);
+  return cudaGetLastError();
+}
+
 static cudaError_t attend_bf16_launches(const AttendParams &p, int grid, int batch, bool qprep, cudaStream_t stream,
                                         bool profiled) {
-  static std::atomic<unsigned long long> opted{0};
-  cudaError_t e = smem_opt_in(reinterpret_cast<const void *>(mla_attend_bf16_kernel), kSmemBytes, opted);
-  if (e != cudaSuccess) return e;
+  cudaError_t e = cudaSuccess;
   if (qprep) {
     ProfScope ps(profiled ? "qprep_bf16" : nullptr, stream);
     qprep_bf16_kernel<<<batch, 128, 0, stream>>>(p.q, const_cast<uint8_t *>(p.qimg));
@@ -472,13 +494,8 @@ static cudaError_t attend_bf16_launches(const AttendParams &p, int grid, int bat
     if (e != cudaSuccess) return e;
   }
   ProfScope ps(profiled ? "mla_attend_bf16" : nullptr, stream);
-  // A programmatic dependent of the prep kernel only (its loader waits for the
-  // images); otherwise an ordinary launch, so every input the kernel reads
-  // directly was complete before it started.
-  if (qprep)
-    return launch_pdl(reinterpret_cast<const void *>(mla_attend_bf16_kernel), grid, kThreads, kSmemBytes, stream, p);
-  mla_attend_bf16_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
-  return cudaGetLastError();
+  return p.first_tile_alone ? attend_bf16_grid<true>(p, grid, qprep, stream)
+                            : attend_bf16_grid<false>(p, grid, qprep, stream);
 }
 
 // Host launcher: the query prep for `batch` sequences (only when some CTA of

@@ -72,6 +72,9 @@ struct AttendParams {
   long long rows;            // rows in the pool
   float scale_log2;          // softmax scale * log2(e)
   uint32_t *err;             // error word (bit-or of kvl::ERR_*)
+  int first_tile_alone;      // bf16 kernel: copies beyond a CTA's first tile wait for it to land
+                             // (launches of few tiles per CTA, where the grid's first tiles all
+                             // arrive in one burst)
 };
 
 #ifdef __CUDACC__

@@ -511,6 +511,10 @@ int DevicePlan::launch(const AttendLaunch &a, cudaStream_t stream) const {
   p.rows = a.rows;
   p.scale_log2 = scale_log2;
   p.err = reinterpret_cast<uint32_t *>(const_cast<uint8_t *>(m + off_err));
+  // few tiles per CTA: each CTA's first tile goes out before any prefetch
+  long long tiles = 0;
+  for (const AttendSegment &sg : host.segs) tiles += (sg.tok_end - sg.tok_begin + kTileTok - 1) / kTileTok;
+  p.first_tile_alone = host.grid > 0 && tiles <= 16LL * host.grid;
   // query images are read only from a CTA's second segment on
   bool multi = false;
   for (int c = 0; c < host.grid && !multi; ++c) multi = host.cta_seg[c + 1] - host.cta_seg[c] > 1;
