@@ -248,6 +248,48 @@ __device__ void rmsnorm_row(float *lat, const float *ka, const uint16_t *w, int 
 // of the n tokens; ka is [n][R + DR] (kv_a_proj output), or `parts` split-K
 // partials of it (stride part_stride floats) added in order 0, 1, ...
 // rows_f32 (optional) receives the fp32 row before bf16 rounding.
+// dst[i] = src[i] + src[stride + i] + ... (parts terms, in order) for one row of
+// n values, by the block: four values per thread per step, with up to eight
+// parts' loads in flight at once.
+__device__ __forceinline__ void sum_parts_row(float *dst, const float *src, int n, int parts, long long stride) {
+  constexpr int kMaxP = 8;
+  const bool vec = ((n | stride) & 3) == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+  if (vec) {
+    for (int i = 4 * threadIdx.x; i < n; i += 4 * blockDim.x) {
+      float4 u[kMaxP];
+#pragma unroll
+      for (int pp = 0; pp < kMaxP; ++pp)
+        if (pp == 0 || pp < parts) u[pp] = *reinterpret_cast<const float4 *>(src + pp * stride + i);
+      float4 v = u[0];
+#pragma unroll
+      for (int pp = 1; pp < kMaxP; ++pp)
+        if (pp < parts) {
+          v.x += u[pp].x;
+          v.y += u[pp].y;
+          v.z += u[pp].z;
+          v.w += u[pp].w;
+        }
+      for (int pp = kMaxP; pp < parts; ++pp) {
+        const float4 w = *reinterpret_cast<const float4 *>(src + pp * stride + i);
+        v.x += w.x;
+        v.y += w.y;
+        v.z += w.z;
+        v.w += w.w;
+      }
+      dst[i] = v.x;
+      dst[i + 1] = v.y;
+      dst[i + 2] = v.z;
+      dst[i + 3] = v.w;
+    }
+  } else {
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      float v = src[i];
+      for (int pp = 1; pp < parts; ++pp) v += src[pp * stride + i];
+      dst[i] = v;
+    }
+  }
+}
+
 __global__ void append_bf16_kernel(uint16_t *kv, long long row0, const float *ka, const uint16_t *norm_w, int R,
                                    int DR, int pos0, float eps, float theta, float *rows_f32,
                                    const long long *row_of, const int *pos_of, int parts, long long part_stride) {
@@ -258,11 +300,7 @@ __global__ void append_bf16_kernel(uint16_t *kv, long long row0, const float *ka
   const int t = blockIdx.x;
   const float *kt = ka + static_cast<size_t>(t) * (R + DR);
   if (parts > 1) {
-    for (int i = threadIdx.x; i < R + DR; i += blockDim.x) {
-      float v = kt[i];
-      for (int pp = 1; pp < parts; ++pp) v += kt[pp * part_stride + i];
-      ksum[i] = v;
-    }
+    sum_parts_row(ksum, kt, R + DR, parts, part_stride);
     __syncthreads();
     kt = ksum;
   }
@@ -437,11 +475,7 @@ __global__ void append_q8_kernel(int8_t *lat8, float *lscale, uint16_t *rope16, 
   const long long row = row_of ? row_of[t] : row0 + pos0 + t;
   const float *kt = ka + static_cast<size_t>(t) * (R + DR);
   if (parts > 1) {
-    for (int i = threadIdx.x; i < R + DR; i += blockDim.x) {
-      float v = kt[i];
-      for (int pp = 1; pp < parts; ++pp) v += kt[pp * part_stride + i];
-      ksum[i] = v;
-    }
+    sum_parts_row(ksum, kt, R + DR, parts, part_stride);
     __syncthreads();
     kt = ksum;
   }
@@ -600,27 +634,55 @@ cudaError_t vup(float *ho, const float *mix, const uint16_t *kvb, int n, int NH,
 // q: `parts` split-K partial products [part][t][h][DN + DR] fp32 (stride
 // part_stride floats), added in order -> qn [h][t][DN] bf16 (head-major: the A
 // operand of the per-head q_nope . W_UK product) and the rotated rope part of
-// qabs [t][h][R + DR] (the rope of absorb_kernel, same arithmetic; cos/sin
-// once per token).  One block per token.
-__global__ void q_split_kernel(uint16_t *qn, float *qabs, const float *q, int parts, long long part_stride, int n,
-                               int NH, int DN, int DR, int R, float theta, const int *pos_of) {
+// qabs [t][h][R + DR] (the rope of absorb_kernel, same arithmetic).  Block
+// (t, y) takes heads kQsHeads y .. + kQsHeads - 1 of token t: four consecutive
+// q_nope values per thread (all of a thread's partial loads in flight at
+// once), then one rope pair per thread; cos/sin once per block.
+constexpr int kQsHeads = 4;
+
+__global__ void __launch_bounds__(128) q_split_kernel(uint16_t *qn, float *qabs, const float *q, int parts,
+                                                      long long part_stride, int n, int NH, int DN, int DR, int R,
+                                                      float theta, const int *pos_of) {
   __shared__ float2 cs[128];
-  const int t = blockIdx.x, half = DR / 2, QD = DN + DR;
+  const int t = blockIdx.x, h0 = blockIdx.y * kQsHeads, half = DR / 2, QD = DN + DR;
+  const int nh = min(kQsHeads, NH - h0);
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
     float c, sn;
     rope_cos_sin(i, DR, pos_of[t], theta, c, sn);
     cs[i] = make_float2(c, sn);
   }
-  __syncthreads();
   const float *qt = q + static_cast<size_t>(t) * NH * QD;
-  for (int idx = threadIdx.x; idx < NH * DN; idx += blockDim.x) {
-    const int h = idx / DN, d = idx % DN;
-    float v = qt[h * QD + d];
-    for (int pp = 1; pp < parts; ++pp) v += qt[pp * part_stride + h * QD + d];
-    qn[(static_cast<size_t>(h) * n + t) * DN + d] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+  const bool vec = (DN & 3) == 0 && (QD & 3) == 0 && (part_stride & 3) == 0 &&
+                   (reinterpret_cast<uintptr_t>(q) & 15) == 0;
+  if (vec) {
+    for (int idx = threadIdx.x; idx < nh * (DN / 4); idx += blockDim.x) {
+      const int h = h0 + idx / (DN / 4), d = 4 * (idx % (DN / 4));
+      const float *src = qt + h * QD + d;
+      float4 v = *reinterpret_cast<const float4 *>(src);
+      for (int pp = 1; pp < parts; ++pp) {
+        const float4 u = *reinterpret_cast<const float4 *>(src + pp * part_stride);
+        v.x += u.x;
+        v.y += u.y;
+        v.z += u.z;
+        v.w += u.w;
+      }
+      const __nv_bfloat162 lo2 = __floats2bfloat162_rn(v.x, v.y), hi2 = __floats2bfloat162_rn(v.z, v.w);
+      uint2 o;
+      o.x = *reinterpret_cast<const uint32_t *>(&lo2);
+      o.y = *reinterpret_cast<const uint32_t *>(&hi2);
+      *reinterpret_cast<uint2 *>(qn + (static_cast<size_t>(h) * n + t) * DN + d) = o;
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < nh * DN; idx += blockDim.x) {
+      const int h = h0 + idx / DN, d = idx % DN;
+      float v = qt[h * QD + d];
+      for (int pp = 1; pp < parts; ++pp) v += qt[pp * part_stride + h * QD + d];
+      qn[(static_cast<size_t>(h) * n + t) * DN + d] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+    }
   }
-  for (int idx = threadIdx.x; idx < NH * half; idx += blockDim.x) {
-    const int h = idx / half, i = idx % half;
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < nh * half; idx += blockDim.x) {
+    const int h = h0 + idx / half, i = idx % half;
     const float *src = qt + h * QD + DN + 2 * i;
     float a = src[0], b = src[1];
     for (int pp = 1; pp < parts; ++pp) {
@@ -640,7 +702,8 @@ cudaError_t q_split(uint16_t *qn, float *qabs, const float *q, int parts, long l
   if (n <= 0) return cudaSuccess;
   if (DR / 2 > 128) return cudaErrorInvalidValue;
   ProfScope ps("q_split", s);
-  q_split_kernel<<<n, 256, 0, s>>>(qn, qabs, q, parts, part_stride, n, NH, DN, DR, R, theta, pos_of);
+  q_split_kernel<<<dim3(n, (NH + kQsHeads - 1) / kQsHeads), 128, 0, s>>>(qn, qabs, q, parts, part_stride, n, NH, DN,
+                                                                        DR, R, theta, pos_of);
   return cudaGetLastError();
 }
 
@@ -650,14 +713,27 @@ __global__ void sum_parts_kernel(float *dst, const float *src, int parts, long l
                                                15) == 0;
   const long long step = static_cast<long long>(gridDim.x) * blockDim.x;
   if (vec) {
+    constexpr int kMaxP = 8;  // up to eight parts' loads in flight at once, then added in order
     for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n / 4; i += step) {
-      float4 v = reinterpret_cast<const float4 *>(src)[i];
-      for (int pp = 1; pp < parts; ++pp) {
-        const float4 u = reinterpret_cast<const float4 *>(src + pp * stride)[i];
-        v.x += u.x;
-        v.y += u.y;
-        v.z += u.z;
-        v.w += u.w;
+      float4 u[kMaxP];
+#pragma unroll
+      for (int pp = 0; pp < kMaxP; ++pp)
+        if (pp == 0 || pp < parts) u[pp] = reinterpret_cast<const float4 *>(src + pp * stride)[i];
+      float4 v = u[0];
+#pragma unroll
+      for (int pp = 1; pp < kMaxP; ++pp)
+        if (pp < parts) {
+          v.x += u[pp].x;
+          v.y += u[pp].y;
+          v.z += u[pp].z;
+          v.w += u[pp].w;
+        }
+      for (int pp = kMaxP; pp < parts; ++pp) {
+        const float4 w = reinterpret_cast<const float4 *>(src + pp * stride)[i];
+        v.x += w.x;
+        v.y += w.y;
+        v.z += w.z;
+        v.w += w.w;
       }
       reinterpret_cast<float4 *>(dst)[i] = v;
     }
