@@ -25,6 +25,7 @@
 //               that qprep_bf16_kernel writes before the attend
 //   warps 4-7   softmax and epilogue (TMEM subpartitions 0-3; thread = KV row)
 #include "attend_common.cuh"
+#include "pdl.cuh"
 #include "prof.cuh"
 #include "sm100.cuh"
 
@@ -462,10 +463,14 @@ __global__ void __maxnreg__(192)
 
 // The query images of a launch: block b converts sequence b's absorbed query
 // ([16][576] fp32) into the bf16 SW128 tile the score MMAs read (128 threads).
-// The attend grid is its programmatic dependent and may start at once; only
-// the attend's loader waits for this grid.
+// The attend grid is its programmatic dependent and may start as soon as this
+// grid is past its own wait; only the attend's loader waits for this grid.
 __global__ void __launch_bounds__(128) qprep_bf16_kernel(const float *q, uint8_t *img) {
-  asm volatile("griddepcontrol.launch_dependents;");
+  // launched as a programmatic dependent of the query's producer: the attend
+  // (this grid's dependent) is released only after that producer is done, so
+  // the query rows it reads before its own wait are complete
+  pdl_wait();
+  pdl_trigger();
   load_query_tile(img + static_cast<size_t>(blockIdx.x) * kQImgStride,
                   q + static_cast<size_t>(blockIdx.x) * kHeads * kRow, threadIdx.x);
 }
@@ -477,8 +482,8 @@ static cudaError_t attend_bf16_grid(const AttendParams &p, int grid, bool qprep,
   cudaError_t e = smem_opt_in(fn, kSmemBytes, opted);
   if (e != cudaSuccess) return e;
   // A programmatic dependent of the prep kernel only (its loader waits for the
-  // images); otherwise an ordinary launch, so every input the kernel reads
-  // directly was complete before it started.
+  // images; the prep releases it after its own wait, so every input the kernel
+  // reads directly is complete by then); otherwise an ordinary launch.
   if (qprep) return launch_pdl(fn, grid, kThreads, kSmemBytes, stream, p);
   mla_attend_bf16_kernel<kFirstAlone><<<grid, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError();
@@ -489,8 +494,7 @@ static cudaError_t attend_bf16_launches(const AttendParams &p, int grid, int bat
   cudaError_t e = cudaSuccess;
   if (qprep) {
     ProfScope ps(profiled ? "qprep_bf16" : nullptr, stream);
-    qprep_bf16_kernel<<<batch, 128, 0, stream>>>(p.q, const_cast<uint8_t *>(p.qimg));
-    e = cudaGetLastError();
+    e = launch_dependent(qprep_bf16_kernel, dim3(batch), dim3(128), 0, stream, p.q, const_cast<uint8_t *>(p.qimg));
     if (e != cudaSuccess) return e;
   }
   ProfScope ps(profiled ? "mla_attend_bf16" : nullptr, stream);

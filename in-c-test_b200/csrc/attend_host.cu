@@ -163,8 +163,10 @@ __global__ void merge_partials_kernel(float *out, float *lse, const float *part_
                                : MergeEntry{(int)blockIdx.x, (int)blockIdx.x, uniform_parts, (int)gridDim.x};
   const int h = blockIdx.y;
   // Launched as a programmatic dependent of the attend kernel: wait until that
-  // grid has completed and its partials are visible.
+  // grid has completed and its partials are visible; then let the next
+  // dependent kernel be scheduled.
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const MergeSlice r = merge_slice(e, h, blockIdx.z, part_o, part_lse, nh, R, pb, rec_o, rec_l,
                                    (reinterpret_cast<uintptr_t>(out) & 15) == 0);
   if (lse && blockIdx.z == 0 && threadIdx.x == 0) lse[(size_t)e.seq * nh + h] = r.m + logf(r.sum);
@@ -197,6 +199,7 @@ __global__ void merge_small_kernel(float *out, float *lse, const float *part_o, 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int h = blockIdx.y * 8 + warp;
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (h >= nh) return;
   auto o_of = [&](int q) {
     const int p = e.first + q * e.step;

@@ -43,6 +43,7 @@
 //                boundary costs one copy latency instead of the softmax warps
 //                splitting the next query after their epilogue
 #include "attend_common.cuh"
+#include "pdl.cuh"
 #include "prof.cuh"
 #include "sm100.cuh"
 
@@ -629,10 +630,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // The query images of a launch: block b writes sequence b's q_lat parts, q_rope
 // and sq in the shared-memory layout of the kernel above (256 threads, one unit
-// each).  The attend grid is its programmatic dependent and may start at once;
-// only the attend's loader waits for this grid.
+// each).  The attend grid is its programmatic dependent and may start as soon
+// as this grid is past its own wait; only the attend's loader waits for this
+// grid.
 __global__ void __launch_bounds__(256) qprep_q8_kernel(const float *q, uint8_t *img) {
-  asm volatile("griddepcontrol.launch_dependents;");
+  // launched as a programmatic dependent of the query's producer: the attend
+  // (this grid's dependent) is released only after that producer is done, so
+  // the query rows it reads before its own wait are complete
+  pdl_wait();
+  pdl_trigger();
   uint8_t *base = img + static_cast<size_t>(blockIdx.x) * kQImgStride;
   load_query_unit(base, base + kQiBytes, reinterpret_cast<float *>(base + kQiBytes + kQrBytes),
                   q + static_cast<size_t>(blockIdx.x) * kHeads * kRow, threadIdx.x);
@@ -646,14 +652,13 @@ cudaError_t launch_attend_q8(const AttendParams &p, int grid, int batch, bool qp
   if (e != cudaSuccess) return e;
   if (qprep) {
     ProfScope ps("qprep_q8", stream);
-    qprep_q8_kernel<<<batch, 256, 0, stream>>>(p.q, const_cast<uint8_t *>(p.qimg));
-    e = cudaGetLastError();
+    e = launch_dependent(qprep_q8_kernel, dim3(batch), dim3(256), 0, stream, p.q, const_cast<uint8_t *>(p.qimg));
     if (e != cudaSuccess) return e;
   }
   ProfScope ps("mla_attend_q8", stream);
   // A programmatic dependent of the prep kernel only (its loader waits for the
-  // images); otherwise an ordinary launch, so every input the kernel reads
-  // directly was complete before it started.
+  // images; the prep releases it after its own wait, so every input the kernel
+  // reads directly is complete by then); otherwise an ordinary launch.
   if (qprep)
     return launch_pdl(reinterpret_cast<const void *>(mla_attend_q8_kernel), grid, kThreads, kSmemBytes, stream, p);
   mla_attend_q8_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);

@@ -28,6 +28,7 @@
 
 #include "gemm.cuh"
 #include "prof.cuh"
+#include "pdl.cuh"
 #include "sm100.cuh"
 
 namespace kvl {
@@ -167,6 +168,21 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
   const int ksteps = (p.K + kBK - 1) / kBK;
   const int kc = ksteps / nsplit;  // K steps per split (the launcher checks divisibility)
 
+  if (p.prefetch_b && threadIdx.x == 0) {
+    // the weight boxes of all this CTA's tiles stream into L2 while the
+    // previous kernel on the stream drains
+    tma_prefetch_desc(&p.tm_b);
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      const int z = tile / tiles_mn, nb = (tile % tiles_mn) / tiles_m;
+      const int kbeg = batched ? 0 : z * kc;
+      for (int ks = kbeg; ks < kbeg + kc; ++ks) {
+        if (batched)
+          tma_prefetch_l2_3d(&p.tm_b, ks * kBK, nb * BN, z);
+        else
+          tma_prefetch_l2_2d(&p.tm_b, ks * kBK, nb * BN);
+      }
+    }
+  }
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&B->full[i], 1);
@@ -188,6 +204,10 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = B->tmem_base;
+  // as a programmatic dependent: the set-up above overlaps the previous
+  // kernel's tail; every global access (loads, epilogue stores) comes after
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -436,7 +456,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
 }
 
 template <int BN, int EPI>
-static cudaError_t launch_gemm_t(const GemmParams &p, int sms, cudaStream_t stream, const char *name) {
+static cudaError_t launch_gemm_t(const GemmParams &p, int sms, cudaStream_t stream, const char *name, bool dep) {
   using L = Layout<BN>;
   cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tn_kernel<BN, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        L::kSmem);
@@ -445,31 +465,33 @@ static cudaError_t launch_gemm_t(const GemmParams &p, int sms, cudaStream_t stre
                     (p.ksplit > 1 ? p.ksplit : 1);
   const int grid = tiles < sms ? tiles : sms;
   ProfScope ps(name, stream);
+  if (dep) return launch_dependent(gemm_bf16_tn_kernel<BN, EPI>, dim3(grid), dim3(192), L::kSmem, stream, p);
   gemm_bf16_tn_kernel<BN, EPI><<<grid, 192, L::kSmem, stream>>>(p);
   return cudaGetLastError();
 }
 
-cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream, const char *name) {
+cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream, const char *name,
+                        bool dep) {
   if (!name) name = epi == EPI_QROPE ? "gemm_qrope" : "gemm_bf16";
   if (p.ksplit > 1 && (p.batch > 1 || epi != EPI_F32 || ((p.K + kBK - 1) / kBK) % p.ksplit != 0))
     return cudaErrorInvalidValue;
   if (epi == EPI_QROPE) {
     if (p.N % 192 != 0 || p.batch > 1) return cudaErrorInvalidValue;
-    if (bn == 256) return launch_gemm_t<256, EPI_QROPE>(p, sms, stream, name);
-    if (bn == 192) return launch_gemm_t<192, EPI_QROPE>(p, sms, stream, name);
+    if (bn == 256) return launch_gemm_t<256, EPI_QROPE>(p, sms, stream, name, dep);
+    if (bn == 192) return launch_gemm_t<192, EPI_QROPE>(p, sms, stream, name, dep);
     return cudaErrorInvalidValue;
   }
   if (bn == 256) {
-    if (epi == EPI_F32) return launch_gemm_t<256, EPI_F32>(p, sms, stream, name);
-    if (epi == EPI_BF16) return launch_gemm_t<256, EPI_BF16>(p, sms, stream, name);
+    if (epi == EPI_F32) return launch_gemm_t<256, EPI_F32>(p, sms, stream, name, dep);
+    if (epi == EPI_BF16) return launch_gemm_t<256, EPI_BF16>(p, sms, stream, name, dep);
   } else if (bn == 192) {
-    if (epi == EPI_F32) return launch_gemm_t<192, EPI_F32>(p, sms, stream, name);
-    if (epi == EPI_BF16) return launch_gemm_t<192, EPI_BF16>(p, sms, stream, name);
+    if (epi == EPI_F32) return launch_gemm_t<192, EPI_F32>(p, sms, stream, name, dep);
+    if (epi == EPI_BF16) return launch_gemm_t<192, EPI_BF16>(p, sms, stream, name, dep);
   } else if (bn == 128) {
-    if (epi == EPI_F32) return launch_gemm_t<128, EPI_F32>(p, sms, stream, name);
-    if (epi == EPI_BF16) return launch_gemm_t<128, EPI_BF16>(p, sms, stream, name);
+    if (epi == EPI_F32) return launch_gemm_t<128, EPI_F32>(p, sms, stream, name, dep);
+    if (epi == EPI_BF16) return launch_gemm_t<128, EPI_BF16>(p, sms, stream, name, dep);
   } else if (bn == 64) {
-    if (epi == EPI_F32) return launch_gemm_t<64, EPI_F32>(p, sms, stream, name);
+    if (epi == EPI_F32) return launch_gemm_t<64, EPI_F32>(p, sms, stream, name, dep);
   }
   return cudaErrorInvalidValue;
 }

@@ -31,6 +31,9 @@ struct GemmParams {
   // order: logical 128-row tile t of chunk j = t / zz_c128 is physical tile
   // (j < world ? 2j : 2 (2 world - 1 - j) + 1) * zz_c128 + t % zz_c128.
   int zz_world, zz_c128;
+  // 1-SM kernel: B is a weight that no kernel before it on the stream writes;
+  // the CTA's B boxes are prefetched into L2 before griddepcontrol.wait
+  int prefetch_b;
 };
 
 // The physical 128-row tile of logical tile t in the zigzag all-gather layout
@@ -43,8 +46,11 @@ __host__ __device__ __forceinline__ int zigzag_tile(int t, int world, int c128) 
 }
 
 // `name` labels the launch in the per-kernel profile (a string literal).
+// `dependent`: launched as a programmatic dependent of the previous kernel on
+// the stream (the kernel orders all its global accesses after
+// griddepcontrol.wait, so any predecessor is safe).
 cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream,
-                        const char *name = nullptr);
+                        const char *name = nullptr, bool dependent = false);
 // CTA-pair (2-SM) form, 256 x bn tiles: B's tensor map box is {64, bn / 2}.
 cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream,
                              const char *name = nullptr);

@@ -1825,6 +1825,7 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   GemmParams g;
   memset(&g, 0, sizeof g);
   g.err = plan->dp.err_word();  // a bounded wait that ran out: reported by kvl_mla_attend_check
+  g.prefetch_b = 1;             // q_proj, kv_a_proj, W_UV and o_proj are weights
   // q = x Wq^T fp32 [B][NH*QD]; ka = x Wkva^T fp32 [B][R+DR]
   if (!bf16_map(&g.tm_a, xb, H, b, H * 2, 128) || !bf16_map(&g.tm_b, w.q_proj, H, NH * QD, H * 2, 256)) {
     set_err("decode step: tensor map (q_proj)");
@@ -1839,7 +1840,7 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   g.ksplit = pick_split(hsteps, kStepQSplit);
   g.c_bstride = static_cast<long long>(b * NH * QD);
   const int q_parts = g.ksplit;
-  CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_q"));
+  CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_q", true));
   if (!bf16_map(&g.tm_b, w.kv_a_proj, H, R + DR, H * 2, 192)) {
     set_err("decode step: tensor map (kv_a_proj)");
     return -1;
@@ -1849,7 +1850,7 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   g.ldc = g.N;
   g.ksplit = pick_split(hsteps, kStepKvaSplit);
   g.c_bstride = static_cast<long long>(b * (R + DR));
-  CK(launch_gemm(g, 192, EPI_F32, sms, s, "gemm_kva"));
+  CK(launch_gemm(g, 192, EPI_F32, sms, s, "gemm_kva", true));
   // the append sums the split-K partials of its row itself
   CK(step_append(pool, cfg, w.kv_a_norm, ka_parts, B, d_row, d_pos, g.ksplit, g.c_bstride, s));
   g.ksplit = 0;
@@ -1873,7 +1874,9 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   g.ldc = static_cast<int>(NH * (R + DR));
   g.batch = static_cast<int>(NH);
   g.c_bstride = static_cast<long long>(R + DR);
-  CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_absorb"));
+  g.prefetch_b = 0;  // W_UK^T is written by this step
+  CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_absorb", true));
+  g.prefetch_b = 1;
 
   if (step_attend(plan, pool, cfg, mix, qabs, rows, s) != 0) return -1;
 
@@ -1895,7 +1898,7 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   g.c = hob;
   g.ldc = static_cast<int>(NH * DV);
   g.c_bstride = static_cast<long long>(DV);
-  CK(launch_gemm(g, 128, EPI_BF16, sms, s, "gemm_vup"));
+  CK(launch_gemm(g, 128, EPI_BF16, sms, s, "gemm_vup", true));
 
   // out = ho Wo^T fp32 [B][H]
   g.batch = 0;
@@ -1911,7 +1914,7 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   g.ldc = static_cast<int>(H);
   g.ksplit = pick_split(static_cast<int>((NH * DV + 63) / 64), kStepOSplit);
   g.c_bstride = static_cast<long long>(b * H);
-  CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_o"));
+  CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_o", true));
   CK(sum_parts(d_out, o_parts, g.ksplit, g.c_bstride, static_cast<long long>(b * H), s));
   return 0;
 }

@@ -20,6 +20,7 @@
 #include <cstdint>
 
 #include "mla_kernels.cuh"
+#include "pdl.cuh"
 #include "prof.cuh"
 
 namespace kvl {
@@ -54,6 +55,25 @@ __device__ __forceinline__ float block_max(float v, float *red) {
   return r;
 }
 
+// The block's threads pull [p, p + bytes) into L2, one 128-byte line each.  The
+// matvec kernels run it on their weight rows before pdl_wait(): weights are
+// never written by a kernel of a decode step, so the rows stream in while the
+// previous kernel drains.
+__device__ __forceinline__ void prefetch_l2(const void *p, size_t bytes) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(p) & ~static_cast<uintptr_t>(127);
+  const uintptr_t a1 = reinterpret_cast<uintptr_t>(p) + bytes;
+  for (uintptr_t a = a0 + 128 * static_cast<uintptr_t>(threadIdx.x); a < a1; a += 128 * static_cast<uintptr_t>(blockDim.x))
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+}
+
+// A warp pulls one row [p, p + bytes) into L2.
+__device__ __forceinline__ void prefetch_row_l2(const void *p, size_t bytes, int lane) {
+  const uintptr_t a0 = reinterpret_cast<uintptr_t>(p) & ~static_cast<uintptr_t>(127);
+  const uintptr_t a1 = reinterpret_cast<uintptr_t>(p) + bytes;
+  for (uintptr_t a = a0 + 128 * static_cast<uintptr_t>(lane); a < a1; a += 128 * 32)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(a));
+}
+
 // --------------------------------------------------------------------- gemv
 // One warp per output row, NB tokens per block share each weight load.  The
 // per-row reduction order depends only on `in`, so a row's result is the same
@@ -61,6 +81,10 @@ __device__ __forceinline__ float block_max(float v, float *red) {
 template <int NB>
 __global__ void gemv_bf16_kernel(float *y, const float *x, const uint16_t *W, int in, int out, int n) {
   extern __shared__ float xs[];  // [NB][in]
+  if (blockIdx.y == 0 && blockIdx.x * 8 < out)
+    prefetch_l2(W + static_cast<size_t>(blockIdx.x) * 8 * in, static_cast<size_t>(min(8, out - blockIdx.x * 8)) * in * 2);
+  pdl_wait();
+  pdl_trigger();
   const int t0 = blockIdx.y * NB;
   const int nb = min(NB, n - t0);
   for (int i = threadIdx.x; i < nb * in; i += blockDim.x) xs[i] = x[static_cast<size_t>(t0) * in + i];
@@ -138,6 +162,11 @@ __global__ void __launch_bounds__(32 * kExactWarps) gemv_bf16_exact_kernel(float
                                                                            int n) {
   extern __shared__ float xs[];                                       // [kExactTok][in]
   uint16_t *rows = reinterpret_cast<uint16_t *>(xs + kExactTok * in);  // [kExactWarps][in]
+  if (blockIdx.y == 0 && blockIdx.x * kExactWarps < out)
+    prefetch_l2(W + static_cast<size_t>(blockIdx.x) * kExactWarps * in,
+                static_cast<size_t>(min(kExactWarps, out - blockIdx.x * kExactWarps)) * in * 2);
+  pdl_wait();
+  pdl_trigger();
   const int t0 = blockIdx.y * kExactTok;
   const int nb = min(kExactTok, n - t0);
   for (int i = threadIdx.x; i < nb * in; i += blockDim.x) xs[i] = x[static_cast<size_t>(t0) * in + i];
@@ -196,8 +225,7 @@ cudaError_t gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int o
     }
     dim3 grid((out + kExactWarps - 1) / kExactWarps, (n + kExactTok - 1) / kExactTok);
     ProfScope ps("gemv_bf16", s);
-    gemv_bf16_exact_kernel<<<grid, 32 * kExactWarps, sm, s>>>(y, x, W, in, out, n);
-    return cudaGetLastError();
+    return launch_dependent(gemv_bf16_exact_kernel, grid, dim3(32 * kExactWarps), sm, s, y, x, W, in, out, n);
   }
   constexpr int NB = 4;
   const size_t sm = static_cast<size_t>(NB) * in * sizeof(float);
@@ -208,8 +236,7 @@ cudaError_t gemv_bf16(float *y, const float *x, const uint16_t *W, int in, int o
   }
   dim3 grid((out + 7) / 8, (n + NB - 1) / NB);
   ProfScope ps("gemv_bf16", s);
-  gemv_bf16_kernel<NB><<<grid, 256, sm, s>>>(y, x, W, in, out, n);
-  return cudaGetLastError();
+  return launch_dependent(gemv_bf16_kernel<NB>, grid, dim3(256), sm, s, y, x, W, in, out, n);
 }
 
 // --------------------------------------------------------------------- rope / rmsnorm
@@ -297,6 +324,8 @@ __global__ void append_bf16_kernel(uint16_t *kv, long long row0, const float *ka
   float *lat = sh;
   double *dred = reinterpret_cast<double *>(sh + ((R + 1) & ~1));
   float *ksum = reinterpret_cast<float *>(dred + 32) + 32;  // [R + DR] when parts > 1
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const float *kt = ka + static_cast<size_t>(t) * (R + DR);
   if (parts > 1) {
@@ -470,6 +499,8 @@ __global__ void append_q8_kernel(int8_t *lat8, float *lscale, uint16_t *rope16, 
   double *dred = reinterpret_cast<double *>(sh + ((R + 1) & ~1));
   float *fred = reinterpret_cast<float *>(dred + 32);
   float *ksum = fred + 32;  // [R + DR] when parts > 1
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int pos = pos_of ? pos_of[t] : pos0 + t;
   const long long row = row_of ? row_of[t] : row0 + pos0 + t;
@@ -499,9 +530,8 @@ cudaError_t append_bf16(uint16_t *kv, long long row0, const float *ka, const uin
   if (n <= 0) return cudaSuccess;
   ProfScope ps("append_bf16", s);
   const size_t sm = parts > 1 ? append_smem_parts(R, DR) : append_smem(R);
-  append_bf16_kernel<<<n, 128, sm, s>>>(kv, row0, ka, norm_w, R, DR, pos0, eps, theta, rows_f32, row_of, pos_of,
-                                        parts, part_stride);
-  return cudaGetLastError();
+  return launch_dependent(append_bf16_kernel, dim3(n), dim3(128), sm, s, kv, row0, ka, norm_w, R, DR, pos0, eps, theta,
+                          rows_f32, row_of, pos_of, parts, part_stride);
 }
 
 cudaError_t append_q8(int8_t *lat8, float *lscale, uint16_t *rope16, long long row0, const float *ka,
@@ -510,9 +540,8 @@ cudaError_t append_q8(int8_t *lat8, float *lscale, uint16_t *rope16, long long r
   if (n <= 0) return cudaSuccess;
   ProfScope ps("append_q8", s);
   const size_t sm = parts > 1 ? append_smem_parts(R, DR) : append_smem(R);
-  append_q8_kernel<<<n, 128, sm, s>>>(lat8, lscale, rope16, row0, ka, norm_w, R, DR, pos0, eps, theta, row_of,
-                                      pos_of, parts, part_stride);
-  return cudaGetLastError();
+  return launch_dependent(append_q8_kernel, dim3(n), dim3(128), sm, s, lat8, lscale, rope16, row0, ka, norm_w, R, DR,
+                          pos0, eps, theta, row_of, pos_of, parts, part_stride);
 }
 
 // --------------------------------------------------------------------- absorb / vup
@@ -520,6 +549,8 @@ cudaError_t append_q8(int8_t *lat8, float *lscale, uint16_t *rope16, long long r
 __global__ void absorb_kernel(float *qabs, const float *q, const uint16_t *kvb, int NH, int DN, int DV, int DR,
                               int R, int pos0, float theta, const int *pos_of) {
   extern __shared__ float qn[];
+  pdl_wait();
+  pdl_trigger();
   const int h = blockIdx.x, t = blockIdx.y;
   const float *qh = q + (static_cast<size_t>(t) * NH + h) * (DN + DR);
   for (int d = threadIdx.x; d < DN; d += blockDim.x) qn[d] = qh[d];
@@ -550,6 +581,11 @@ __global__ void __launch_bounds__(256) absorb_r64_kernel(float *qabs, const floa
   __shared__ float part[8][64];
   const int h = blockIdx.x, rb = blockIdx.y, t = blockIdx.z;
   const int g = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (t == 0)
+    for (int d = threadIdx.x; d < DN; d += blockDim.x)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(kvb + (static_cast<size_t>(h) * (DN + DV) + d) * R + 64 * rb));
+  pdl_wait();
+  pdl_trigger();
   const float *qh = q + (static_cast<size_t>(t) * NH + h) * (DN + DR);
   const uint16_t *wh = kvb + static_cast<size_t>(h) * (DN + DV) * R + 64 * rb + 2 * lane;
   const int dpg = DN / 8;
@@ -587,12 +623,11 @@ cudaError_t absorb(float *qabs, const float *q, const uint16_t *kvb, int n, int 
   if (n <= 0) return cudaSuccess;
   ProfScope ps("absorb", s);
   if (R % 64 == 0 && DN % 8 == 0 && (reinterpret_cast<uintptr_t>(kvb) & 3) == 0) {
-    absorb_r64_kernel<<<dim3(NH, R / 64, n), 256, 0, s>>>(qabs, q, kvb, NH, DN, DV, DR, R, pos0, theta, pos_of);
-  } else {
-    absorb_kernel<<<dim3(NH, n), 256, DN * sizeof(float), s>>>(qabs, q, kvb, NH, DN, DV, DR, R, pos0, theta,
-                                                               pos_of);
+    return launch_dependent(absorb_r64_kernel, dim3(NH, R / 64, n), dim3(256), 0, s, qabs, q, kvb, NH, DN, DV, DR, R,
+                            pos0, theta, pos_of);
   }
-  return cudaGetLastError();
+  return launch_dependent(absorb_kernel, dim3(NH, n), dim3(256), DN * sizeof(float), s, qabs, q, kvb, NH, DN, DV, DR,
+                          R, pos0, theta, pos_of);
 }
 
 // ho[t][h*DV + d] = sum_r W_UV[h][d][r] * mix[t][h][r]; one warp per (h, d).
@@ -600,6 +635,11 @@ __global__ void vup_kernel(float *ho, const float *mix, const uint16_t *kvb, int
   const int t = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hd = blockIdx.x * 8 + warp;
+  if (t == 0 && hd < NH * DV)
+    prefetch_row_l2(kvb + (static_cast<size_t>(hd / DV) * (DN + DV) + DN + hd % DV) * R, static_cast<size_t>(R) * 2,
+                    lane);
+  pdl_wait();
+  pdl_trigger();
   if (hd >= NH * DV) return;
   const int h = hd / DV, d = hd % DV;
   const uint16_t *row = kvb + (static_cast<size_t>(h) * (DN + DV) + DN + d) * R;
@@ -626,8 +666,7 @@ cudaError_t vup(float *ho, const float *mix, const uint16_t *kvb, int n, int NH,
                 cudaStream_t s) {
   if (n <= 0) return cudaSuccess;
   ProfScope ps("vup", s);
-  vup_kernel<<<dim3((NH * DV + 7) / 8, n), 256, 0, s>>>(ho, mix, kvb, NH, DN, DV, R);
-  return cudaGetLastError();
+  return launch_dependent(vup_kernel, dim3((NH * DV + 7) / 8, n), dim3(256), 0, s, ho, mix, kvb, NH, DN, DV, R);
 }
 
 // Tensor-core decode step helpers (batches of sequences).
@@ -644,6 +683,8 @@ __global__ void __launch_bounds__(128) q_split_kernel(uint16_t *qn, float *qabs,
                                                       long long part_stride, int n, int NH, int DN, int DR, int R,
                                                       float theta, const int *pos_of) {
   __shared__ float2 cs[128];
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x, h0 = blockIdx.y * kQsHeads, half = DR / 2, QD = DN + DR;
   const int nh = min(kQsHeads, NH - h0);
   for (int i = threadIdx.x; i < half; i += blockDim.x) {
@@ -702,13 +743,14 @@ cudaError_t q_split(uint16_t *qn, float *qabs, const float *q, int parts, long l
   if (n <= 0) return cudaSuccess;
   if (DR / 2 > 128) return cudaErrorInvalidValue;
   ProfScope ps("q_split", s);
-  q_split_kernel<<<dim3(n, (NH + kQsHeads - 1) / kQsHeads), 128, 0, s>>>(qn, qabs, q, parts, part_stride, n, NH, DN,
-                                                                        DR, R, theta, pos_of);
-  return cudaGetLastError();
+  return launch_dependent(q_split_kernel, dim3(n, (NH + kQsHeads - 1) / kQsHeads), dim3(128), 0, s, qn, qabs, q, parts,
+                          part_stride, n, NH, DN, DR, R, theta, pos_of);
 }
 
 // dst[i] = src[i] + src[stride + i] + ... (parts terms, in order), fp32.
 __global__ void sum_parts_kernel(float *dst, const float *src, int parts, long long stride, long long n) {
+  pdl_wait();
+  pdl_trigger();
   const bool vec = ((n | stride) & 3) == 0 && ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) &
                                                15) == 0;
   const long long step = static_cast<long long>(gridDim.x) * blockDim.x;
@@ -751,13 +793,14 @@ cudaError_t sum_parts(float *dst, const float *src, int parts, long long stride,
   const long long work = (n + 3) / 4;
   const int grid = static_cast<int>((work + 255) / 256 < 148 * 8 ? (work + 255) / 256 : 148 * 8);
   ProfScope ps("sum_parts", s);
-  sum_parts_kernel<<<grid, 256, 0, s>>>(dst, src, parts, stride, n);
-  return cudaGetLastError();
+  return launch_dependent(sum_parts_kernel, dim3(grid), dim3(256), 0, s, dst, src, parts, stride, n);
 }
 
 // mix [t][h][R] fp32 -> [h][t][R] bf16 (round to nearest even), the
 // head-major A operand of the per-head mix . W_UV^T product (R % 4 == 0).
 __global__ void mix_heads_bf16_kernel(uint16_t *out, const float *mix, int n, int NH, int R) {
+  pdl_wait();
+  pdl_trigger();
   const int r4n = R / 4;
   const long long total = static_cast<long long>(n) * NH * r4n;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
@@ -782,8 +825,7 @@ cudaError_t mix_heads_bf16(uint16_t *out, const float *mix, int n, int NH, int R
   const long long total = static_cast<long long>(n) * NH * (R / 4);
   const int grid = static_cast<int>((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
   ProfScope ps("mix_heads_bf16", s);
-  mix_heads_bf16_kernel<<<grid, 256, 0, s>>>(out, mix, n, NH, R);
-  return cudaGetLastError();
+  return launch_dependent(mix_heads_bf16_kernel, dim3(grid), dim3(256), 0, s, out, mix, n, NH, R);
 }
 
 // W_UK of every head (kv_b_proj rows h*(DN+DV) + d, d < DN: [d][R]) ->
@@ -791,6 +833,8 @@ cudaError_t mix_heads_bf16(uint16_t *out, const float *mix, int n, int NH, int R
 // through shared memory; grid (ceil(R/32), ceil(DN/32), NH), 32 x 8 threads.
 __global__ void wuk_transpose_kernel(uint16_t *wukT, const uint16_t *kvb, int DN, int DV, int R) {
   __shared__ uint16_t tile[32][33];
+  pdl_wait();
+  pdl_trigger();
   const int h = blockIdx.z, r0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
   const uint16_t *src = kvb + static_cast<size_t>(h) * (DN + DV) * R;
   for (int i = threadIdx.y; i < 32; i += blockDim.y) {
@@ -807,8 +851,8 @@ __global__ void wuk_transpose_kernel(uint16_t *wukT, const uint16_t *kvb, int DN
 
 cudaError_t wuk_transpose(uint16_t *wukT, const uint16_t *kvb, int NH, int DN, int DV, int R, cudaStream_t s) {
   ProfScope ps("wuk_transpose", s);
-  wuk_transpose_kernel<<<dim3((R + 31) / 32, (DN + 31) / 32, NH), dim3(32, 8), 0, s>>>(wukT, kvb, DN, DV, R);
-  return cudaGetLastError();
+  return launch_dependent(wuk_transpose_kernel, dim3((R + 31) / 32, (DN + 31) / 32, NH), dim3(32, 8), 0, s, wukT, kvb,
+                          DN, DV, R);
 }
 
 // --------------------------------------------------------------------- Q8 helpers
@@ -845,6 +889,8 @@ cudaError_t dequant(float *out, const int8_t *q, const float *scale, long long r
 }
 
 __global__ void bf16_rne_kernel(uint16_t *out, const float *x, long long n) {
+  pdl_wait();
+  pdl_trigger();
   const long long step = static_cast<long long>(gridDim.x) * blockDim.x;
   const bool vec = (n & 3) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
                    (reinterpret_cast<uintptr_t>(out) & 7) == 0;
@@ -867,8 +913,7 @@ cudaError_t bf16_rne(uint16_t *out, const float *x, long long n, cudaStream_t s)
   ProfScope ps("bf16_rne", s);
   const long long work = (n + 3) / 4;
   const int grid = static_cast<int>((work + 255) / 256 < 148 * 8 ? (work + 255) / 256 : 148 * 8);
-  bf16_rne_kernel<<<grid, 256, 0, s>>>(out, x, n);
-  return cudaGetLastError();
+  return launch_dependent(bf16_rne_kernel, dim3(grid), dim3(256), 0, s, out, x, n);
 }
 
 // bf16 state row -> fp32 (the host mirror of the reference's fp32 state).

@@ -169,6 +169,20 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
 
+// L2 prefetch of one box of a tensor map (no shared memory, no barrier; the
+// coordinates follow the rules of a load).
+__device__ __forceinline__ void tma_prefetch_l2_2d(const CUtensorMap *m, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(m)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_l2_3d(const CUtensorMap *m, int32_t x, int32_t y, int32_t z) {
+  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(m)),
+               "r"(x), "r"(y), "r"(z)
+               : "memory");
+}
+
 // 2-D tiled load of one box into shared memory, completing on `bar`.
 // x (innermost coordinate) must be a multiple of 16 bytes / element size.
 __device__ __forceinline__ void tma_load_2d(void *smem_dst, const CUtensorMap *m, uint64_t *bar,
