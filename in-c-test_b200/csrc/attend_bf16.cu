@@ -301,6 +301,7 @@ __global__ void __maxnreg__(192)
       const uint32_t ob = seg_i % kOBufs;  // this segment's O buffer
       const uint32_t col_o = tmem + kColO + kOCols * ob;
       if (seg_i == 0) {
+        if (p.q_after_wait) pdl_wait();
         load_query_tile(smem + OFF_Q, p.q + static_cast<size_t>(sg.seq) * kHeads * kRow, tt);
         fence_proxy_async_smem();
         __syncwarp();
@@ -481,10 +482,11 @@ static cudaError_t attend_bf16_grid(const AttendParams &p, int grid, bool qprep,
   const void *fn = reinterpret_cast<const void *>(mla_attend_bf16_kernel<kFirstAlone>);
   cudaError_t e = smem_opt_in(fn, kSmemBytes, opted);
   if (e != cudaSuccess) return e;
-  // A programmatic dependent of the prep kernel only (its loader waits for the
+  // A programmatic dependent of the prep kernel (its loader waits for the
   // images; the prep releases it after its own wait, so every input the kernel
-  // reads directly is complete by then); otherwise an ordinary launch.
-  if (qprep) return launch_pdl(fn, grid, kThreads, kSmemBytes, stream, p);
+  // reads directly is complete by then), or of the query's producer when
+  // q_after_wait is set; otherwise an ordinary launch.
+  if (qprep || p.q_after_wait) return launch_pdl(fn, grid, kThreads, kSmemBytes, stream, p);
   mla_attend_bf16_kernel<kFirstAlone><<<grid, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError();
 }

@@ -75,6 +75,10 @@ struct AttendParams {
   int first_tile_alone;      // bf16 kernel: copies beyond a CTA's first tile wait for it to land
                              // (launches of few tiles per CTA, where the grid's first tiles all
                              // arrive in one burst)
+  int q_after_wait;          // launched as a programmatic dependent of the kernel that writes q
+                             // (a kernel that releases its dependents only after its own
+                             // griddepcontrol.wait, so the KV rows are complete): the copies
+                             // start at once, the first query is read after griddepcontrol.wait
 };
 
 #ifdef __CUDACC__

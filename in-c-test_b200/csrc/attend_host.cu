@@ -521,6 +521,8 @@ int DevicePlan::launch(const AttendLaunch &a, cudaStream_t stream) const {
   // query images are read only from a CTA's second segment on
   bool multi = false;
   for (int c = 0; c < host.grid && !multi; ++c) multi = host.cta_seg[c + 1] - host.cta_seg[c] > 1;
+  // with query images the attend is already the prep kernel's dependent
+  p.q_after_wait = a.q_dependent && !multi;
   cudaError_t e = a.q8 ? launch_attend_q8(p, host.grid, host.batch, multi, stream)
                        : launch_attend_bf16(p, host.grid, host.batch, multi, stream);
   if (e != cudaSuccess) return -1;

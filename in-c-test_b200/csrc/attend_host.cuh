@@ -51,6 +51,10 @@ struct AttendLaunch {
   const uint16_t *rope16 = nullptr;   // q8 pool [rows][DR]
   float softmax_scale = 0.f;
   bool skip_merge = false;            // leave split sequences as partials (a cross-GPU combine reads them)
+  // the previous kernel on the stream writes q and was launched as a
+  // programmatic dependent that releases its own dependents only after its
+  // wait (the decode step's absorb kernels): the attend may start during it
+  bool q_dependent = false;
 };
 
 // Device-resident copy of a plan plus the partial-output workspace.

@@ -395,6 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // the first segment's query is split here (no wait for the prep kernel)
         if (wg < 2) {
           uint8_t *qi = smem + OFF_QI;
+          if (p.q_after_wait) pdl_wait();
           load_query_unit(qi, qi + kQiBytes, reinterpret_cast<float *>(smem + OFF_QS),
                           p.q + static_cast<size_t>(sg.seq) * kHeads * kRow, 128 * wg + tt);
           fence_proxy_async_smem();
@@ -656,10 +657,11 @@ cudaError_t launch_attend_q8(const AttendParams &p, int grid, int batch, bool qp
     if (e != cudaSuccess) return e;
   }
   ProfScope ps("mla_attend_q8", stream);
-  // A programmatic dependent of the prep kernel only (its loader waits for the
+  // A programmatic dependent of the prep kernel (its loader waits for the
   // images; the prep releases it after its own wait, so every input the kernel
-  // reads directly is complete by then); otherwise an ordinary launch.
-  if (qprep)
+  // reads directly is complete by then), or of the query's producer when
+  // q_after_wait is set; otherwise an ordinary launch.
+  if (qprep || p.q_after_wait)
     return launch_pdl(reinterpret_cast<const void *>(mla_attend_q8_kernel), grid, kThreads, kSmemBytes, stream, p);
   mla_attend_q8_kernel<<<grid, kThreads, kSmemBytes, stream>>>(p);
   return cudaGetLastError();

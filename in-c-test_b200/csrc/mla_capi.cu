@@ -337,7 +337,8 @@ bool cfg_dims_ok(const KvlMlaConfig &c) {
 }
 
 // Attends the single-sequence plan [0, L) of a state into c.mix.
-int attend_state(Ctx &c, const DevState &ds, int L, int nh, float scale) {
+// The single-sequence plan of a state of L rows, uploaded on the call's stream.
+int plan_state(Ctx &c, const DevState &ds, int L, int nh) {
   HostPlan hp;
   const long long row0 = 0;
   if (build_attend_plan(hp, 1, &L, &row0, c.sms) != 0) {
@@ -349,6 +350,12 @@ int attend_state(Ctx &c, const DevState &ds, int L, int nh, float scale) {
     set_err("attend plan upload failed");
     return -1;
   }
+  return 0;
+}
+
+// The attend of a state over the plan plan_state() uploaded.  q_dependent: the
+// previous kernel on the stream is the absorb kernel that writes the query.
+int attend_state(Ctx &c, const DevState &ds, int nh, float scale, bool q_dependent) {
   AttendLaunch a;
   a.q8 = ds.fmt == FMT_Q8;
   a.nh = nh;
@@ -363,6 +370,7 @@ int attend_state(Ctx &c, const DevState &ds, int L, int nh, float scale) {
   a.lscale = ds.lscale;
   a.rope16 = ds.rope16;
   a.softmax_scale = scale;
+  a.q_dependent = q_dependent;
   if (c.plan.launch(a, c.stream) != 0) {
     set_err("attend launch failed: %s", cudaGetErrorString(cudaGetLastError()));
     return -1;
@@ -407,8 +415,11 @@ int decode_one(Ctx &c, DevState &ds, const KvlMlaConfig &cfg, const DevW &W, con
   } else
     CK(append_q8(ds.lat8, ds.lscale, ds.rope16, 0, c.ka.as<float>(), W.kvan, 1, R, DR, position, cfg.rms_eps,
                  cfg.rope_theta, c.stream));
+  // the plan's upload goes before the absorb kernel, so that the attend follows
+  // it directly and may start while it runs (the rows are complete by then)
+  if (plan_state(c, ds, position + 1, NH) != 0) return -1;
   CK(absorb(c.qabs.as<float>(), c.q.as<float>(), W.kvb, 1, NH, DN, DV, DR, R, position, cfg.rope_theta, c.stream));
-  if (attend_state(c, ds, position + 1, NH, 1.0f / sqrtf(static_cast<float>(QD))) != 0) return -1;
+  if (attend_state(c, ds, NH, 1.0f / sqrtf(static_cast<float>(QD)), true) != 0) return -1;
   CK(vup(c.ho.as<float>(), c.mix.as<float>(), W.kvb, 1, NH, DN, DV, R, c.stream));
   CK(gemv_bf16(c.y.as<float>(), c.ho.as<float>(), W.o, NH * DV, H, 1, c.stream));
   CK(cudaMemcpyAsync(py, c.y.p, H * 4, cudaMemcpyDeviceToHost, c.stream));
@@ -1796,6 +1807,7 @@ static int step_attend(const KvlMlaAttendPlan *plan, const StepPool &pool, const
   a.lscale = pool.lscale;
   a.rope16 = pool.rope16;
   a.softmax_scale = 1.0f / sqrtf(static_cast<float>(cfg.qk_nope_dim + cfg.qk_rope_dim));
+  a.q_dependent = true;  // qabs comes from the absorb kernel just before (absorb or gemm_absorb)
   return attend_common(plan, a, cfg.num_heads, cfg.kv_lora_rank, cfg.qk_rope_dim, s);
 }
 
