@@ -36,6 +36,7 @@
 
 #include "flash_prefill.cuh"
 #include "gemm.cuh"
+#include "pdl.cuh"
 #include "prof.cuh"
 #include "sm100.cuh"
 
@@ -210,6 +211,9 @@ __global__ void __launch_bounds__(kThreads, 1) flash_prefill_kernel(const __grid
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = B->tmem_base;
+  // as a programmatic dependent: every global access comes after the wait
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 8) {
     // ---------------------------------------------------------------- Q and K copies
@@ -556,7 +560,7 @@ static double snake_max_load(const FlashParams &p, int nq, int n_hi, int kpiece,
   return *std::max_element(load.begin(), load.end());
 }
 
-cudaError_t launch_flash_prefill(const FlashParams &p_in, int sms, cudaStream_t stream) {
+cudaError_t launch_flash_prefill(const FlashParams &p_in, int sms, cudaStream_t stream, bool dep) {
   cudaError_t e = cudaFuncSetAttribute(flash_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem);
   if (e != cudaSuccess) return e;
   FlashParams p = p_in;
@@ -588,8 +592,12 @@ cudaError_t launch_flash_prefill(const FlashParams &p_in, int sms, cudaStream_t 
   const int grid = units < sms ? units : sms;
   {
     ProfScope ps("flash_prefill", stream);
-    flash_prefill_kernel<<<grid, kThreads, kSmem, stream>>>(p);
-    e = cudaGetLastError();
+    if (dep) {
+      e = launch_dependent(flash_prefill_kernel, dim3(grid), dim3(kThreads), kSmem, stream, p);
+    } else {
+      flash_prefill_kernel<<<grid, kThreads, kSmem, stream>>>(p);
+      e = cudaGetLastError();
+    }
     if (e != cudaSuccess) return e;
   }
   if (p.kpiece > 0) {

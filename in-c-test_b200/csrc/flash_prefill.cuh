@@ -39,7 +39,9 @@ struct FlashParams {
 // Work units (pieces) a launch may hold when items are cut.
 constexpr int kFlashMaxUnits = 296;
 
-cudaError_t launch_flash_prefill(const FlashParams &p, int sms, cudaStream_t stream);
+// dep: launched as a programmatic dependent of the previous kernel on the
+// stream (the kernel orders all its global accesses after griddepcontrol.wait)
+cudaError_t launch_flash_prefill(const FlashParams &p, int sms, cudaStream_t stream, bool dep = false);
 
 bool make_tmap_3d(CUtensorMap *m, const void *base, CUtensorMapDataType dt, const uint64_t dims[3],
                   const uint64_t strides_bytes[2], const uint32_t box[3], CUtensorMapSwizzle sw);

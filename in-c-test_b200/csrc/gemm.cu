@@ -372,6 +372,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   cluster_sync_all();  // both CTAs' barriers exist before any remote arrival
   tc_fence_after();
   const uint32_t tmem = B->tmem_base;
+  // as a programmatic dependent: every global access comes after the wait
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -497,7 +500,7 @@ cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStrea
 }
 
 template <int BN, int EPI>
-static cudaError_t launch_gemm_pair_t(const GemmParams &p, int sms, cudaStream_t stream, const char *name) {
+static cudaError_t launch_gemm_pair_t(const GemmParams &p, int sms, cudaStream_t stream, const char *name, bool dep) {
   using L = PairLayout<BN>;
   static_assert(L::kSmem <= 232448, "shared memory budget");
   cudaError_t e = cudaFuncSetAttribute(gemm_pair_bf16_tn_kernel<BN, EPI>,
@@ -508,20 +511,22 @@ static cudaError_t launch_gemm_pair_t(const GemmParams &p, int sms, cudaStream_t
   if (pairs > tiles) pairs = tiles;
   if (pairs < 1) pairs = 1;
   ProfScope ps(name, stream);
+  if (dep) return launch_dependent(gemm_pair_bf16_tn_kernel<BN, EPI>, dim3(2 * pairs), dim3(192), L::kSmem, stream, p);
   gemm_pair_bf16_tn_kernel<BN, EPI><<<2 * pairs, 192, L::kSmem, stream>>>(p);
   return cudaGetLastError();
 }
 
 // B's tensor map box must be {64, bn / 2} rows for the pair form.
-cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream, const char *name) {
+cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream, const char *name,
+                             bool dep) {
   if (bn != 256 || p.batch > 1 || p.ksplit > 1) return cudaErrorInvalidValue;
   if (!name) name = epi == EPI_QROPE ? "gemm_qrope" : "gemm_bf16";
   if (epi == EPI_QROPE) {
     if (p.N % 192 != 0) return cudaErrorInvalidValue;
-    return launch_gemm_pair_t<256, EPI_QROPE>(p, sms, stream, name);
+    return launch_gemm_pair_t<256, EPI_QROPE>(p, sms, stream, name, dep);
   }
-  if (epi == EPI_F32) return launch_gemm_pair_t<256, EPI_F32>(p, sms, stream, name);
-  if (epi == EPI_BF16) return launch_gemm_pair_t<256, EPI_BF16>(p, sms, stream, name);
+  if (epi == EPI_F32) return launch_gemm_pair_t<256, EPI_F32>(p, sms, stream, name, dep);
+  if (epi == EPI_BF16) return launch_gemm_pair_t<256, EPI_BF16>(p, sms, stream, name, dep);
   return cudaErrorInvalidValue;
 }
 

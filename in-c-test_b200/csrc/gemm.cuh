@@ -53,7 +53,7 @@ cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStrea
                         const char *name = nullptr, bool dependent = false);
 // CTA-pair (2-SM) form, 256 x bn tiles: B's tensor map box is {64, bn / 2}.
 cudaError_t launch_gemm_pair(const GemmParams &p, int bn, int epi, int sms, cudaStream_t stream,
-                             const char *name = nullptr);
+                             const char *name = nullptr, bool dependent = false);
 cudaError_t launch_rope_table(float2 *cs, int rows, int dim, float theta, cudaStream_t stream);
 // Table rows of two position ranges: row j < split is position pos_a + j, row
 // j >= split position pos_b + j - split.

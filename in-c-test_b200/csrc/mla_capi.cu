@@ -1034,6 +1034,9 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
     CK(cudaStreamWaitEvent(fk->s2, fk->fork, 0));
   }
 
+  // Every kernel below is a programmatic dependent of the one before it on its
+  // stream (each orders its global accesses after griddepcontrol.wait), so a
+  // kernel's launch and set-up overlap the previous one's tail.
   // kva = x Wkva^T, fp32 [S][576], launched first: its 96 tiles (S = 4096) fill
   // 96 SMs for one round, and the q GEMM's CTA pairs take the idle SMs meanwhile.
   // When 3 tiles per 128 rows would leave more than half of the SMs idle (up to
@@ -1053,7 +1056,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   g.N = 576;
   g.c = kva + R0 * 576;
   g.ldc = 576;
-  CK(launch_gemm(g, kva_bn, EPI_F32, sms, st, "gemm_kva"));
+  CK(launch_gemm(g, kva_bn, EPI_F32, sms, st, "gemm_kva", true));
   // q = x Wq^T with RoPE on each head's last 64 columns, bf16 [S][16][192]
   // (on the second stream when forked, after the RoPE table)
   GemmParams gq;
@@ -1071,7 +1074,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   gq.rope_cs = cs + R0 * 32;
   if (r0 == 0) CK(launch_rope_table(cs, S, 64, cfg.rope_theta, sq));
   if (fork) CK(cudaEventRecord(fk->rope, sq));
-  CK(launch_gemm_pair(gq, 256, EPI_QROPE, sms, sq, "gemm_q"));
+  CK(launch_gemm_pair(gq, 256, EPI_QROPE, sms, sq, "gemm_q", true));
   if (fork) CK(cudaEventRecord(fk->qdone, sq));
 
   // latent = rmsnorm(kva[:512]) * kv_a_norm, k_rope = rope(kva[512:]) -> pool [S][576] bf16
@@ -1087,7 +1090,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   g.K = 512;
   g.c = kv + R0 * 4096;
   g.ldc = 4096;
-  CK(launch_gemm_pair(g, 256, EPI_BF16, sms, st, "gemm_kvb"));
+  CK(launch_gemm_pair(g, 256, EPI_BF16, sms, st, "gemm_kvb", true));
   if (fork) CK(cudaStreamWaitEvent(st, fk->qdone, 0));  // join the second stream
   // causal attention of the queries [r0, r1) over the keys [0, r1) -> o bf16 [S][16][128]
   FlashParams f;
@@ -1109,7 +1112,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   f.scale_log2 = (1.0f / sqrtf(192.0f)) * 1.4426950408889634f;
   f.out = reinterpret_cast<__nv_bfloat16 *>(o);
   f.err = err;
-  CK(launch_flash_prefill(f, sms, st));
+  CK(launch_flash_prefill(f, sms, st, true));
   // out = o Wo^T, fp32 [S][H]
   // (CTA-pair GEMM: 256 x 256 tiles, each CTA of a pair loads 128 rows of Wo)
   if (!bf16_map(&g.tm_a, o + R0 * 2048, 2048, m, 2048 * 2, 128) ||
@@ -1122,7 +1125,7 @@ int prefill_fast(int sms, const KvlMlaConfig &cfg, const DevW &W, float *d_out, 
   g.c = d_out + R0 * H;
   g.ldc = static_cast<int>(H);
   g.rope_cs = nullptr;
-  CK(launch_gemm_pair(g, 256, EPI_F32, sms, st, "gemm_o"));
+  CK(launch_gemm_pair(g, 256, EPI_F32, sms, st, "gemm_o", true));
   return 0;
 }
 

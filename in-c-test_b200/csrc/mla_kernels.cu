@@ -360,6 +360,8 @@ __global__ void append_bf16_kernel(uint16_t *kv, long long row0, const float *ka
 __global__ void append_rows_bf16_kernel(uint16_t *pool, const float *ka, const uint16_t *norm_w,
                                         const float2 *cs, int n, float eps, int parts, long long part_stride) {
   constexpr int R = 512, DR = 64;
+  pdl_wait();
+  pdl_trigger();
   const int warp = static_cast<int>((blockIdx.x * static_cast<unsigned>(blockDim.x) + threadIdx.x) >> 5);
   const int lane = threadIdx.x & 31;
   if (warp >= n) return;
@@ -419,8 +421,8 @@ cudaError_t append_rows_bf16(uint16_t *pool, const float *ka, const uint16_t *no
   if (n <= 0) return cudaSuccess;
   if (parts < 1) return cudaErrorInvalidValue;
   ProfScope ps("append_bf16", s);
-  append_rows_bf16_kernel<<<(n + 7) / 8, 256, 0, s>>>(pool, ka, norm_w, cs, n, eps, parts, part_stride);
-  return cudaGetLastError();
+  return launch_dependent(append_rows_bf16_kernel, dim3((n + 7) / 8), dim3(256), 0, s, pool, ka, norm_w, cs, n, eps,
+                          parts, part_stride);
 }
 
 // q = sum of split-K partial products [parts][n][16 * 192] fp32 with RoPE on
