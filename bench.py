@@ -634,9 +634,36 @@ class Prefill:
             call()
         dt = (time.perf_counter() - t0) * 1e3 / K_steps
         dt = self.dist.max(torch, dt)
+        # The same call with the runtime's own kind of buffers: x and out in
+        # pageable (malloc'd) memory and the layer's weights uploaded on every
+        # call (no trunk cache).
+        x_page = np.array(x, copy=True)
+        out_page = np.empty_like(out)
+        wbytes = int(sum(a.nbytes for a in self.w_host))
+        lib.kvl_mla_cuda_weight_cache(0)
+        try:
+            def call_page():
+                rc = lib.kvl_mla_prefill_bf16(K.ptr(out_page, K.f32p), K.ptr(x_page, K.f32p), self.S,
+                                              C.byref(self.cfg), C.byref(hw.c))
+                if rc != 0:
+                    raise RuntimeError(K.last_error())
+            for _ in range(min(W_steps, 2)):
+                call_page()
+            self.dist.barrier()
+            t0 = time.perf_counter()
+            for _ in range(K_steps):
+                call_page()
+            dtp = self.dist.max(torch, (time.perf_counter() - t0) * 1e3 / K_steps)
+        finally:
+            lib.kvl_mla_cuda_weight_cache(1)
         return {"value": self.value(dt), "unit": self.unit, "ms_per_step": dt,
                 "h2d_bytes_per_step": int(x.nbytes), "d2h_bytes_per_step": int(out.nbytes),
-                "path": "kvl_mla_prefill_bf16 (host fp32 in/out)"}
+                "path": "kvl_mla_prefill_bf16 (host fp32 in/out)",
+                "pageable_uncached": {"value": self.value(dtp), "unit": self.unit, "ms_per_step": dtp,
+                                      "h2d_bytes_per_step": int(x.nbytes) + wbytes,
+                                      "d2h_bytes_per_step": int(out.nbytes),
+                                      "path": "kvl_mla_prefill_bf16, x and out in pageable host memory, the "
+                                              "layer's weights uploaded on every call (no weight cache)"}}
 
     def _e2e_cp(self, K_steps, W_steps):
         import kvl_b200.parallel as PAR

@@ -38,6 +38,7 @@ constexpr int kStages = 4;
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr uint32_t kABytes = kBM * kBK * 2;  // 16 KB
+constexpr uint32_t kBMnBox = kBK * 64 * 2;     // MN-major B box: 64 K rows x 64 N columns, 8 KB
 
 template <int BN>
 struct Layout {
@@ -176,10 +177,13 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
       const int z = tile / tiles_mn, nb = (tile % tiles_mn) / tiles_m;
       const int kbeg = batched ? 0 : z * kc;
       for (int ks = kbeg; ks < kbeg + kc; ++ks) {
-        if (batched)
+        if (batched && p.b_mn) {
+          for (int j = 0; j < BN / 64; ++j) tma_prefetch_l2_3d(&p.tm_b, nb * BN + 64 * j, ks * kBK, z);
+        } else if (batched) {
           tma_prefetch_l2_3d(&p.tm_b, ks * kBK, nb * BN, z);
-        else
+        } else {
           tma_prefetch_l2_2d(&p.tm_b, ks * kBK, nb * BN);
+        }
       }
     }
   }
@@ -227,7 +231,13 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
           mbar_arrive_expect_tx(&B->full[s], L::kStageBytes);
           if (batched) {
             tma_load_3d(st, &p.tm_a, &B->full[s], ks * kBK, mb * kBM, z);
-            tma_load_3d(st + kABytes, &p.tm_b, &B->full[s], ks * kBK, nb * BN, z);
+            if (p.b_mn) {
+              // BN / 64 boxes of [64 K rows][64 N columns], kBMnBox bytes apart
+              for (int j = 0; j < BN / 64; ++j)
+                tma_load_3d(st + kABytes + j * kBMnBox, &p.tm_b, &B->full[s], nb * BN + 64 * j, ks * kBK, z);
+            } else {
+              tma_load_3d(st + kABytes, &p.tm_b, &B->full[s], ks * kBK, nb * BN, z);
+            }
           } else {
             tma_load_2d(st, &p.tm_a, &B->full[s], ks * kBK, mb * kBM);
             tma_load_2d(st + kABytes, &p.tm_b, &B->full[s], ks * kBK, nb * BN);
@@ -243,7 +253,9 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_f16(1, 1, 0, 0, kBM, BN);
+      constexpr uint32_t idesc_k = idesc_f16(1, 1, 0, 0, kBM, BN), idesc_mn = idesc_f16(1, 1, 0, 1, kBM, BN);
+      const bool b_mn = batched && p.b_mn;
+      const uint32_t idesc = b_mn ? idesc_mn : idesc_k;
       uint32_t it = 0, lt = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++lt) {
@@ -260,10 +272,15 @@ __global__ void __launch_bounds__(192, 1) gemm_bf16_tn_kernel(const __grid_const
           const uint32_t a_addr = s_base + s * L::kStageBytes;
           const uint32_t b_addr = a_addr + kABytes;
 #pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk)
-            mma_f16_ss(tmem + ab * L::kAccCols, smem_desc(a_addr + kk * 32, 16, 1024, LAYOUT_SW128),
-                       smem_desc(b_addr + kk * 32, 16, 1024, LAYOUT_SW128), idesc,
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            // MN-major B: K step kk is rows 16 kk.. of every box (2048 bytes
+            // in), the boxes (64 N columns each) kBMnBox apart, 8-row groups
+            // 1024 bytes apart
+            const uint64_t bd = b_mn ? smem_desc(b_addr + kk * 2048, kBMnBox, 1024, LAYOUT_SW128)
+                                     : smem_desc(b_addr + kk * 32, 16, 1024, LAYOUT_SW128);
+            mma_f16_ss(tmem + ab * L::kAccCols, smem_desc(a_addr + kk * 32, 16, 1024, LAYOUT_SW128), bd, idesc,
                        (ks != kbeg || kk) ? 1u : 0u);
+          }
           mma_commit(&B->empty[s]);
         }
         if (ok) mma_commit(&B->acc_full[ab]);
@@ -478,6 +495,7 @@ cudaError_t launch_gemm(const GemmParams &p, int bn, int epi, int sms, cudaStrea
   if (!name) name = epi == EPI_QROPE ? "gemm_qrope" : "gemm_bf16";
   if (p.ksplit > 1 && (p.batch > 1 || epi != EPI_F32 || ((p.K + kBK - 1) / kBK) % p.ksplit != 0))
     return cudaErrorInvalidValue;
+  if (p.b_mn && p.batch <= 1) return cudaErrorInvalidValue;
   if (epi == EPI_QROPE) {
     if (p.N % 192 != 0 || p.batch > 1) return cudaErrorInvalidValue;
     if (bn == 256) return launch_gemm_t<256, EPI_QROPE>(p, sms, stream, name, dep);

@@ -34,6 +34,9 @@ struct GemmParams {
   // 1-SM kernel: B is a weight that no kernel before it on the stream writes;
   // the CTA's B boxes are prefetched into L2 before griddepcontrol.wait
   int prefetch_b;
+  // 1-SM kernel, batch > 1: B is stored MN-major ([K][N] per product, N
+  // contiguous; 3D map {N, K, batch}, box {64, 64, 1}), BN / 64 boxes per stage
+  int b_mn;
 };
 
 // The physical 128-row tile of logical tile t in the zigzag all-gather layout

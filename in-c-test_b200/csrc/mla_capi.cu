@@ -1732,14 +1732,14 @@ static int pick_split(int ksteps, int want) {
 // (kStepQSplit partials on the tensor-core path), [1] ka fp32 [B][R+DR] (matvec path),
 // [2] qabs fp32 [B][NH][R+DR], [3] mix fp32 [B][NH][R], [4] ho fp32 [B][NH*DV]
 // (bf16 on the tensor-core path), [5] x bf16 [B][H], [6] q_nope bf16
-// [NH][B][DN], [7] W_UK^T bf16 [NH][R][DN], [8] mix bf16 [NH][B][R],
+// [NH][B][DN], [7] unused (0 bytes), [8] mix bf16 [NH][B][R],
 // [9] kv_a partials [kStepKvaSplit][B][R+DR], [10] o_proj partials
 // [kStepOSplit][B][H].
 static size_t step_ws_layout(const KvlMlaConfig &c, int B, size_t off[12]) {
   const size_t NH = c.num_heads, QD = c.qk_nope_dim + c.qk_rope_dim, R = c.kv_lora_rank, DR = c.qk_rope_dim;
   const size_t DV = c.v_head_dim, DN = c.qk_nope_dim, H = c.hidden_size;
   const size_t sz[11] = {kStepQSplit * B * NH * QD * 4, B * (R + DR) * 4, B * NH * (R + DR) * 4, B * NH * R * 4,
-                         B * NH * DV * 4, B * H * 2, B * NH * DN * 2, NH * R * DN * 2, B * NH * R * 2,
+                         B * NH * DV * 4, B * H * 2, B * NH * DN * 2, 0, B * NH * R * 2,
                          kStepKvaSplit * B * (R + DR) * 4, kStepOSplit * B * H * 4};
   size_t o = 0;
   for (int i = 0; i < 11; ++i) {
@@ -1826,7 +1826,6 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   uint16_t *hob = reinterpret_cast<uint16_t *>(ws + off[4]);
   uint16_t *xb = reinterpret_cast<uint16_t *>(ws + off[5]);
   uint16_t *qn = reinterpret_cast<uint16_t *>(ws + off[6]);
-  uint16_t *wukT = reinterpret_cast<uint16_t *>(ws + off[7]);
   uint16_t *mixb = reinterpret_cast<uint16_t *>(ws + off[8]);
   float *ka_parts = reinterpret_cast<float *>(ws + off[9]);
   float *o_parts = reinterpret_cast<float *>(ws + off[10]);
@@ -1835,12 +1834,10 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
 
   CK(bf16_rne(xb, d_x, static_cast<long long>(b * H), s));
-  CK(wuk_transpose(wukT, w.kv_b_proj, static_cast<int>(NH), static_cast<int>(DN), static_cast<int>(DV),
-                   static_cast<int>(R), s));
   GemmParams g;
   memset(&g, 0, sizeof g);
   g.err = plan->dp.err_word();  // a bounded wait that ran out: reported by kvl_mla_attend_check
-  g.prefetch_b = 1;             // q_proj, kv_a_proj, W_UV and o_proj are weights
+  g.prefetch_b = 1;             // every B operand of the step is a weight
   // q = x Wq^T fp32 [B][NH*QD]; ka = x Wkva^T fp32 [B][R+DR]
   if (!bf16_map(&g.tm_a, xb, H, b, H * 2, 128) || !bf16_map(&g.tm_b, w.q_proj, H, NH * QD, H * 2, 256)) {
     set_err("decode step: tensor map (q_proj)");
@@ -1872,13 +1869,16 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   g.c_bstride = 0;
   CK(q_split(qn, qabs, q, q_parts, static_cast<long long>(b * NH * QD), B, static_cast<int>(NH),
              static_cast<int>(DN), static_cast<int>(DR), static_cast<int>(R), cfg.rope_theta, d_pos, s));
-  // qabs[:, h, :R] = q_nope[:, h] . W_UK[h]   (NH products, M = B, N = R, K = DN)
+  // qabs[:, h, :R] = q_nope[:, h] . W_UK[h]   (NH products, M = B, N = R, K = DN);
+  // W_UK[h] ([DN][R], rows h (DN + DV) + d of kv_b_proj) is read in place as
+  // an MN-major B operand
   {
     const uint64_t ad[3] = {DN, b, NH}, as[2] = {DN * 2, b * DN * 2};
-    const uint64_t bd[3] = {DN, R, NH}, bs[2] = {DN * 2, R * DN * 2};
-    const uint32_t abox[3] = {64, 128, 1}, bbox[3] = {64, 256, 1};
+    const uint64_t bd[3] = {R, DN, NH}, bs[2] = {R * 2, (DN + DV) * R * 2};
+    const uint32_t abox[3] = {64, 128, 1}, bbox[3] = {64, 64, 1};
     if (!make_tmap_3d(&g.tm_a, qn, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, ad, as, abox, CU_TENSOR_MAP_SWIZZLE_128B) ||
-        !make_tmap_3d(&g.tm_b, wukT, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, bd, bs, bbox, CU_TENSOR_MAP_SWIZZLE_128B)) {
+        !make_tmap_3d(&g.tm_b, w.kv_b_proj, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, bd, bs, bbox,
+                      CU_TENSOR_MAP_SWIZZLE_128B)) {
       set_err("decode step: tensor map (absorb)");
       return -1;
     }
@@ -1889,9 +1889,9 @@ static int decode_step_gemm(const KvlMlaConfig &cfg, const KvlMlaDeviceWeights &
   g.ldc = static_cast<int>(NH * (R + DR));
   g.batch = static_cast<int>(NH);
   g.c_bstride = static_cast<long long>(R + DR);
-  g.prefetch_b = 0;  // W_UK^T is written by this step
+  g.b_mn = 1;
   CK(launch_gemm(g, 256, EPI_F32, sms, s, "gemm_absorb", true));
-  g.prefetch_b = 1;
+  g.b_mn = 0;
 
   if (step_attend(plan, pool, cfg, mix, qabs, rows, s) != 0) return -1;
 

@@ -830,33 +830,6 @@ cudaError_t mix_heads_bf16(uint16_t *out, const float *mix, int n, int NH, int R
   return launch_dependent(mix_heads_bf16_kernel, dim3(grid), dim3(256), 0, s, out, mix, n, NH, R);
 }
 
-// W_UK of every head (kv_b_proj rows h*(DN+DV) + d, d < DN: [d][R]) ->
-// wukT [h][R][DN], the K-major B operand of q_nope . W_UK.  32 x 32 tiles
-// through shared memory; grid (ceil(R/32), ceil(DN/32), NH), 32 x 8 threads.
-__global__ void wuk_transpose_kernel(uint16_t *wukT, const uint16_t *kvb, int DN, int DV, int R) {
-  __shared__ uint16_t tile[32][33];
-  pdl_wait();
-  pdl_trigger();
-  const int h = blockIdx.z, r0 = blockIdx.x * 32, d0 = blockIdx.y * 32;
-  const uint16_t *src = kvb + static_cast<size_t>(h) * (DN + DV) * R;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int d = d0 + i, r = r0 + threadIdx.x;
-    if (d < DN && r < R) tile[i][threadIdx.x] = src[static_cast<size_t>(d) * R + r];
-  }
-  __syncthreads();
-  uint16_t *dst = wukT + static_cast<size_t>(h) * R * DN;
-  for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-    const int r = r0 + i, d = d0 + threadIdx.x;
-    if (d < DN && r < R) dst[static_cast<size_t>(r) * DN + d] = tile[threadIdx.x][i];
-  }
-}
-
-cudaError_t wuk_transpose(uint16_t *wukT, const uint16_t *kvb, int NH, int DN, int DV, int R, cudaStream_t s) {
-  ProfScope ps("wuk_transpose", s);
-  return launch_dependent(wuk_transpose_kernel, dim3((R + 31) / 32, (DN + 31) / 32, NH), dim3(32, 8), 0, s, wukT, kvb,
-                          DN, DV, R);
-}
-
 // --------------------------------------------------------------------- Q8 helpers
 __global__ void quantize_rows_kernel(int8_t *q, float *scale, const float *x, int R) {
   extern __shared__ float sh[];

@@ -36,7 +36,6 @@ cudaError_t q_split(uint16_t *qn, float *qabs, const float *q, int parts, long l
                     int DN, int DR, int R, float theta, const int *pos_of, cudaStream_t s);
 cudaError_t sum_parts(float *dst, const float *src, int parts, long long stride, long long n, cudaStream_t s);
 cudaError_t mix_heads_bf16(uint16_t *out, const float *mix, int n, int NH, int R, cudaStream_t s);
-cudaError_t wuk_transpose(uint16_t *wukT, const uint16_t *kvb, int NH, int DN, int DV, int R, cudaStream_t s);
 cudaError_t quantize_rows(int8_t *q, float *scale, const float *x, int rows, int R, cudaStream_t s);
 cudaError_t dequant(float *out, const int8_t *q, const float *scale, long long rows, int R, cudaStream_t s);
 cudaError_t bf16_rne(uint16_t *out, const float *x, long long n, cudaStream_t s);
